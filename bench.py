@@ -1,0 +1,320 @@
+"""Benchmark of tbf16's hot path on B200: the scaled bf16-on-fp16 GEMM (the
+headline M = N = K = 8192 case) through the library's C ABI.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one scaled linear y = x @ W^T over the synthetic config-2 input (x: bf16 [8192, 8192] with
+log-uniform row magnitudes 2^-16..2^20 and 2% outlier channels x 2^12; W: N(0, 1/K), prepared once as
+fp16 + row scales, as tbf16.convert stores it): the row-amax -> exponent kernel, then the tcgen05 GEMM.
+Under torchrun each rank runs its own 8192-row shard against the replicated weight (M-sharded,
+no collective: "weak" scaling). Inputs (384 MB per step) exceed the 126 MB L2.
+
+One JSON line on rank 0: value = whole-job TFLOPS (device time, CUDA events, max over ranks);
+e2e = the same through the C ABI with the x upload from pinned host memory and the y download
+inside the timed region; roofline = the GEMM kernel's own CUDA-event time against the measured bf16
+tensor peak; cpu_baseline = the reference's torch-level algorithm (oracle port) on the host cores.
+--impl reference times that CPU implementation alone (the reference has no B200 path of its own).
+"""
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "turing-bf16_b200"))
+sys.path.insert(0, str(ROOT / "tests" / "golden"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+M_DEFAULT = N_DEFAULT = K_DEFAULT = 8192
+METRIC = "scaled GEMM TFLOPS (M=N=K=8192, config 2) & % of dense fp16 tensor peak"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "tflops_sustained": d.get("bf16_tflops_sustained"),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+# ----------------------------------------------------------------------------- CPU baseline (oracle port)
+
+def cpu_linear_sample(x, w16, ws, rows):
+    """The reference's torch-level linear on CPU for a sample of rows (tbf16/ops.py:163-178 with the
+    fused path's t=15 max row scales): quantize rows (oracle C port), torch CPU fp16 GEMM, epilogue."""
+    from oracle import oracle as orc
+    xs = x[:rows]
+    x16, sx = orc.quantize_rows(xs, 15, l1=False)
+    c = x16 @ w16.t()
+    return ((c.float() * sx[:, None]) * ws[None, :]).bfloat16()
+
+
+def run_cpu_reference(M, N, K, steps, warmup, rows=256):
+    """Time the CPU implementation on `rows`-row samples of the workload; returns (TFLOPS, sample text)."""
+    import inputs
+    from oracle import oracle as orc
+    orc.lib()
+    threads = torch.get_num_threads()
+    x = inputs.gemm_x(rows, K, seed=0)
+    w = inputs.gemm_w(N, K, seed=1)
+    w16, ws = orc.prepare_weight(w)
+    for _ in range(max(1, warmup)):
+        cpu_linear_sample(x, w16, ws, rows)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_linear_sample(x, w16, ws, rows)
+    dt = time.perf_counter() - t0
+    tflops = 2.0 * rows * N * K * steps / dt / 1e12
+    return tflops, threads, f"{rows} rows x N={N} x K={K} per step, {steps} steps ({dt:.1f} s), torch CPU fp16 GEMM"
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--M", type=int, default=M_DEFAULT)
+    ap.add_argument("--N", type=int, default=N_DEFAULT)
+    ap.add_argument("--K", type=int, default=K_DEFAULT)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_init() if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
+                                                                  int(os.environ.get("RANK", "0")), 0)
+    M, N, K = args.M, args.N, args.K
+    config = {"workload": "scaled_linear (row-amax exponent + tcgen05 GEMM), BASELINE config 2", "M_per_rank": M,
+              "N": N, "K": K, "global_M": M * world, "parallelism": f"M-sharded x{world} (no collective)",
+              "l2": "inputs larger than L2 (384 MB per step)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        tflops, threads, sample = run_cpu_reference(M, N, K, args.steps, args.warmup)
+        line = {"metric": METRIC, "value": round(tflops, 4), "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp16 operands, fp32 accumulation", "data": "synthetic (config 2 distribution)",
+                "config": config, "impl": "reference",
+                "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(tflops, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import inputs
+    from tbf16 import _ext as E
+    from tbf16 import ops
+    dev = torch.device("cuda", torch.cuda.current_device())
+    pk = peaks()
+    # inputs resident in HBM; each rank its own seed (its own rows)
+    x = inputs.gemm_x(M, K, seed=100 + rank, device=dev)
+    w = inputs.gemm_w(N, K, seed=1, device=dev)
+    w16, ws = ops.prepare_weight(w)
+    del w
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    s_inv = torch.empty(M, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    L = E.lib()
+
+    def row_scale():
+        return L.tbf16_row_scale(E.ptr(x), M, K, K, 15, 0, E.ptr(s_inv), None, sp)
+
+    def gemm():
+        return L.tbf16_linear_scaled(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N, E.ptr(s_inv), sp)
+
+    def step():
+        a = row_scale()
+        b = gemm()
+        if a or b:
+            raise RuntimeError(f"launch failed: {a} {b}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # per-kernel timing: events around each launch of every step, on the launching stream
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            if row_scale():
+                raise RuntimeError("row_scale failed")
+            ev[i][1].record(stream)
+            if gemm():
+                raise RuntimeError("gemm failed")
+            ev[i][2].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = max_over_ranks(start.elapsed_time(end), world)
+    rs_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    gemm_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    flop = 2.0 * M * N * K
+    value = flop * world * args.steps / (total_ms / 1e3) / 1e12
+    gemm_tflops = flop / (gemm_ms / 1e3) / 1e12
+    rs_gbs = (2.0 * M * K + 4.0 * M) / (rs_ms / 1e3) / 1e9
+    if E.device_status():
+        raise RuntimeError("a kernel reported a timeout")
+
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 operands (exact pow2-scaled bf16), fp32 accumulate, bf16 out",
+            "data": "synthetic (config 2 distribution, seeded)", "config": config,
+            "gpu_launches": 2 * args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
+                         "frac": round(gemm_tflops / pk["tflops"], 4), "traffic": None,
+                         "peak_source": f"{pk['source']} bf16 dense (burst); sustained {pk['tflops_sustained']}",
+                         "kernel": "scaled_gemm_kernel (tcgen05, fused bf16->fp16 converter)",
+                         "ms_per_launch": round(gemm_ms, 4)},
+            "row_amax_kernel": {"ms": round(rs_ms, 4), "achieved_gbs": round(rs_gbs, 1), "peak_gbs": pk["hbm_gbs"],
+                                "frac": round(rs_gbs / pk["hbm_gbs"], 4), "bytes": 2 * M * K + 4 * M},
+            "clocks": clocks.summary()}
+
+    if not args.no_e2e:
+        line["e2e"] = e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
+        line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world):
+    """Same metric through the public C ABI call (tbf16_linear), with x uploaded from pinned host memory
+    and y read back each step inside the timed region."""
+    from tbf16 import _ext as E
+    hx = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
+    hx.copy_(x.cpu())
+    hy = torch.empty(M, N, dtype=torch.bfloat16, pin_memory=True)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    L = E.lib()
+
+    def step():
+        x.copy_(hx, non_blocking=True)
+        st = L.tbf16_linear(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N, E.ptr(s_inv), 15, 0, sp)
+        if st:
+            raise RuntimeError(f"tbf16_linear failed: {st}")
+        hy.copy_(y, non_blocking=True)
+
+    steps = max(3, args.steps // 3)
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e), world)
+    return {"value": round(2.0 * M * N * K * world * steps / (ms / 1e3) / 1e12, 3), "unit": "TFLOPS",
+            "h2d_bytes_per_step": 2 * M * K, "d2h_bytes_per_step": 2 * M * N, "steps": steps,
+            "ms_per_step": round(ms / steps, 3), "path": "tbf16_linear via ctypes, pinned host buffers"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,148 @@
+/*
+ * libtbf16_sm100 -- C ABI of the B200 (sm_100a) kernels behind tbf16's scaled bf16-on-fp16 path.
+ *
+ * Conventions
+ *   - Plain pointers to device memory, sizes and strides in ELEMENTS, an explicit CUDA stream
+ *     (a cudaStream_t passed as void*; NULL = the legacy default stream). Every call is
+ *     asynchronous on that stream and never synchronises the host.
+ *   - The library never allocates or frees device memory: outputs and any workspace are passed in.
+ *   - bf16 / fp16 tensors are passed as void* holding 16-bit values; dtype codes below.
+ *   - Returns 0 (TBF16_OK) or a status code. Argument checks (shape, alignment, dtype) happen on
+ *     the host before any launch; a kernel that gives up on a bounded wait records it in a device
+ *     word read by tbf16_device_status().
+ *   - Requires an sm_100 device (B200). The reference's compute_75 kernels are replaced, not wrapped.
+ *
+ * Each entry point names the reference interface it replaces (tech-cosmos/turing-bf16; paths relative
+ * to that project's root).
+ */
+#ifndef TBF16_SM100_H
+#define TBF16_SM100_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum tbf16_status {
+  TBF16_OK = 0,
+  TBF16_ERR_INVALID = 1,     /* bad shape / stride / argument */
+  TBF16_ERR_ALIGN = 2,       /* pointer or leading dimension not aligned for 16-byte / TMA access */
+  TBF16_ERR_DTYPE = 3,       /* unsupported dtype code */
+  TBF16_ERR_LAUNCH = 4,      /* CUDA launch or runtime error */
+  TBF16_ERR_DEVICE = 5,      /* not an sm_100 device */
+  TBF16_ERR_UNSUPPORTED = 6, /* a valid request this build does not implement */
+  TBF16_ERR_TIMEOUT = 7      /* a kernel gave up on a bounded wait (see tbf16_device_status) */
+};
+
+enum tbf16_dtype { TBF16_BF16 = 0, TBF16_F16 = 1 };
+
+/* ------------------------------------------------------------------ library */
+
+/* ABI version (major * 100 + minor). */
+int tbf16_abi_version(void);
+/* Human-readable text for a status code. */
+const char* tbf16_status_string(int status);
+/* TBF16_OK if `device` is an sm_100 GPU this build runs on. */
+int tbf16_device_check(int device);
+/* Bits set by kernels on the current device since the last reset (1 = a bounded wait timed out,
+ * 2 = attention backward produced a non-finite value). Synchronises the device; reset != 0 clears. */
+int tbf16_device_status(unsigned int* bits, int reset);
+
+/* ------------------------------------------------------------------ row / column power-of-two scales */
+
+/* Row scales of the fused GEMM's pre-pass. Replaces row_scale(x, t, l1)
+ * (tbf16/csrc/gemm_sm75.cu:243-253, kernel :27-47). x: bf16 [rows, K], row stride ldx.
+ * s_inv[r] = 1 / s[r], s[r] = 2^(min(253 + t - e, 254) - 127) with e the clamped biased exponent of
+ * the row max (l1 = 0) or L1 norm (l1 = 1). exp_out (nullable): int8 log2(s[r]). t must be >= 0. */
+int tbf16_row_scale(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, float* s_inv,
+                    int8_t* exp_out, void* stream);
+
+/* Row quantisation. Replaces quantize_rows(x, t, l1) (tbf16/csrc/small_kernels.cu:275-287, kernel
+ * :35-74; Python tbf16/ops.py:74-89). y16 = fp16_rn(x * s[r]) with s from small_kernels.cu:12-18
+ * (row amax or L1 norm into [2^(t-1), 2^t)); s_inv = 1 / s. y16 row stride ldy. */
+int tbf16_quantize_rows(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, void* y16,
+                        int64_t ldy, float* s_inv, void* stream);
+
+/* Column quantisation. Replaces quantize_cols(x, t, row_mul) (tbf16/csrc/small_kernels.cu:318-340,
+ * kernels :136-184; Python tbf16/autograd.py:26-36). amax[c] = max_r |x[r,c]| * |row_mul[r]|,
+ * s[c] from small_kernels.cu:12-18, y16 = fp16_rn(x * row_mul[r] * s[c]) (row stride ldy), s_inv[c] = 1/s[c].
+ * row_mul nullable. amax_ws: workspace of K floats (overwritten). rows == 0 gives s_inv = 1. */
+int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, const float* row_mul,
+                        void* y16, int64_t ldy, float* s_inv, float* amax_ws, void* stream);
+
+/* ------------------------------------------------------------------ attention scales */
+
+/* Per-(b, h) amax of a strided (B, H, S, D) tensor with contiguous D. Replaces head_amax(x)
+ * (tbf16/csrc/small_kernels.cu:342-359, kernel :221-243). amax: fp32 [B*H], overwritten. */
+int tbf16_head_amax(const void* x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb, int64_t sh,
+                    int64_t ss, float* amax, void* stream);
+
+/* head_exp (tbf16/attention.py:24-27): e[b*H+h] = frexp exponent of amax (0 for all-zero heads).
+ * amax_ws: workspace of B*H floats. */
+int tbf16_head_exp(const void* x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb, int64_t sh,
+                   int64_t ss, int32_t* e, float* amax_ws, void* stream);
+
+/* y (contiguous B, H, S, D) = cast(x * 2^e[b, h]). Replaces head_scale_cast(x, e, dtype)
+ * (tbf16/csrc/small_kernels.cu:361-379, kernel :246-263; Python attention.py:30-35). e is int32
+ * indexed e[b * e_sb + h * e_sh] (broadcast strides may be 0). */
+int tbf16_head_scale_cast(const void* x, int in_dtype, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb,
+                          int64_t sh, int64_t ss, const int32_t* e, int64_t e_sb, int64_t e_sh, void* y, int out_dtype,
+                          void* stream);
+
+/* prepare_qkv (tbf16/attention.py:38-48) on the device, no host sync: eq, ek = max over (b, h) of the
+ * frexp exponents of q and k head maxima; a = clamp(floor((ek - eq) / 2), ek - 14, 14 - eq);
+ * ev[b, hk] = head_exp(v) - v_exp; q16 = fp16(q * 2^a), k16 = fp16(k * 2^-a), v16 = fp16(v * 2^-ev),
+ * all contiguous (B, H, S, D). q is (B, Hq, Sq, D), k and v (B, Hkv, Sk, D), each with its own
+ * strides (sb, sh, ss) and contiguous D. a_out: one int32; ev_out: int32 [B*Hkv].
+ * ws: workspace of (B*Hq + 2*B*Hkv) floats. */
+int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb, int64_t ksh,
+                      int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B, int64_t Hq,
+                      int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int v_exp, void* q16, void* k16, void* v16,
+                      int32_t* a_out, int32_t* ev_out, float* ws, void* stream);
+
+/* ------------------------------------------------------------------ scaled GEMMs (tcgen05) */
+
+/* Fused scaled linear. Replaces linear(x, w16, ws, bias, cfg, t, l1) (tbf16/csrc/gemm_sm75.cu:257-284,
+ * kernel :78-226) and, since the cuBLAS small-M branch is gone, scaled_linear for every M
+ * (tbf16/ops.py:153-164). x bf16 [M, K] (row stride ldx); w16 fp16 [N, K] (ldw); ws fp32 [N];
+ * bias bf16 [N] or NULL; y bf16 [M, N] (ldy).
+ *   s_inv[m] = row_scale(x, t, l1)                           (written to x_sinv, M floats)
+ *   y[m, n]  = bf16_rn((sum_k fp16(x[m,k] / s_inv[m]) * w16[n,k]) * s_inv[m] * ws[n] + bias[n])
+ * with fp32 accumulation in TMEM and no fp16 rounding of the product. K, N, ldx, ldw multiples of 8. */
+int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
+                 const float* ws, const void* bias, void* y, int64_t ldy, float* x_sinv, int target_exp, int l1,
+                 void* stream);
+
+/* The GEMM half of tbf16_linear with the row scales given (x_sinv: M powers of two, e.g. from
+ * tbf16_row_scale or from a producer kernel that already knows its rows' maxima). Same semantics as the
+ * reference's gemm_kernel (tbf16/csrc/gemm_sm75.cu:78-226) launched after its row_scale pre-pass. */
+int tbf16_linear_scaled(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
+                        const float* ws, const void* bias, void* y, int64_t ldy, const float* x_sinv, void* stream);
+
+/* Scaled fp16 GEMM with a bf16 epilogue: y[m, n] = bf16_rn((sum_k A[m,k] B[n,k]) * sa[m] * sb[n] + bias[n]).
+ * Replaces the cuBLAS GEMM + epilogue pair of linear_q (tbf16/ops.py:167-178, small_kernels.cu:289-302)
+ * and _scaled_mm (tbf16/autograd.py:114-120), i.e. the training dX and dW contractions.
+ * A is a16 [M, K] (a_mn = 0, row stride lda) or a16 [K, M] (a_mn = 1); B is b16 [N, K] (b_mn = 0)
+ * or b16 [K, N] (b_mn = 1). sb and bias nullable. Contiguous dimensions and leading dimensions
+ * must be multiples of 8. */
+int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int b_mn, int64_t ldb, int64_t M, int64_t N,
+                   int64_t K, const float* sa, const float* sb, const void* bias, void* y, int64_t ldy, void* stream);
+
+/* ------------------------------------------------------------------ scaled attention (tcgen05) */
+
+/* Flash-attention forward on the fp16 copies from tbf16_prepare_qkv. Replaces the torch fp16 SDPA call of
+ * the reference's sdpa (tbf16/attention.py:63-65) and the efficient-attention forward of ScaledSDPAFn
+ * (tbf16/autograd.py:159-164). q16 (B, Hq, Sq, D), k16 and v16 (B, Hkv, Sk, D), contiguous fp16; GQA by
+ * Hq / Hkv. out (B, Hq, Sq, D) bf16 = bf16_rn(softmax(scale * q16 k16^T + mask) v16 * 2^ev[b, h / (Hq/Hkv)]);
+ * causal keeps key j <= query i (top-left). mask: optional additive fp16 bias, element (b, h, i, j) at
+ * b*mask_sb + h*mask_sh + i*mask_sq + j (strides may be 0 to broadcast). lse (nullable): fp32 (B*Hq*Sq)
+ * natural-log logsumexp of the scaled, masked logits. D in {64, 128}. */
+int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                   int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev, const void* mask, int64_t mask_sb,
+                   int64_t mask_sh, int64_t mask_sq, void* out, float* lse, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TBF16_SM100_H */

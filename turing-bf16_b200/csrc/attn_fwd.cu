@@ -1,0 +1,361 @@
+// Scaled fp16 flash-attention forward for sm_100a (tcgen05 + TMA), the compute step of the
+// reference's scaled SDPA (tbf16/attention.py:56-65 inference, tbf16/autograd.py:153-164 training).
+//
+// Inputs are the exact fp16 copies from prepare_qkv: q16 = q * 2^a, k16 = k * 2^-a (so q16 . k16 =
+// q . k), v16 = v * 2^-ev. Output: out = bf16_rn(softmax(scale * q16 k16^T + mask) v16 * 2^ev), written
+// straight from the fp32 accumulator (the reference rounds to fp16 first), plus the natural-log
+// logsumexp per row for the backward pass.
+//
+// CTA = one 128-row query tile of one (batch, head); keys in 128-column tiles.
+//   warp 0      TMA producer: Q once, then K and V tiles through 2-deep rings (3-D tensor maps over
+//               (head, seq, dim), so tiles never cross heads; rows past the end read as zeros).
+//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers (M=128, N=128, K=D), then
+//               O += P_{j-1} V_{j-1} (M=128, N=D, K=128) with P from shared memory and V MN-major.
+//   warps 2-5   softmax, one query row per thread: tcgen05.ld the S row, mask, online max with a lazy
+//               rescale of O in TMEM (only when the running max grows by more than 2^8), exp2, row
+//               sum, P -> fp16 into a 128B-swizzled K-major shared tile; epilogue O / l * 2^ev -> bf16.
+// TMEM: S0 [0,128), S1 [128,256), O [256, 256+D). Every mbarrier wait is bounded.
+#include <algorithm>
+
+#include "common.cuh"
+
+using namespace tbf16;
+
+namespace {
+
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // keys per tile
+constexpr int kSoftmaxWarps = 4;
+constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
+constexpr float kRescaleLog2 = 8.0f;  // keep a stale max until the true one exceeds it by 2^8
+
+struct AttnFwdParams {
+  int B, Hq, Hkv, Sq, Sk;
+  int group;          // Hq / Hkv
+  float scale_log2;   // softmax scale * log2(e)
+  int causal;         // keys j <= query i (top-left aligned, as torch's is_causal)
+  const int32_t* ev;  // [B * Hkv]: output multiplied by 2^ev
+  __nv_bfloat16* out; // [B, Hq, Sq, D] contiguous
+  float* lse;         // [B * Hq * Sq] natural-log logsumexp, nullable
+  const uint16_t* mask;  // additive fp16 bias, nullable; element (b,h,i,j) at b*mb + h*mh + i*mi + j
+  int64_t mb, mh, mi;
+  unsigned int* err;
+  int m_tiles;
+};
+
+template <int D>
+struct FwdCfg {
+  static constexpr int ATOMS = D / 64;            // 64-column swizzle atoms per row
+  static constexpr int TILE_BYTES = ATOMS * 128 * 128;  // 128 rows x D fp16
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
+  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int P_BYTES = 2 * 128 * 128;        // 128 rows x 128 keys fp16
+  static constexpr int BAR_OFF = P_OFF + P_BYTES;
+  static constexpr int SMEM = 1024 + BAR_OFF + 256;
+  static constexpr int O_COL = 256;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of 16-byte chunk c (0..15 for 128 fp16 columns) of row r in a K-major tile made of
+// 64-column 128B-swizzled atoms of 128 rows each.
+__device__ __forceinline__ uint32_t swz_off(int r, int c) {
+  return (uint32_t)((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
+  using C = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_empty = bars + 11; // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int bhk = b * p.Hkv + h / p.group;
+  const int m_tile = p.causal ? (p.m_tiles - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy tiles first
+  const int m0 = m_tile * BM;
+  const int kv_end = p.causal ? min(p.Sk, m0 + BM) : p.Sk;
+  const int n_kv = (kv_end + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kSoftmaxWarps);
+    }
+    mbar_init(p_full, kSoftmaxWarps);
+    mbar_init(pv_done, 1);
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && n_kv > 0) {
+      mbar_arrive_expect_tx(q_full, C::TILE_BYTES);
+#pragma unroll
+      for (int a = 0; a < C::ATOMS; ++a) tma_load_3d(smem + C::Q_OFF + a * 16384, &tmQ, q_full, a * 64, m0, bh);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::K_OFF + st * C::TILE_BYTES + a * 16384, &tmK, &k_full[st], a * 64, j * BN, bhk);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + a * 16384, &tmV, &v_full[st], a * 64, j * BN, bhk);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, false, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(BM, D, false, true);
+      const uint32_t q_addr = smem_u32(smem + C::Q_OFF);
+      const uint32_t p_addr = smem_u32(smem + C::P_OFF);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i & 1;
+        if (!mbar_wait(p_full, i & 1, abort, p.err)) return false;
+        if (!mbar_wait(&v_full[st], (i >> 1) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t ad = smem_desc_sw128(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          // V tile is MN-major: D contiguous (64-wide atoms 16 KB apart), keys = 8-row groups 1 KB apart.
+          const uint64_t bd = smem_desc_sw128(v_addr + kk * 2048, 16384, 1024);
+          umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done);
+        umma_commit(&v_empty[st]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort, p.err);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_full[st], ph, abort, p.err) || !mbar_wait(&s_empty[st], ph ^ 1, abort, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + C::K_OFF + st * C::TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16_ss(tmem + st * BN, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+                      idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) issue_pv(n_kv - 1);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row within the tile
+    const int qi = m0 + r;           // query index
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, abort, p.err)) { ok = false; break; }
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(tmem + lane_base + st * BN + c * 32, rr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[st]);
+      const int k0 = j * BN;
+      float mx = -INFINITY;
+      const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int kj = k0 + c;
+        bool valid = kj < p.Sk && (!p.causal || kj <= qi);
+        float v = s[c] * p.scale_log2;
+        if (mrow && valid) v += __half2float(__ushort_as_half(mrow[c])) * 1.4426950408889634f;
+        s[c] = valid ? v : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
+        alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+        rescale = j > 0;
+        m_used = mx;
+        l *= alpha;
+      }
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      float rowsum = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const float p0 = ex2(s[c] - base), p1 = ex2(s[c + 1] - base);
+        rowsum += p0 + p1;
+        pk[c / 2] = pack_f16(p0, p1);
+      }
+      l += rowsum;
+      // O and the P buffer are free once the previous P.V has completed
+      if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, abort, p.err)) { ok = false; break; }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + C::O_COL + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * (rescale ? alpha : 1.f));
+          tmem_st32(tmem + lane_base + C::O_COL + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      uint8_t* pbuf = smem + C::P_OFF;
+#pragma unroll
+      for (int c = 0; c < BN / 8; ++c)
+        *reinterpret_cast<uint4*>(pbuf + swz_off(r, c)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && n_kv > 0 && mbar_wait(pv_done, (n_kv - 1) & 1, abort, p.err)) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float sc = exp2i(__ldg(p.ev + bhk));
+      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + C::O_COL + c * 32, o);
+        tmem_ld_wait();
+        if (qi < p.Sq) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[8 * g + 0]) * inv_l * sc, __uint_as_float(o[8 * g + 1]) * inv_l * sc);
+            w.y = pack_bf16(__uint_as_float(o[8 * g + 2]) * inv_l * sc, __uint_as_float(o[8 * g + 3]) * inv_l * sc);
+            w.z = pack_bf16(__uint_as_float(o[8 * g + 4]) * inv_l * sc, __uint_as_float(o[8 * g + 5]) * inv_l * sc);
+            w.w = pack_bf16(__uint_as_float(o[8 * g + 6]) * inv_l * sc, __uint_as_float(o[8 * g + 7]) * inv_l * sc);
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = w;
+          }
+        }
+      }
+      if (p.lse && qi < p.Sq)
+        p.lse[(int64_t)bh * p.Sq + qi] = (m_used + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
+  using C = FwdCfg<D>;
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  if (!dev) return TBF16_ERR_DEVICE;
+  CUtensorMap tq, tk, tv;
+  const int64_t BHq = (int64_t)prm.B * prm.Hq, BHk = (int64_t)prm.B * prm.Hkv;
+  if (int rc = tbf16_host::make_tmap_3d(&tq, q16, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 64, BM)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tk, k16, D, prm.Sk, BHk, D, (uint64_t)prm.Sk * D, 64, BN)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, prm.Sk, BHk, D, (uint64_t)prm.Sk * D, 64, BN)) return rc;
+  static bool attr_done[64] = {false};
+  if (!attr_done[dev->device & 63]) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return tbf16_host::check_launch();
+    attr_done[dev->device & 63] = true;
+  }
+  dim3 grid(prm.m_tiles, (unsigned)BHq);
+  attn_fwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
+  return tbf16_host::check_launch();
+}
+
+}  // namespace
+
+extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
+                              int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
+                              const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, float* lse,
+                              void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq < 0 || Sk < 0 || !ev || !out || B * Hq > 65535 ||
+      Sq > INT32_MAX || Sk > INT32_MAX)
+    return TBF16_ERR_INVALID;
+  if (D != 64 && D != 128) return TBF16_ERR_UNSUPPORTED;
+  if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16) ||
+      !tbf16_host::aligned16(out))
+    return TBF16_ERR_ALIGN;
+  if (B == 0 || Sq == 0) return TBF16_OK;
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  AttnFwdParams prm;
+  prm.B = (int)B; prm.Hq = (int)Hq; prm.Hkv = (int)Hkv; prm.Sq = (int)Sq; prm.Sk = (int)Sk;
+  prm.group = (int)(Hq / Hkv);
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.causal = causal;
+  prm.ev = ev;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.lse = lse;
+  prm.mask = static_cast<const uint16_t*>(mask);
+  prm.mb = mask_sb; prm.mh = mask_sh; prm.mi = mask_sq;
+  prm.err = dev->err;
+  prm.m_tiles = (int)((Sq + BM - 1) / BM);
+  if (Sk == 0) return TBF16_ERR_UNSUPPORTED;
+  auto st = static_cast<cudaStream_t>(stream);
+  return D == 64 ? launch_fwd<64>(q16, k16, v16, prm, st) : launch_fwd<128>(q16, k16, v16, prm, st);
+}

@@ -1,0 +1,361 @@
+// Scaled bf16-on-fp16 GEMM for sm_100a: TMA -> (converter warps) -> tcgen05.mma (fp32 in TMEM) ->
+// epilogue warps -> bf16.
+//
+//   y[m, n] = bf16_rn((sum_k A16[m,k] * B16[n,k]) * sa[m] * sb[n] + bias[n])
+//
+// A16 is either an fp16 operand in memory (K-major or MN-major) or, in the fused linear, the bf16
+// activation x converted in shared memory to fp16(x[m,k] / sa[m]) by converter warps (exact for
+// values inside fp16's range: sa is a power of two). B16 is fp16 (K-major or MN-major).
+//
+// One CTA per SM, persistent over 128 x BN output tiles (grouped raster for L2 reuse):
+//   warp 0      TMA producer: one elected lane streams 128x64 A and BNx64 B tiles (128-byte swizzle)
+//               into a STAGES-deep ring guarded by full/empty mbarriers.
+//   warp 1      MMA issuer: allocates 2*BN TMEM columns (two fp32 accumulators), one lane issues
+//               tcgen05.mma.kind::f16 (M=128, N=BN, K=16) x 4 per stage and commits to the stage's
+//               empty barrier, and to the accumulator's full barrier after the last k-block.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, apply the scales and bias, store bf16;
+//               the other accumulator is being filled meanwhile.
+//   warps 6-9   converters (fused linear only): bf16 -> fp16 with the row's power-of-two scale,
+//               in place in the A stage, then fence.proxy.async and arrive on the stage's conv barrier.
+// Every mbarrier wait is bounded (2 s); on timeout the kernel records it in the device error word,
+// every role leaves its loop, and the CTA drains and frees its TMEM before returning.
+#include <algorithm>
+
+#include "common.cuh"
+
+using namespace tbf16;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle atom of 16-bit elements
+constexpr int kEpiWarps = 4;
+constexpr int kConvWarps = 4;
+constexpr int kGroupM = 8;
+
+struct GemmParams {
+  int M, N, K;
+  const float* sa;            // [M]
+  const float* sb;            // [N] or null
+  const __nv_bfloat16* bias;  // [N] or null
+  __nv_bfloat16* y;
+  int64_t ldy;
+  unsigned int* err;
+  int tiles_m, tiles_n;
+};
+
+template <int BN, int STAGES, bool CONVERT>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int WARPS = 2 + kEpiWarps + (CONVERT ? kConvWarps : 0);
+  static constexpr int THREADS = 32 * WARPS;
+  static constexpr int TMEM_COLS = 2 * BN;  // power of two >= 32
+  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = kGroupM * tiles_n;
+  const int group = tile / per_group;
+  const int first = group * kGroupM;
+  const int gsize = min(tiles_m - first, kGroupM);
+  const int r = tile % per_group;
+  tm = first + r % gsize;
+  tn = r / gsize;
+}
+
+template <int BN, int STAGES, bool CONVERT, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
+    scaled_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const GemmParams p) {
+  using C = Cfg<BN, STAGES, CONVERT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* conv = full + STAGES;
+  uint64_t* empty = conv + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int KB = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpiWarps);
+    }
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], kb * BK, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sA + j * 64 * BK * 2, &tmA, &full[stage], m0 + j * 64, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d(sB, &tmB, &full[stage], kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * 64 * BK * 2, &tmB, &full[stage], n0 + j * 64, kb * BK);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(CONVERT ? &conv[stage] : &full[stage], phase, abort, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: advance 32 bytes inside the swizzle atom; MN-major: two 8-row K groups (2 KB).
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                     : smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else if (warp < 2 + kEpiWarps) {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, abort, p.err)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      const int m = tm * BM + row;
+      const bool mok = m < p.M;
+      const float a = mok ? __ldg(p.sa + m) : 0.f;
+      __nv_bfloat16* yrow = p.y + (int64_t)(mok ? m : 0) * p.ldy;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + acc * BN + c * 32 + ((uint32_t)(quad * 32) << 16), r);
+        tmem_ld_wait();
+        const int n0 = tn * BN + c * 32;
+        if (mok && n0 < p.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int n = n0 + 8 * j;
+            if (n < p.N) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float sbv = p.sb ? __ldg(p.sb + n + e) : 1.f;
+                v[e] = (__uint_as_float(r[8 * j + e]) * a) * sbv;
+                if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+              }
+              uint4 o;
+              o.x = pack_bf16(v[0], v[1]);
+              o.y = pack_bf16(v[2], v[3]);
+              o.z = pack_bf16(v[4], v[5]);
+              o.w = pack_bf16(v[6], v[7]);
+              *reinterpret_cast<uint4*>(yrow + n) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  } else if (CONVERT) {
+    // ------------------------------------------------------------ converters: bf16 -> fp16(x * s) in place
+    const int row = (warp - 2 - kEpiWarps) * 32 + lane;  // 0..127, one row of the A tile per thread
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      const int m = tm * BM + row;
+      const float s = m < p.M ? 1.0f / __ldg(p.sa + m) : 0.f;  // exact: sa is a power of two
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort, p.err)) { ok = false; break; }
+        uint8_t* rowp = smem + stage * C::STAGE_BYTES + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          // Rotate the chunk order by row so the 8 threads of a quarter-warp hit distinct banks.
+          uint4* q = reinterpret_cast<uint4*>(rowp + ((c + row) & 7) * 16);
+          const uint4 v = *q;
+          uint4 o;
+          o.x = pack_f16(bf16lo(v.x) * s, bf16hi(v.x) * s);
+          o.y = pack_f16(bf16lo(v.y) * s, bf16hi(v.y) * s);
+          o.z = pack_f16(bf16lo(v.z) * s, bf16hi(v.z) * s);
+          o.w = pack_f16(bf16lo(v.w) * s, bf16hi(v.w) * s);
+          *q = o;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {  // let copies and MMAs already in flight land before the CTA's memory goes away
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int BN, int STAGES, bool CONVERT, bool A_MN, bool B_MN>
+int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
+                const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
+  using C = Cfg<BN, STAGES, CONVERT>;
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  if (!d) return TBF16_ERR_DEVICE;
+  CUtensorMap ta, tb;
+  int rc = A_MN ? tbf16_host::make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64)
+                : tbf16_host::make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, BM);
+  if (rc) return rc;
+  rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
+            : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, BN);
+  if (rc) return rc;
+  auto kern = scaled_gemm_kernel<BN, STAGES, CONVERT, A_MN, B_MN>;
+  static bool attr_done[64] = {false};
+  if (!attr_done[d->device & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return tbf16_host::check_launch();
+    attr_done[d->device & 63] = true;
+  }
+  GemmParams p;
+  p.M = M; p.N = N; p.K = K;
+  p.sa = sa; p.sb = sb;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.err = d->err;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, d->sms);
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
+  return tbf16_host::check_launch();
+}
+
+bool ok8(int64_t v) { return v % 8 == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
+                 const float* ws, const void* bias, void* y, int64_t ldy, float* x_sinv, int target_exp, int l1,
+                 void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || ldx < K || ldw < K || ldy < N ||
+      !ws || !x_sinv || !y)
+    return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(N) || !ok8(ldx) || !ok8(ldw) || !ok8(ldy) || !tbf16_host::aligned16(x) ||
+      !tbf16_host::aligned16(w16) || !tbf16_host::aligned16(y))
+    return TBF16_ERR_ALIGN;
+  if (M == 0 || N == 0) return TBF16_OK;
+  if (K == 0) return TBF16_ERR_UNSUPPORTED;
+  if (int st = tbf16_row_scale(x, M, K, ldx, target_exp, l1, x_sinv, nullptr, stream)) return st;
+  return tbf16_linear_scaled(x, M, K, ldx, w16, N, ldw, ws, bias, y, ldy, x_sinv, stream);
+}
+
+int tbf16_linear_scaled(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
+                        const float* ws, const void* bias, void* y, int64_t ldy, const float* x_sinv, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || N < 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || ldx < K || ldw < K || ldy < N ||
+      !ws || !x_sinv || !y)
+    return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(N) || !ok8(ldx) || !ok8(ldw) || !ok8(ldy) || !tbf16_host::aligned16(x) ||
+      !tbf16_host::aligned16(w16) || !tbf16_host::aligned16(y))
+    return TBF16_ERR_ALIGN;
+  if (M == 0 || N == 0) return TBF16_OK;
+  return launch_gemm<256, 4, true, false, false>(x, ldx, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy,
+                                                 static_cast<cudaStream_t>(stream));
+}
+
+int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int b_mn, int64_t ldb, int64_t M, int64_t N,
+                   int64_t K, const float* sa, const float* sb, const void* bias, void* y, int64_t ldy, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || N < 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || ldy < N || !sa || !y)
+    return TBF16_ERR_INVALID;
+  if (lda < (a_mn ? M : K) || ldb < (b_mn ? N : K)) return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(N) || !ok8(lda) || !ok8(ldb) || !ok8(ldy) || (a_mn && !ok8(M)) ||
+      !tbf16_host::aligned16(a16) || !tbf16_host::aligned16(b16) || !tbf16_host::aligned16(y))
+    return TBF16_ERR_ALIGN;
+  if (M == 0 || N == 0) return TBF16_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (!a_mn && !b_mn) return launch_gemm<256, 4, false, false, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+  if (!a_mn && b_mn) return launch_gemm<256, 4, false, false, true>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+  if (a_mn && !b_mn) return launch_gemm<256, 4, false, true, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+  return launch_gemm<256, 4, false, true, true>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+}
+
+}  // extern "C"

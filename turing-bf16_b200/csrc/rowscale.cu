@@ -1,0 +1,473 @@
+// HBM-bound scale kernels: row amax -> exponent (+ optional fp16 materialisation), column scales,
+// per-head amax / exponents, head scale-cast and the device-side prepare_qkv.
+//
+// All loads and stores are 128-bit (8 x 16-bit); rows, strides and base pointers are checked on the
+// host for 16-byte alignment. Max reductions use fmaxf (NaN ignored, as the reference's kernels do);
+// L1 norms accumulate in fp64 so that the exponent does not depend on the reduction order except
+// when the sum lies within ~2^-45 (relative) of a power of two.
+#include "common.cuh"
+
+using namespace tbf16;
+
+namespace {
+
+constexpr int kRowWarps = 8;  // rows per 256-thread block (one warp per row)
+
+// Max |x| (or L1 norm) of one bf16 row of K8 16-byte chunks, reduced over the warp.
+template <bool L1>
+__device__ __forceinline__ float warp_row_reduce(const uint4* __restrict__ xr, int K8, int lane) {
+  float m = 0.f;
+  double s = 0.0;
+  int i = lane;
+  for (; i + 96 < K8; i += 128) {  // four independent 16-byte loads in flight per lane
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(xr + i + 32 * u);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = fabsf(bf16lo(w[j])), b = fabsf(bf16hi(w[j]));
+        if (L1) s += (double)a + (double)b;
+        else m = fmaxf(m, fmaxf(a, b));
+      }
+    }
+  }
+  for (; i < K8; i += 32) {
+    const uint4 v = __ldg(xr + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = fabsf(bf16lo(w[j])), b = fabsf(bf16hi(w[j]));
+      if (L1) s += (double)a + (double)b;
+      else m = fmaxf(m, fmaxf(a, b));
+    }
+  }
+  if (L1) return (float)warp_sum(s);
+  return warp_max(m);
+}
+
+// Fused-GEMM row scales (gemm_sm75.cu:27-47): s_inv = 1 / 2^(se - 127), se from the fused rule.
+template <bool L1>
+__global__ void __launch_bounds__(256) row_scale_kernel(const uint4* __restrict__ x, int64_t rows, int K8, int64_t ldx8,
+                                                        int t, float* __restrict__ s_inv, int8_t* __restrict__ exp_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float red = warp_row_reduce<L1>(x + row * ldx8, K8, lane);
+  if (lane == 0) {
+    const int se = scale_biased_exp_fused(red, t);
+    s_inv[row] = inv_pow2_from_biased(se);
+    if (exp_out) exp_out[row] = (int8_t)(se - 127);
+  }
+}
+
+// quantize_rows (small_kernels.cu:35-74): s from the small rule; y = fp16_rn(x * s); s_inv = 1 / s.
+template <bool L1>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const uint4* __restrict__ x, int64_t rows, int K8,
+                                                            int64_t ldx8, int t, uint4* __restrict__ y, int64_t ldy8,
+                                                            float* __restrict__ s_inv) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint4* xr = x + row * ldx8;
+  const float red = warp_row_reduce<L1>(xr, K8, lane);
+  const int se = scale_biased_exp_small(red, t);
+  const float s = pow2_from_biased(se);
+  uint4* yr = y + row * ldy8;
+  for (int i = lane; i < K8; i += 32) {
+    const uint4 v = __ldg(xr + i);
+    uint4 o;
+    o.x = pack_f16(bf16lo(v.x) * s, bf16hi(v.x) * s);
+    o.y = pack_f16(bf16lo(v.y) * s, bf16hi(v.y) * s);
+    o.z = pack_f16(bf16lo(v.z) * s, bf16hi(v.z) * s);
+    o.w = pack_f16(bf16lo(v.w) * s, bf16hi(v.w) * s);
+    yr[i] = o;
+  }
+  if (lane == 0) s_inv[row] = inv_pow2_from_biased(se);
+}
+
+// Column amax (small_kernels.cu:136-155): 8 adjacent columns per thread over a chunk of rows,
+// merged with atomicMax on the bits of the non-negative maxima.
+__global__ void __launch_bounds__(128) col_amax_kernel(const uint4* __restrict__ x, const float* __restrict__ row_mul,
+                                                       float* __restrict__ amax, int64_t R, int K8, int64_t ldx8,
+                                                       int64_t rows_per_chunk) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 >= K8) return;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_chunk;
+  const int64_t r1 = min(R, r0 + rows_per_chunk);
+  float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int64_t r = r0; r < r1; ++r) {
+    const uint4 v = __ldg(x + r * ldx8 + c8);
+    const float rm = row_mul ? fabsf(__ldg(row_mul + r)) : 1.f;
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m[2 * j] = fmaxf(m[2 * j], fabsf(bf16lo(w[j])) * rm);
+      m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(bf16hi(w[j])) * rm);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) atomicMax(reinterpret_cast<int*>(amax) + c8 * 8 + j, __float_as_int(m[j]));
+}
+
+// Column convert (small_kernels.cu:158-184): y = fp16_rn((x * row_mul[r]) * s[c]); row 0 writes s_inv.
+__global__ void __launch_bounds__(256) col_convert_kernel(const uint4* __restrict__ x, const float* __restrict__ row_mul,
+                                                          const float* __restrict__ amax, uint4* __restrict__ y,
+                                                          float* __restrict__ s_inv, int64_t R, int K8, int64_t ldx8,
+                                                          int64_t ldy8, int t) {
+  const int64_t total = R * K8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K8;
+    const int c8 = (int)(i - r * K8);
+    const uint4 v = __ldg(x + r * ldx8 + c8);
+    const float rm = row_mul ? __ldg(row_mul + r) : 1.f;
+    float s[8];
+    int se[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      se[j] = scale_biased_exp_small(__ldg(amax + c8 * 8 + j), t);
+      s[j] = pow2_from_biased(se[j]);
+    }
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = pack_f16(bf16lo(w[j]) * rm * s[2 * j], bf16hi(w[j]) * rm * s[2 * j + 1]);
+    y[r * ldy8 + c8] = make_uint4(o[0], o[1], o[2], o[3]);
+    if (r == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s_inv[c8 * 8 + j] = inv_pow2_from_biased(se[j]);
+    }
+  }
+}
+
+__global__ void fill_kernel(float* p, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+// ---------------------------------------------------------------- attention scale helpers
+
+struct Head4 {
+  const uint16_t* x;
+  int64_t sb, sh, ss;  // element strides
+  int H, S, D8;
+  float* amax;         // [B*H]
+  int is_f16;
+};
+
+__device__ __forceinline__ void load8(const uint16_t* p, int is_f16, float (&f)[8]) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = is_f16 ? f16lo(w[j]) : bf16lo(w[j]);
+    f[2 * j + 1] = is_f16 ? f16hi(w[j]) : bf16hi(w[j]);
+  }
+}
+
+// grid (B*H, chunks, ntensors): amax of each (b, h) slice, merged with atomicMax (small_kernels.cu:221-243).
+__global__ void __launch_bounds__(256) head_amax_kernel(Head4 t0, Head4 t1, Head4 t2, int rows_per_chunk) {
+  const Head4 t = blockIdx.z == 0 ? t0 : blockIdx.z == 1 ? t1 : t2;
+  const int bh = blockIdx.x;
+  const int b = bh / t.H, h = bh % t.H;
+  const int s0 = blockIdx.y * rows_per_chunk;
+  const int s1 = min(t.S, s0 + rows_per_chunk);
+  const uint16_t* base = t.x + b * t.sb + h * t.sh;
+  float m = 0.f;
+  const int n = (s1 - s0) * t.D8;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int s = s0 + i / t.D8, d = (i % t.D8) * 8;
+    float f[8];
+    load8(base + s * t.ss + d, t.is_f16, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+  }
+  __shared__ float red[8];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(t.amax) + bh, __float_as_int(v));
+  }
+}
+
+__global__ void head_exp_kernel(const float* __restrict__ amax, int32_t* __restrict__ e, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) e[i] = frexp_exp(amax[i]);
+}
+
+// prepare_qkv exponents (attention.py:41-46), one block: eq, ek = max frexp exponents over (b, h);
+// a = clamp(floor((ek - eq) / 2), ek - 14, 14 - eq); ev = frexp(amax_v) - v_exp.
+__global__ void __launch_bounds__(256) qkv_exponents_kernel(const float* __restrict__ amax_q, int nq,
+                                                            const float* __restrict__ amax_k, int nk,
+                                                            const float* __restrict__ amax_v, int v_exp,
+                                                            int32_t* __restrict__ a_out, int32_t* __restrict__ ev_out) {
+  __shared__ int red[2][8];
+  int eq = INT_MIN, ek = INT_MIN;
+  for (int i = threadIdx.x; i < nq; i += blockDim.x) eq = max(eq, frexp_exp(amax_q[i]));
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+    ek = max(ek, frexp_exp(amax_k[i]));
+    ev_out[i] = frexp_exp(amax_v[i]) - v_exp;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    eq = max(eq, __shfl_xor_sync(0xffffffffu, eq, o));
+    ek = max(ek, __shfl_xor_sync(0xffffffffu, ek, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = eq;
+    red[1][threadIdx.x >> 5] = ek;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)blockDim.x / 32; ++w) {
+      eq = max(eq, red[0][w]);
+      ek = max(ek, red[1][w]);
+    }
+    eq = max(eq, red[0][0]);
+    ek = max(ek, red[1][0]);
+    int a = ek - eq;
+    a = (a >= 0) ? a / 2 : -((-a + 1) / 2);  // floor division by 2
+    a = max(min(a, 14 - eq), ek - 14);
+    *a_out = a;
+  }
+}
+
+struct ScaleCast {
+  const uint16_t* x;
+  int64_t sb, sh, ss;
+  int H, S, D8;
+  const int32_t* e;      // exponent source
+  int64_t e_sb, e_sh;    // broadcast strides into e
+  int e_sign;            // multiply the exponent by this (+1 / -1)
+  uint16_t* y;           // contiguous (B, H, S, D)
+  int in_f16, out_f16;
+  int64_t total8;        // B*H*S*D/8
+};
+
+// y = cast(x * 2^(sign * e[b, h])), contiguous output (small_kernels.cu:246-263). grid.z selects the tensor.
+__global__ void __launch_bounds__(256) head_scale_cast_kernel(ScaleCast c0, ScaleCast c1, ScaleCast c2) {
+  const ScaleCast c = blockIdx.z == 0 ? c0 : blockIdx.z == 1 ? c1 : c2;
+  if (c.x == nullptr) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < c.total8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % c.D8) * 8;
+    const int64_t row = i / c.D8;
+    const int s = (int)(row % c.S);
+    const int64_t bh = row / c.S;
+    const int b = (int)(bh / c.H), h = (int)(bh % c.H);
+    const float sc = exp2i(c.e_sign * __ldg(c.e + b * c.e_sb + h * c.e_sh));
+    float f[8];
+    load8(c.x + b * c.sb + h * c.sh + (int64_t)s * c.ss + d, c.in_f16, f);
+    uint4 o;
+    if (c.out_f16) {
+      o.x = pack_f16(f[0] * sc, f[1] * sc); o.y = pack_f16(f[2] * sc, f[3] * sc);
+      o.z = pack_f16(f[4] * sc, f[5] * sc); o.w = pack_f16(f[6] * sc, f[7] * sc);
+    } else {
+      o.x = pack_bf16(f[0] * sc, f[1] * sc); o.y = pack_bf16(f[2] * sc, f[3] * sc);
+      o.z = pack_bf16(f[4] * sc, f[5] * sc); o.w = pack_bf16(f[6] * sc, f[7] * sc);
+    }
+    reinterpret_cast<uint4*>(c.y)[i] = o;
+  }
+}
+
+bool ok8(int64_t v) { return v % 8 == 0; }
+
+int grid_for(int64_t work, int threads, int waves = 8) {
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  const int64_t cap = (int64_t)(d ? d->sms : 148) * waves;
+  const int64_t g = (work + threads - 1) / threads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(g, cap));
+}
+
+int check_4d(const void* x, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb, int64_t sh, int64_t ss) {
+  if (B < 0 || H < 0 || S < 0 || D <= 0 || B * H > INT32_MAX || S > INT32_MAX) return TBF16_ERR_INVALID;
+  if (!ok8(D) || !ok8(sb) || !ok8(sh) || !ok8(ss) || !tbf16_host::aligned16(x)) return TBF16_ERR_ALIGN;
+  return TBF16_OK;
+}
+
+Head4 make_head4(const void* x, int64_t H, int64_t S, int64_t D, int64_t sb, int64_t sh, int64_t ss, float* amax,
+                 int is_f16) {
+  Head4 h;
+  h.x = static_cast<const uint16_t*>(x);
+  h.sb = sb; h.sh = sh; h.ss = ss;
+  h.H = (int)H; h.S = (int)S; h.D8 = (int)(D / 8);
+  h.amax = amax;
+  h.is_f16 = is_f16;
+  return h;
+}
+
+int launch_head_amax(const Head4& a, const Head4& b, const Head4& c, int ntensors, int64_t BH, int64_t S,
+                     cudaStream_t st) {
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  const int sms = d ? d->sms : 148;
+  const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>((sms * 8 + BH - 1) / BH, (S + 63) / 64));
+  const int rows = (int)((S + chunks - 1) / chunks);
+  head_amax_kernel<<<dim3((unsigned)BH, chunks, ntensors), 256, 0, st>>>(a, b, c, rows);
+  return tbf16_host::check_launch();
+}
+
+}  // namespace
+
+extern "C" {
+
+int tbf16_row_scale(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, float* s_inv,
+                    int8_t* exp_out, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (rows < 0 || K < 0 || ldx < K || target_exp < 0 || target_exp > 64 || !s_inv) return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(ldx) || !tbf16_host::aligned16(x)) return TBF16_ERR_ALIGN;
+  if (rows == 0) return TBF16_OK;
+  const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
+  auto st = static_cast<cudaStream_t>(stream);
+  if (l1)
+    row_scale_kernel<true><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8, target_exp,
+                                                 s_inv, exp_out);
+  else
+    row_scale_kernel<false><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8,
+                                                  target_exp, s_inv, exp_out);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_quantize_rows(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, void* y16,
+                        int64_t ldy, float* s_inv, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (rows < 0 || K < 0 || ldx < K || ldy < K || target_exp < -126 || target_exp > 126 || !s_inv)
+    return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(ldx) || !ok8(ldy) || !tbf16_host::aligned16(x) || !tbf16_host::aligned16(y16))
+    return TBF16_ERR_ALIGN;
+  if (rows == 0) return TBF16_OK;
+  const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
+  auto st = static_cast<cudaStream_t>(stream);
+  if (l1)
+    quantize_rows_kernel<true><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8,
+                                                     target_exp, static_cast<uint4*>(y16), ldy / 8, s_inv);
+  else
+    quantize_rows_kernel<false><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8,
+                                                      target_exp, static_cast<uint4*>(y16), ldy / 8, s_inv);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, const float* row_mul,
+                        void* y16, int64_t ldy, float* s_inv, float* amax_ws, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (rows < 0 || K < 0 || ldx < K || ldy < K || target_exp < -126 || target_exp > 126 || !s_inv || !amax_ws)
+    return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(ldx) || !ok8(ldy) || !tbf16_host::aligned16(x) || !tbf16_host::aligned16(y16))
+    return TBF16_ERR_ALIGN;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (K == 0) return TBF16_OK;
+  if (rows == 0) {
+    fill_kernel<<<grid_for(K, 256), 256, 0, st>>>(s_inv, K, 1.0f);
+    return tbf16_host::check_launch();
+  }
+  if (cudaMemsetAsync(amax_ws, 0, sizeof(float) * K, st) != cudaSuccess) return TBF16_ERR_LAUNCH;
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  const int sms = d ? d->sms : 148;
+  const int K8 = (int)(K / 8);
+  const int col_blocks = (K8 + 127) / 128;
+  const int64_t chunks =
+      std::max<int64_t>(1, std::min<int64_t>((rows + 63) / 64, ((int64_t)sms * 16 + col_blocks - 1) / col_blocks));
+  const int64_t rows_per_chunk = (rows + chunks - 1) / chunks;
+  col_amax_kernel<<<dim3(col_blocks, (unsigned)chunks), 128, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws,
+                                                                      rows, K8, ldx / 8, rows_per_chunk);
+  col_convert_kernel<<<grid_for(rows * K8, 256), 256, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws,
+                                                              static_cast<uint4*>(y16), s_inv, rows, K8, ldx / 8,
+                                                              ldy / 8, target_exp);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_head_amax(const void* x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb, int64_t sh,
+                    int64_t ss, float* amax, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (dtype != TBF16_BF16 && dtype != TBF16_F16) return TBF16_ERR_DTYPE;
+  if (int st = check_4d(x, B, H, S, D, sb, sh, ss)) return st;
+  if (!amax) return TBF16_ERR_INVALID;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (B * H == 0) return TBF16_OK;
+  if (cudaMemsetAsync(amax, 0, sizeof(float) * B * H, st) != cudaSuccess) return TBF16_ERR_LAUNCH;
+  if (S == 0) return TBF16_OK;
+  Head4 h = make_head4(x, H, S, D, sb, sh, ss, amax, dtype == TBF16_F16);
+  return launch_head_amax(h, h, h, 1, B * H, S, st);
+}
+
+int tbf16_head_exp(const void* x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb, int64_t sh,
+                   int64_t ss, int32_t* e, float* amax_ws, void* stream) {
+  if (!e) return TBF16_ERR_INVALID;
+  if (int st = tbf16_head_amax(x, dtype, B, H, S, D, sb, sh, ss, amax_ws, stream)) return st;
+  if (B * H == 0) return TBF16_OK;
+  head_exp_kernel<<<(unsigned)((B * H + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(amax_ws, e,
+                                                                                                  (int)(B * H));
+  return tbf16_host::check_launch();
+}
+
+int tbf16_head_scale_cast(const void* x, int in_dtype, int64_t B, int64_t H, int64_t S, int64_t D, int64_t sb,
+                          int64_t sh, int64_t ss, const int32_t* e, int64_t e_sb, int64_t e_sh, void* y, int out_dtype,
+                          void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if ((in_dtype != TBF16_BF16 && in_dtype != TBF16_F16) || (out_dtype != TBF16_BF16 && out_dtype != TBF16_F16))
+    return TBF16_ERR_DTYPE;
+  if (int st = check_4d(x, B, H, S, D, sb, sh, ss)) return st;
+  if (!e || !y) return TBF16_ERR_INVALID;
+  if (!tbf16_host::aligned16(y)) return TBF16_ERR_ALIGN;
+  const int64_t total8 = B * H * S * D / 8;
+  if (total8 == 0) return TBF16_OK;
+  ScaleCast c;
+  c.x = static_cast<const uint16_t*>(x);
+  c.sb = sb; c.sh = sh; c.ss = ss;
+  c.H = (int)H; c.S = (int)S; c.D8 = (int)(D / 8);
+  c.e = e; c.e_sb = e_sb; c.e_sh = e_sh; c.e_sign = 1;
+  c.y = static_cast<uint16_t*>(y);
+  c.in_f16 = in_dtype == TBF16_F16; c.out_f16 = out_dtype == TBF16_F16;
+  c.total8 = total8;
+  ScaleCast none = c;
+  none.x = nullptr;
+  head_scale_cast_kernel<<<dim3(grid_for(total8, 256), 1, 1), 256, 0, static_cast<cudaStream_t>(stream)>>>(c, none, none);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb, int64_t ksh,
+                      int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B, int64_t Hq,
+                      int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int v_exp, void* q16, void* k16, void* v16,
+                      int32_t* a_out, int32_t* ev_out, float* ws, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (int st = check_4d(q, B, Hq, Sq, D, qsb, qsh, qss)) return st;
+  if (int st = check_4d(k, B, Hkv, Sk, D, ksb, ksh, kss)) return st;
+  if (int st = check_4d(v, B, Hkv, Sk, D, vsb, vsh, vss)) return st;
+  if (!q16 || !k16 || !v16 || !a_out || !ev_out || !ws || Hkv <= 0 || Hq % Hkv != 0) return TBF16_ERR_INVALID;
+  if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16)) return TBF16_ERR_ALIGN;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (B == 0) return TBF16_OK;
+  float* amax_q = ws;
+  float* amax_k = ws + B * Hq;
+  float* amax_v = amax_k + B * Hkv;
+  if (cudaMemsetAsync(ws, 0, sizeof(float) * (B * Hq + 2 * B * Hkv), st) != cudaSuccess) return TBF16_ERR_LAUNCH;
+  Head4 hq = make_head4(q, Hq, Sq, D, qsb, qsh, qss, amax_q, 0);
+  Head4 hk = make_head4(k, Hkv, Sk, D, ksb, ksh, kss, amax_k, 0);
+  Head4 hv = make_head4(v, Hkv, Sk, D, vsb, vsh, vss, amax_v, 0);
+  // q has B*Hq slices, k and v B*Hkv each: one launch for q, one for k and v together.
+  if (Sq > 0) {
+    if (int st2 = launch_head_amax(hq, hq, hq, 1, B * Hq, Sq, st)) return st2;
+  }
+  if (Sk > 0) {
+    if (int st2 = launch_head_amax(hk, hv, hv, 2, B * Hkv, Sk, st)) return st2;
+  }
+  qkv_exponents_kernel<<<1, 256, 0, st>>>(amax_q, (int)(B * Hq), amax_k, (int)(B * Hkv), amax_v, v_exp, a_out, ev_out);
+  ScaleCast cq;
+  cq.x = static_cast<const uint16_t*>(q); cq.sb = qsb; cq.sh = qsh; cq.ss = qss;
+  cq.H = (int)Hq; cq.S = (int)Sq; cq.D8 = (int)(D / 8);
+  cq.e = a_out; cq.e_sb = 0; cq.e_sh = 0; cq.e_sign = 1;
+  cq.y = static_cast<uint16_t*>(q16); cq.in_f16 = 0; cq.out_f16 = 1; cq.total8 = B * Hq * Sq * D / 8;
+  ScaleCast ck = cq;
+  ck.x = static_cast<const uint16_t*>(k); ck.sb = ksb; ck.sh = ksh; ck.ss = kss;
+  ck.H = (int)Hkv; ck.S = (int)Sk; ck.e_sign = -1; ck.y = static_cast<uint16_t*>(k16); ck.total8 = B * Hkv * Sk * D / 8;
+  ScaleCast cv = ck;
+  cv.x = static_cast<const uint16_t*>(v); cv.sb = vsb; cv.sh = vsh; cv.ss = vss;
+  cv.e = ev_out; cv.e_sb = Hkv; cv.e_sh = 1; cv.y = static_cast<uint16_t*>(v16);
+  const int64_t work = std::max(cq.total8, ck.total8);
+  if (work > 0) head_scale_cast_kernel<<<dim3(grid_for(work, 256), 1, 3), 256, 0, st>>>(cq, ck, cv);
+  return tbf16_host::check_launch();
+}
+
+}  // extern "C"

@@ -1,0 +1,201 @@
+"""bf16 matmuls on fp16 tensor cores with exact power-of-two scaling, on B200 (sm_100a).
+
+Same public surface as the reference's tbf16/ops.py (quantize_rows, prepare_weight, scaled_linear,
+linear_q, small_m_linear, quantize_rows_shared, _target_exp). The work runs in libtbf16_sm100.so:
+a row-amax -> exponent kernel and a warp-specialised TMA + tcgen05 GEMM that converts bf16 rows to
+fp16 in shared memory, accumulates in fp32 in TMEM and writes bf16 straight from the accumulator.
+The reference's Triton kernels, its cuBLAS small-M branch and its GEMV are gone: every M takes the
+same kernel, and there is no CPU fallback.
+"""
+import math
+import os
+import weakref
+
+import torch
+
+from . import _ext
+from ._ext import BF16, F16, available, call, ptr, require_cuda, stream_ptr
+
+# Kept for callers that set them (reference tbf16/ops.py:19-23); this build has one path for every M.
+_USE_CUDA = os.environ.get("TBF16_BACKEND", "cuda") == "cuda"
+_GEMM = os.environ.get("TBF16_GEMM", "")
+FUSED_MIN_M = 1
+# Row scaling of the fused GEMM: row max -> [2^14, 2^15) (reference tbf16/ops.py:24-26).
+_FUSED_SCALE = (15, False)
+# Rows scaled by their L1 norm for the training dX GEMM (reference tbf16/ops.py:129-130).
+L1_TARGET = 15
+SMALL_M = 2
+
+
+def _target_exp(K: int) -> int:
+    """Rows are scaled to amax in [2^(t-1), 2^t) so that an fp16 product of K terms stays below
+    K * 4^t <= 65504; t = 0 covers K <= 32768 (reference tbf16/ops.py:29-32)."""
+    return min(0, (15 - math.ceil(math.log2(max(K, 1)))) // 2)
+
+
+def _check_bf16_2d(x, name):
+    require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise RuntimeError(f"tbf16: {name} must be a 2-D bf16 CUDA tensor, got {x.dtype} {tuple(x.shape)}")
+
+
+def _rows_ok(t):
+    return t.stride(-1) == 1 and t.shape[-1] % 8 == 0 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+
+
+def quantize_rows(x: torch.Tensor, target_exp: int = 0, l1: bool = False):
+    """bf16 (R, K) -> (fp16 (R, K), fp32 (R,) inverse scales). Lossless for normal bf16 values inside
+    fp16's range after scaling. Each row's max (or with l1=True its L1 norm) goes to [2^(t-1), 2^t)."""
+    _check_bf16_2d(x, "x")
+    if not _rows_ok(x):
+        x = _pad_cols(x)
+    R, Kp = x.shape
+    y = torch.empty((R, Kp), device=x.device, dtype=torch.float16)
+    s_inv = torch.empty((R,), device=x.device, dtype=torch.float32)
+    call("tbf16_quantize_rows", ptr(x), R, Kp, x.stride(0), int(target_exp), int(bool(l1)), ptr(y), Kp, ptr(s_inv),
+         stream_ptr(x.device))
+    return y, s_inv
+
+
+def _pad_cols(x: torch.Tensor, mult: int = 8) -> torch.Tensor:
+    """Contiguous copy with the last dimension zero-padded to a multiple of `mult` (16-byte rows)."""
+    K = x.shape[-1]
+    Kp = (K + mult - 1) // mult * mult
+    out = torch.zeros((*x.shape[:-1], Kp), device=x.device, dtype=x.dtype)
+    out[..., :K] = x
+    return out
+
+
+class _RowCache:
+    """Reuses quantize_rows results when the same activation feeds several linear layers
+    (Q/K/V, gate/up). Keyed by tensor identity through a weakref plus the version counter, so
+    freed or modified tensors never hit (reference tbf16/ops.py:107-123)."""
+
+    def __init__(self, size=8):
+        self.size, self.entries = size, []
+
+    def get(self, x, t, make):
+        for ref, ver, tt, val in self.entries:
+            if ref() is x and ver == x._version and tt == t:
+                return val
+        val = make()
+        self.entries.append((weakref.ref(x), x._version, t, val))
+        if len(self.entries) > self.size:
+            self.entries.pop(0)
+        return val
+
+
+_row_cache = _RowCache()
+
+
+def quantize_rows_shared(x: torch.Tensor, l1: bool = False):
+    """quantize_rows of x viewed as (-1, K), shared across calls on the same tensor."""
+    K = x.shape[-1]
+    t = L1_TARGET if l1 else _target_exp(K)
+    return _row_cache.get(x, (t, l1), lambda: quantize_rows(x.reshape(-1, K).contiguous(), t, l1))
+
+
+def prepare_weight(w: torch.Tensor):
+    """nn.Linear weight (N, K) bf16 -> (fp16 (N, K), fp32 (N,) inverse scales). Do this once."""
+    return quantize_rows(w.contiguous(), _target_exp(w.shape[1]))
+
+
+def _bias_ok(bias, N, device):
+    if bias is None:
+        return None
+    require_cuda(bias)
+    if bias.dtype != torch.bfloat16:
+        bias = bias.to(torch.bfloat16)
+    bias = bias.contiguous()
+    if bias.numel() != N:
+        raise RuntimeError(f"tbf16: bias has {bias.numel()} elements, expected {N}")
+    return bias
+
+
+@torch.autocast("cuda", enabled=False)
+def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None):
+    """y = x @ W^T + b for bf16 x, with W given by prepare_weight. Returns bf16.
+
+    One fused launch pair for every M: the row-scale kernel, then the tcgen05 GEMM whose converter
+    warps turn x into fp16(x * 2^s) in shared memory (reference fused path, gemm_sm75.cu:257-284)."""
+    require_cuda(x, w16, w_sinv)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"tbf16.scaled_linear: x must be bf16, got {x.dtype}")
+    if w16.dtype != torch.float16 or w16.dim() != 2:
+        raise RuntimeError("tbf16.scaled_linear: w16 must be fp16 (N, K) from prepare_weight")
+    shape = x.shape
+    K = shape[-1]
+    N = w16.shape[0]
+    if w16.shape[1] < K or w_sinv.numel() != N:
+        raise RuntimeError(f"tbf16.scaled_linear: weight {tuple(w16.shape)} does not match K={K}")
+    x2 = x.reshape(-1, K)
+    if not _rows_ok(x2):
+        x2 = _pad_cols(x2) if K % 8 else x2.contiguous()
+    if not _rows_ok(w16) or w16.shape[1] != x2.shape[1]:
+        w16 = _pad_cols(w16[:, :K]) if K % 8 else w16.contiguous()
+    M, Kp = x2.shape
+    Np = (N + 7) // 8 * 8
+    b = _bias_ok(bias, N, x.device)
+    ws = w_sinv.contiguous().float()
+    if Np != N:  # the GEMM writes 16-byte rows: pad the output columns and slice them off
+        w16 = torch.cat([w16, w16.new_zeros(Np - N, w16.shape[1])])
+        ws = torch.cat([ws, ws.new_ones(Np - N)])
+        b = None if b is None else torch.cat([b, b.new_zeros(Np - N)])
+    y = torch.empty((M, Np), device=x.device, dtype=torch.bfloat16)
+    s_inv = torch.empty((M,), device=x.device, dtype=torch.float32)
+    t, l1 = _FUSED_SCALE
+    call("tbf16_linear", ptr(x2), M, Kp, x2.stride(0), ptr(w16), Np, w16.stride(0), ptr(ws), ptr(b), ptr(y), Np,
+         ptr(s_inv), t, int(l1), stream_ptr(x.device))
+    if Np != N:
+        y = y[:, :N]
+    return y.reshape(*shape[:-1], N)
+
+
+def _gemm_f16(a16, a_mn, b16, b_mn, M, N, K, sa, sb=None, bias=None):
+    """y (M, N) bf16 = (A @ B^T) * sa[:, None] * sb[None, :] + bias on the tcgen05 GEMM.
+    A = a16 (M, K) or, with a_mn, a16 (K, M); B = b16 (N, K) or, with b_mn, b16 (K, N)."""
+    require_cuda(a16, b16, sa)
+    dev = a16.device
+    y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+    sa = sa.contiguous().float()
+    sb = None if sb is None else sb.contiguous().float()
+    call("tbf16_gemm_f16", ptr(a16), int(a_mn), a16.stride(0), ptr(b16), int(b_mn), b16.stride(0), M, N, K, ptr(sa),
+         ptr(sb), ptr(bias), ptr(y), N, stream_ptr(dev))
+    return y
+
+
+@torch.autocast("cuda", enabled=False)
+def linear_q(x16, x_sinv, w16, w_sinv, bias=None):
+    """GEMM + epilogue on already-quantized rows: (x16 * x_sinv) @ (w16 * w_sinv)^T + bias, bf16 (M, N).
+    The product goes from the fp32 accumulator to bf16 once (the reference rounds it to fp16 first,
+    reference tbf16/ops.py:167-178)."""
+    require_cuda(x16, w16)
+    M, K = x16.shape
+    N = w16.shape[0]
+    b = _bias_ok(bias, N, x16.device)
+    if K % 8 or N % 8 or not _rows_ok(x16) or not _rows_ok(w16):
+        return (_gemm_padded(x16, x_sinv, w16, w_sinv, b))
+    return _gemm_f16(x16, 0, w16, 0, M, N, K, x_sinv, w_sinv, b)
+
+
+def _gemm_padded(x16, x_sinv, w16, w_sinv, b):
+    M, K = x16.shape
+    N = w16.shape[0]
+    Np = (N + 7) // 8 * 8
+    xp, wp = _pad_cols(x16), _pad_cols(w16)
+    ws = w_sinv.contiguous().float()
+    if Np != N:
+        wp = torch.cat([wp, wp.new_zeros(Np - N, wp.shape[1])])
+        ws = torch.cat([ws, ws.new_ones(Np - N)])
+        b = None if b is None else torch.cat([b, b.new_zeros(Np - N)])
+    return _gemm_f16(xp, 0, wp, 0, M, Np, xp.shape[1], x_sinv, ws, b)[:, :N]
+
+
+def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None):
+    """Kept for callers of the reference's small-M entry point (reference tbf16/ops.py:207-218): the
+    tcgen05 kernel handles any M, so this is scaled_linear."""
+    return scaled_linear(x2, w16, w_sinv, bias)
+
+
+__all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
+           "available", "_target_exp"]
