@@ -174,6 +174,10 @@ def main():
     ap.add_argument("--K", type=int, default=K_DEFAULT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-attention", action="store_true")
+    ap.add_argument("--gemm", default="materialise", choices=["materialise", "fused"],
+                    help="materialise (default, what tbf16_linear does with its x16 workspace): the row pass writes "
+                         "fp16(x * s) and the GEMM runs on fp16 operands; fused: bf16 x converted inside the GEMM")
     args = ap.parse_args()
     world, rank, local = dist_init() if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
                                                                   int(os.environ.get("RANK", "0")), 0)
@@ -212,11 +216,20 @@ def main():
     sp = ctypes.c_void_p(stream.cuda_stream)
     L = E.lib()
 
-    def row_scale():
-        return L.tbf16_row_scale(E.ptr(x), M, K, K, 15, 0, E.ptr(s_inv), None, sp)
+    x16 = torch.empty(M, K, device=dev, dtype=torch.float16) if args.gemm == "materialise" else None
 
-    def gemm():
-        return L.tbf16_linear_scaled(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N, E.ptr(s_inv), sp)
+    # the two launches of tbf16_linear, issued separately so each gets its own CUDA-event time
+    def row_scale():
+        return L.tbf16_row_scale(E.ptr(x), M, K, K, 15, 0, E.ptr(s_inv), None, E.ptr(x16), K, sp)
+
+    if args.gemm == "materialise":
+        def gemm():
+            return L.tbf16_gemm_f16(E.ptr(x16), 0, K, E.ptr(w16), 0, K, M, N, K, E.ptr(s_inv), E.ptr(ws), None, E.ptr(y), N,
+                                    sp)
+    else:
+        def gemm():
+            return L.tbf16_linear_scaled(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N,
+                                         E.ptr(s_inv), sp)
 
     def step():
         a = row_scale()
@@ -251,7 +264,8 @@ def main():
     flop = 2.0 * M * N * K
     value = flop * world * args.steps / (total_ms / 1e3) / 1e12
     gemm_tflops = flop / (gemm_ms / 1e3) / 1e12
-    rs_gbs = (2.0 * M * K + 4.0 * M) / (rs_ms / 1e3) / 1e9
+    rs_bytes = 2 * M * K + 4 * M + (2 * M * K if x16 is not None else 0)
+    rs_gbs = rs_bytes / (rs_ms / 1e3) / 1e9
     if E.device_status():
         raise RuntimeError("a kernel reported a timeout")
 
@@ -263,14 +277,22 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                          "frac": round(gemm_tflops / pk["tflops"], 4), "traffic": None,
                          "peak_source": f"{pk['source']} bf16 dense (burst); sustained {pk['tflops_sustained']}",
-                         "kernel": "scaled_gemm_kernel (tcgen05, fused bf16->fp16 converter)",
+                         "kernel": ("scaled_gemm_kernel<fp16 operands> (tcgen05, TMA, TMEM accumulators)"
+                                    if x16 is not None else "scaled_gemm_kernel<bf16 x converted in smem> (tcgen05)"),
                          "ms_per_launch": round(gemm_ms, 4)},
             "row_amax_kernel": {"ms": round(rs_ms, 4), "achieved_gbs": round(rs_gbs, 1), "peak_gbs": pk["hbm_gbs"],
-                                "frac": round(rs_gbs / pk["hbm_gbs"], 4), "bytes": 2 * M * K + 4 * M},
+                                "frac": round(rs_gbs / pk["hbm_gbs"], 4), "bytes": rs_bytes,
+                                "writes_fp16_copy": x16 is not None},
             "clocks": clocks.summary()}
-
     if not args.no_e2e:
-        line["e2e"] = e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world)
+        line["e2e"] = e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16)
+    if not args.no_attention:
+        del x, y, w16
+        torch.cuda.empty_cache()
+        try:
+            line["attention"] = attention_run(pk)
+        except Exception as exc:  # the headline GEMM line still prints
+            line["attention"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
@@ -282,7 +304,37 @@ def main():
         dist.destroy_process_group()
 
 
-def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world):
+def attention_run(pk, S=16384, H=16, D=128, iters=5):
+    """Config 3 (B=1, H=16, D=128, S=16k, Q/K overflow fp16): the scaled attention forward (prepare_qkv
+    + tcgen05 flash attention) in TFLOPS, causal and not; kernel-only time against the bf16 peak."""
+    import inputs
+    from tbf16 import attention
+    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda")
+    res = {"config": f"B=1 H={H} S={S} D={D}, Q,K x2^8, V x2^h"}
+    for causal in (False, True):
+        flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)
+        q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
+        for _ in range(2):
+            attention.sdpa(q, k, v, is_causal=causal)
+        torch.cuda.synchronize()
+        s0, s1, s2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        s0.record()
+        for _ in range(iters):
+            attention.sdpa(q, k, v, is_causal=causal)
+        s1.record()
+        for _ in range(iters):
+            attention.attn_forward(q16, k16, v16, ev, is_causal=causal)
+        s2.record()
+        torch.cuda.synchronize()
+        t_all, t_k = s0.elapsed_time(s1) / iters, s1.elapsed_time(s2) / iters
+        key = "causal" if causal else "noncausal"
+        res[key] = {"tflops": round(flop / (t_all / 1e3) / 1e12, 1), "ms": round(t_all, 3),
+                    "kernel_tflops": round(flop / (t_k / 1e3) / 1e12, 1),
+                    "kernel_frac": round(flop / (t_k / 1e3) / 1e12 / pk["tflops"], 4)}
+    return res
+
+
+def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16=None):
     """Same metric through the public C ABI call (tbf16_linear), with x uploaded from pinned host memory
     and y read back each step inside the timed region."""
     from tbf16 import _ext as E
@@ -294,7 +346,8 @@ def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world):
 
     def step():
         x.copy_(hx, non_blocking=True)
-        st = L.tbf16_linear(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N, E.ptr(s_inv), 15, 0, sp)
+        st = L.tbf16_linear(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N, E.ptr(s_inv), E.ptr(x16),
+                            15, 0, sp)
         if st:
             raise RuntimeError(f"tbf16_linear failed: {st}")
         hy.copy_(y, non_blocking=True)

@@ -54,9 +54,12 @@ int tbf16_device_status(unsigned int* bits, int reset);
 /* Row scales of the fused GEMM's pre-pass. Replaces row_scale(x, t, l1)
  * (tbf16/csrc/gemm_sm75.cu:243-253, kernel :27-47). x: bf16 [rows, K], row stride ldx.
  * s_inv[r] = 1 / s[r], s[r] = 2^(min(253 + t - e, 254) - 127) with e the clamped biased exponent of
- * the row max (l1 = 0) or L1 norm (l1 = 1). exp_out (nullable): int8 log2(s[r]). t must be >= 0. */
+ * the row max (l1 = 0) or L1 norm (l1 = 1). exp_out (nullable): int8 log2(s[r]). t must be >= 0.
+ * y16 (nullable): also write fp16_rn(x * s[r]) there (row stride ldy) in the same read of x, the
+ * operand the fused kernel converts on the fly (gemm_sm75.cu:108,132). Rows up to 8192 elements are
+ * read once (held in registers). */
 int tbf16_row_scale(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, float* s_inv,
-                    int8_t* exp_out, void* stream);
+                    int8_t* exp_out, void* y16, int64_t ldy, void* stream);
 
 /* Row quantisation. Replaces quantize_rows(x, t, l1) (tbf16/csrc/small_kernels.cu:275-287, kernel
  * :35-74; Python tbf16/ops.py:74-89). y16 = fp16_rn(x * s[r]) with s from small_kernels.cu:12-18
@@ -109,10 +112,12 @@ int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, cons
  * bias bf16 [N] or NULL; y bf16 [M, N] (ldy).
  *   s_inv[m] = row_scale(x, t, l1)                           (written to x_sinv, M floats)
  *   y[m, n]  = bf16_rn((sum_k fp16(x[m,k] / s_inv[m]) * w16[n,k]) * s_inv[m] * ws[n] + bias[n])
- * with fp32 accumulation in TMEM and no fp16 rounding of the product. K, N, ldx, ldw multiples of 8. */
+ * with fp32 accumulation in TMEM and no fp16 rounding of the product. K, N, ldx, ldw multiples of 8.
+ * x16_ws (nullable): fp16 [M, K] workspace. Given, the row pass writes fp16(x / s_inv) there in the same
+ * read of x and the GEMM takes fp16 operands (the fast path); NULL converts x inside the GEMM. */
 int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
-                 const float* ws, const void* bias, void* y, int64_t ldy, float* x_sinv, int target_exp, int l1,
-                 void* stream);
+                 const float* ws, const void* bias, void* y, int64_t ldy, float* x_sinv, void* x16_ws, int target_exp,
+                 int l1, void* stream);
 
 /* The GEMM half of tbf16_linear with the row scales given (x_sinv: M powers of two, e.g. from
  * tbf16_row_scale or from a producer kernel that already knows its rows' maxima). Same semantics as the
@@ -136,11 +141,35 @@ int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int 
  * (tbf16/autograd.py:159-164). q16 (B, Hq, Sq, D), k16 and v16 (B, Hkv, Sk, D), contiguous fp16; GQA by
  * Hq / Hkv. out (B, Hq, Sq, D) bf16 = bf16_rn(softmax(scale * q16 k16^T + mask) v16 * 2^ev[b, h / (Hq/Hkv)]);
  * causal keeps key j <= query i (top-left). mask: optional additive fp16 bias, element (b, h, i, j) at
- * b*mask_sb + h*mask_sh + i*mask_sq + j (strides may be 0 to broadcast). lse (nullable): fp32 (B*Hq*Sq)
- * natural-log logsumexp of the scaled, masked logits. D in {64, 128}. */
+ * b*mask_sb + h*mask_sh + i*mask_sq + j (strides may be 0 to broadcast). lse (nullable): fp32 (B*Hq, lse_ld)
+ * natural-log logsumexp of the scaled, masked logits (the backward wants lse_ld = Sq rounded up to a
+ * multiple of 128). o16 (nullable): fp16 (B, Hq, Sq, D) copy of the output before the 2^ev scale (the
+ * reference's out16, kept for the backward). D in {64, 128}. */
 int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev, const void* mask, int64_t mask_sb,
-                   int64_t mask_sh, int64_t mask_sq, void* out, float* lse, void* stream);
+                   int64_t mask_sh, int64_t mask_sq, void* out, float* lse, int64_t lse_ld, void* o16, void* stream);
+
+/* Bytes of workspace tbf16_attn_bwd needs (fp32 dQ accumulator, fp16 dO16, delta, head maxima). */
+int64_t tbf16_attn_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D);
+
+/* Flash-attention backward with the reference's per-call power-of-two dO scaling. Replaces the
+ * efficient-attention backward of ScaledSDPAFn.backward (tbf16/autograd.py:166-193):
+ *   G = t_do - max_{b,h}(head_exp(dout) + ev_q)          (t_do = 12 - ceil(log2 D), minus 8 per retry)
+ *   dO16 = fp16(dout * 2^(ev_q + G)); P, dS from q16, k16, v16, lse, delta = rowsum(dO16 * o16)
+ *   dq = bf16(dq16 * 2^(a - G)), dk = bf16(dk16 * 2^(-a - G)), dv = bf16(dv16 * 2^(-ev - G))
+ * (GQA heads summed in fp32 inside the kernel). q16, k16, v16, o16, lse, a, ev come from
+ * tbf16_prepare_qkv (v_exp = 0) and tbf16_attn_fwd; lse_ld must be Sq rounded up to a multiple of 128
+ * (each 128-row block of lse is bulk-copied). dout: bf16 (B, Hq, Sq, dout_d) with strides
+ * (dout_sb, dout_sh, dout_ss) and contiguous last dim (dout_d <= D; missing columns are zero).
+ * dq (B, Hq, Sq, D), dk, dv (B, Hkv, Sk, D): contiguous bf16. G_out: one int32 (device). flag: device
+ * word, bit 2 set if any dS or gradient is non-finite (the caller's overflow check). ws: workspace of
+ * tbf16_attn_bwd_workspace_size bytes. D in {64, 128}. */
+int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse, int64_t lse_ld,
+                   const void* dout,
+                   int64_t dout_sb, int64_t dout_sh, int64_t dout_ss, int64_t dout_d, const int32_t* a, const int32_t* ev,
+                   int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
+                   const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk,
+                   void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, void* stream);
 
 #ifdef __cplusplus
 }

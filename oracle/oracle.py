@@ -251,12 +251,13 @@ def sdpa_fwd(q, k, v, attn_mask=None, is_causal=False, scale=None, v_exp=13):
     lse = torch.logsumexp(s, -1)
     p = torch.exp(s - lse[..., None])
     o = p @ vv
+    zmax = torch.where(torch.isfinite(s), s.abs(), torch.zeros_like(s)).amax(-1)  # largest |scaled logit| per row
     ev_q = expand_heads(ev, Hq)
     scale_o = torch.ldexp(torch.ones(()), ev_q.double())[..., None, None]
     out = bf16_rn(o * scale_o)
     out_ref = bf16_rn(f16_rn(o).double() * scale_o)
     return {"out": out, "out_ref": out_ref, "lse": lse, "o16": o, "p": p, "a": a, "ev": ev, "q16": q16,
-            "k16": k16, "v16": v16, "scale": sc}
+            "k16": k16, "v16": v16, "scale": sc, "zmax": zmax, "pv_abs": p @ vv.abs()}
 
 
 def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None):

@@ -27,7 +27,8 @@ def test_library_exports_every_declared_symbol():
 def test_ctypes_table_matches_header():
     from tbf16 import _ext
     names = declared_symbols() - {"tbf16_abi_version", "tbf16_status_string"}
-    assert names <= set(_ext.SIGNATURES), sorted(names - set(_ext.SIGNATURES))
+    table = set(_ext.SIGNATURES) | set(_ext.SIGNATURES_I64)
+    assert names <= table, sorted(names - table)
 
 
 def test_status_strings_and_version():
@@ -46,7 +47,7 @@ def test_no_device_is_an_error_not_a_fallback():
         return
     x = torch.zeros(8, 8, dtype=torch.bfloat16)
     s = torch.zeros(8)
-    st = _ext.lib().tbf16_row_scale(_ext.ptr(x), 8, 8, 8, 15, 0, _ext.ptr(s), None, None)
+    st = _ext.lib().tbf16_row_scale(_ext.ptr(x), 8, 8, 8, 15, 0, _ext.ptr(s), None, None, 0, None)
     assert st == 5  # TBF16_ERR_DEVICE
 
 

@@ -49,7 +49,7 @@ def test_row_scale_vs_reference_kernel():
     x = edge_rows(300, 2048, seed=2).cuda()
     s_ref = ref.row_scale(x, 15, False)
     s = torch.empty(300, device="cuda")
-    E.call("tbf16_row_scale", E.ptr(x), 300, 2048, 2048, 15, 0, E.ptr(s), None, E.stream_ptr())
+    E.call("tbf16_row_scale", E.ptr(x), 300, 2048, 2048, 15, 0, E.ptr(s), None, None, 0, E.stream_ptr())
     amax = torch.nan_to_num(x.float(), nan=0.0).abs().amax(1)  # fmaxf semantics: NaN ignored
     normal = amax >= 2.0 ** -113  # below: the reference flushes s_inv = 2^-127 to 0
     assert torch.equal(s[normal], s_ref[normal])
@@ -67,7 +67,8 @@ def test_quantize_rows_vs_reference_kernel(t):
     keep = s_ref != 0
     assert torch.equal(s[keep], s_ref[keep])
     # rows with fp32-subnormal products differ under flush-to-zero: compare rows above that range
-    keep &= torch.nan_to_num(x.float(), nan=0.0).abs().amax(1) * s.reciprocal() >= 2.0 ** -100
+    # and rows of bf16-subnormal inputs (the reference's flush-to-zero zeroes them before scaling)
+    keep &= torch.nan_to_num(x.float(), nan=0.0).abs().amax(1) >= 2.0 ** -126
     assert bits_equal(y[keep], y_ref[keep])
 
 

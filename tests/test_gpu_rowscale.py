@@ -24,11 +24,19 @@ def test_row_scale_fused(R, K, l1):
     x = edge_rows(R, K, seed=R + K).cuda()
     s_inv = torch.empty(R, device="cuda")
     e8 = torch.empty(R, device="cuda", dtype=torch.int8)
-    E.call("tbf16_row_scale", E.ptr(x), R, K, x.stride(0), 15, int(l1), E.ptr(s_inv), E.ptr(e8), E.stream_ptr())
+    y16 = torch.empty(R, K, device="cuda", dtype=torch.float16)
+    E.call("tbf16_row_scale", E.ptr(x), R, K, x.stride(0), 15, int(l1), E.ptr(s_inv), E.ptr(e8), E.ptr(y16), K,
+           E.stream_ptr())
     ref = orc.row_scale_fused(x.cpu(), 15, l1)
     # both sides sum L1 norms (near) exactly (fp64 on the GPU, binary128 in the oracle): all rows compare
     assert torch.equal(s_inv.cpu(), ref)
     assert torch.equal(e8.cpu().int(), -torch.log2(ref.double()).round().int())
+    # the materialised operand is fp16_rn(x * s) with the same s (gemm_sm75.cu:108,132)
+    s = torch.ldexp(torch.ones(R, dtype=torch.float64), -torch.log2(ref.double()).round().int())
+    assert bits_equal(y16, orc.f16_rn((x.cpu().double() * s[:, None]).float()))
+    s2 = torch.empty(R, device="cuda")
+    E.call("tbf16_row_scale", E.ptr(x), R, K, x.stride(0), 15, int(l1), E.ptr(s2), None, None, 0, E.stream_ptr())
+    assert torch.equal(s2, s_inv)
 
 
 @pytest.mark.parametrize("R,K", [(64, 64), (37, 1032), (8, 20000), (257, 4096)])
@@ -124,8 +132,8 @@ def test_status_codes():
     E = _ext()
     x = torch.zeros(4, 12, device="cuda", dtype=torch.bfloat16)  # K = 12 is not a multiple of 8
     s = torch.empty(4, device="cuda")
-    st = E.lib().tbf16_row_scale(E.ptr(x), 4, 12, 12, 15, 0, E.ptr(s), None, E.stream_ptr())
+    st = E.lib().tbf16_row_scale(E.ptr(x), 4, 12, 12, 15, 0, E.ptr(s), None, None, 0, E.stream_ptr())
     assert st == 2  # TBF16_ERR_ALIGN
-    st = E.lib().tbf16_row_scale(E.ptr(x), -1, 8, 8, 15, 0, E.ptr(s), None, E.stream_ptr())
+    st = E.lib().tbf16_row_scale(E.ptr(x), -1, 8, 8, 15, 0, E.ptr(s), None, None, 0, E.stream_ptr())
     assert st == 1  # TBF16_ERR_INVALID
     assert E.device_status() == 0

@@ -36,7 +36,9 @@ struct AttnFwdParams {
   int causal;         // keys j <= query i (top-left aligned, as torch's is_causal)
   const int32_t* ev;  // [B * Hkv]: output multiplied by 2^ev
   __nv_bfloat16* out; // [B, Hq, Sq, D] contiguous
-  float* lse;         // [B * Hq * Sq] natural-log logsumexp, nullable
+  float* lse;         // [B * Hq, lse_ld] natural-log logsumexp, nullable
+  int64_t lse_ld;
+  __half* o16;        // [B, Hq, Sq, D] fp16 O before the 2^ev scale (training), nullable
   const uint16_t* mask;  // additive fp16 bias, nullable; element (b,h,i,j) at b*mb + h*mh + i*mi + j
   int64_t mb, mh, mi;
   unsigned int* err;
@@ -198,32 +200,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, abort, p.err)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[st], (j >> 1) & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
       float s[BN];
+      {
+        uint32_t rr[BN];  // all four 32-column loads in flight, one wait
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_base + st * BN + c * 32, rr);
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_ld32(tmem + lane_base + st * BN + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
+        for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(rr[e]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[st]);
       const int k0 = j * BN;
-      float mx = -INFINITY;
-      const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
+      // Logits are kept raw (s) and scaled inside the exp: p = 2^(s * c - m) with c = scale * log2(e)
+      // (scale > 0, so the max commutes with it). Partial tiles (sequence end, causal diagonal, user
+      // mask) first turn s into the scaled, masked value and use c = 1. Reductions use 8 independent
+      // partial accumulators: a single softmax warp per sub-partition has no other latency hiding.
+      const bool full_tile = p.mask == nullptr && k0 + BN <= p.Sk && (!p.causal || k0 + BN - 1 <= m0);
+      float c_scale = p.scale_log2;
+      if (!full_tile) {
+        const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const int kj = k0 + c;
-        bool valid = kj < p.Sk && (!p.causal || kj <= qi);
-        float v = s[c] * p.scale_log2;
-        if (mrow && valid) v += __half2float(__ushort_as_half(mrow[c])) * 1.4426950408889634f;
-        s[c] = valid ? v : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+        for (int c = 0; c < BN; ++c) {
+          const int kj = k0 + c;
+          const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
+          float v = s[c] * p.scale_log2;
+          if (mrow && valid) v += __half2float(__ushort_as_half(mrow[c])) * 1.4426950408889634f;
+          s[c] = valid ? v : -INFINITY;
+        }
+        c_scale = 1.f;
       }
+      float m8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m8[e] = s[e];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * c_scale;
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
@@ -233,17 +250,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
       }
       const float base = m_used == -INFINITY ? 0.f : m_used;
-      float rowsum = 0.f;
+      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2(s[c] - base), p1 = ex2(s[c + 1] - base);
-        rowsum += p0 + p1;
+        const float p0 = ex2(fmaf(s[c], c_scale, -base)), p1 = ex2(fmaf(s[c + 1], c_scale, -base));
+        sum8[(c >> 1) & 7] += p0 + p1;
         pk[c / 2] = pack_f16(p0, p1);
       }
-      l += rowsum;
+      l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       // O and the P buffer are free once the previous P.V has completed
-      if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, abort, p.err)) { ok = false; break; }
+      if (j > 0 && !mbar_wait_warp(pv_done, (j - 1) & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
@@ -266,11 +283,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && n_kv > 0 && mbar_wait(pv_done, (n_kv - 1) & 1, abort, p.err)) {
+    if (ok && n_kv > 0 && mbar_wait_warp(pv_done, (n_kv - 1) & 1, abort, p.err)) {
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
       __nv_bfloat16* orow = p.out + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D;
+      __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -285,11 +303,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             w.z = pack_bf16(__uint_as_float(o[8 * g + 4]) * inv_l * sc, __uint_as_float(o[8 * g + 5]) * inv_l * sc);
             w.w = pack_bf16(__uint_as_float(o[8 * g + 6]) * inv_l * sc, __uint_as_float(o[8 * g + 7]) * inv_l * sc);
             *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = w;
+            if (o16row) {
+              uint4 h;
+              h.x = pack_f16(__uint_as_float(o[8 * g + 0]) * inv_l, __uint_as_float(o[8 * g + 1]) * inv_l);
+              h.y = pack_f16(__uint_as_float(o[8 * g + 2]) * inv_l, __uint_as_float(o[8 * g + 3]) * inv_l);
+              h.z = pack_f16(__uint_as_float(o[8 * g + 4]) * inv_l, __uint_as_float(o[8 * g + 5]) * inv_l);
+              h.w = pack_f16(__uint_as_float(o[8 * g + 6]) * inv_l, __uint_as_float(o[8 * g + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(o16row + c * 32 + g * 8) = h;
+            }
           }
         }
       }
       if (p.lse && qi < p.Sq)
-        p.lse[(int64_t)bh * p.Sq + qi] = (m_used + log2f(l)) * 0.6931471805599453f;
+        p.lse[(int64_t)bh * p.lse_ld + qi] = (m_used + log2f(l)) * 0.6931471805599453f;
     }
   }
 
@@ -332,14 +358,14 @@ int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdP
 extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
                               int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
                               const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, float* lse,
-                              void* stream) {
+                              int64_t lse_ld, void* o16, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq < 0 || Sk < 0 || !ev || !out || B * Hq > 65535 ||
       Sq > INT32_MAX || Sk > INT32_MAX)
     return TBF16_ERR_INVALID;
   if (D != 64 && D != 128) return TBF16_ERR_UNSUPPORTED;
   if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16) ||
-      !tbf16_host::aligned16(out))
+      !tbf16_host::aligned16(out) || !tbf16_host::aligned16(o16))
     return TBF16_ERR_ALIGN;
   if (B == 0 || Sq == 0) return TBF16_OK;
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
@@ -351,6 +377,9 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
   prm.ev = ev;
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.lse = lse;
+  prm.lse_ld = lse_ld;
+  if (lse && lse_ld < Sq) return TBF16_ERR_INVALID;
+  prm.o16 = static_cast<__half*>(o16);
   prm.mask = static_cast<const uint16_t*>(mask);
   prm.mb = mask_sb; prm.mh = mask_sh; prm.mi = mask_sq;
   prm.err = dev->err;

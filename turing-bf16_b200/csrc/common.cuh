@@ -140,6 +140,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-wide bounded wait: lane 0 polls (so 32 lanes do not hammer the barrier word), then every lane
+// takes its own acquire of the completed phase. Safe when the barrier cannot complete its next phase
+// before this warp has consumed the current one (true for every ring below).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned int* err) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (ok) (void)mbar_try_wait(bar, parity);
+  return ok;
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -158,6 +169,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+// 1-D bulk copy global -> shared (no multicast); both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (UMMA reads).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -262,6 +280,11 @@ int require_sm100();
 // Maps the last CUDA error to a status (clears it).
 int check_launch();
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// Row amax / L1 -> power-of-two scale (fused rule if fused_rule, else the small-kernel rule), s_inv and
+// optional int8 log2(s); with y non-null also y = fp16_rn(x * s) (row stride ldy). Rows up to 8192
+// elements take one HBM read (row in registers). Arguments already validated by the caller.
+int row_pass(const void* x, int64_t rows, int64_t K, int64_t ldx, int t, int l1, int fused_rule, void* y, int64_t ldy,
+             float* s_inv, int8_t* exp_out, cudaStream_t st);
 // Encode a 2-D tiled tensor map (16-bit elements, 128-byte swizzle) for a row-major [rows, cols]
 // matrix with leading dimension ld (elements). Returns 0 on success.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,

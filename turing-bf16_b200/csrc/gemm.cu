@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort, p.err)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort, p.err)) break;
       tc_fence_after();
       int tm, tn;
       tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
       const float s = m < p.M ? 1.0f / __ldg(p.sa + m) : 0.f;  // exact: sa is a power of two
       bool ok = true;
       for (int kb = 0; kb < KB; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort, p.err)) { ok = false; break; }
+        if (!mbar_wait_warp(&full[stage], phase, abort, p.err)) { ok = false; break; }
         uint8_t* rowp = smem + stage * C::STAGE_BYTES + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -311,8 +311,8 @@ bool ok8(int64_t v) { return v % 8 == 0; }
 extern "C" {
 
 int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
-                 const float* ws, const void* bias, void* y, int64_t ldy, float* x_sinv, int target_exp, int l1,
-                 void* stream) {
+                 const float* ws, const void* bias, void* y, int64_t ldy, float* x_sinv, void* x16_ws, int target_exp,
+                 int l1, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
   if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || ldx < K || ldw < K || ldy < N ||
       !ws || !x_sinv || !y)
@@ -322,7 +322,18 @@ int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w
     return TBF16_ERR_ALIGN;
   if (M == 0 || N == 0) return TBF16_OK;
   if (K == 0) return TBF16_ERR_UNSUPPORTED;
-  if (int st = tbf16_row_scale(x, M, K, ldx, target_exp, l1, x_sinv, nullptr, stream)) return st;
+  if (x16_ws) {
+    // Materialise fp16(x * s) once in the row pass (one HBM read of x), then the fp16-operand GEMM:
+    // converting inside the GEMM would redo it for every N tile and compete with the tensor core for
+    // shared-memory bandwidth.
+    if (!tbf16_host::aligned16(x16_ws)) return TBF16_ERR_ALIGN;
+    if (target_exp < 0 || target_exp > 64) return TBF16_ERR_INVALID;
+    auto st = static_cast<cudaStream_t>(stream);
+    if (int rc = tbf16_host::row_pass(x, M, K, ldx, target_exp, l1, 1, x16_ws, K, x_sinv, nullptr, st)) return rc;
+    return launch_gemm<256, 4, false, false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y,
+                                                    ldy, st);
+  }
+  if (int st = tbf16_row_scale(x, M, K, ldx, target_exp, l1, x_sinv, nullptr, nullptr, 0, stream)) return st;
   return tbf16_linear_scaled(x, M, K, ldx, w16, N, ldw, ws, bias, y, ldy, x_sinv, stream);
 }
 
@@ -346,7 +357,9 @@ int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int 
   if (M < 0 || N < 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || ldy < N || !sa || !y)
     return TBF16_ERR_INVALID;
   if (lda < (a_mn ? M : K) || ldb < (b_mn ? N : K)) return TBF16_ERR_INVALID;
-  if (!ok8(K) || !ok8(N) || !ok8(lda) || !ok8(ldb) || !ok8(ldy) || (a_mn && !ok8(M)) ||
+  // K is a row length (must give 16-byte rows) only for a K-major operand; MN-major operands run along K
+  // by rows of stride lda / ldb, and TMA fills the tail past K with zeros.
+  if (((!a_mn || !b_mn) && !ok8(K)) || !ok8(N) || !ok8(lda) || !ok8(ldb) || !ok8(ldy) ||
       !tbf16_host::aligned16(a16) || !tbf16_host::aligned16(b16) || !tbf16_host::aligned16(y))
     return TBF16_ERR_ALIGN;
   if (M == 0 || N == 0) return TBF16_OK;

@@ -63,17 +63,18 @@ __global__ void __launch_bounds__(256) row_scale_kernel(const uint4* __restrict_
   }
 }
 
-// quantize_rows (small_kernels.cu:35-74): s from the small rule; y = fp16_rn(x * s); s_inv = 1 / s.
-template <bool L1>
+// quantize_rows (small_kernels.cu:35-74) for long rows (two reads of the row): s from the small rule
+// (or the fused rule); y = fp16_rn(x * s); s_inv = 1 / s.
+template <bool L1, bool FUSED_RULE>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const uint4* __restrict__ x, int64_t rows, int K8,
                                                             int64_t ldx8, int t, uint4* __restrict__ y, int64_t ldy8,
-                                                            float* __restrict__ s_inv) {
+                                                            float* __restrict__ s_inv, int8_t* __restrict__ exp_out) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
   const uint4* xr = x + row * ldx8;
   const float red = warp_row_reduce<L1>(xr, K8, lane);
-  const int se = scale_biased_exp_small(red, t);
+  const int se = FUSED_RULE ? scale_biased_exp_fused(red, t) : scale_biased_exp_small(red, t);
   const float s = pow2_from_biased(se);
   uint4* yr = y + row * ldy8;
   for (int i = lane; i < K8; i += 32) {
@@ -85,8 +86,120 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const uint4* __restr
     o.w = pack_f16(bf16lo(v.w) * s, bf16hi(v.w) * s);
     yr[i] = o;
   }
-  if (lane == 0) s_inv[row] = inv_pow2_from_biased(se);
+  if (lane == 0) {
+    s_inv[row] = inv_pow2_from_biased(se);
+    if (exp_out) exp_out[row] = (int8_t)(se - 127);
+  }
 }
+
+// Single-pass row kernel for rows of up to 32 * NCH 16-byte chunks: one warp per row, the whole row held
+// in registers (all loads in flight at once), one HBM read. Computes the row max or L1 norm, the scale
+// exponent by the fused rule (gemm_sm75.cu:19-23) or the small-kernel rule (small_kernels.cu:12-18),
+// s_inv, optional int8 log2(s), and optionally y = fp16_rn(x * s) from the registers.
+template <int NCH, bool L1, bool FUSED_RULE, bool WRITE_Y>
+__global__ void __launch_bounds__(256) row_pass_kernel(const uint4* __restrict__ x, int64_t rows, int K8, int64_t ldx8,
+                                                       int t, uint4* __restrict__ y, int64_t ldy8,
+                                                       float* __restrict__ s_inv, int8_t* __restrict__ exp_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint4* xr = x + row * ldx8;
+  uint4 v[NCH];
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const int i = lane + 32 * u;
+    v[u] = i < K8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
+  }
+  float m = 0.f;
+  double s = 0.0;
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = fabsf(bf16lo(w[j])), b = fabsf(bf16hi(w[j]));
+      if (L1) s += (double)a + (double)b;
+      else m = fmaxf(m, fmaxf(a, b));
+    }
+  }
+  const float red = L1 ? (float)warp_sum(s) : warp_max(m);
+  const int se = FUSED_RULE ? scale_biased_exp_fused(red, t) : scale_biased_exp_small(red, t);
+  if (WRITE_Y) {
+    const float sc = pow2_from_biased(se);
+    uint4* yr = y + row * ldy8;
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int i = lane + 32 * u;
+      if (i < K8) {
+        uint4 o;
+        o.x = pack_f16(bf16lo(v[u].x) * sc, bf16hi(v[u].x) * sc);
+        o.y = pack_f16(bf16lo(v[u].y) * sc, bf16hi(v[u].y) * sc);
+        o.z = pack_f16(bf16lo(v[u].z) * sc, bf16hi(v[u].z) * sc);
+        o.w = pack_f16(bf16lo(v[u].w) * sc, bf16hi(v[u].w) * sc);
+        yr[i] = o;
+      }
+    }
+  }
+  if (lane == 0) {
+    s_inv[row] = inv_pow2_from_biased(se);
+    if (exp_out) exp_out[row] = (int8_t)(se - 127);
+  }
+}
+
+template <bool L1, bool FUSED_RULE, bool WRITE_Y>
+bool launch_row_pass_t(const void* x, int64_t rows, int K8, int64_t ldx8, int t, void* y, int64_t ldy8, float* s_inv,
+                       int8_t* exp_out, cudaStream_t st) {
+  const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
+  const uint4* xp = static_cast<const uint4*>(x);
+  uint4* yp = static_cast<uint4*>(y);
+#define TBF16_ROW_PASS(N) row_pass_kernel<N, L1, FUSED_RULE, WRITE_Y><<<grid, 256, 0, st>>>(xp, rows, K8, ldx8, t, yp, ldy8, s_inv, exp_out)
+  if (K8 <= 32) TBF16_ROW_PASS(1);
+  else if (K8 <= 64) TBF16_ROW_PASS(2);
+  else if (K8 <= 128) TBF16_ROW_PASS(4);
+  else if (K8 <= 256) TBF16_ROW_PASS(8);
+  else if (K8 <= 512) TBF16_ROW_PASS(16);
+  else if (K8 <= 1024) TBF16_ROW_PASS(32);
+  else return false;
+#undef TBF16_ROW_PASS
+  return true;
+}
+
+}  // namespace
+
+namespace tbf16_host {
+int row_pass(const void* x, int64_t rows, int64_t K, int64_t ldx, int t, int l1, int fused_rule, void* y, int64_t ldy,
+             float* s_inv, int8_t* exp_out, cudaStream_t st) {
+  const int K8 = (int)(K / 8);
+  const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
+  const uint4* xp = static_cast<const uint4*>(x);
+  uint4* yp = static_cast<uint4*>(y);
+  bool done;
+  if (y) {
+    done = l1 ? (fused_rule ? launch_row_pass_t<true, true, true>(x, rows, K8, ldx / 8, t, y, ldy / 8, s_inv, exp_out, st)
+                            : launch_row_pass_t<true, false, true>(x, rows, K8, ldx / 8, t, y, ldy / 8, s_inv, exp_out, st))
+              : (fused_rule ? launch_row_pass_t<false, true, true>(x, rows, K8, ldx / 8, t, y, ldy / 8, s_inv, exp_out, st)
+                            : launch_row_pass_t<false, false, true>(x, rows, K8, ldx / 8, t, y, ldy / 8, s_inv, exp_out, st));
+    if (!done) {  // rows longer than 8192 elements: two reads of the row
+      const int64_t ldx8 = ldx / 8, ldy8 = ldy / 8;
+      if (l1 && fused_rule) quantize_rows_kernel<true, true><<<grid, 256, 0, st>>>(xp, rows, K8, ldx8, t, yp, ldy8, s_inv, exp_out);
+      else if (l1) quantize_rows_kernel<true, false><<<grid, 256, 0, st>>>(xp, rows, K8, ldx8, t, yp, ldy8, s_inv, exp_out);
+      else if (fused_rule) quantize_rows_kernel<false, true><<<grid, 256, 0, st>>>(xp, rows, K8, ldx8, t, yp, ldy8, s_inv, exp_out);
+      else quantize_rows_kernel<false, false><<<grid, 256, 0, st>>>(xp, rows, K8, ldx8, t, yp, ldy8, s_inv, exp_out);
+    }
+  } else {
+    if (!fused_rule) return TBF16_ERR_UNSUPPORTED;
+    done = l1 ? launch_row_pass_t<true, true, false>(x, rows, K8, ldx / 8, t, nullptr, 0, s_inv, exp_out, st)
+              : launch_row_pass_t<false, true, false>(x, rows, K8, ldx / 8, t, nullptr, 0, s_inv, exp_out, st);
+    if (!done) {
+      if (l1) row_scale_kernel<true><<<grid, 256, 0, st>>>(xp, rows, K8, ldx / 8, t, s_inv, exp_out);
+      else row_scale_kernel<false><<<grid, 256, 0, st>>>(xp, rows, K8, ldx / 8, t, s_inv, exp_out);
+    }
+  }
+  return check_launch();
+}
+}  // namespace tbf16_host
+
+namespace {
 
 // Column amax (small_kernels.cu:136-155): 8 adjacent columns per thread over a chunk of rows,
 // merged with atomicMax on the bits of the non-negative maxima.
@@ -314,20 +427,15 @@ int launch_head_amax(const Head4& a, const Head4& b, const Head4& c, int ntensor
 extern "C" {
 
 int tbf16_row_scale(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, float* s_inv,
-                    int8_t* exp_out, void* stream) {
+                    int8_t* exp_out, void* y16, int64_t ldy, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
-  if (rows < 0 || K < 0 || ldx < K || target_exp < 0 || target_exp > 64 || !s_inv) return TBF16_ERR_INVALID;
-  if (!ok8(K) || !ok8(ldx) || !tbf16_host::aligned16(x)) return TBF16_ERR_ALIGN;
+  if (rows < 0 || K < 0 || ldx < K || target_exp < 0 || target_exp > 64 || !s_inv || (y16 && ldy < K))
+    return TBF16_ERR_INVALID;
+  if (!ok8(K) || !ok8(ldx) || !tbf16_host::aligned16(x) || (y16 && (!ok8(ldy) || !tbf16_host::aligned16(y16))))
+    return TBF16_ERR_ALIGN;
   if (rows == 0) return TBF16_OK;
-  const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
-  auto st = static_cast<cudaStream_t>(stream);
-  if (l1)
-    row_scale_kernel<true><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8, target_exp,
-                                                 s_inv, exp_out);
-  else
-    row_scale_kernel<false><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8,
-                                                  target_exp, s_inv, exp_out);
-  return tbf16_host::check_launch();
+  return tbf16_host::row_pass(x, rows, K, ldx, target_exp, l1, 1, y16, ldy, s_inv, exp_out,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int tbf16_quantize_rows(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, int l1, void* y16,
@@ -338,15 +446,8 @@ int tbf16_quantize_rows(const void* x, int64_t rows, int64_t K, int64_t ldx, int
   if (!ok8(K) || !ok8(ldx) || !ok8(ldy) || !tbf16_host::aligned16(x) || !tbf16_host::aligned16(y16))
     return TBF16_ERR_ALIGN;
   if (rows == 0) return TBF16_OK;
-  const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
-  auto st = static_cast<cudaStream_t>(stream);
-  if (l1)
-    quantize_rows_kernel<true><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8,
-                                                     target_exp, static_cast<uint4*>(y16), ldy / 8, s_inv);
-  else
-    quantize_rows_kernel<false><<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), rows, (int)(K / 8), ldx / 8,
-                                                      target_exp, static_cast<uint4*>(y16), ldy / 8, s_inv);
-  return tbf16_host::check_launch();
+  return tbf16_host::row_pass(x, rows, K, ldx, target_exp, l1, 0, y16, ldy, s_inv, nullptr,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, const float* row_mul,

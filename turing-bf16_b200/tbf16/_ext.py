@@ -23,7 +23,7 @@ _vp, _i64, _i32, _u32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_
 
 # name -> argtypes; every entry point returns an int status. Mirrors include/tbf16_sm100.h.
 SIGNATURES = {
-    "tbf16_row_scale": [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp],
+    "tbf16_row_scale": [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tbf16_quantize_rows": [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _vp],
     "tbf16_quantize_cols": [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _vp, _vp, _vp],
     "tbf16_head_amax": [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp],
@@ -31,13 +31,21 @@ SIGNATURES = {
     "tbf16_head_scale_cast": [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp],
     "tbf16_prepare_qkv": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
-    "tbf16_linear": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _vp],
+    "tbf16_linear": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i32, _i32, _vp],
     "tbf16_linear_scaled": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp],
     "tbf16_gemm_f16": [_vp, _i32, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp],
     "tbf16_attn_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64, _i64,
-                       _i64, _vp, _vp, _vp],
+                       _i64, _vp, _vp, _i64, _vp, _vp],
+    "tbf16_attn_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                       _i64,
+                       ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
     "tbf16_device_check": [_i32],
     "tbf16_device_status": [_vp, _i32],
+}
+
+# entry points returning a size (int64) rather than a status
+SIGNATURES_I64 = {
+    "tbf16_attn_bwd_workspace_size": [_i64, _i64, _i64, _i64, _i64, _i64],
 }
 
 BF16, F16 = 0, 1
@@ -81,6 +89,10 @@ def lib():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = ctypes.c_int
+        for name, args in SIGNATURES_I64.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int64
         L.tbf16_status_string.argtypes = [_i32]
         L.tbf16_status_string.restype = ctypes.c_char_p
         L.tbf16_abi_version.argtypes = []

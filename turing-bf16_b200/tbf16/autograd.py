@@ -1,0 +1,246 @@
+"""Training: backward passes on fp16 tensor cores, B200 kernels.
+
+Same public surface as the reference's tbf16/autograd.py (quantize_cols, ScaledLinearFn,
+FP32LinearFn, linear, ScaledSDPAFn, sdpa, CHECK_OVERFLOW).
+
+Linear: dX = dY @ W and dW = dY^T @ X are fp16 GEMMs too. The contraction dimension changes, so
+dY, W and X are scaled per column (exact powers of two, the reference's exponent conventions) where
+the forward scaled per row. All three GEMMs are this build's tcgen05 kernel, which reads MN-major
+operands directly (no transposed copies) and writes bf16 from the fp32 accumulator.
+
+Attention: the tcgen05 flash-attention forward and backward, with dO multiplied by a power of two
+2^G picked per call so the internal dS stays in fp16's normal range. If the kernel reports a
+non-finite value the backward is redone with a smaller G (the reference's retry, autograd.py:177-189);
+with gradients written from fp32 accumulators this practically never triggers.
+"""
+import math
+import os
+
+import torch
+import torch.nn.functional as F
+
+from . import attention, ops
+from ._ext import call, lib, ptr, require_cuda, stream_ptr
+
+# Check attention gradients for fp16 overflow and redo them at a smaller scale if needed.
+# Costs one host sync per attention backward; TBF16_ATTN_CHECK=0 turns it off.
+CHECK_OVERFLOW = os.environ.get("TBF16_ATTN_CHECK", "1") != "0"
+
+
+def quantize_cols(x: torch.Tensor, target_exp: int = 0, row_mul=None):
+    """bf16 (R, K) -> (fp16 (R, K), fp32 (K,) inverse scales), one power-of-two scale per column.
+    row_mul (R,) powers of two, optional: quantize x * row_mul[:, None] instead (exact)."""
+    require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise RuntimeError("tbf16.quantize_cols: 2-D bf16 CUDA tensor expected")
+    if x.stride(1) != 1 or x.shape[1] % 8 or (x.shape[0] > 1 and x.stride(0) % 8) or x.data_ptr() % 16:
+        x = ops._pad_cols(x)
+    R, K = x.shape
+    y = torch.empty((R, K), device=x.device, dtype=torch.float16)
+    s_inv = torch.empty((K,), device=x.device, dtype=torch.float32)
+    ws = torch.empty((K,), device=x.device, dtype=torch.float32)
+    rm = None if row_mul is None else row_mul.contiguous().float()
+    call("tbf16_quantize_cols", ptr(x), R, K, x.stride(0) if R > 1 else K, int(target_exp), ptr(rm), ptr(y), K,
+         ptr(s_inv), ptr(ws), stream_ptr(x.device))
+    return y, s_inv
+
+
+_ONES = {}
+
+
+def _ones(n, device):
+    key = (n, device)
+    if key not in _ONES:
+        _ONES[key] = torch.ones(n, device=device)
+    return _ONES[key]
+
+
+@torch.autocast("cuda", enabled=False)
+def _scaled_mm(a16, sa, b16, sb, a_mn=False, b_mn=False):
+    """(A @ B^T) * sa[:, None] * sb[None, :] as bf16, with A = a16 (M, K) or a16 (K, M) if a_mn, and
+    B = b16 (N, K) or b16 (K, N) if b_mn (reference autograd.py:114-120 took a16 @ b16 explicitly)."""
+    M = a16.shape[1] if a_mn else a16.shape[0]
+    K = a16.shape[0] if a_mn else a16.shape[1]
+    N = b16.shape[1] if b_mn else b16.shape[0]
+    return ops._gemm_f16(a16, a_mn, b16, b_mn, M, N, K, sa, sb)
+
+
+def _aligned(*ts):
+    return all(t.shape[-1] % 8 == 0 and t.stride(-1) == 1 and t.data_ptr() % 16 == 0 for t in ts)
+
+
+class ScaledLinearFn(torch.autograd.Function):
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def forward(ctx, x, w, bias):
+        N, K = w.shape
+        x16, sx = ops.quantize_rows_shared(x)  # Q/K/V (and gate/up) share one fp16 copy of x
+        w16, sw = ops.prepare_weight(w)
+        # Saved instead of x (same size). dW reuses it with the row scales folded into dY.
+        ctx.save_for_backward(x16, sx, w)
+        ctx.has_bias = bias is not None
+        ctx.x_shape = x.shape
+        return ops.linear_q(x16, sx, w16, sw, bias).reshape(*x.shape[:-1], N)
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def backward(ctx, dy):
+        x16, sx, w = ctx.saved_tensors
+        N, K = w.shape
+        dy2 = dy.reshape(-1, N).contiguous()
+        if dy2.dtype != torch.bfloat16:
+            dy2 = dy2.bfloat16()
+        M = dy2.shape[0]
+        dx = dw = db = None
+        pad = N % 8 or K % 8
+        if ctx.needs_input_grad[0]:  # contraction over N: dY rows (L1, t=15) x W columns (t = _target_exp(N))
+            t = ops._target_exp(N)
+            dy16, sdy = ops.quantize_rows(dy2, ops.L1_TARGET, l1=True)
+            w16c, swc = quantize_cols(w.contiguous(), t)
+            if pad:
+                dx = _padded_mm(dy16, sdy, w16c, swc, M, N, K, kind="dx")
+            else:
+                dx = _scaled_mm(dy16, sdy, w16c, swc, a_mn=False, b_mn=True)  # B[k, n] = w16c[n, k]
+            dx = dx.reshape(ctx.x_shape)
+        if ctx.needs_input_grad[1]:  # contraction over M: dW[n, k] = sum_m dy[m, n] sx[m] x16[m, k]
+            # |x16| < 1, so |dW16| < M * 2^t; keep that under fp16's max (reference autograd.py:84-87).
+            t = min(0, 15 - math.ceil(math.log2(max(M, 1))))
+            dy16c, sdyc = quantize_cols(dy2, t, sx)
+            if pad:
+                dw = _padded_mm(dy16c, sdyc, x16, None, M, N, K, kind="dw")
+            else:
+                dw = _scaled_mm(dy16c, sdyc, x16, _ones(K, x16.device), a_mn=True, b_mn=True)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = dy2.float().sum(0).to(dy.dtype)
+        return dx, dw, db
+
+
+def _padded_mm(a16, sa, b16, sb, M, N, K, kind):
+    """dX / dW for layers whose N or K is not a multiple of 8: zero-pad the fp16 operands so every
+    row is 16-byte aligned, run the same GEMM, slice the result."""
+    Np, Kp = (N + 7) // 8 * 8, (K + 7) // 8 * 8
+    dev = a16.device
+    if kind == "dx":  # a16 = dy16 (M, Np'), b16 = w16c (N, K') -> dX (M, K)
+        A = torch.zeros(M, Np, device=dev, dtype=torch.float16)
+        A[:, :N] = a16[:, :N]
+        Bm = torch.zeros(Np, Kp, device=dev, dtype=torch.float16)
+        Bm[:N, :K] = b16[:N, :K]
+        sbp = torch.ones(Kp, device=dev)
+        sbp[:K] = sb[:K]
+        return ops._gemm_f16(A, 0, Bm, 1, M, Kp, Np, sa, sbp)[:, :K]
+    # dw: a16 = dy16c (M, N'), b16 = x16 (M, K') -> dW (N, K)
+    A = torch.zeros(M, Np, device=dev, dtype=torch.float16)
+    A[:, :N] = a16[:, :N]
+    Bm = torch.zeros(M, Kp, device=dev, dtype=torch.float16)
+    Bm[:, :K] = b16[:, :K]
+    sap = torch.ones(Np, device=dev)
+    sap[:N] = sa[:N]
+    return ops._gemm_f16(A, 1, Bm, 1, Np, Kp, M, sap, None)[:N, :K]
+
+
+class FP32LinearFn(torch.autograd.Function):
+    """bf16 in/out, fp32 math. Saves the bf16 input (shared with sibling layers), not an fp32 copy
+    (reference autograd.py:93-112; used for skinny layers such as LoRA adapters)."""
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def forward(ctx, x, w, bias):
+        ctx.save_for_backward(x, w)
+        ctx.has_bias = bias is not None
+        return F.linear(x.float(), w.float(), None if bias is None else bias.float()).to(x.dtype)
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dyf = dy.float()
+        dx = (dyf @ w.float()).to(x.dtype) if ctx.needs_input_grad[0] else None
+        dw = (dyf.reshape(-1, dy.shape[-1]).t() @ x.reshape(-1, x.shape[-1]).float()).to(w.dtype) \
+            if ctx.needs_input_grad[1] else None
+        db = dyf.reshape(-1, dy.shape[-1]).sum(0).to(dy.dtype) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
+def linear(x, w, bias=None):
+    """Differentiable F.linear for bf16 x and w on fp16 tensor cores."""
+    return ScaledLinearFn.apply(x, w, bias)
+
+
+def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale, d_orig):
+    """Runs tbf16_attn_bwd with the reference's retry loop: t_do = 12 - ceil(log2 d), lowered by 8 and
+    redone while the kernel reports a non-finite value (at most 6 attempts)."""
+    B, Hq, Sq, Dk = q16.shape
+    Hkv, Sk = k16.shape[1], k16.shape[2]
+    dev = q16.device
+    if dout.dtype != torch.bfloat16:
+        dout = dout.bfloat16()
+    if not attention._fast(dout):
+        dout = dout.contiguous()
+    dq = torch.empty((B, Hq, Sq, Dk), device=dev, dtype=torch.bfloat16)
+    dk = torch.empty((B, Hkv, Sk, Dk), device=dev, dtype=torch.bfloat16)
+    dv = torch.empty((B, Hkv, Sk, Dk), device=dev, dtype=torch.bfloat16)
+    G = torch.empty((), device=dev, dtype=torch.int32)
+    flag = torch.zeros((), device=dev, dtype=torch.int32)
+    nbytes = lib().tbf16_attn_bwd_workspace_size(B, Hq, Hkv, Sq, Sk, Dk)
+    ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+    ms = mask16.stride()[:3] if mask16 is not None else (0, 0, 0)
+    t_do = 12 - math.ceil(math.log2(d_orig))
+    for _attempt in range(6):
+        flag.zero_()
+        call("tbf16_attn_bwd", ptr(q16), ptr(k16), ptr(v16), ptr(o16), ptr(lse), lse.shape[-1], ptr(dout),
+             *dout.stride()[:3],
+             dout.shape[-1], ptr(a), ptr(ev), B, Hq, Hkv, Sq, Sk, Dk, float(scale), int(bool(is_causal)), ptr(mask16),
+             *ms, int(t_do), ptr(dq), ptr(dk), ptr(dv), ptr(G), ptr(flag), ptr(ws), nbytes, stream_ptr(dev))
+        if not CHECK_OVERFLOW:
+            break
+        if not bool(flag):  # host sync, once per attention call
+            break
+        t_do -= 8
+    else:
+        raise FloatingPointError("tbf16 attention backward overflowed fp16 even after rescaling")
+    return dq, dk, dv, G
+
+
+class ScaledSDPAFn(torch.autograd.Function):
+    """Scaled attention forward and backward on the tcgen05 kernels; keeps everything in
+    save_for_backward, so activation checkpointing can drop and recompute it."""
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def forward(ctx, q, k, v, attn_mask, dropout_p, is_causal, scale, enable_gqa):
+        if dropout_p:
+            raise NotImplementedError("tbf16 attention dropout is not implemented on B200")
+        if q.shape[1] != k.shape[1] and not enable_gqa:
+            raise RuntimeError("tbf16.sdpa: different numbers of query and key heads need enable_gqa=True")
+        D0 = q.shape[-1]
+        q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v)
+        B, Hq, Sq, D = q16.shape
+        Dk = 64 if D <= 64 else 128
+        if D > 128:
+            raise NotImplementedError("tbf16 attention on B200: head dims up to 128 in this build")
+        if Dk != D:
+            q16, k16, v16 = (F.pad(t, (0, Dk - D)) for t in (q16, k16, v16))
+        sc = 1.0 / math.sqrt(D0) if scale is None else float(scale)
+        mask16 = attention.additive_mask(attn_mask, B, Hq, Sq, k.shape[2], q.device)
+        out, lse, o16 = attention.attn_forward(q16, k16, v16, ev, mask16, is_causal, sc, need_lse=True, need_o16=True)
+        ctx.save_for_backward(q16, k16, v16, o16, lse, a, ev, mask16)
+        ctx.args = (is_causal, sc, D0)
+        return out[..., :D0].contiguous() if Dk != D0 else out
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def backward(ctx, dout):
+        q16, k16, v16, o16, lse, a, ev, mask16 = ctx.saved_tensors
+        is_causal, sc, D0 = ctx.args
+        Dk = q16.shape[-1]
+        if D0 % 8:
+            dout = F.pad(dout, (0, 8 - D0 % 8))
+        dq, dk, dv, _ = attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, sc, D0)
+        if Dk != D0:
+            dq, dk, dv = (t[..., :D0].contiguous() for t in (dq, dk, dv))
+        return dq, dk, dv, None, None, None, None, None
+
+
+def sdpa(q, k, v, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, enable_gqa=False):
+    """Differentiable bf16 scaled_dot_product_attention on fp16 tensor cores."""
+    return ScaledSDPAFn.apply(q, k, v, attn_mask, dropout_p, is_causal, scale, enable_gqa)

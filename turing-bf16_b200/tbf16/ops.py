@@ -112,6 +112,18 @@ def _bias_ok(bias, N, device):
     return bias
 
 
+def _materialise(M, N, K) -> bool:
+    """Whether the linear should write an fp16 copy of x in its row pass (TBF16_LINEAR=fused forces
+    the in-GEMM conversion, =materialise the copy). The in-GEMM conversion is redone once per 256-wide
+    N tile, so it only pays when N fits in one or two tiles."""
+    mode = os.environ.get("TBF16_LINEAR", "")
+    if mode == "fused":
+        return False
+    if mode == "materialise":
+        return True
+    return N > 512
+
+
 @torch.autocast("cuda", enabled=False)
 def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None):
     """y = x @ W^T + b for bf16 x, with W given by prepare_weight. Returns bf16.
@@ -143,9 +155,11 @@ def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias
         b = None if b is None else torch.cat([b, b.new_zeros(Np - N)])
     y = torch.empty((M, Np), device=x.device, dtype=torch.bfloat16)
     s_inv = torch.empty((M,), device=x.device, dtype=torch.float32)
+    # fp16 copy of x written by the row pass (one read of x); the GEMM then runs on fp16 operands
+    x16 = torch.empty((M, Kp), device=x.device, dtype=torch.float16) if _materialise(M, Np, Kp) else None
     t, l1 = _FUSED_SCALE
     call("tbf16_linear", ptr(x2), M, Kp, x2.stride(0), ptr(w16), Np, w16.stride(0), ptr(ws), ptr(b), ptr(y), Np,
-         ptr(s_inv), t, int(l1), stream_ptr(x.device))
+         ptr(s_inv), ptr(x16), t, int(l1), stream_ptr(x.device))
     if Np != N:
         y = y[:, :N]
     return y.reshape(*shape[:-1], N)

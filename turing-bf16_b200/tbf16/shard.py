@@ -1,0 +1,83 @@
+"""Multi-GPU partitions of the scaled path: one process per GPU, torch.distributed (NCCL over
+NVLink/NVSwitch) for the one exchange that exists.
+
+The path shards without changing any result:
+  - linear over rows (M): row scales depend only on their own row, so each rank runs its rows against
+    a replicated weight; nothing is exchanged (linear_rows).
+  - linear column-parallel over N: each rank holds N/P weight rows with their scales and bias and
+    computes y[:, its columns]; all_gather_into_tensor reassembles y (linear_column_parallel).
+  - attention over batch x heads: each rank takes a slice of the heads. The reference takes eq and ek,
+    the exponents that place q and k, as maxima over ALL (b, h) (attention.py:41), so the sharded call
+    makes them global with one all_reduce(MAX) of two int32 and then scales exactly as the unsharded
+    call would (prepare_qkv_sharded, sdpa_heads).
+The compute ops are parameters so the exchange logic can be checked on CPU with gloo.
+"""
+import torch
+import torch.distributed as dist
+
+from . import attention
+from .ops import scaled_linear
+
+
+def shard_range(n: int, rank: int, world: int, multiple: int = 1):
+    """Contiguous [start, stop) of n items for `rank`, in blocks of `multiple` (balanced)."""
+    blocks = (n + multiple - 1) // multiple
+    per, extra = divmod(blocks, world)
+    start = rank * per + min(rank, extra)
+    stop = start + per + (1 if rank < extra else 0)
+    return min(start * multiple, n), min(stop * multiple, n)
+
+
+def linear_rows(x, w16, w_sinv, bias=None, linear=scaled_linear):
+    """Row-sharded linear: this rank's rows of x against the full (replicated) weight. No collective."""
+    return linear(x, w16, w_sinv, bias)
+
+
+def shard_weight(w16, w_sinv, bias, rank, world):
+    """This rank's column-parallel slice of a prepared weight (rows of w16 in multiples of 8)."""
+    a, b = shard_range(w16.shape[0], rank, world, multiple=8)
+    return w16[a:b].contiguous(), w_sinv[a:b].contiguous(), None if bias is None else bias[a:b].contiguous()
+
+
+def linear_column_parallel(x, w16_shard, ws_shard, bias_shard=None, group=None, linear=scaled_linear):
+    """y = x @ W^T with W's rows split across ranks: local y[:, shard], then all_gather over the group.
+    Every rank's shard must have the same width (use shard_weight with N divisible by 8 * world)."""
+    world = dist.get_world_size(group)
+    y_local = linear(x, w16_shard, ws_shard, bias_shard)
+    x_shape = y_local.shape[:-1]
+    y2 = y_local.reshape(-1, y_local.shape[-1]).contiguous()
+    if dist.get_backend(group) == "nccl":
+        gathered = torch.empty((world, *y2.shape), device=y2.device, dtype=y2.dtype)
+        dist.all_gather_into_tensor(gathered, y2, group=group)
+    else:  # gloo (CPU tests): no all_gather_into_tensor and no bf16; a gather is a copy, so move the bytes
+        raw = torch.empty((world, y2.shape[0], y2.shape[1] * 2), device=y2.device, dtype=torch.uint8)
+        dist.all_gather(list(raw.unbind(0)), y2.view(torch.uint8), group=group)
+        gathered = raw.view(y2.dtype)
+    return gathered.permute(1, 0, 2).reshape(*x_shape, world * y2.shape[-1])
+
+
+def global_qk_exponents(q, k, group=None, head_exp=attention.head_exp):
+    """(eq, ek): maxima over every rank's (b, h) of the q and k head exponents (attention.py:41)."""
+    e = torch.stack([head_exp(q).amax(), head_exp(k).amax()]).to(torch.int32)
+    dist.all_reduce(e, op=dist.ReduceOp.MAX, group=group)
+    return e[0], e[1]
+
+
+def prepare_qkv_sharded(q, k, v, v_exp=0, group=None, head_exp=attention.head_exp, head_scale=attention.head_scale):
+    """prepare_qkv for this rank's heads with the global eq, ek: (q16, k16, v16, a, ev), identical to the
+    corresponding slice of the unsharded prepare_qkv (ev is per (b, h_kv), so it needs no exchange)."""
+    eq, ek = global_qk_exponents(q, k, group, head_exp)
+    a = torch.div(ek - eq, 2, rounding_mode="floor")
+    a = torch.maximum(torch.minimum(a, 14 - eq), ek - 14)
+    ev = head_exp(v) - v_exp
+    return head_scale(q, a, torch.float16), head_scale(k, -a, torch.float16), head_scale(v, -ev, torch.float16), a, ev
+
+
+@torch.autocast("cuda", enabled=False)
+def sdpa_heads(q, k, v, attn_mask=None, is_causal=False, scale=None, enable_gqa=False, group=None):
+    """Inference scaled attention on this rank's heads (q, k, v already sliced by head; GQA groups must not
+    straddle ranks). Same result as the matching heads of tbf16.sdpa on the full tensors."""
+    D0 = q.shape[-1]
+    q16, k16, v16, _, ev = prepare_qkv_sharded(q, k, v, v_exp=13, group=group)
+    out, _ = attention.attn_forward(q16, k16, v16, ev, attn_mask, is_causal, scale, d_orig=D0)
+    return out[..., :D0] if out.shape[-1] != D0 else out
