@@ -175,6 +175,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-attention", action="store_true")
+    ap.add_argument("--only-attention", action="store_true",
+                    help="time only the config-3 attention forward (S from --attn-S) and print its JSON; for profiling")
+    ap.add_argument("--attn-S", type=int, default=16384)
     ap.add_argument("--gemm", default="materialise", choices=["materialise", "fused"],
                     help="materialise (default, what tbf16_linear does with its x16 workspace): the row pass writes "
                          "fp16(x * s) and the GEMM runs on fp16 operands; fused: bf16 x converted inside the GEMM")
@@ -185,6 +188,11 @@ def main():
     config = {"workload": "scaled_linear (row-amax exponent + tcgen05 GEMM), BASELINE config 2", "M_per_rank": M,
               "N": N, "K": K, "global_M": M * world, "parallelism": f"M-sharded x{world} (no collective)",
               "l2": "inputs larger than L2 (384 MB per step)"}
+
+    if args.only_attention:
+        print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
+                                                     train=False)}))
+        return
 
     if args.impl == "reference":
         if rank != 0:
@@ -304,7 +312,7 @@ def main():
         dist.destroy_process_group()
 
 
-def attention_run(pk, S=16384, H=16, D=128, iters=5):
+def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
     """Config 3 (B=1, H=16, D=128, S=16k, Q/K overflow fp16): the scaled attention forward (prepare_qkv
     + tcgen05 flash attention) in TFLOPS, causal and not; kernel-only time against the bf16 peak."""
     import inputs
@@ -331,6 +339,27 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5):
         res[key] = {"tflops": round(flop / (t_all / 1e3) / 1e12, 1), "ms": round(t_all, 3),
                     "kernel_tflops": round(flop / (t_k / 1e3) / 1e12, 1),
                     "kernel_frac": round(flop / (t_k / 1e3) / 1e12 / pk["tflops"], 4)}
+    del q, k, v
+    if not train:
+        return res
+    # training attention (config 4 shape: B=2, H=16, S=4096, D=128, causal), forward + backward
+    from tbf16 import autograd
+    B2, S2 = 2, 4096
+    q, k, v = (t.requires_grad_() for t in inputs.attention_qkv(B2, H, S2, D, seed=4, device="cuda", qk_exp=0))
+    do = torch.randn(B2, H, S2, D, device="cuda").bfloat16() * 2.0 ** -20
+    flop = 3.5 * 4.0 * B2 * H * S2 * S2 * D * 0.5
+    for _ in range(2):
+        autograd.sdpa(q, k, v, is_causal=True).backward(do)
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(iters):
+        autograd.sdpa(q, k, v, is_causal=True).backward(do)
+    s1.record()
+    torch.cuda.synchronize()
+    t = s0.elapsed_time(s1) / iters
+    res["train_fwd_bwd_causal"] = {"config": f"B={B2} H={H} S={S2} D={D}, dY x2^-20", "ms": round(t, 3),
+                                   "tflops": round(flop / (t / 1e3) / 1e12, 1)}
     return res
 
 
