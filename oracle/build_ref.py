@@ -1,7 +1,8 @@
 """Builds the REFERENCE's own CUDA sources into oracle/_ref/ (TEST INFRASTRUCTURE ONLY).
 
 Compiles tbf16/csrc/gemm_sm75.cu and tbf16/csrc/small_kernels.cu of tech-cosmos/turing-bf16 where
-they lie (TBF16_REFERENCE, default /root/reference), as torch extensions for sm_100a, with the
+they lie (TBF16_REFERENCE, default: a `reference` directory beside this repository), as torch
+extensions for sm_100a, with the
 reference's own arithmetic flags (-O3 --use_fast_math, reference tbf16/_ext.py:52-53) and only the
 architecture changed. The reference's build system (its JIT loader) is not run. Outputs go only to
 oracle/_ref/ (git-ignored; the .so files travel to the GPU box with the source tree), where the GPU
@@ -17,7 +18,7 @@ import sys
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF = pathlib.Path(os.environ.get("TBF16_REFERENCE", "/root/reference"))
+REF = pathlib.Path(os.environ.get("TBF16_REFERENCE", str(HERE.parent.parent / "reference")))
 TARGETS = {"tbf16_ref_gemm": "gemm_sm75.cu", "tbf16_ref_small": "small_kernels.cu"}
 FLAGS = ["-O3", "-gencode=arch=compute_100a,code=sm_100a", "--use_fast_math"]
 

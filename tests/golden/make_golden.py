@@ -1,7 +1,7 @@
 """Generate golden vectors by running the REFERENCE's own code (tech-cosmos/turing-bf16) on CPU.
 
-Run in a container where the reference checkout is available (default /root/reference, override
-with TBF16_REFERENCE). Its CUDA kernels need a GPU, but its Triton kernels run on CPU under
+Run where the reference checkout is available (TBF16_REFERENCE, default: a `reference` directory
+beside this repository). Its CUDA kernels need a GPU, but its Triton kernels run on CPU under
 TRITON_INTERPRET=1 and its torch fallbacks run on CPU with tbf16.ops._USE_CUDA = False, so these
 reference code paths produce the fixtures:
   - ops.quantize_rows / ops.prepare_weight        (Triton _quantize_rows_kernel, ops.py:48-89)
@@ -21,7 +21,7 @@ import sys
 
 os.environ["TRITON_INTERPRET"] = "1"
 HERE = pathlib.Path(__file__).resolve().parent
-REF = os.environ.get("TBF16_REFERENCE", "/root/reference")
+REF = os.environ.get("TBF16_REFERENCE", str(HERE.parents[2] / "reference"))
 sys.path.insert(0, REF)
 sys.path.insert(0, str(HERE))
 
