@@ -74,6 +74,19 @@ int tbf16_quantize_rows(const void* x, int64_t rows, int64_t K, int64_t ldx, int
 int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp, const float* row_mul,
                         void* y16, int64_t ldy, float* s_inv, float* amax_ws, void* stream);
 
+/* Allocation-free variant of tbf16_quantize_cols, for callers that cannot allocate device memory where
+ * they call in (an arena that owns every allocation, a plugin without access to its host's allocator, a
+ * path where cudaMalloc's implicit synchronisation is not allowed). Same inputs, outputs and results;
+ * the K-float column-maximum workspace lives in a file-scope device array of TBF16_NOALLOC_MAX_COLS
+ * floats (256 KB) that every GPU loading the library holds until exit. K > TBF16_NOALLOC_MAX_COLS
+ * returns TBF16_ERR_INVALID. No cudaMalloc / cudaFree. All calls on a GPU share the array: calls that
+ * overlap on the GPU race. The first call on each device resolves the array's address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * No counterpart in the reference (its extension allocates every workspace with torch::empty). */
+#define TBF16_NOALLOC_MAX_COLS 65536
+int tbf16_quantize_cols_noalloc(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp,
+                                const float* row_mul, void* y16, int64_t ldy, float* s_inv, void* stream);
+
 /* ------------------------------------------------------------------ attention scales */
 
 /* Per-(b, h) amax of a strided (B, H, S, D) tensor with contiguous D. Replaces head_amax(x)

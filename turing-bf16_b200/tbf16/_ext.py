@@ -26,6 +26,7 @@ SIGNATURES = {
     "tbf16_row_scale": [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tbf16_quantize_rows": [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _vp],
     "tbf16_quantize_cols": [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _vp, _vp, _vp],
+    "tbf16_quantize_cols_noalloc": [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _vp, _vp],
     "tbf16_head_amax": [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp],
     "tbf16_head_exp": [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp],
     "tbf16_head_scale_cast": [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp],
