@@ -175,9 +175,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-attention", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-5 Gemma-shaped prefill")
     ap.add_argument("--only-attention", action="store_true",
                     help="time only the config-3 attention forward (S from --attn-S) and print its JSON; for profiling")
     ap.add_argument("--attn-S", type=int, default=16384)
+    ap.add_argument("--attn-train", action="store_true", help="with --only-attention: also time fwd+bwd (config 4)")
     ap.add_argument("--gemm", default="materialise", choices=["materialise", "fused"],
                     help="materialise (default, what tbf16_linear does with its x16 workspace): the row pass writes "
                          "fp16(x * s) and the GEMM runs on fp16 operands; fused: bf16 x converted inside the GEMM")
@@ -191,7 +193,7 @@ def main():
 
     if args.only_attention:
         print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
-                                                     train=False)}))
+                                                     train=args.attn_train)}))
         return
 
     if args.impl == "reference":
@@ -301,6 +303,9 @@ def main():
             line["attention"] = attention_run(pk)
         except Exception as exc:  # the headline GEMM line still prints
             line["attention"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    if not args.no_prefill:
+        torch.cuda.empty_cache()
+        line["prefill"] = prefill_run(world)  # every rank runs its own sequence (replicas)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
@@ -310,6 +315,106 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+class _RMSNorm(torch.nn.Module):
+    def __init__(self, n):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.zeros(n))
+
+    def forward(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * (1.0 + self.weight.float())).to(x.dtype)
+
+
+class _GemmaLayer(torch.nn.Module):
+    """One Gemma-3-shaped decoder layer (hidden 2560, 8 query / 4 KV heads of 256, GeGLU 10240,
+    RMSNorm before and after each block, QK-norm, RoPE)."""
+
+    def __init__(self, hidden=2560, heads=8, kv_heads=4, head_dim=256, inter=10240):
+        super().__init__()
+        L = lambda i, o: torch.nn.Linear(i, o, bias=False)
+        self.h, self.kv, self.d = heads, kv_heads, head_dim
+        self.q_proj, self.k_proj = L(hidden, heads * head_dim), L(hidden, kv_heads * head_dim)
+        self.v_proj, self.o_proj = L(hidden, kv_heads * head_dim), L(heads * head_dim, hidden)
+        self.gate_proj, self.up_proj, self.down_proj = L(hidden, inter), L(hidden, inter), L(inter, hidden)
+        self.in_norm, self.post_attn_norm = _RMSNorm(hidden), _RMSNorm(hidden)
+        self.pre_ff_norm, self.post_ff_norm = _RMSNorm(hidden), _RMSNorm(hidden)
+        self.q_norm, self.k_norm = _RMSNorm(head_dim), _RMSNorm(head_dim)
+
+    def forward(self, x, cos, sin):
+        import torch.nn.functional as F
+        B, S, _ = x.shape
+        h = self.in_norm(x)
+        q = self.q_norm(self.q_proj(h).view(B, S, self.h, self.d)).transpose(1, 2)
+        k = self.k_norm(self.k_proj(h).view(B, S, self.kv, self.d)).transpose(1, 2)
+        v = self.v_proj(h).view(B, S, self.kv, self.d).transpose(1, 2)
+        rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
+        q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        x = x + self.post_attn_norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)))
+        h = self.pre_ff_norm(x)
+        g = F.gelu(self.gate_proj(h), approximate="tanh") * self.up_proj(h)
+        return x + self.post_ff_norm(self.down_proj(g))
+
+
+def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
+    """Config 5: Gemma-3-4B-shaped decoder prefill, random bf16 weights N(0, 0.02^2), one 2048-token
+    sequence of uniform random ids per GPU, a few residual channels scaled to ~1e5 (plain .half()
+    overflows), logits for the last token through the tied embedding. tbf16.convert puts every
+    linear on the tcgen05 GEMM and the attention on the head-dim-256 kernel (all layers causal here:
+    Gemma's sliding-window layers are run as global attention, the larger attention cost)."""
+    import tbf16
+    torch.manual_seed(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    with torch.device(dev):
+        embed = torch.nn.Embedding(vocab, hidden).bfloat16()
+        torch.nn.init.normal_(embed.weight, std=0.02)
+        model = torch.nn.ModuleList([_GemmaLayer() for _ in range(layers)]).bfloat16()
+        for m in model.modules():
+            if isinstance(m, torch.nn.Linear):
+                torch.nn.init.normal_(m.weight, std=0.02)
+        final_norm = _RMSNorm(hidden).bfloat16()
+    tbf16.convert(model)  # nn.Linear -> tbf16.Linear (fp16 + row scales); SDPA routed to the scaled kernels
+    pos = torch.arange(seq, device=dev, dtype=torch.float32)
+    inv = 1.0 / (1e6 ** (torch.arange(0, 256, 2, device=dev, dtype=torch.float32) / 256))
+    ang = torch.outer(pos, inv)
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16()[None, None]
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16()[None, None]
+    ids = torch.randint(0, vocab, (1, seq), device=dev, generator=torch.Generator(device=dev).manual_seed(1 + dist_rank()))
+    outlier = torch.zeros(hidden, device=dev, dtype=torch.bfloat16)
+    outlier[torch.randperm(hidden, device=dev)[:4]] = 1.0
+
+    @torch.no_grad()
+    def step():
+        x = embed(ids) * (hidden ** 0.5)
+        x = x + outlier * 1e5
+        for layer in model:
+            x = layer(x, cos, sin)
+        return final_norm(x[:, -1]) @ embed.weight.t()
+
+    for _ in range(2):
+        logits = step()
+    torch.cuda.synchronize()
+    finite = bool(torch.isfinite(logits.float()).all())
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    s.record()
+    for _ in range(iters):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / iters, world)
+    tbf16.uninstall_sdpa()
+    lin_params = layers * (hidden * (2048 + 1024 + 1024) + 2048 * hidden + 3 * hidden * 10240)
+    flop = 2.0 * seq * lin_params + layers * 4.0 * 8 * seq * seq * 256 * 0.5 + 2.0 * hidden * vocab
+    return {"config": f"Gemma-3-4B-shaped, {layers} layers, {seq} tokens per GPU, {world} GPU(s) (replicas)",
+            "ms_per_prefill": round(ms, 2), "tokens_per_s_all_gpus": round(world * seq / (ms / 1e3), 1),
+            "tflops_per_gpu": round(flop / (ms / 1e3) / 1e12, 1), "finite_logits": finite}
+
+
+def dist_rank():
+    return int(os.environ.get("RANK", "0"))
 
 
 def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):

@@ -70,10 +70,19 @@ def test_sdpa_cross_lengths_and_masks():
         _check_out(out, q, k, v, False, mask=mask)
 
 
-def test_sdpa_head_dim_padding():
-    """Head dims that are not 64/128 are zero-padded (logits unchanged) and sliced back."""
+@pytest.mark.parametrize("B,H,Hkv,S,causal", [(1, 8, 4, 2048, True), (2, 2, 1, 333, False)])
+def test_sdpa_head_dim_256(B, H, Hkv, S, causal):
+    """Gemma-3-shaped attention (head dim 256, GQA 8/4, causal prefill) through the D=256 kernel."""
     from tbf16 import attention
-    for D in (32, 112):
+    q, k, v = inputs.attention_qkv(B, H, S, 256, seed=S + 256, Hkv=Hkv, qk_exp=4)
+    out = attention.sdpa(q.cuda(), k.cuda(), v.cuda(), is_causal=causal, enable_gqa=Hkv != H)
+    _check_out(out, q, k, v, causal)
+
+
+def test_sdpa_head_dim_padding():
+    """Head dims that are not 64/128/256 are zero-padded (logits unchanged) and sliced back."""
+    from tbf16 import attention
+    for D in (32, 112, 200):
         q, k, v = inputs.attention_qkv(1, 2, 130, D, seed=D)
         out = attention.sdpa(q.cuda(), k.cuda(), v.cuda())
         assert out.shape == (1, 2, 130, D)

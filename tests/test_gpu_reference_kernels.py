@@ -43,6 +43,24 @@ def test_linear_vs_reference_fused_kernel(M, K, N):
     assert rel_err(y, exact) < 2e-3 and rel_err(y_ref, exact) < 2e-3
 
 
+def test_reference_fused_kernel_zero_row_behaviour():
+    """Documents the reference's fast-math behaviour on an all-zero row: its s_inv = 2^-127 flushes to 0,
+    the kernel converts with 1/0 and the row comes out NaN; this build returns the bias for that row."""
+    from tbf16 import ops
+    ref = _ref("tbf16_ref_gemm")
+    x = inputs.gemm_x(256, 512, seed=1, device="cuda")
+    x[3] = 0
+    w = inputs.gemm_w(256, 512, seed=2, device="cuda")
+    b = (torch.randn(256, device="cuda") * 0.1).bfloat16()
+    w16, ws = ops.prepare_weight(w)
+    y_ref = ref.linear(x, w16, ws, b, -1, 15, False)
+    y = ops.scaled_linear(x, w16, ws, b)
+    assert torch.isnan(y_ref[3].float()).all()
+    assert torch.equal(y[3], b)
+    others = torch.arange(256, device="cuda") != 3
+    assert torch.isfinite(y_ref[others].float()).all()
+
+
 def test_row_scale_vs_reference_kernel():
     ref = _ref("tbf16_ref_gemm")
     from tbf16 import _ext as E

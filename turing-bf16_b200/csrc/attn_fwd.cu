@@ -50,9 +50,12 @@ struct FwdCfg {
   static constexpr int ATOMS = D / 64;            // 64-column swizzle atoms per row
   static constexpr int TILE_BYTES = ATOMS * 128 * 128;  // 128 rows x D fp16
   static constexpr int Q_OFF = 0;
+  // K/V ring depth: 2 stages up to D = 128; at D = 256 one stage fits in shared memory (the next V
+  // tile loads while the softmax of the next S runs, so the single stage costs little).
+  static constexpr int KS = D == 256 ? 1 : 2;
   static constexpr int K_OFF = Q_OFF + TILE_BYTES;
-  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
-  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + KS * TILE_BYTES;
+  static constexpr int P_OFF = V_OFF + KS * TILE_BYTES;
   static constexpr int P_BYTES = 2 * 128 * 128;        // 128 rows x 128 keys fp16
   static constexpr int BAR_OFF = P_OFF + P_BYTES;
   static constexpr int SMEM = 1024 + BAR_OFF + 256;
@@ -131,8 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int a = 0; a < C::ATOMS; ++a) tma_load_3d(smem + C::Q_OFF + a * 16384, &tmQ, q_full, a * 64, m0, bh);
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % C::KS;
+        const uint32_t ph = (j / C::KS) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) break;
         mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
 #pragma unroll
@@ -152,9 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_addr = smem_u32(smem + C::Q_OFF);
       const uint32_t p_addr = smem_u32(smem + C::P_OFF);
       auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
+        const int st = i % C::KS;
         if (!mbar_wait(p_full, i & 1, abort, p.err)) return false;
-        if (!mbar_wait(&v_full[st], (i >> 1) & 1, abort, p.err)) return false;
+        if (!mbar_wait(&v_full[st], (i / C::KS) & 1, abort, p.err)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::TILE_BYTES);
 #pragma unroll
@@ -170,22 +173,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       bool ok = mbar_wait(q_full, 0, abort, p.err);
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, abort, p.err) || !mbar_wait(&s_empty[st], ph ^ 1, abort, p.err)) {
+        const int sb = j & 1;  // S buffer in TMEM (always two)
+        const int ks = j % C::KS;  // K stage in shared memory
+        if (!mbar_wait(&k_full[ks], (j / C::KS) & 1, abort, p.err) ||
+            !mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, abort, p.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + C::K_OFF + st * C::TILE_BYTES);
+        const uint32_t k_addr = smem_u32(smem + C::K_OFF + ks * C::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16_ss(tmem + st * BN, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+          umma_f16_ss(tmem + sb * BN, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
                       idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
-        umma_commit(&k_empty[st]);
+        umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[ks]);
         if (j >= 1) ok = issue_pv(j - 1);
       }
       if (ok) issue_pv(n_kv - 1);
@@ -363,7 +367,7 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq < 0 || Sk < 0 || !ev || !out || B * Hq > 65535 ||
       Sq > INT32_MAX || Sk > INT32_MAX)
     return TBF16_ERR_INVALID;
-  if (D != 64 && D != 128) return TBF16_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128 && D != 256) return TBF16_ERR_UNSUPPORTED;
   if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16) ||
       !tbf16_host::aligned16(out) || !tbf16_host::aligned16(o16))
     return TBF16_ERR_ALIGN;
@@ -386,5 +390,7 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
   prm.m_tiles = (int)((Sq + BM - 1) / BM);
   if (Sk == 0) return TBF16_ERR_UNSUPPORTED;
   auto st = static_cast<cudaStream_t>(stream);
-  return D == 64 ? launch_fwd<64>(q16, k16, v16, prm, st) : launch_fwd<128>(q16, k16, v16, prm, st);
+  if (D == 64) return launch_fwd<64>(q16, k16, v16, prm, st);
+  if (D == 128) return launch_fwd<128>(q16, k16, v16, prm, st);
+  return launch_fwd<256>(q16, k16, v16, prm, st);
 }

@@ -17,7 +17,8 @@ from . import _ext
 from ._ext import BF16, F16, call, ptr, require_cuda, stream_ptr
 
 _DTYPE = {torch.bfloat16: BF16, torch.float16: F16}
-KERNEL_D = (64, 128)
+KERNEL_D = (64, 128, 256)      # forward kernel head dims (others are zero-padded up)
+KERNEL_D_TRAIN = (64, 128)     # backward kernel head dims
 
 
 def _fast(x: torch.Tensor):
@@ -113,9 +114,9 @@ def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None,
     Hkv, Sk = k16.shape[1], k16.shape[2]
     d_orig = d_orig or D
     sc = (1.0 / math.sqrt(d_orig)) if scale is None else float(scale)
-    Dk = 64 if D <= 64 else 128
-    if D > 128:
-        raise NotImplementedError("tbf16 attention on B200: head dims up to 128 in this build")
+    Dk = 64 if D <= 64 else 128 if D <= 128 else 256
+    if D > 256:
+        raise NotImplementedError("tbf16 attention on B200: head dims up to 256")
     if D != Dk:  # zero columns leave the logits unchanged and give zero output columns
         pad = (0, Dk - D)
         q16, k16, v16 = (torch.nn.functional.pad(t, pad) for t in (q16, k16, v16))

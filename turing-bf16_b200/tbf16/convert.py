@@ -32,8 +32,10 @@ MIN_DIM = int(os.environ.get("TBF16_MIN_DIM", 128))
 # Attention with fewer query rows (decoding) runs natively (reference convert.py:30).
 MIN_QUERY_ROWS = 16
 
-# Head dims the scaled attention kernels take (others are zero-padded up to these).
-MAX_HEAD_DIM = 128
+# Head dims the scaled attention kernels take (smaller ones are zero-padded up to 64 / 128 / 256): the
+# forward up to 256 (the reference's routing limit), the backward up to 128.
+MAX_HEAD_DIM = 256
+MAX_HEAD_DIM_TRAIN = 128
 
 
 class Linear(nn.Module):
@@ -93,7 +95,9 @@ def _sdpa(query, key, value, *args, **kwargs):  # torch's parameter names: calle
     if (q.dtype == k.dtype == v.dtype == torch.bfloat16 and q.is_cuda and q.dim() == 4
             and q.shape[-1] <= MAX_HEAD_DIM and q.shape[-2] >= MIN_QUERY_ROWS):
         if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-            return autograd.sdpa(q, k, v, *args, **kwargs)
+            if q.shape[-1] <= MAX_HEAD_DIM_TRAIN:
+                return autograd.sdpa(q, k, v, *args, **kwargs)
+            return _native_sdpa(q, k, v, *args, **kwargs)  # no head-dim-256 backward kernel yet
         return sdpa(q, k, v, *args, **kwargs)
     return _native_sdpa(q, k, v, *args, **kwargs)
 
