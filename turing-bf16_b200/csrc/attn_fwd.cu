@@ -69,6 +69,20 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x for x <= 0 (or -inf) on the FMA pipe: Cody-Waite split x = n + f with n = rint(x) (adding
+// 1.5 * 2^23 rounds to an integer in the low mantissa bits), 2^f on [-1/2, 1/2] by a degree-3
+// polynomial fitted here for minimum maximum relative error (7.5e-5, below fp16's half ulp 2.4e-4,
+// the precision P is kept in), and 2^n added into the exponent field. Inputs below -120 give 2^-120,
+// which rounds to zero in fp16 and is negligible in the fp32 row sum.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -120.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  const float q = fmaf(fmaf(fmaf(0.0551716685295105f, f, 0.2426111400127411f), f, 0.6932609677314758f), f,
+                       0.9999280571937561f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
 // Byte offset of 16-byte chunk c (0..15 for 128 fp16 columns) of row r in a K-major tile made of
 // 64-column 128B-swizzled atoms of 128 rows each.
 __device__ __forceinline__ uint32_t swz_off(int r, int c) {
@@ -336,6 +350,327 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Head dims 64 and 128: one CTA per SM works on two 128-row query tiles of the same head ("tile 0"
+// and "tile 1") that share every K and V tile. TMEM holds S and O of both tiles (S0 [0,128),
+// O0 [128,256), S1 [256,384), O1 [384,512)); P is written back over its S columns as packed fp16 and
+// the P.V MMA reads its A operand from TMEM. The MMA warp alternates the tiles,
+//   S0_0 S1_0 | PV0_0 S0_1 | PV1_0 S1_1 | PV0_1 S0_2 | PV1_1 S1_2 | ...
+// so the tensor core computes one tile's P.V and next S while the other tile's softmax runs. The
+// MMA pipe executes one CTA's MMAs in issue order: S0_{j+1} overwrites P0_j only after PV0_j has
+// read it, and when S0_{j+1} completes PV0_j has completed too (O0 may be rescaled without another
+// wait). K and V go through two-stage rings.
+//   warps 0-3  softmax + epilogue of tile 0 (warp w reads TMEM lanes 32 (w % 4) ..)
+//   warps 4-7  softmax + epilogue of tile 1
+//   warp 8     TMA producer          warp 9  MMA issuer (+ TMEM allocation)
+constexpr int kPPThreads = 320;
+
+template <int D>
+struct FwdPPCfg {
+  static constexpr int ATOMS = D / 64;
+  static constexpr int TILE_BYTES = ATOMS * 128 * 128;
+  static constexpr int STAGES = 2;
+  static constexpr int Q_OFF = 0;  // two Q tiles
+  static constexpr int K_OFF = 2 * TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + STAGES * TILE_BYTES;
+  static constexpr int BAR_OFF = V_OFF + STAGES * TILE_BYTES;
+  static constexpr int SMEM = 1024 + BAR_OFF + 256;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kPPThreads, 1)
+    attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
+  using C = FwdPPCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [tile]
+  uint64_t* p_full = bars + 11;  // [tile]
+  uint64_t* pv_done = bars + 13; // [tile]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int bhk = b * p.Hkv + h / p.group;
+  const int pairs = (p.m_tiles + 1) >> 1;
+  const int pair = p.causal ? (pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy pairs first
+  const int m0 = pair * 2 * BM;
+  // key tiles per query tile (tile 1 may lie past the end of the sequence: no work)
+  auto kv_tiles = [&](int t) -> int {
+    const int r0 = m0 + t * BM;
+    if (r0 >= p.Sq) return 0;
+    const int kv_end = p.causal ? min(p.Sk, r0 + BM) : p.Sk;
+    return (kv_end + BN - 1) / BN;
+  };
+  const int n0 = kv_tiles(0), n1 = kv_tiles(1);
+  const int n_kv = max(n0, n1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && n_kv > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::Q_OFF + t * C::TILE_BYTES + a * 16384, &tmQ, q_full, a * 64, m0 + t * BM, bh);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::K_OFF + st * C::TILE_BYTES + a * 16384, &tmK, &k_full[st], a * 64, j * BN, bhk);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + a * 16384, &tmV, &v_full[st], a * 64, j * BN, bhk);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, false, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(BM, D, false, true);
+      // descriptors: a k16 step adds its byte offset / 16 to the 14-bit start-address field (shared
+      // addresses stay below 2^18 bytes, so it cannot carry out)
+      const uint64_t qd0 = smem_desc_sw128(smem_u32(smem + C::Q_OFF), 16, 1024);
+      const uint64_t kd0 = smem_desc_sw128(smem_u32(smem + C::K_OFF), 16, 1024);
+      const uint64_t vd0 = smem_desc_sw128(smem_u32(smem + C::V_OFF), 16384, 1024);
+      constexpr uint32_t kTile16 = C::TILE_BYTES >> 4;
+      auto issue_s = [&](int t, int j) {  // S_t = Q_t K_j^T into the S columns of tile t
+        const uint64_t qd = qd0 + t * kTile16, kd = kd0 + (j & 1) * kTile16;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off16 = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_f16_ss(tmem + t * 256, qd + off16, kd + off16, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {  // O_t += P_t V_j, P (128 x 128 fp16) from TMEM
+        const uint64_t vd = vd0 + (j & 1) * kTile16;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&k_full[0], 0, abort, p.err);
+      if (ok) {
+        tc_fence_after();
+        if (n0 > 0) issue_s(0, 0);
+        if (n1 > 0) issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        const bool next = j + 1 < n_kv;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort, p.err)) break;
+        if (next && !mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, abort, p.err)) break;
+        for (int t = 0; t < 2; ++t) {
+          const int nt = t == 0 ? n0 : n1;
+          if (j >= nt) continue;
+          if (!mbar_wait(&p_full[t], j & 1, abort, p.err)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < nt) issue_s(t, j + 1);
+          else umma_commit(&pv_done[t]);
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[st]);
+        if (next) umma_commit(&k_empty[st ^ 1]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int t = warp >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int m_t = m0 + t * BM;
+    const int qi = m_t + r;
+    const int nt = t == 0 ? n0 : n1;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + t * 256;
+    const uint32_t o_addr = s_addr + 128;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!mbar_wait_warp(&s_full[t], j & 1, abort, p.err)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = j * BN;
+      const bool full_tile = p.mask == nullptr && k0 + BN <= p.Sk && (!p.causal || k0 + BN - 1 <= m_t);
+      // Logits of a full tile stay raw (s) and are scaled inside the exp, p = 2^(s * c - m) with
+      // c = scale * log2(e) > 0 (the max commutes with it). A partial tile (sequence end, causal
+      // diagonal, user mask) maps s to the scaled, masked logit first and uses c = 1.
+      const float c_scale = full_tile ? p.scale_log2 : 1.f;
+      // the whole 128-column S row in registers: four loads in flight, one wait
+      uint32_t rr[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
+      tmem_ld_wait();
+      if (!full_tile) {
+        const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
+#pragma unroll
+        for (int e = 0; e < BN; ++e) {
+          const int kj = k0 + e;
+          const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
+          float v = __uint_as_float(rr[e]) * p.scale_log2;
+          if (mrow && valid) v += __half2float(__ushort_as_half(mrow[e])) * 1.4426950408889634f;
+          rr[e] = __float_as_uint(valid ? v : -INFINITY);
+        }
+      }
+      float m8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
+#pragma unroll
+      for (int e = 8; e < BN; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(rr[e]));
+      const float mx =
+          fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * c_scale;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
+        alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+        rescale = j > 0;
+        m_used = mx;
+        l *= alpha;
+      }
+      // P = 2^(logit - m) packed to fp16 in place (pair e/2 overwrites a register already read), one
+      // pair in four through the FMA-pipe exp2 so the MUFU pipe is not the only exp unit
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int e = 0; e < BN; e += 2) {
+        const float x0 = fmaf(__uint_as_float(rr[e]), c_scale, -base);
+        const float x1 = fmaf(__uint_as_float(rr[e + 1]), c_scale, -base);
+        float p0, p1;
+        if (((e >> 1) & 3) == 3) {
+          p0 = ex2_poly(x0);
+          p1 = ex2_poly(x1);
+        } else {
+          p0 = ex2(x0);
+          p1 = ex2(x1);
+        }
+        sum8[(e >> 1) & 7] += p0 + p1;
+        rr[e >> 1] = pack_f16(p0, p1);
+      }
+      l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      // P of keys [0, 128) onto S columns [0, 64)
+      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+      // O is complete up to P.V_{j-1} (it precedes S_j in the MMA pipe): rescale it in place if needed
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * (rescale ? alpha : 1.f));
+          tmem_st32(o_addr + c * 32, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && nt > 0 && mbar_wait_warp(&pv_done[t], 0, abort, p.err)) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float sc = exp2i(__ldg(p.ev + bhk));
+      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D;
+      __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c * 32, o);
+        tmem_ld_wait();
+        if (qi < p.Sq) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(o[8 * g + e]) * inv_l;
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) =
+                make_uint4(pack_bf16(v[0] * sc, v[1] * sc), pack_bf16(v[2] * sc, v[3] * sc),
+                           pack_bf16(v[4] * sc, v[5] * sc), pack_bf16(v[6] * sc, v[7] * sc));
+            if (o16row)
+              *reinterpret_cast<uint4*>(o16row + c * 32 + g * 8) = make_uint4(
+                  pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
+          }
+        }
+      }
+      if (p.lse && qi < p.Sq) p.lse[(int64_t)bh * p.lse_ld + qi] = (m_used + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch_fwd_pp(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
+  using C = FwdPPCfg<D>;
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  if (!dev) return TBF16_ERR_DEVICE;
+  CUtensorMap tq, tk, tv;
+  const int64_t BHq = (int64_t)prm.B * prm.Hq, BHk = (int64_t)prm.B * prm.Hkv;
+  if (int rc = tbf16_host::make_tmap_3d(&tq, q16, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 64, BM)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tk, k16, D, prm.Sk, BHk, D, (uint64_t)prm.Sk * D, 64, BN)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, prm.Sk, BHk, D, (uint64_t)prm.Sk * D, 64, BN)) return rc;
+  static bool attr_done[64] = {false};
+  if (!attr_done[dev->device & 63]) {
+    if (cudaFuncSetAttribute(attn_fwd_pp_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return tbf16_host::check_launch();
+    attr_done[dev->device & 63] = true;
+  }
+  dim3 grid((prm.m_tiles + 1) / 2, (unsigned)BHq);
+  attn_fwd_pp_kernel<D><<<grid, kPPThreads, C::SMEM, st>>>(tq, tk, tv, prm);
+  return tbf16_host::check_launch();
+}
+
 template <int D>
 int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
   using C = FwdCfg<D>;
@@ -390,7 +725,12 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
   prm.m_tiles = (int)((Sq + BM - 1) / BM);
   if (Sk == 0) return TBF16_ERR_UNSUPPORTED;
   auto st = static_cast<cudaStream_t>(stream);
-  if (D == 64) return launch_fwd<64>(q16, k16, v16, prm, st);
-  if (D == 128) return launch_fwd<128>(q16, k16, v16, prm, st);
+  // D <= 128: the two-query-tile kernel (P in TMEM); TBF16_ATTN_FWD=1 selects the one-tile kernel
+  static const bool one_cta = [] {
+    const char* e = getenv("TBF16_ATTN_FWD");
+    return e && e[0] == '1';
+  }();
+  if (D == 64) return one_cta ? launch_fwd<64>(q16, k16, v16, prm, st) : launch_fwd_pp<64>(q16, k16, v16, prm, st);
+  if (D == 128) return one_cta ? launch_fwd<128>(q16, k16, v16, prm, st) : launch_fwd_pp<128>(q16, k16, v16, prm, st);
   return launch_fwd<256>(q16, k16, v16, prm, st);
 }
