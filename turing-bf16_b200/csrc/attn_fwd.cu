@@ -28,6 +28,7 @@ constexpr int BN = 128;  // keys per tile
 constexpr int kSoftmaxWarps = 4;
 constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
 constexpr float kRescaleLog2 = 8.0f;  // keep a stale max until the true one exceeds it by 2^8
+constexpr int kPolyPairsOf8 = 3;      // exp2 pairs (of every 8) computed on the FMA pipe
 
 struct AttnFwdParams {
   int B, Hq, Hkv, Sq, Sk;
@@ -69,18 +70,49 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x for x <= 0 (or -inf) on the FMA pipe: Cody-Waite split x = n + f with n = rint(x) (adding
-// 1.5 * 2^23 rounds to an integer in the low mantissa bits), 2^f on [-1/2, 1/2] by a degree-3
+// Packed fp32 pairs (sm_100 executes one f32x2 add / mul / fma per lane per instruction).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t d, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 0 (or -inf) on the FMA pipe: Cody-Waite split x = n + f with n = rint(x)
+// (adding 1.5 * 2^23 rounds to an integer in the low mantissa bits), 2^f on [-1/2, 1/2] by a degree-3
 // polynomial fitted here for minimum maximum relative error (7.5e-5, below fp16's half ulp 2.4e-4,
 // the precision P is kept in), and 2^n added into the exponent field. Inputs below -120 give 2^-120,
 // which rounds to zero in fp16 and is negligible in the fp32 row sum.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -120.f);
-  const float t = __fadd_rn(x, 12582912.f);
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
-  const float q = fmaf(fmaf(fmaf(0.0551716685295105f, f, 0.2426111400127411f), f, 0.6932609677314758f), f,
-                       0.9999280571937561f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -120.f), fmaxf(x1, -120.f));
+  const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);
+  uint64_t q = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), f, f2_pack(0.2426111400127411f, 0.2426111400127411f));
+  q = f2_fma(q, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  q = f2_fma(q, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
 // Byte offset of 16-byte chunk c (0..15 for 128 fp16 columns) of row r in a K-major tile made of
@@ -362,8 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // wait). K and V go through two-stage rings.
 //   warps 0-3  softmax + epilogue of tile 0 (warp w reads TMEM lanes 32 (w % 4) ..)
 //   warps 4-7  softmax + epilogue of tile 1
-//   warp 8     TMA producer          warp 9  MMA issuer (+ TMEM allocation)
-constexpr int kPPThreads = 320;
+//   warp 8     TMA producer          warp 9  MMA issuer (+ TMEM allocation)     warps 10-11 idle
+// The CTA launches with 168 registers per thread (12 warps); the third warpgroup (warps 8-11) drops
+// to 72 and the two softmax warpgroups rise to 216, so a thread holds its whole 128-logit row with
+// room for the exp pipeline: 72 * 128 + 216 * 256 = 64512 = 168 * 384 (and per sub-partition the
+// 216 + 216 + 72 registers of its three warps fit its 16384).
+constexpr int kPPThreads = 384;
+constexpr uint32_t kPPRegsLaunch = 168, kPPRegsSoftmax = 216, kPPRegsOther = 72;
+static_assert(kPPRegsOther * 128 + kPPRegsSoftmax * 256 <= kPPRegsLaunch * kPPThreads, "register split");
 
 template <int D>
 struct FwdPPCfg {
@@ -437,7 +475,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  // each role's code sits under its warpgroup's register re-split
+  if (warp >= 8) {
+    setmaxnreg_dec<kPPRegsOther>();
+    if (warp == 8) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n_kv > 0) {
       mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
@@ -461,9 +502,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + a * 16384, &tmV, &v_full[st], a * 64, j * BN, bhk);
       }
     }
-  } else if (warp == 9) {
+    } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && n_kv > 0) {
+    // The whole warp runs the loop so operands stay warp-uniform; one elected lane issues.
+    if (n_kv > 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(BM, D, false, true);
       // descriptors: a k16 step adds its byte offset / 16 to the 14-bit start-address field (shared
@@ -488,33 +530,44 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
                       (j > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&k_full[0], 0, abort, p.err);
+      bool ok = mbar_wait_warp(q_full, 0, abort, p.err) && mbar_wait_warp(&k_full[0], 0, abort, p.err);
       if (ok) {
         tc_fence_after();
-        if (n0 > 0) issue_s(0, 0);
-        if (n1 > 0) issue_s(1, 0);
-        umma_commit(&k_empty[0]);
+        if (elect_one()) {
+          if (n0 > 0) issue_s(0, 0);
+          if (n1 > 0) issue_s(1, 0);
+          umma_commit(&k_empty[0]);
+        }
+        __syncwarp();
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j & 1;
         const bool next = j + 1 < n_kv;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort, p.err)) break;
-        if (next && !mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, abort, p.err)) break;
+        if (!mbar_wait_warp(&v_full[st], (j >> 1) & 1, abort, p.err)) break;
+        if (next && !mbar_wait_warp(&k_full[st ^ 1], ((j + 1) >> 1) & 1, abort, p.err)) break;
         for (int t = 0; t < 2; ++t) {
           const int nt = t == 0 ? n0 : n1;
           if (j >= nt) continue;
-          if (!mbar_wait(&p_full[t], j & 1, abort, p.err)) { ok = false; break; }
+          if (!mbar_wait_warp(&p_full[t], j & 1, abort, p.err)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < nt) issue_s(t, j + 1);
-          else umma_commit(&pv_done[t]);
+          if (elect_one()) {
+            issue_pv(t, j);
+            if (j + 1 < nt) issue_s(t, j + 1);
+            else umma_commit(&pv_done[t]);
+          }
+          __syncwarp();
         }
         if (!ok) break;
-        umma_commit(&v_empty[st]);
-        if (next) umma_commit(&k_empty[st ^ 1]);
+        if (elect_one()) {
+          umma_commit(&v_empty[st]);
+          if (next) umma_commit(&k_empty[st ^ 1]);
+        }
+        __syncwarp();
       }
     }
+    }
   } else {
+    setmaxnreg_inc<kPPRegsSoftmax>();
     // ---------------------------------------------------------------- softmax + epilogue
     const int t = warp >> 2;
     const int quad = warp & 3;
@@ -552,13 +605,13 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           rr[e] = __float_as_uint(valid ? v : -INFINITY);
         }
       }
+      // row max: 8 independent 3-input max chains
       float m8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
 #pragma unroll
-      for (int e = 8; e < BN; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(rr[e]));
-      const float mx =
-          fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * c_scale;
+      for (int e = 8; e < BN; e += 2) m8[(e >> 1) & 7] = max3f(m8[(e >> 1) & 7], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+      const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * c_scale;
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
@@ -567,26 +620,30 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         m_used = mx;
         l *= alpha;
       }
-      // P = 2^(logit - m) packed to fp16 in place (pair e/2 overwrites a register already read), one
-      // pair in four through the FMA-pipe exp2 so the MUFU pipe is not the only exp unit
+      // P = 2^(logit - m) packed to fp16 in place (pair e/2 overwrites a register already read); the
+      // scaling and the row sum run on fp32 pairs, and three pairs in eight take the FMA-pipe exp2 so
+      // the MUFU pipe is not the only exp unit
       const float base = m_used == -INFINITY ? 0.f : m_used;
-      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const uint64_t c2 = f2_pack(c_scale, c_scale), nb2 = f2_pack(-base, -base);
+      uint64_t sum4[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int e = 0; e < BN; e += 2) {
-        const float x0 = fmaf(__uint_as_float(rr[e]), c_scale, -base);
-        const float x1 = fmaf(__uint_as_float(rr[e + 1]), c_scale, -base);
-        float p0, p1;
-        if (((e >> 1) & 3) == 3) {
-          p0 = ex2_poly(x0);
-          p1 = ex2_poly(x1);
+        float x0, x1, p0, p1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), c2, nb2), x0, x1);
+        if (((e >> 1) & 7) >= 8 - kPolyPairsOf8) {
+          ex2_poly2(x0, x1, p0, p1);
         } else {
           p0 = ex2(x0);
           p1 = ex2(x1);
         }
-        sum8[(e >> 1) & 7] += p0 + p1;
+        sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
         rr[e >> 1] = pack_f16(p0, p1);
       }
-      l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      {
+        float a0, a1;
+        f2_unpack(f2_add(f2_add(sum4[0], sum4[1]), f2_add(sum4[2], sum4[3])), a0, a1);
+        l += a0 + a1;
+      }
       // P of keys [0, 128) onto S columns [0, 64)
       tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
       tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
