@@ -647,17 +647,24 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       // P of keys [0, 128) onto S columns [0, 64)
       tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
       tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
-      // O is complete up to P.V_{j-1} (it precedes S_j in the MMA pipe): rescale it in place if needed
+      // O is complete up to P.V_{j-1} (it precedes S_j in the MMA pipe): rescale it in place if needed,
+      // the whole row in one TMEM round trip (the S registers are free again)
       if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c * 32, o);
-          tmem_ld_wait();
+        uint32_t o[D];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * (rescale ? alpha : 1.f));
-          tmem_st32(o_addr + c * 32, o);
+        for (int c = 0; c < D / 32; ++c) tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        tmem_ld_wait();
+        const float a = rescale ? alpha : 1.f;
+        const uint64_t a2 = f2_pack(a, a);
+#pragma unroll
+        for (int e = 0; e < D; e += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2, 0), x0, x1);
+          o[e] = __float_as_uint(x0);
+          o[e + 1] = __float_as_uint(x1);
         }
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) tmem_st32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
       }
       tmem_st_wait();
       tc_fence_before();
