@@ -46,7 +46,8 @@ const char* tbf16_status_string(int status);
 /* TBF16_OK if `device` is an sm_100 GPU this build runs on. */
 int tbf16_device_check(int device);
 /* Bits set by kernels on the current device since the last reset (1 = a bounded wait timed out,
- * 2 = attention backward produced a non-finite value). Synchronises the device; reset != 0 clears. */
+ * 2 = attention backward produced a non-finite value, 4 = a kernel found its dynamic shared memory
+ * window not 1024-byte aligned and did nothing). Synchronises the device; reset != 0 clears. */
 int tbf16_device_status(unsigned int* bits, int reset);
 
 /* ------------------------------------------------------------------ row / column power-of-two scales */

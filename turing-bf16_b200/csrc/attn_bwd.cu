@@ -11,11 +11,13 @@
 // Main kernel: one CTA per 128-key tile of one (batch, kv head), looping over the GQA group's query
 // heads and 128-row query tiles. Everything is computed with keys as TMEM lanes, so no operand needs a
 // transpose: the same shared tiles serve as K-major or MN-major UMMA operands.
-//   warp 0     TMA: K, V once; Q_i, dO_i per query tile
+//   warp 0     TMA: K, V once; Q_i (+ lse, delta) per query tile, 2 stages
+//   warp 10    TMA: dO_i, 1 stage
 //   warp 1     MMA: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q, dQ = dS K
-//   warps 2-5  one key per thread: P^T, dS^T (fp16, 128B-swizzled K-major tiles in shared memory);
-//              at the end dK, dV from TMEM -> bf16
-//   warps 6-9  one query per thread: dQ from TMEM, float4 atomic adds into an fp32 accumulator
+//   warps 2-9  two warps per TMEM lane quadrant, each half of the query columns: P^T (packed fp16
+//              back into TMEM), dS^T (fp16, 128B-swizzled K-major tile in shared memory), half the D
+//              columns of dQ (TMEM -> shared -> TMA reduce-add into an fp32 accumulator), and at the
+//              end half the columns of dK, dV from TMEM -> bf16
 // TMEM: S^T [0,128), dP^T / dQ [128,256), dV [256,256+D), dK [256+D,256+2D). Bounded waits throughout.
 #include <algorithm>
 
@@ -27,7 +29,7 @@ namespace {
 
 constexpr int BQ = 128;   // queries per tile
 constexpr int BKV = 128;  // keys per CTA
-constexpr int kThreads = 32 * 10;
+constexpr int kThreads = 32 * 11;
 
 struct AttnBwdParams {
   int B, Hq, Hkv, Sq, Sk, group;
@@ -55,74 +57,72 @@ struct BwdCfg {
   static constexpr int TILE = ATOMS * 16384;  // 128 rows x D fp16
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + TILE;
-  static constexpr int Q_OFF = V_OFF + TILE;
-  static constexpr int DO_OFF = Q_OFF + TILE;
-  static constexpr int P_OFF = DO_OFF + TILE;
-  static constexpr int DS_OFF = P_OFF + 32768;
-  static constexpr int VEC_OFF = DS_OFF + 32768;  // lse (log2 units) and delta of the query tile
-  static constexpr int BAR_OFF = VEC_OFF + 1024;
-  static constexpr int SMEM = 1024 + BAR_OFF + 256;
+  static constexpr int Q_OFF = V_OFF + TILE;      // [2 stages]
+  static constexpr int DO_OFF = Q_OFF + 2 * TILE; // one stage: its readers dP(t), dV(t) finish early
+  static constexpr int DS_OFF = DO_OFF + TILE;
+  static constexpr int DQS_OFF = DS_OFF + 32768;  // dQ staging: 4 warps x (32 rows x 64 fp32)
+  static constexpr int VEC_OFF = DQS_OFF + 32768; // [2 stages] lse (natural log) and delta of the query tile
+  static constexpr int BAR_OFF = VEC_OFF + 2048;
+  // the dynamic shared window starts 1024-byte aligned (checked on entry), so no alignment slack
+  static constexpr int SMEM = BAR_OFF + 256;
   static constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(256 + 2 * D <= 512, "TMEM");
 };
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ uint32_t swz_off(int r, int c) {
-  return (uint32_t)((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const AttnBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const AttnBwdParams p) {
   using C = BwdCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {  // the layout below has no alignment slack
+    if (threadIdx.x == 0) atomicOr(p.err, kErrSmemAlign);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* s_full = bars + 3;
-  uint64_t* dp_full = bars + 4;
-  uint64_t* p_ready = bars + 5;
-  uint64_t* ds_ready = bars + 6;
-  uint64_t* s_free = bars + 7;
-  uint64_t* pds_free = bars + 8;
+  uint64_t* q_full = bars + 1;     // [2]: Q, lse, delta of a query tile
+  uint64_t* q_empty = bars + 3;    // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* dp_full = bars + 6;
+  uint64_t* p_ready = bars + 7;
+  uint64_t* ds_ready = bars + 8;
   uint64_t* dq_full = bars + 9;
   uint64_t* dq_empty = bars + 10;
   uint64_t* kv_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* do_full = bars + 12;
+  uint64_t* do_empty = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* lse_s = reinterpret_cast<float*>(smem + C::VEC_OFF);
-  float* delta_s = lse_s + 128;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bhk = blockIdx.y;
+  // (kv head) fastest, key tiles in increasing order: under a causal mask the low key tiles see the
+  // most query tiles, so the longest CTAs start first
+  const int bhk = blockIdx.x;
   const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
-  const int k0 = blockIdx.x * BKV;
+  const int k0 = blockIdx.y * BKV;
   const int i_first = p.causal ? k0 / BQ : 0;  // query tiles that see these keys (top-left causal)
   const int n_i = max(0, p.q_tiles - i_first);
   const int n_t = p.group * n_i;              // (query head, query tile) pairs
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qdo_full, 1);
-    mbar_init(qdo_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_ready, 4);
-    mbar_init(ds_ready, 4);
-    mbar_init(s_free, 4);
-    mbar_init(pds_free, 1);
+    mbar_init(p_ready, 8);
+    mbar_init(ds_ready, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 4);
+    mbar_init(dq_empty, 8);
     mbar_init(kv_done, 1);
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     *abort = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -137,188 +137,299 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
+    // ---------------------------------------------------------------- TMA producer: K, V, then Q (2 stages)
+    if (lane == 0 && n_t > 0) {  // no copies in flight when the CTA has no query tile
       mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
 #pragma unroll
       for (int a = 0; a < C::ATOMS; ++a) {
         tma_load_3d(smem + C::K_OFF + a * 16384, &tmK, kv_full, a * 64, k0, bhk);
         tma_load_3d(smem + C::V_OFF + a * 16384, &tmV, kv_full, a * 64, k0, bhk);
       }
+      // Q, lse and delta of query tile t go to stage t & 1: the next tile loads while this one runs
       for (int t = 0; t < n_t; ++t) {
         const int h = hk * p.group + t / n_i;
         const int q0 = (i_first + t % n_i) * BQ;
         const int bh = b * p.Hq + h;
-        if (!mbar_wait(qdo_empty, (t & 1) ^ 1, abort, p.err)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * C::TILE + 1024);
+        const int st = t & 1;
+        if (!mbar_wait(&q_empty[st], ((t >> 1) & 1) ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(&q_full[st], C::TILE + 1024);
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a) {
-          tma_load_3d(smem + C::Q_OFF + a * 16384, &tmQ, qdo_full, a * 64, q0, bh);
-          tma_load_3d(smem + C::DO_OFF + a * 16384, &tmDO, qdo_full, a * 64, q0, bh);
-        }
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::Q_OFF + st * C::TILE + a * 16384, &tmQ, &q_full[st], a * 64, q0, bh);
         // this tile's 128 lse and delta values (rows padded to 128, so always in bounds and aligned)
-        bulk_load(lse_s, p.lse + (int64_t)bh * p.lse_ld + q0, 512, qdo_full);
-        bulk_load(delta_s, p.delta + (int64_t)bh * p.lse_ld + q0, 512, qdo_full);
+        float* vec = reinterpret_cast<float*>(smem + C::VEC_OFF + st * 1024);
+        bulk_load(vec, p.lse + (int64_t)bh * p.lse_ld + q0, 512, &q_full[st]);
+        bulk_load(vec + 128, p.delta + (int64_t)bh * p.lse_ld + q0, 512, &q_full[st]);
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------------------------------------------------------- TMA producer: dO (one stage)
+    if (lane == 0 && n_t > 0) {
+      for (int t = 0; t < n_t; ++t) {
+        const int h = hk * p.group + t / n_i;
+        const int q0 = (i_first + t % n_i) * BQ;
+        if (!mbar_wait(do_empty, (t & 1) ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(do_full, C::TILE);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(smem + C::DO_OFF + a * 16384, &tmDO, do_full, a * 64, q0, b * p.Hq + h);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // Order per query tile t: S(t) dP(t) | dV(t) S(t+1) | dK(t) dQ(t) | dP(t+1) ... so the key warps
+    // find S(t+1) ready when they finish dS(t). The MMA pipe executes in issue order: S(t+1) overwrites
+    // P^T(t) after dV(t) read it; dQ(t) overwrites dP^T(t) after the key warps read it (ds_ready); when
+    // dP(t+1) completes, dK(t) and dQ(t) have read dS(t), so dS(t+1) may overwrite it.
+    if (lane == 0 && n_t > 0) {
       constexpr uint32_t id_sq = idesc_f16_f32(128, 128, false, false);  // S^T, dP^T
       constexpr uint32_t id_kd = idesc_f16_f32(128, D, false, true);     // dV, dK
       constexpr uint32_t id_q = idesc_f16_f32(128, D, true, true);       // dQ
-      const uint32_t k_addr = smem_u32(smem + C::K_OFF), v_addr = smem_u32(smem + C::V_OFF);
-      const uint32_t q_addr = smem_u32(smem + C::Q_OFF), do_addr = smem_u32(smem + C::DO_OFF);
-      const uint32_t p_addr = smem_u32(smem + C::P_OFF), ds_addr = smem_u32(smem + C::DS_OFF);
-      bool ok = mbar_wait(kv_full, 0, abort, p.err);
-      for (int t = 0; ok && t < n_t; ++t) {
-        const uint32_t ph = t & 1;
-        if (!mbar_wait(qdo_full, ph, abort, p.err) || !mbar_wait(s_free, ph ^ 1, abort, p.err)) { ok = false; break; }
-        tc_fence_after();
+      // a k16 step adds its byte offset / 16 to the 14-bit start-address field (no carry: < 2^18 bytes)
+      const uint64_t kd = smem_desc_sw128(smem_u32(smem + C::K_OFF), 16, 1024);
+      const uint64_t vd = smem_desc_sw128(smem_u32(smem + C::V_OFF), 16, 1024);
+      const uint64_t qd = smem_desc_sw128(smem_u32(smem + C::Q_OFF), 16, 1024);
+      const uint64_t dod = smem_desc_sw128(smem_u32(smem + C::DO_OFF), 16, 1024);
+      const uint64_t qd_mn = smem_desc_sw128(smem_u32(smem + C::Q_OFF), 16384, 1024);
+      const uint64_t dod_mn = smem_desc_sw128(smem_u32(smem + C::DO_OFF), 16384, 1024);  // one stage
+      const uint64_t dsd = smem_desc_sw128(smem_u32(smem + C::DS_OFF), 16, 1024);
+      const uint64_t dsd_mn = smem_desc_sw128(smem_u32(smem + C::DS_OFF), 16384, 1024);
+      const uint64_t kd_mn = smem_desc_sw128(smem_u32(smem + C::K_OFF), 16384, 1024);
+      constexpr uint32_t kTile16 = C::TILE >> 4;
+      auto issue_s = [&](int t) {  // S^T = K Q^T
+        const uint64_t q = qd + (t & 1) * kTile16;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {  // S^T = K Q^T
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16_ss(tmem + C::T_S, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(q_addr + off, 16, 1024),
-                      id_sq, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off16 = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_f16_ss(tmem + C::T_S, kd + off16, q + off16, id_sq, kk > 0);
         }
         umma_commit(s_full);
-        if (!mbar_wait(dq_empty, ph ^ 1, abort, p.err)) { ok = false; break; }
-        tc_fence_after();
+      };
+      auto issue_dp = [&]() {  // dP^T = V dO^T
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {  // dP^T = V dO^T
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16_ss(tmem + C::T_DP, smem_desc_sw128(v_addr + off, 16, 1024), smem_desc_sw128(do_addr + off, 16, 1024),
-                      id_sq, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off16 = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_f16_ss(tmem + C::T_DP, vd + off16, dod + off16, id_sq, kk > 0);
         }
         umma_commit(dp_full);
-        if (!mbar_wait(p_ready, ph, abort, p.err)) { ok = false; break; }
+      };
+      bool ok = mbar_wait(kv_full, 0, abort, p.err) && mbar_wait(&q_full[0], 0, abort, p.err);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        ok = mbar_wait(do_full, 0, abort, p.err);
+        if (ok) {
+          tc_fence_after();
+          issue_dp();
+        }
+      }
+      for (int t = 0; ok && t < n_t; ++t) {
+        const int st = t & 1;
+        const bool next = t + 1 < n_t;
+        if (!mbar_wait(p_ready, t & 1, abort, p.err)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO   (dO MN-major: D contiguous)
-          umma_f16_ss(tmem + C::T_DV, smem_desc_sw128(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                      smem_desc_sw128(do_addr + kk * 2048, 16384, 1024), id_kd, (t > 0 || kk > 0));
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO   (P^T from TMEM: queries 64h.. at column 64h; dO MN-major)
+          umma_f16_ts(tmem + C::T_DV, tmem + C::T_S + (kk >> 2) * 64 + (kk & 3) * 8, dod_mn + (kk * 2048 >> 4), id_kd,
+                      (t > 0 || kk > 0));
+        umma_commit(do_empty);  // dP(t) and dV(t) were the readers of dO(t)
+        if (next) {
+          if (!mbar_wait(&q_full[st ^ 1], ((t + 1) >> 1) & 1, abort, p.err)) break;
+          tc_fence_after();
+          issue_s(t + 1);
         }
-        if (!mbar_wait(ds_ready, ph, abort, p.err)) { ok = false; break; }
+        if (!mbar_wait(ds_ready, t & 1, abort, p.err)) break;
         tc_fence_after();
+        // dQ first: its extraction (the dQ warps) gates dP(t+1)
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)  // dQ = dS K   (dS^T read MN-major, K MN-major)
+          umma_f16_ss(tmem + C::T_DP, dsd_mn + (kk * 2048 >> 4), kd_mn + (kk * 2048 >> 4), id_q, kk > 0);
+        umma_commit(dq_full);
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q   (Q MN-major)
-          umma_f16_ss(tmem + C::T_DK, smem_desc_sw128(ds_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                      smem_desc_sw128(q_addr + kk * 2048, 16384, 1024), id_kd, (t > 0 || kk > 0));
+          const uint32_t off16 = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_f16_ss(tmem + C::T_DK, dsd + off16, qd_mn + st * kTile16 + (kk * 2048 >> 4), id_kd, (t > 0 || kk > 0));
         }
-        umma_commit(qdo_empty);
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {  // dQ = dS K   (dS^T read MN-major, K MN-major)
-          umma_f16_ss(tmem + C::T_DP, smem_desc_sw128(ds_addr + kk * 2048, 16384, 1024),
-                      smem_desc_sw128(k_addr + kk * 2048, 16384, 1024), id_q, kk > 0);
+        umma_commit(&q_empty[st]);
+        if (next) {
+          if (!mbar_wait(dq_empty, t & 1, abort, p.err) || !mbar_wait(do_full, (t + 1) & 1, abort, p.err)) break;
+          tc_fence_after();
+          issue_dp();
         }
-        umma_commit(dq_full);
-        umma_commit(pds_free);
       }
       if (ok) umma_commit(kv_done);
     }
-  } else if (warp < 6) {
-    // ---------------------------------------------------------------- P^T and dS^T, one key per thread
+  } else if (warp >= 2 && warp < 10) {
+    // ---------------------------------------------------------------- compute warps
+    // Two warps per TMEM lane quadrant: warp w handles keys 32 (w % 4) .. (one key per thread, as TMEM
+    // lanes) and half h = (w - 2) / 4 of every query tile's 128 columns, i.e. queries [64 h, 64 h + 64)
+    // of P^T and dS^T, and half the D columns of dQ (there TMEM lanes are queries) and of dK, dV.
+    // Per query tile: dS(t), then dQ(t) out of TMEM (this frees the columns for dP(t+1)), then P(t+1)
+    // while dP(t+1) runs.
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // key within the tile
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;  // key within the tile (P, dS, dK, dV); query within the tile (dQ)
     const int kj = k0 + r;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int cq = half * 64;        // this warp's query columns
+    uint8_t* stage = smem + C::DQS_OFF + (warp - 2) * 4096;
     bool ok = true;
     bool bad = false;
-    for (int t = 0; t < n_t; ++t) {
-      const uint32_t ph = t & 1;
+    uint32_t pp[32];  // P of this thread's key against the warp's 64 queries, packed fp16 pairs
+
+    // P(t): 2^(scale s - lse) for queries [cq, cq + 64), written to TMEM over S^T columns
+    // [cq, cq + 32) (inside this warp's own S^T columns) as the A operand of dV += P^T dO
+    auto compute_p = [&](int t) -> bool {
       const int h = hk * p.group + t / n_i;
       const int q0 = (i_first + t % n_i) * BQ;
-      // Q, dO, lse and delta of this tile have landed (qdo_full), and S^T is in TMEM (s_full)
-      if (!mbar_wait_warp(qdo_full, ph, abort, p.err) || !mbar_wait_warp(s_full, ph, abort, p.err)) {
-        ok = false;
-        break;
-      }
+      const float* lse_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * 1024);
+      if (!mbar_wait_warp(&q_full[t & 1], (t >> 1) & 1, abort, p.err) || !mbar_wait_warp(s_full, t & 1, abort, p.err))
+        return false;
       tc_fence_after();
-      // P for this thread's key against the 128 queries, kept as packed fp16 pairs (the operand the dV
-      // MMA consumes; dS below reuses it, so P is rounded once for both). 32 logits at a time.
-      uint32_t pp[BQ / 2];
-      // Fully valid tiles (no user mask, all keys and queries in range, whole tile below the causal
-      // diagonal) skip the per-element checks: P = 2^(s * c - lse * log2 e).
+      uint32_t rr[64];
+      tmem_ld32(tmem + lane_base + C::T_S + cq, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+      tmem_ld32(tmem + lane_base + C::T_S + cq + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+      tmem_ld_wait();
+      // fully valid tiles (no user mask, keys and queries in range, whole tile below the causal
+      // diagonal) skip the per-element checks; 3 of every 8 exp2 pairs run on the FMA pipe
       const bool full_tile = p.mask == nullptr && k0 + BKV <= p.Sk && q0 + BQ <= p.Sq && (!p.causal || k0 + BKV - 1 <= q0);
-      const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
+      if (full_tile) {
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2e = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
 #pragma unroll
-      for (int c = 0; c < BQ / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_base + C::T_S + c * 32, rr);
-        tmem_ld_wait();
-        float pc[32];
-        if (full_tile) {
+        for (int e = 0; e < 64; e += 4) {
+          const float4 ls = reinterpret_cast<const float4*>(lse_s)[(cq + e) >> 2];
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            pc[e] = ex2(fmaf(__uint_as_float(rr[e]), p.scale_log2, -lse_s[c * 32 + e] * 1.4426950408889634f));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = c * 32 + e;
-            const int qi = q0 + col;
-            const bool valid = kj < p.Sk && qi < p.Sq && (!p.causal || kj <= qi);
-            float s = __uint_as_float(rr[e]) * p.scale_log2;
-            if (mrow && valid) s += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
-            pc[e] = valid ? ex2(s - lse_s[col] * 1.4426950408889634f) : 0.f;
+          for (int u = 0; u < 4; u += 2) {
+            float x0, x1, p0, p1;
+            const uint64_t nl = f2_mul(u == 0 ? f2_pack(ls.x, ls.y) : f2_pack(ls.z, ls.w), nl2e);
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])), c2, nl), x0, x1);
+            if ((((e + u) >> 1) & 7) >= 5) {
+              ex2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            pp[(e + u) >> 1] = pack_f16(p0, p1);
           }
         }
+      } else {
+        const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) pp[c * 16 + e / 2] = pack_f16(pc[e], pc[e + 1]);
+        for (int e = 0; e < 64; e += 2) {
+          float pc[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = cq + e + u;
+            const int qi = q0 + col;
+            const bool valid = kj < p.Sk && qi < p.Sq && (!p.causal || kj <= qi);
+            float s = __uint_as_float(rr[e + u]) * p.scale_log2;
+            if (mrow && valid) s += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
+            pc[u] = valid ? ex2(s - lse_s[col] * 1.4426950408889634f) : 0.f;
+          }
+          pp[e >> 1] = pack_f16(pc[0], pc[1]);
+        }
       }
-      if (t > 0 && !mbar_wait_warp(pds_free, (t - 1) & 1, abort, p.err)) { ok = false; break; }
-      uint8_t* pt = smem + C::P_OFF;
-#pragma unroll
-      for (int c = 0; c < BQ / 8; ++c)
-        *reinterpret_cast<uint4*>(pt + swz_off(r, c)) = make_uint4(pp[4 * c], pp[4 * c + 1], pp[4 * c + 2], pp[4 * c + 3]);
-      fence_async_smem();
+      // dV(t-1) has read the previous P^T: it precedes S(t) in the MMA pipe
+      tmem_st32(tmem + lane_base + C::T_S + cq, pp);
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      if (!mbar_wait_warp(dp_full, ph, abort, p.err)) { ok = false; break; }
+      return true;
+    };
+
+    ok = n_t > 0 && compute_p(0);
+    for (int t = 0; ok && t < n_t; ++t) {
+      const int h = hk * p.group + t / n_i;
+      const int q0 = (i_first + t % n_i) * BQ;
+      const float* delta_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * 1024) + 128;
+      // ---- dS(t) = P (dP - delta) for this warp's 64 queries (when dP(t) completes, dK(t-1) and
+      // dQ(t-1) have read dS(t-1)); masked / padded queries have P = 0 and a finite dP and delta
+      // (padding rows of delta are zeroed), so their dS is 0. A dS that does not fit fp16 raises the flag.
+      if (!mbar_wait_warp(dp_full, t & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
-      uint8_t* dst = smem + C::DS_OFF;
-#pragma unroll
-      for (int c = 0; c < BQ / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_base + C::T_DP + c * 32, rr);
+      {
+        uint32_t rr[64];
+        tmem_ld32(tmem + lane_base + C::T_DP + cq, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+        tmem_ld32(tmem + lane_base + C::T_DP + cq + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
         tmem_ld_wait();
-        uint32_t pk[16];
+        uint32_t pk[32];
+        uint32_t ovf = 0;
+        const uint64_t m1 = f2_pack(-1.f, -1.f);
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int col = c * 32 + e;
-          const float p0 = f16lo(pp[col / 2]), p1 = f16hi(pp[col / 2]);
-          // masked / padded queries have P = 0 (their delta slot may hold padding): dS = 0 there
-          const float d0 = p0 != 0.f ? p0 * (__uint_as_float(rr[e]) - delta_s[col]) : 0.f;
-          const float d1 = p1 != 0.f ? p1 * (__uint_as_float(rr[e + 1]) - delta_s[col + 1]) : 0.f;
-          bad |= !isfinite(d0) || !isfinite(d1);
-          pk[e / 2] = pack_f16(d0, d1);
+        for (int e = 0; e < 64; e += 4) {
+          const float4 dl = reinterpret_cast<const float4*>(delta_s)[(cq + e) >> 2];
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pp[(e + u) >> 1]));
+            const uint64_t dd = f2_fma(u == 0 ? f2_pack(dl.x, dl.y) : f2_pack(dl.z, dl.w), m1,
+                                       f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])));
+            float d0, d1;
+            f2_unpack(f2_mul(f2_pack(pf.x, pf.y), dd), d0, d1);
+            pk[(e + u) >> 1] = pack_f16(d0, d1);
+            ovf |= __vcmpeq2(pk[(e + u) >> 1] & 0x7c007c00u, 0x7c007c00u);
+          }
         }
+        bad |= ovf != 0;
+        uint8_t* dst = smem + C::DS_OFF;
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
-          *reinterpret_cast<uint4*>(dst + swz_off(r, c * 4 + g)) = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+        for (int g = 0; g < 8; ++g)
+          *reinterpret_cast<uint4*>(dst + swz_off(r, half * 8 + g)) = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(ds_ready);
-        mbar_arrive(s_free);
+      if (lane == 0) mbar_arrive(ds_ready);
+      // ---- dQ(t): D/2 columns of 32 queries out of TMEM at once (frees the columns for dP(t+1)), then
+      // staged in this warp's 4 KB 128B-swizzled box, 32 columns at a time, and added into the fp32
+      // accumulator with TMA reductions in the background (rows past the sequence end are clipped)
+      if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) { ok = false; break; }
+      tc_fence_after();
+      {
+        constexpr int DH = D / 2;
+        uint32_t o[DH];
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c)
+          tmem_ld32(tmem + lane_base + C::T_DP + half * DH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          if (lane == 0) bulk_wait_group_read<0>();  // the previous reduction has read the box
+          __syncwarp();
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+                make_uint4(o[c * 32 + 4 * g], o[c * 32 + 4 * g + 1], o[c * 32 + 4 * g + 2], o[c * 32 + 4 * g + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_3d(&tmDQ, stage, half * DH + c * 32, q0 + quad * 32, b * p.Hq + h);
+            bulk_commit_group();
+          }
+        }
       }
+      // ---- P(t+1) while dP(t+1) runs
+      if (t + 1 < n_t && !compute_p(t + 1)) { ok = false; break; }
     }
+    if (lane == 0) bulk_wait_group<0>();
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.flag, kErrOverflow);
-    // dK, dV epilogue
+    // dK, dV epilogue: this warp's D/2 columns of its 32 keys
     if (ok && n_t > 0 && mbar_wait_warp(kv_done, 0, abort, p.err)) {
       tc_fence_after();
       const float sk = p.scale * exp2i(-__ldg(p.a) - __ldg(p.G));
       const float sv = exp2i(-__ldg(p.ev + bhk) - __ldg(p.G));
-      const int64_t orow = ((int64_t)bhk * p.Sk + min(kj, p.Sk - 1)) * D;
+      const int64_t orow = ((int64_t)bhk * p.Sk + min(kj, p.Sk - 1)) * D + half * (D / 2);
       bool nf = false;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         __nv_bfloat16* dst = (which ? p.dk : p.dv) + orow;
         const float f = which ? sk : sv;
-        const uint32_t col0 = which ? C::T_DK : C::T_DV;
+        const uint32_t col0 = (which ? C::T_DK : C::T_DV) + half * (D / 2);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t o[32];
           tmem_ld32(tmem + lane_base + col0 + c * 32, o);
           tmem_ld_wait();
@@ -339,39 +450,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (__any_sync(0xffffffffu, nf) && lane == 0) atomicOr(p.flag, kErrOverflow);
     } else if (n_t == 0 && kj < p.Sk) {  // keys no query sees (causal, Sk > Sq): zero gradients
-      const int64_t orow = ((int64_t)bhk * p.Sk + kj) * D;
-      for (int c = 0; c < D; c += 8) {
+      const int64_t orow = ((int64_t)bhk * p.Sk + kj) * D + half * (D / 2);
+      for (int c = 0; c < D / 2; c += 8) {
         *reinterpret_cast<uint4*>(p.dk + orow + c) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(p.dv + orow + c) = make_uint4(0, 0, 0, 0);
       }
-    }
-  } else {
-    // ---------------------------------------------------------------- dQ: one query per thread, atomics
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    for (int t = 0; t < n_t; ++t) {
-      const int h = hk * p.group + t / n_i;
-      const int qi = (i_first + t % n_i) * BQ + r;
-      if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) break;
-      tc_fence_after();
-      float* dst = p.dq_acc + ((int64_t)(b * p.Hq + h) * p.Sq + min(qi, p.Sq - 1)) * D;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + C::T_DP + c * 32, o);
-        tmem_ld_wait();
-        if (qi < p.Sq) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + 4 * g),
-                      make_float4(__uint_as_float(o[4 * g]), __uint_as_float(o[4 * g + 1]), __uint_as_float(o[4 * g + 2]),
-                                  __uint_as_float(o[4 * g + 3])));
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
     }
   }
 
@@ -498,20 +581,21 @@ int launch_bwd(const void* q16, const void* k16, const void* v16, const void* do
                int64_t Sk, cudaStream_t st) {
   using C = BwdCfg<D>;
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   const int64_t BHq = (int64_t)prm.B * prm.Hq, BHk = (int64_t)prm.B * prm.Hkv;
   if (int rc = tbf16_host::make_tmap_3d(&tq, q16, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 64, BQ)) return rc;
   if (int rc = tbf16_host::make_tmap_3d(&tdo, do16, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 64, BQ)) return rc;
   if (int rc = tbf16_host::make_tmap_3d(&tk, k16, D, Sk, BHk, D, (uint64_t)Sk * D, 64, BKV)) return rc;
   if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, Sk, BHk, D, (uint64_t)Sk * D, 64, BKV)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d_f32(&tdq, prm.dq_acc, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 32, 32)) return rc;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->device & 63]) {
     if (cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
-  dim3 grid((unsigned)((Sk + BKV - 1) / BKV), (unsigned)BHk);
-  attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, prm);
+  dim3 grid((unsigned)BHk, (unsigned)((Sk + BKV - 1) / BKV));
+  attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
   return tbf16_host::check_launch();
 }
 
@@ -550,8 +634,10 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
   // 1. G from the global max of head_exp(dout) + ev_q
   if (int rc = tbf16_head_amax(dout, TBF16_BF16, B, Hq, Sq, dout_d, dout_sb, dout_sh, dout_ss, w.amax, stream)) return rc;
   attn_bwd_exp_kernel<<<1, 256, 0, st>>>(w.amax, (int)(B * Hq), (int)Hq, (int)Hkv, group, ev, t_do, G_out);
-  // 2. dO16 and delta
+  // 2. dO16 and delta (the padding rows of delta are zeroed: the main kernel reads whole 128-row tiles)
   const int64_t rows = B * Hq * Sq;
+  if (lse_ld != Sq && cudaMemsetAsync(w.delta, 0, sizeof(float) * B * Hq * lse_ld, st) != cudaSuccess)
+    return TBF16_ERR_LAUNCH;
   const int rpb = 256 / (int)(D / 8);
   const unsigned pgrid = (unsigned)((rows + rpb - 1) / rpb);
   if (D == 64)

@@ -64,63 +64,6 @@ struct FwdCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// Packed fp32 pairs (sm_100 executes one f32x2 add / mul / fma per lane per instruction).
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-  return d;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t d, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// 2^x for a pair of x <= 0 (or -inf) on the FMA pipe: Cody-Waite split x = n + f with n = rint(x)
-// (adding 1.5 * 2^23 rounds to an integer in the low mantissa bits), 2^f on [-1/2, 1/2] by a degree-3
-// polynomial fitted here for minimum maximum relative error (7.5e-5, below fp16's half ulp 2.4e-4,
-// the precision P is kept in), and 2^n added into the exponent field. Inputs below -120 give 2^-120,
-// which rounds to zero in fp16 and is negligible in the fp32 row sum.
-__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
-  const uint64_t x = f2_pack(fmaxf(x0, -120.f), fmaxf(x1, -120.f));
-  const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
-  const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
-  const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);
-  uint64_t q = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), f, f2_pack(0.2426111400127411f, 0.2426111400127411f));
-  q = f2_fma(q, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
-  q = f2_fma(q, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
-  float q0, q1, t0, t1;
-  f2_unpack(q, q0, q1);
-  f2_unpack(t, t0, t1);
-  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
-}
-
-// Byte offset of 16-byte chunk c (0..15 for 128 fp16 columns) of row r in a K-major tile made of
-// 64-column 128B-swizzled atoms of 128 rows each.
-__device__ __forceinline__ uint32_t swz_off(int r, int c) {
-  return (uint32_t)((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -436,11 +379,13 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
+  // causal: heads fastest and the heaviest (last) query pairs first, so the longest CTAs start first;
+  // otherwise query pairs fastest, so the CTAs in flight share a head's K and V in L2
+  const int bh = p.causal ? (int)blockIdx.x : (int)blockIdx.y;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int bhk = b * p.Hkv + h / p.group;
   const int pairs = (p.m_tiles + 1) >> 1;
-  const int pair = p.causal ? (pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy pairs first
+  const int pair = p.causal ? (pairs - 1 - (int)blockIdx.y) : (int)blockIdx.x;
   const int m0 = pair * 2 * BM;
   // key tiles per query tile (tile 1 may lie past the end of the sequence: no work)
   auto kv_tiles = [&](int t) -> int {
@@ -730,7 +675,7 @@ int launch_fwd_pp(const void* q16, const void* k16, const void* v16, const AttnF
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
-  dim3 grid((prm.m_tiles + 1) / 2, (unsigned)BHq);
+  dim3 grid = prm.causal ? dim3((unsigned)BHq, (prm.m_tiles + 1) / 2) : dim3((prm.m_tiles + 1) / 2, (unsigned)BHq);
   attn_fwd_pp_kernel<D><<<grid, kPPThreads, C::SMEM, st>>>(tq, tk, tv, prm);
   return tbf16_host::check_launch();
 }

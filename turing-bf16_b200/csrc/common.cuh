@@ -16,6 +16,7 @@ namespace tbf16 {
 // kernels as a pointer) and return. Read and cleared through tbf16_device_status().
 constexpr unsigned int kErrWaitTimeout = 1u;
 constexpr unsigned int kErrOverflow = 2u;
+constexpr unsigned int kErrSmemAlign = 4u;  // dynamic shared window not 1024-byte aligned
 
 // ------------------------------------------------------------------ scale rules
 // The scale is an exact power of two built from exponent bits, never exp2/log2.
@@ -178,6 +179,26 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (UMMA reads).
+// Element-wise add of a shared tile into global memory through a 3-D tensor map (TMA reduction, no
+// multicast); x (innermost) must be a multiple of 16 bytes and no coordinate may be negative.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const void* src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups of this thread still read their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups of this thread are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ------------------------------------------------------------------ tcgen05
@@ -281,6 +302,69 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// ------------------------------------------------------------------ softmax arithmetic (attention)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Packed fp32 pairs (sm_100 executes one f32x2 add / mul / fma per lane per instruction).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t d, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 0 (or -inf) on the FMA pipe: Cody-Waite split x = n + f with n = rint(x)
+// (adding 1.5 * 2^23 rounds to an integer in the low mantissa bits), 2^f on [-1/2, 1/2] by a degree-3
+// polynomial fitted here for minimum maximum relative error (7.5e-5, below fp16's half ulp 2.4e-4,
+// the precision P is kept in), and 2^n added into the exponent field. Inputs below -120 give 2^-120,
+// which rounds to zero in fp16 and is negligible in the fp32 row sum.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -120.f), fmaxf(x1, -120.f));
+  const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);
+  uint64_t q = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), f, f2_pack(0.2426111400127411f, 0.2426111400127411f));
+  q = f2_fma(q, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  q = f2_fma(q, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+// Byte offset of 16-byte chunk c (0..15 for 128 fp16 columns) of row r in a K-major tile made of
+// 64-column 128B-swizzled atoms of 128 rows each.
+__device__ __forceinline__ uint32_t swz_off(int r, int c) {
+  return (uint32_t)((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
 }  // namespace tbf16
 
 // Host helpers shared by the .cu files.
@@ -312,4 +396,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t row
 // strides of dims 1 and 2, box {box0, box1, 1}.
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                  uint64_t stride2, uint32_t box0, uint32_t box1);
+// The same for fp32 elements (box0 * 4 <= 128 bytes, the swizzle span).
+int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
+                     uint64_t stride2, uint32_t box0, uint32_t box1);
 }  // namespace tbf16_host
