@@ -382,37 +382,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(ds_ready);
       // ---- dQ(t): D/2 columns of 32 queries out of TMEM at once (frees the columns for dP(t+1)), then
       // staged in this warp's 4 KB 128B-swizzled box, 32 columns at a time, and added into the fp32
-      // accumulator with TMA reductions in the background (rows past the sequence end are clipped)
+      // accumulator with TMA reductions (rows past the sequence end are clipped). The first box goes
+      // out before P(t+1), the rest after it, so the wait for the box to be read is hidden.
       if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
-      {
-        constexpr int DH = D / 2;
-        uint32_t o[DH];
+      constexpr int DH = D / 2;
+      uint32_t o[DH];
 #pragma unroll
-        for (int c = 0; c < DH / 32; ++c)
-          tmem_ld32(tmem + lane_base + C::T_DP + half * DH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
-        tmem_ld_wait();
-        tc_fence_before();
+      for (int c = 0; c < DH / 32; ++c)
+        tmem_ld32(tmem + lane_base + C::T_DP + half * DH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      auto stage_box = [&](int c) {
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous reduction has read the box
         __syncwarp();
-        if (lane == 0) mbar_arrive(dq_empty);
 #pragma unroll
-        for (int c = 0; c < DH / 32; ++c) {
-          if (lane == 0) bulk_wait_group_read<0>();  // the previous reduction has read the box
-          __syncwarp();
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            *reinterpret_cast<uint4*>(stage + lane * 128 + ((g ^ (lane & 7)) << 4)) =
-                make_uint4(o[c * 32 + 4 * g], o[c * 32 + 4 * g + 1], o[c * 32 + 4 * g + 2], o[c * 32 + 4 * g + 3]);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_reduce_add_3d(&tmDQ, stage, half * DH + c * 32, q0 + quad * 32, b * p.Hq + h);
-            bulk_commit_group();
-          }
+        for (int g = 0; g < 8; ++g)
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+              make_uint4(o[c * 32 + 4 * g], o[c * 32 + 4 * g + 1], o[c * 32 + 4 * g + 2], o[c * 32 + 4 * g + 3]);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tmDQ, stage, half * DH + c * 32, q0 + quad * 32, b * p.Hq + h);
+          bulk_commit_group();
         }
-      }
+      };
+      stage_box(0);
       // ---- P(t+1) while dP(t+1) runs
       if (t + 1 < n_t && !compute_p(t + 1)) { ok = false; break; }
+#pragma unroll
+      for (int c = 1; c < DH / 32; ++c) stage_box(c);
     }
     if (lane == 0) bulk_wait_group<0>();
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.flag, kErrOverflow);
