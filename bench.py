@@ -180,6 +180,10 @@ def main():
                     help="time only the config-3 attention forward (S from --attn-S) and print its JSON; for profiling")
     ap.add_argument("--attn-S", type=int, default=16384)
     ap.add_argument("--attn-train", action="store_true", help="with --only-attention: also time fwd+bwd (config 4)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config-2 GEMM sweep (M = 1 .. 16384 at N = K = 4096 and 8192, L2 flushed) and the "
+                         "config-4 MLP linears fwd+bwd; prints one JSON line and exits")
+    ap.add_argument("--no-train-linear", action="store_true", help="skip the config-4 MLP linear fwd+bwd")
     ap.add_argument("--gemm", default="materialise", choices=["materialise", "fused"],
                     help="materialise (default, what tbf16_linear does with its x16 workspace): the row pass writes "
                          "fp16(x * s) and the GEMM runs on fp16 operands; fused: bf16 x converted inside the GEMM")
@@ -194,6 +198,10 @@ def main():
     if args.only_attention:
         print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
                                                      train=args.attn_train)}))
+        return
+    if args.sweep:
+        pk = peaks()
+        print(json.dumps({"gemm_sweep": sweep_run(pk), "train_linear": train_linear_run(pk)}))
         return
 
     if args.impl == "reference":
@@ -303,6 +311,9 @@ def main():
             line["attention"] = attention_run(pk)
         except Exception as exc:  # the headline GEMM line still prints
             line["attention"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    if not args.no_train_linear:
+        torch.cuda.empty_cache()
+        line["train_linear"] = train_linear_run(pk)
     if not args.no_prefill:
         torch.cuda.empty_cache()
         line["prefill"] = prefill_run(world)  # every rank runs its own sequence (replicas)
@@ -415,6 +426,77 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
 
 def dist_rank():
     return int(os.environ.get("RANK", "0"))
+
+
+def sweep_run(pk, iters=7):
+    """Config 2 sweep: scaled_linear (bf16 x, weights as tbf16.convert stores them) at M = 1 .. 16384 and
+    N = K in {4096, 8192}, each timed alone with CUDA events between L2 flushes (a 512 MB write, long
+    enough that the host has queued the linear's launches before the GPU reaches them). M <= 8 runs the
+    weight-streaming kernel (HBM-bound: weight GB/s against the copy peak), larger M the row pass plus
+    the tcgen05 GEMM (TFLOPS against the bf16 peak)."""
+    import inputs
+    from tbf16 import ops
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    rows = []
+    for NK in (4096, 8192):
+        w16, ws = ops.prepare_weight(inputs.gemm_w(NK, NK, seed=1, device="cuda"))
+        for M in (1, 2, 4, 8, 16, 64, 128, 256, 1024, 4096, 8192, 16384):
+            x = inputs.gemm_x(M, NK, seed=M, device="cuda")
+            for _ in range(2):
+                ops.scaled_linear(x, w16, ws)
+            ts = []
+            for _ in range(iters):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                ops.scaled_linear(x, w16, ws)
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            t = statistics.median(ts)
+            flop = 2.0 * M * NK * NK
+            nbytes = 2.0 * NK * NK + 4.0 * M * NK  # weight + x read + y written
+            rows.append({"M": M, "N": NK, "K": NK, "ms": round(t, 4), "tflops": round(flop / t / 1e9, 1),
+                         "gbs": round(nbytes / t / 1e6, 1),
+                         "frac": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3) if M <= ops.GEMV_ROWS
+                         else round(flop / t / 1e9 / pk["tflops"], 3),
+                         "bound": "hbm" if M <= ops.GEMV_ROWS else "tensor"})
+            del x
+        del w16, ws
+    del flush
+    return rows
+
+
+def train_linear_run(pk, iters=5):
+    """Config 4 MLP linears (8192 tokens, hidden 2048, SwiGLU 8192): gate, up, down through
+    tbf16.autograd.linear (ScaledLinearFn: fwd + dX + dW each a tcgen05 GEMM with its scale passes),
+    fwd + bwd per step; 6 * M * K * N flop per linear."""
+    import inputs
+    from tbf16 import autograd
+    M, Hd, I = 8192, 2048, 8192
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = inputs.gemm_x(M, Hd, seed=5, device="cuda").requires_grad_()
+    wg, wu = ((torch.randn(I, Hd, device="cuda", generator=g) * 0.02).bfloat16().requires_grad_() for _ in range(2))
+    wd = (torch.randn(Hd, I, device="cuda", generator=g) * 0.02).bfloat16().requires_grad_()
+    dy = (torch.randn(M, Hd, device="cuda", generator=g) * 2.0 ** -20).bfloat16()
+    flop = 3 * 6.0 * M * Hd * I
+
+    def step():
+        h = torch.nn.functional.silu(autograd.linear(x, wg)) * autograd.linear(x, wu)
+        autograd.linear(h, wd).backward(dy)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / iters
+    return {"config": f"M={M} h={Hd} i={I} (gate, up, down) fwd+bwd", "ms": round(t, 3),
+            "tflops": round(flop / (t / 1e3) / 1e12, 1), "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 3)}
 
 
 def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):

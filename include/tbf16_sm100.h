@@ -148,6 +148,16 @@ int tbf16_linear_scaled(const void* x, int64_t M, int64_t K, int64_t ldx, const 
 int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int b_mn, int64_t ldb, int64_t M, int64_t N,
                    int64_t K, const float* sa, const float* sb, const void* bias, void* y, int64_t ldy, void* stream);
 
+/* Few-row linear for decode: y[m, n] = bf16_rn((sum_k x[m,k] w16[n,k]) * ws[n] + bias[n]) for M <= 8 rows,
+ * fp32 products of bf16 x and fp16 w (no activation scaling). Replaces the reference's single-row gemv
+ * (tbf16/csrc/small_kernels.cu:107-132, called by tbf16/ops.py:207-218) and extends it to 8 rows that
+ * share one pass over the weight. x bf16 [M, K] (row stride ldx), w16 fp16 [N, K] (ldw), ws fp32 [N],
+ * bias bf16 [N] nullable, y bf16 [M, N] (ldy). K, ldx, ldw multiples of 8; x, w16 16-byte aligned.
+ * M > TBF16_GEMV_MAX_ROWS returns TBF16_ERR_UNSUPPORTED (use tbf16_linear). */
+#define TBF16_GEMV_MAX_ROWS 8
+int tbf16_gemv(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
+               const float* ws, const void* bias, void* y, int64_t ldy, void* stream);
+
 /* ------------------------------------------------------------------ scaled attention (tcgen05) */
 
 /* Flash-attention forward on the fp16 copies from tbf16_prepare_qkv. Replaces the torch fp16 SDPA call of

@@ -347,6 +347,16 @@ def linear_small_m_ref(x, w16, ws, bias=None, rounding="rn"):
     return bf16_trunc(v) if rounding == "trunc" else bf16_rn(v)
 
 
+def gemv_ref(x, w16, ws, bias=None):
+    """The reference's single-row linear (tbf16/csrc/small_kernels.cu:107-132): fp32 products of bf16 x and
+    fp16 w summed, times ws, plus bias, rounded to bf16 once. Summed in fp64 here; the kernel's fp32 sum
+    order differs, so results agree to a bf16 ulp (plus fp32 rounding under cancellation)."""
+    v = _cpu(x).double() @ _cpu(w16).double().t() * _cpu(ws).double()[None, :]
+    if bias is not None:
+        v = v + _cpu(bias).double()[None, :]
+    return bf16_rn(v.float())
+
+
 def linear_train(x, w, bias, dy):
     """tbf16/autograd.py:58-90 (ScaledLinearFn) with this build's GEMM semantics (fp32/fp64
     accumulation, one bf16 rounding). Exponent conventions kept from the reference:

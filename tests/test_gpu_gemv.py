@@ -1,0 +1,64 @@
+"""Parity of the few-row linear (decode path, M <= 8) with the oracle's restatement of the reference's
+single-row kernel (small_kernels.cu:107-132): fp32 products of bf16 x and fp16 w, times ws, plus
+bias, one bf16 rounding. Elementwise within one bf16 ulp plus the fp32 summation bound
+(K * 2^-24 * sum |x w| ws). Called through tbf16.ops (ctypes -> C ABI)."""
+import pytest
+import torch
+
+import inputs
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(y, x, w16, ws, b):
+    ref = orc.gemv_ref(x, w16, ws, b)
+    absprod = (x.double().abs() @ w16.double().abs().t()) * ws.double()[None, :]
+    tol = orc.bf16_ulp(ref.double()) + x.shape[1] * 2.0 ** -24 * absprod
+    d = (y.double() - ref.double()).abs()
+    assert (d <= tol).all(), float((d - tol).max())
+    assert torch.isfinite(y.float()).all()
+
+
+@pytest.mark.parametrize("M,K,N,bias", [(1, 4096, 4096, False), (1, 1024, 1000, True), (2, 520, 264, True),
+                                        (3, 8192, 1024, False), (5, 72, 33, True), (8, 4096, 4096, True),
+                                        (8, 16384, 256, False)])
+def test_gemv_vs_oracle(M, K, N, bias):
+    from tbf16 import ops
+    x = inputs.gemm_x(M, K, seed=M + K)
+    w = inputs.gemm_w(N, K, seed=N)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(3)) * 0.1).bfloat16() if bias else None
+    w16, ws = ops.prepare_weight(w.cuda())
+    y = ops.small_m_linear(x.cuda(), w16, ws, None if b is None else b.cuda()).cpu()
+    assert y.shape == (M, N) and y.dtype == torch.bfloat16
+    _check(y, x, w16.cpu(), ws.cpu(), b)
+
+
+def test_gemv_strided_rows_and_3d_input():
+    """Rows with a leading dimension larger than K, and a (B, T, K) input reshaped by scaled_linear."""
+    from tbf16 import _ext as E
+    from tbf16 import ops
+    K, N = 1024, 768
+    big = inputs.gemm_x(4, 2 * K, seed=11)
+    x = big[:, :K]
+    w16, ws = ops.prepare_weight(inputs.gemm_w(N, K, seed=12).cuda())
+    xc = big.cuda()[:, :K]
+    y = torch.empty(4, N, device="cuda", dtype=torch.bfloat16)
+    E.call("tbf16_gemv", E.ptr(xc), 4, K, xc.stride(0), E.ptr(w16), N, w16.stride(0), E.ptr(ws), None, E.ptr(y), N,
+           E.stream_ptr(xc.device))
+    _check(y.cpu(), x.contiguous(), w16.cpu(), ws.cpu(), None)
+    x3 = inputs.gemm_x(6, K, seed=13).reshape(2, 3, K)
+    y3 = ops.scaled_linear(x3.cuda(), w16, ws).cpu()
+    assert y3.shape == (2, 3, N)
+    _check(y3.reshape(6, N), x3.reshape(6, K), w16.cpu(), ws.cpu(), None)
+
+
+def test_gemv_rejects_too_many_rows():
+    from tbf16 import _ext as E
+    x = torch.zeros(9, 64, device="cuda", dtype=torch.bfloat16)
+    w16 = torch.zeros(32, 64, device="cuda", dtype=torch.float16)
+    ws = torch.ones(32, device="cuda")
+    y = torch.empty(9, 32, device="cuda", dtype=torch.bfloat16)
+    rc = E.lib().tbf16_gemv(E.ptr(x), 9, 64, 64, E.ptr(w16), 32, 64, E.ptr(ws), None, E.ptr(y), 32,
+                            E.stream_ptr(x.device))
+    assert rc == 6  # TBF16_ERR_UNSUPPORTED

@@ -25,6 +25,7 @@ _FUSED_SCALE = (15, False)
 # Rows scaled by their L1 norm for the training dX GEMM (reference tbf16/ops.py:129-130).
 L1_TARGET = 15
 SMALL_M = 2
+GEMV_ROWS = 8  # rows handled by the weight-streaming kernel (TBF16_GEMV_MAX_ROWS)
 
 
 def _target_exp(K: int) -> int:
@@ -146,6 +147,8 @@ def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias
     if not _rows_ok(w16) or w16.shape[1] != x2.shape[1]:
         w16 = _pad_cols(w16[:, :K]) if K % 8 else w16.contiguous()
     M, Kp = x2.shape
+    if M <= GEMV_ROWS:  # decode: one pass over the weight for all rows
+        return _gemv(x2, w16, w_sinv, _bias_ok(bias, N, x.device), N).reshape(*shape[:-1], N)
     Np = (N + 7) // 8 * 8
     b = _bias_ok(bias, N, x.device)
     ws = w_sinv.contiguous().float()
@@ -205,9 +208,20 @@ def _gemm_padded(x16, x_sinv, w16, w_sinv, b):
     return _gemm_f16(xp, 0, wp, 0, M, Np, xp.shape[1], x_sinv, ws, b)[:, :N]
 
 
+def _gemv(x2, w16, w_sinv, b, N):
+    """y (M, N) bf16 for M <= GEMV_ROWS rows: fp32 products of bf16 x and fp16 w, times w_sinv, plus bias
+    (the reference's single-row kernel, small_kernels.cu:107-132), one pass over the weight."""
+    M, K = x2.shape
+    y = torch.empty((M, N), device=x2.device, dtype=torch.bfloat16)
+    ws = w_sinv.contiguous().float()
+    call("tbf16_gemv", ptr(x2), M, K, x2.stride(0), ptr(w16), N, w16.stride(0), ptr(ws), ptr(b), ptr(y), N,
+         stream_ptr(x2.device))
+    return y
+
+
 def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None):
-    """Kept for callers of the reference's small-M entry point (reference tbf16/ops.py:207-218): the
-    tcgen05 kernel handles any M, so this is scaled_linear."""
+    """The reference's small-M entry point (reference tbf16/ops.py:207-218): up to GEMV_ROWS rows go
+    through the weight-streaming kernel, more through the tcgen05 GEMM (scaled_linear routes the same way)."""
     return scaled_linear(x2, w16, w_sinv, bias)
 
 
