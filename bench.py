@@ -47,57 +47,55 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """SM clock and throttle reasons sampled every 5 ms through NVML while the timed region runs (the
+    nvidia-smi CLI, 200 ms at best, sees nothing of a 25 ms region). Entering waits for the first sample."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
     def __init__(self, device_index):
         self.idx = device_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.stop = threading.Event()
+        self.ok = False
+
+    def _run(self):
+        import pynvml
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while not self.stop.is_set():
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                reasons = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((sm, reasons))
+                self.first.set()
+                time.sleep(0.005)
+        except Exception:
+            self.first.set()
 
     def __enter__(self):
+        self.first = threading.Event()
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            import pynvml
+            pynvml.nvmlInit()
+            self.ok = True
         except Exception:
-            self.proc = None
+            return self
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        self.first.wait(timeout=2.0)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.ok:
+            self.t.join(timeout=2.0)
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [s for s, _ in self.samples]
+        reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": getattr(self, "max_mhz", None),
+                "reasons": reasons, "samples": len(sm), "source": "NVML, 5 ms"}
 
 
 def dist_init():
@@ -551,22 +549,16 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
 
 
 def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16=None):
-    """Same metric through the public C ABI call (tbf16_linear), with x uploaded from pinned host memory
-    and y read back each step inside the timed region."""
-    from tbf16 import _ext as E
+    """Same metric through the public API for host-resident activations (tbf16.ops.linear_host): every
+    step uploads x from pinned host memory and reads y back into pinned host memory inside the timed
+    region; the call pipelines 1024-row chunks over three streams (upload, tbf16_linear, download)."""
+    from tbf16 import ops
     hx = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
     hx.copy_(x.cpu())
     hy = torch.empty(M, N, dtype=torch.bfloat16, pin_memory=True)
-    sp = ctypes.c_void_p(stream.cuda_stream)
-    L = E.lib()
 
     def step():
-        x.copy_(hx, non_blocking=True)
-        st = L.tbf16_linear(E.ptr(x), M, K, K, E.ptr(w16), N, K, E.ptr(ws), None, E.ptr(y), N, E.ptr(s_inv), E.ptr(x16),
-                            15, 0, sp)
-        if st:
-            raise RuntimeError(f"tbf16_linear failed: {st}")
-        hy.copy_(y, non_blocking=True)
+        ops.linear_host(hx, w16, ws, out=hy)
 
     steps = max(3, args.steps // 3)
     for _ in range(2):
@@ -582,7 +574,8 @@ def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16=None):
     ms = max_over_ranks(s.elapsed_time(e), world)
     return {"value": round(2.0 * M * N * K * world * steps / (ms / 1e3) / 1e12, 3), "unit": "TFLOPS",
             "h2d_bytes_per_step": 2 * M * K, "d2h_bytes_per_step": 2 * M * N, "steps": steps,
-            "ms_per_step": round(ms / steps, 3), "path": "tbf16_linear via ctypes, pinned host buffers"}
+            "ms_per_step": round(ms / steps, 3),
+            "path": "tbf16.ops.linear_host: pinned host x and y, 1024-row chunks pipelined over upload / tbf16_linear / download streams"}
 
 
 if __name__ == "__main__":

@@ -62,3 +62,21 @@ def test_gemv_rejects_too_many_rows():
     rc = E.lib().tbf16_gemv(E.ptr(x), 9, 64, 64, E.ptr(w16), 32, 64, E.ptr(ws), None, E.ptr(y), 32,
                             E.stream_ptr(x.device))
     assert rc == 6  # TBF16_ERR_UNSUPPORTED
+
+
+def test_linear_host_matches_device_path():
+    """linear_host (pinned host x and y, chunked over three streams) gives the device path's rows:
+    bit-equal where a chunk goes through the GEMM, within the GEMV bound for a final chunk of <= 8 rows."""
+    from tbf16 import ops
+    M, K, N = 2 * 1024 + 5, 512, 768
+    x = inputs.gemm_x(M, K, seed=21)
+    w16, ws = ops.prepare_weight(inputs.gemm_w(N, K, seed=22).cuda())
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(23)) * 0.1).bfloat16()
+    hx = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
+    hx.copy_(x)
+    y = ops.linear_host(hx, w16, ws, b.cuda())
+    torch.cuda.synchronize()
+    assert y.shape == (M, N) and not y.is_cuda
+    ref = ops.scaled_linear(x.cuda(), w16, ws, b.cuda()).cpu()
+    assert torch.equal(y[:2048].view(torch.int16), ref[:2048].view(torch.int16))
+    _check(y[2048:], x[2048:], w16.cpu(), ws.cpu(), b)

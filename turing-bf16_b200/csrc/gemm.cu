@@ -31,7 +31,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of 16-bit elements
 constexpr int kEpiWarps = 4;
 constexpr int kConvWarps = 4;
-constexpr int kGroupM = 8;
+constexpr int kGroupM = 16;  // M tiles per raster group (TBF16_GEMM_GROUP overrides, for tuning)
 
 struct GemmParams {
   int M, N, K;
@@ -42,6 +42,7 @@ struct GemmParams {
   int64_t ldy;
   unsigned int* err;
   int tiles_m, tiles_n;
+  int group_m;  // M tiles per raster group
 };
 
 template <int BN, int STAGES, bool CONVERT>
@@ -58,11 +59,13 @@ struct Cfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
-  const int per_group = kGroupM * tiles_n;
+// Grouped raster: group_m M tiles x all N tiles per group, M fastest, so the CTAs in flight share a few
+// A panels and B panels in L2.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
+  const int per_group = group_m * tiles_n;
   const int group = tile / per_group;
-  const int first = group * kGroupM;
-  const int gsize = min(tiles_m - first, kGroupM);
+  const int first = group * group_m;
+  const int gsize = min(tiles_m - first, group_m);
   const int r = tile % per_group;
   tm = first + r % gsize;
   tn = r / gsize;
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
         int tm, tn;
-        tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+        tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
         const int m0 = tm * BM, n0 = tn * BN;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort, p.err)) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
       const int m = tm * BM + row;
       const bool mok = m < p.M;
       const float a = mok ? __ldg(p.sa + m) : 0.f;
@@ -228,7 +231,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int tm, tn;
-      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
       const int m = tm * BM + row;
       const float s = m < p.M ? 1.0f / __ldg(p.sa + m) : 0.f;  // exact: sa is a power of two
       bool ok = true;
@@ -297,6 +300,11 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, i
   p.ldy = ldy;
   p.err = d->err;
   p.tiles_m = (M + BM - 1) / BM;
+  static const int group_env = [] {
+    const char* e = getenv("TBF16_GEMM_GROUP");
+    return e ? atoi(e) : 0;
+  }();
+  p.group_m = group_env > 0 ? group_env : kGroupM;
   p.tiles_n = (N + BN - 1) / BN;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, d->sms);

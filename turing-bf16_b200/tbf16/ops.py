@@ -1,11 +1,12 @@
 """bf16 matmuls on fp16 tensor cores with exact power-of-two scaling, on B200 (sm_100a).
 
 Same public surface as the reference's tbf16/ops.py (quantize_rows, prepare_weight, scaled_linear,
-linear_q, small_m_linear, quantize_rows_shared, _target_exp). The work runs in libtbf16_sm100.so:
-a row-amax -> exponent kernel and a warp-specialised TMA + tcgen05 GEMM that converts bf16 rows to
-fp16 in shared memory, accumulates in fp32 in TMEM and writes bf16 straight from the accumulator.
-The reference's Triton kernels, its cuBLAS small-M branch and its GEMV are gone: every M takes the
-same kernel, and there is no CPU fallback.
+linear_q, small_m_linear, quantize_rows_shared, _target_exp), plus linear_host for activations that
+live in pinned host memory. The work runs in libtbf16_sm100.so: a row-amax -> exponent pass (which
+also writes the fp16 copy of x for large N) and a warp-specialised TMA + tcgen05 GEMM that
+accumulates in fp32 in TMEM and writes bf16 straight from the accumulator; up to 8 rows take a
+weight-streaming kernel instead (the reference's single-row GEMV, extended). The reference's Triton
+kernels and its cuBLAS small-M branch are gone, and there is no CPU fallback.
 """
 import math
 import os
@@ -168,6 +169,72 @@ def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias
     return y.reshape(*shape[:-1], N)
 
 
+def linear_host(x_host: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None, out=None,
+                chunk_rows: int = 1024) -> torch.Tensor:
+    """scaled_linear for activations in pinned host memory: y_host (M, N) bf16 = x_host @ W^T + b.
+
+    Rows go through in chunks on three streams, so the upload of chunk c+1, the linear of chunk c and
+    the download of chunk c-1 overlap (PCIe copies in both directions run on separate copy engines);
+    two device buffers per direction. Returns `out` (pinned, allocated if None) once the last chunk's
+    download is enqueued: it is complete when the current stream reaches this point (synchronise
+    before reading it on the host). Same arithmetic as scaled_linear on each row."""
+    if x_host.is_cuda or x_host.dtype != torch.bfloat16 or x_host.dim() != 2:
+        raise RuntimeError("tbf16.linear_host: x_host must be a 2-D bf16 tensor in host memory")
+    require_cuda(w16, w_sinv)
+    M, K = x_host.shape
+    N = w16.shape[0]
+    dev = w16.device
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True)
+    if M == 0:
+        return out
+    if K % 8 or N % 8 or w16.shape[1] != K or w16.stride(0) != K:
+        raise RuntimeError("tbf16.linear_host: K and N must be multiples of 8 (use scaled_linear)")
+    cur = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    rows = max(1, min(chunk_rows, M))
+    xb = [torch.empty((rows, K), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    yb = [torch.empty((rows, N), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    s_inv = torch.empty((rows,), device=dev, dtype=torch.float32)
+    x16 = torch.empty((rows, K), device=dev, dtype=torch.float16) if _materialise(rows, N, K) else None
+    ws = w_sinv.contiguous().float()
+    bb = _bias_ok(bias, N, dev)
+    t, l1 = _FUSED_SCALE
+    sp = stream_ptr(dev)
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    downloaded = [torch.cuda.Event() for _ in range(2)]
+    start = torch.cuda.Event()
+    start.record(cur)
+    up.wait_event(start)
+    down.wait_event(start)
+    for c, r0 in enumerate(range(0, M, rows)):
+        b, n = c & 1, min(rows, M - r0)
+        with torch.cuda.stream(up):
+            if c >= 2:
+                up.wait_event(computed[b])  # the linear of chunk c-2 has read this x buffer
+            xb[b][:n].copy_(x_host[r0:r0 + n], non_blocking=True)
+            uploaded[b].record(up)
+        cur.wait_event(uploaded[b])
+        if c >= 2:
+            cur.wait_event(downloaded[b])  # chunk c-2's result has left this y buffer
+        if n <= GEMV_ROWS:
+            yb[b][:n] = _gemv(xb[b][:n], w16, w_sinv, bb, N)
+        else:
+            call("tbf16_linear", ptr(xb[b]), n, K, K, ptr(w16), N, K, ptr(ws), ptr(bb), ptr(yb[b]), N, ptr(s_inv),
+                 ptr(x16), t, int(l1), sp)
+        computed[b].record(cur)
+        with torch.cuda.stream(down):
+            down.wait_event(computed[b])
+            out[r0:r0 + n].copy_(yb[b][:n], non_blocking=True)
+            downloaded[b].record(down)
+    for t in (*xb, *yb):
+        t.record_stream(up)
+        t.record_stream(down)
+    cur.wait_stream(down)
+    return out
+
+
 def _gemm_f16(a16, a_mn, b16, b_mn, M, N, K, sa, sb=None, bias=None):
     """y (M, N) bf16 = (A @ B^T) * sa[:, None] * sb[None, :] + bias on the tcgen05 GEMM.
     A = a16 (M, K) or, with a_mn, a16 (K, M); B = b16 (N, K) or, with b_mn, b16 (K, N)."""
@@ -226,4 +293,5 @@ def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bi
 
 
 __all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
+           "linear_host",
            "available", "_target_exp"]
