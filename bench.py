@@ -302,6 +302,8 @@ def main():
             "clocks": clocks.summary()}
     if not args.no_e2e:
         line["e2e"] = e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16)
+    if not args.no_train_linear:
+        line["train_linear"] = train_linear_run(pk)
     if not args.no_attention:
         del x, y, w16
         torch.cuda.empty_cache()
@@ -309,9 +311,6 @@ def main():
             line["attention"] = attention_run(pk)
         except Exception as exc:  # the headline GEMM line still prints
             line["attention"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
-    if not args.no_train_linear:
-        torch.cuda.empty_cache()
-        line["train_linear"] = train_linear_run(pk)
     if not args.no_prefill:
         torch.cuda.empty_cache()
         line["prefill"] = prefill_run(world)  # every rank runs its own sequence (replicas)
