@@ -312,6 +312,260 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, i
   return tbf16_host::check_launch();
 }
 
+// ------------------------------------------------------------------------------------------------
+// CTA-pair GEMM (fp16 operands): a cluster of two CTAs on two SMs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256: each CTA holds 128 rows of A and of the accumulator; N = 256:
+// each CTA holds half of the B tile). Per SM and k16 step the tensor core reads 8 KB of shared memory
+// instead of 12 KB, and each SM loads 32 KB per 64-wide K block instead of 48 KB. The even CTA's
+// thread issues the MMAs; both CTAs' TMA loads count their bytes on the even CTA's full barrier; the
+// MMA completion is multicast to both CTAs' empty / accumulator-full barriers; both CTAs' epilogue
+// warps release an accumulator on the even CTA's barrier. No multicast loads.
+constexpr int kPairStages = 6;
+struct PairCfg {
+  static constexpr int A_BYTES = BM * BK * 2;          // this CTA's 128 rows
+  static constexpr int B_BYTES = 128 * BK * 2;         // this CTA's half of the 256 B rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int THREADS = 32 * (2 + kEpiWarps);
+  static constexpr int TMEM_COLS = 512;                // two 256-column accumulators
+  static constexpr int BAR_BYTES = 8 * (2 * kPairStages + 4) + 16;
+  static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(PairCfg::THREADS, 1)
+    scaled_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            const GemmParams p) {
+  using C = PairCfg;
+  constexpr int S = kPairStages;
+  constexpr int PN = 256;  // pair tile: 256 x 256
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES);  // even CTA's are used
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;                                             // even CTA's are used
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int num_tiles = p.tiles_m * p.tiles_n;  // in 256 x 256 pair tiles
+  const int KB = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cid; tile < num_tiles && !*abort; tile += nclusters) {
+        int tm, tn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+        const int m0 = tm * 256 + (int)rank * 128, n0 = tn * PN + (int)rank * 128;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both CTAs' bytes
+          if (!A_MN) {
+            tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(sA + j * 64 * BK * 2, &tmA, &full[stage], m0 + j * 64, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(sB, &tmB, &full[stage], kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(sB + j * 64 * BK * 2, &tmB, &full[stage], n0 + j * 64, kb * BK);
+          }
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, PN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = cid; tile < num_tiles && !*abort; tile += nclusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * PN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                     : smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs, own 128 rows)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cid; tile < num_tiles; tile += nclusters) {
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort, p.err)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      const int m = tm * 256 + (int)rank * 128 + row;
+      const bool mok = m < p.M;
+      const float a = mok ? __ldg(p.sa + m) : 0.f;
+      __nv_bfloat16* yrow = p.y + (int64_t)(mok ? m : 0) * p.ldy;
+#pragma unroll 1
+      for (int c = 0; c < PN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + acc * PN + c * 32 + ((uint32_t)(quad * 32) << 16), r);
+        tmem_ld_wait();
+        const int n0 = tn * PN + c * 32;
+        if (mok && n0 < p.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int n = n0 + 8 * j;
+            if (n < p.N) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float sbv = p.sb ? __ldg(p.sb + n + e) : 1.f;
+                v[e] = (__uint_as_float(r[8 * j + e]) * a) * sbv;
+                if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+              }
+              uint4 o;
+              o.x = pack_bf16(v[0], v[1]);
+              o.y = pack_bf16(v[2], v[3]);
+              o.z = pack_bf16(v[4], v[5]);
+              o.w = pack_bf16(v[6], v[7]);
+              *reinterpret_cast<uint4*>(yrow + n) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(&tempty[acc], 0);  // the even CTA's MMA may reuse the accumulator
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {  // let copies and MMAs already in flight land before the CTA's memory goes away
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  cluster_sync();  // the even CTA's MMAs have finished reading the odd CTA's shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <bool A_MN, bool B_MN>
+int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
+                     const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
+  using C = PairCfg;
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  if (!d) return TBF16_ERR_DEVICE;
+  CUtensorMap ta, tb;
+  int rc = A_MN ? tbf16_host::make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64)
+                : tbf16_host::make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, BM);
+  if (rc) return rc;
+  rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
+            : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 128);
+  if (rc) return rc;
+  auto kern = scaled_gemm_pair_kernel<A_MN, B_MN>;
+  static bool attr_done[64] = {false};
+  if (!attr_done[d->device & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return tbf16_host::check_launch();
+    attr_done[d->device & 63] = true;
+  }
+  GemmParams p;
+  p.M = M; p.N = N; p.K = K;
+  p.sa = sa; p.sb = sb;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.err = d->err;
+  p.tiles_m = (M + 255) / 256;
+  p.tiles_n = (N + 255) / 256;
+  static const int group_env = [] {
+    const char* e = getenv("TBF16_GEMM_GROUP");
+    return e ? atoi(e) : 0;
+  }();
+  p.group_m = group_env > 0 ? group_env : kGroupM / 2;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int clusters = std::min(tiles, d->sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return tbf16_host::check_launch();
+  return tbf16_host::check_launch();
+}
+
+// The pair kernel for large products (both dimensions span several 256 tiles); TBF16_GEMM_PAIR=0 / 1
+// forces the single-CTA / pair kernel.
+bool use_pair(int M, int N) {
+  static const int env = [] {
+    const char* e = getenv("TBF16_GEMM_PAIR");
+    return e ? atoi(e) : -1;
+  }();
+  if (env >= 0) return env != 0;
+  return (int64_t)((M + 255) / 256) * ((N + 255) / 256) >= 148;
+}
+
 bool ok8(int64_t v) { return v % 8 == 0; }
 
 }  // namespace
@@ -338,6 +592,8 @@ int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w
     if (target_exp < 0 || target_exp > 64) return TBF16_ERR_INVALID;
     auto st = static_cast<cudaStream_t>(stream);
     if (int rc = tbf16_host::row_pass(x, M, K, ldx, target_exp, l1, 1, x16_ws, K, x_sinv, nullptr, st)) return rc;
+    if (use_pair((int)M, (int)N))
+      return launch_gemm_pair<false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy, st);
     return launch_gemm<256, 4, false, false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y,
                                                     ldy, st);
   }
@@ -373,6 +629,12 @@ int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int 
   if (M == 0 || N == 0) return TBF16_OK;
   auto st = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
+  if (use_pair(m, n)) {
+    if (!a_mn && !b_mn) return launch_gemm_pair<false, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+    if (!a_mn && b_mn) return launch_gemm_pair<false, true>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+    if (a_mn && !b_mn) return launch_gemm_pair<true, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+    return launch_gemm_pair<true, true>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
+  }
   if (!a_mn && !b_mn) return launch_gemm<256, 4, false, false, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
   if (!a_mn && b_mn) return launch_gemm<256, 4, false, false, true>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
   if (a_mn && !b_mn) return launch_gemm<256, 4, false, true, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
