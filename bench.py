@@ -293,8 +293,9 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                          "frac": round(gemm_tflops / pk["tflops"], 4), "traffic": None,
                          "peak_source": f"{pk['source']} bf16 dense (burst); sustained {pk['tflops_sustained']}",
-                         "kernel": ("scaled_gemm_kernel<fp16 operands> (tcgen05, TMA, TMEM accumulators)"
-                                    if x16 is not None else "scaled_gemm_kernel<bf16 x converted in smem> (tcgen05)"),
+                         "kernel": ("scaled_gemm_pair_kernel<fp16 operands> (CTA pairs, tcgen05.mma.cta_group::2, TMA, "
+                                    "TMEM accumulators)" if x16 is not None
+                                    else "scaled_gemm_kernel<bf16 x converted in smem> (tcgen05)"),
                          "ms_per_launch": round(gemm_ms, 4)},
             "row_amax_kernel": {"ms": round(rs_ms, 4), "achieved_gbs": round(rs_gbs, 1), "peak_gbs": pk["hbm_gbs"],
                                 "frac": round(rs_gbs / pk["hbm_gbs"], 4), "bytes": rs_bytes,
@@ -464,7 +465,7 @@ def sweep_run(pk, iters=7):
     return rows
 
 
-def train_linear_run(pk, iters=5):
+def train_linear_run(pk, iters=9):
     """Config 4 MLP linears (8192 tokens, hidden 2048, SwiGLU 8192): gate, up, down through
     tbf16.autograd.linear (ScaledLinearFn: fwd + dX + dW each a tcgen05 GEMM with its scale passes),
     fwd + bwd per step; 6 * M * K * N flop per linear."""
@@ -485,13 +486,15 @@ def train_linear_run(pk, iters=5):
     for _ in range(2):
         step()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(iters):
+    ts = []
+    for _ in range(iters):  # median of per-step times: robust to a host hiccup in one step
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         step()
-    e1.record()
-    torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / iters
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    t = statistics.median(ts)
     return {"config": f"M={M} h={Hd} i={I} (gate, up, down) fwd+bwd", "ms": round(t, 3),
             "tflops": round(flop / (t / 1e3) / 1e12, 1), "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 3)}
 

@@ -191,12 +191,8 @@ def linear_host(x_host: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, b
     if K % 8 or N % 8 or w16.shape[1] != K or w16.stride(0) != K:
         raise RuntimeError("tbf16.linear_host: K and N must be multiples of 8 (use scaled_linear)")
     cur = torch.cuda.current_stream(dev)
-    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     rows = max(1, min(chunk_rows, M))
-    xb = [torch.empty((rows, K), device=dev, dtype=torch.bfloat16) for _ in range(2)]
-    yb = [torch.empty((rows, N), device=dev, dtype=torch.bfloat16) for _ in range(2)]
-    s_inv = torch.empty((rows,), device=dev, dtype=torch.float32)
-    x16 = torch.empty((rows, K), device=dev, dtype=torch.float16) if _materialise(rows, N, K) else None
+    up, down, xb, yb, s_inv, x16 = _host_pipeline(dev, cur, rows, K, N)
     ws = w_sinv.contiguous().float()
     bb = _bias_ok(bias, N, dev)
     t, l1 = _FUSED_SCALE
@@ -228,11 +224,32 @@ def linear_host(x_host: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, b
             down.wait_event(computed[b])
             out[r0:r0 + n].copy_(yb[b][:n], non_blocking=True)
             downloaded[b].record(down)
-    for t in (*xb, *yb):
-        t.record_stream(up)
-        t.record_stream(down)
     cur.wait_stream(down)
     return out
+
+
+# Copy streams and chunk buffers of linear_host, kept per (device, calling stream, shape): calls on one
+# stream are ordered (each waits for the previous call's downloads), so they can share the buffers,
+# and nothing is freed while the copy streams may still use it.
+_HOST_PIPES = {}
+
+
+def _host_pipeline(dev, cur, rows, K, N):
+    key = (dev.index, cur.cuda_stream, rows, K, N)
+    pipe = _HOST_PIPES.get(key)
+    if pipe is None:
+        if len(_HOST_PIPES) >= 8:  # drop the cache, once its copy streams are idle
+            for old in _HOST_PIPES.values():
+                old[0].synchronize()
+                old[1].synchronize()
+            _HOST_PIPES.clear()
+        pipe = (torch.cuda.Stream(dev), torch.cuda.Stream(dev),
+                [torch.empty((rows, K), device=dev, dtype=torch.bfloat16) for _ in range(2)],
+                [torch.empty((rows, N), device=dev, dtype=torch.bfloat16) for _ in range(2)],
+                torch.empty((rows,), device=dev, dtype=torch.float32),
+                torch.empty((rows, K), device=dev, dtype=torch.float16) if _materialise(rows, N, K) else None)
+        _HOST_PIPES[key] = pipe
+    return pipe
 
 
 def _gemm_f16(a16, a_mn, b16, b_mn, M, N, K, sa, sb=None, bias=None):
