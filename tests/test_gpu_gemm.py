@@ -108,3 +108,21 @@ def test_linear_q_matches_linear():
     y_q = ops.linear_q(x16, sx, w16, ws)
     exact = x.double() @ w.double().t()
     assert rel_err(y_q, exact) < 2e-3
+
+
+@pytest.mark.parametrize("M,K,N,bias", [(9, 4096, 4096, True), (16, 8192, 8192, False), (100, 520, 264, True),
+                                        (129, 64, 1000, False), (256, 2048, 768, True), (33, 4104, 1032, True),
+                                        (200, 1000, 136, False)])
+def test_skinny_linear_vs_oracle(M, K, N, bias):
+    """9 <= M <= 256 runs the split-K skinny GEMM (weight rows on the MMA's 128-row side, K split over a
+    cluster of up to 8 CTAs, partials reduced through distributed shared memory): uneven K splits, a
+    single K block, N tails, M padded to 16 columns, all within the oracle bound; two runs bit-equal."""
+    from tbf16 import ops
+    x = inputs.gemm_x(M, K, seed=M * 7 + K)
+    w = inputs.gemm_w(N, K, seed=N + 3)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(5)) * 0.1).bfloat16() if bias else None
+    y, y_ref, absprod, *_ = _linear_case(x, w, b)
+    assert_close_ulp(y, y_ref, gemm_tolerance(y_ref, absprod, K), what=f"skinny {M}x{K}x{N}")
+    w16, ws = ops.prepare_weight(w.cuda())
+    y2 = ops.scaled_linear(x.cuda(), w16, ws, None if b is None else b.cuda()).cpu()
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))

@@ -292,6 +292,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
+// 32 lanes x 32 bits, 16 consecutive columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -302,6 +310,14 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// Lets the next kernel of the stream, when launched with the programmatic-serialization attribute, start
+// before this grid ends (no-op otherwise).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the preceding grid of the stream has completed and its memory is visible (returns at once
+// for a kernel launched without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ CTA pairs (cluster of 2, cta_group::2)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -311,6 +327,17 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 // All threads of both CTAs of the cluster.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the same shared offset in CTA `cta` of the cluster.
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t saddr, uint32_t cta) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(cta));
+  return remote;
+}
+// 16-byte store into (possibly another CTA's) distributed shared memory.
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
 // Arrive on the mbarrier at the same shared offset in CTA `cta` of the cluster.
 __device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar_local, uint32_t cta) {
@@ -439,6 +466,15 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // elements take one HBM read (row in registers). Arguments already validated by the caller.
 int row_pass(const void* x, int64_t rows, int64_t K, int64_t ldx, int t, int l1, int fused_rule, void* y, int64_t ldy,
              float* s_inv, int8_t* exp_out, cudaStream_t st);
+// Scaled GEMM for few activation rows (M <= kSkinnyMaxRows), both operands K-major fp16:
+// y[m, n] = bf16((sum_k A[m,k] B[n,k]) * sa[m] * sb[n] + bias[n]) (gemm_skinny.cu). Validated by the caller.
+constexpr int kSkinnyMaxRows = 256;
+// after_row_pass: the preceding kernel of the stream is the row pass that writes A and sa (and nothing
+// the GEMM reads otherwise); the GEMM is then launched as its programmatic dependent.
+int skinny_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
+                const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st, bool after_row_pass);
+// Whether skinny_gemm takes an M x N product (TBF16_GEMM_SKINNY=0 / 1 forces it off / on for M <= 256).
+bool use_skinny(int M, int N);
 // Encode a 2-D tiled tensor map (16-bit elements, 128-byte swizzle) for a row-major [rows, cols]
 // matrix with leading dimension ld (elements). Returns 0 on success.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,

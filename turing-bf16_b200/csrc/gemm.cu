@@ -592,6 +592,9 @@ int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w
     if (target_exp < 0 || target_exp > 64) return TBF16_ERR_INVALID;
     auto st = static_cast<cudaStream_t>(stream);
     if (int rc = tbf16_host::row_pass(x, M, K, ldx, target_exp, l1, 1, x16_ws, K, x_sinv, nullptr, st)) return rc;
+    if (tbf16_host::use_skinny((int)M, (int)N))
+      return tbf16_host::skinny_gemm(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy, st,
+                                       true);
     if (use_pair((int)M, (int)N))
       return launch_gemm_pair<false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy, st);
     return launch_gemm<256, 4, false, false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y,
@@ -629,6 +632,8 @@ int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int 
   if (M == 0 || N == 0) return TBF16_OK;
   auto st = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
+  if (!a_mn && !b_mn && tbf16_host::use_skinny(m, n))
+    return tbf16_host::skinny_gemm(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st, false);
   if (use_pair(m, n)) {
     if (!a_mn && !b_mn) return launch_gemm_pair<false, false>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);
     if (!a_mn && b_mn) return launch_gemm_pair<false, true>(a16, lda, b16, ldb, m, n, k, sa, sb, bias, y, ldy, st);

@@ -100,6 +100,7 @@ template <int NCH, bool L1, bool FUSED_RULE, bool WRITE_Y>
 __global__ void __launch_bounds__(256) row_pass_kernel(const uint4* __restrict__ x, int64_t rows, int K8, int64_t ldx8,
                                                        int t, uint4* __restrict__ y, int64_t ldy8,
                                                        float* __restrict__ s_inv, int8_t* __restrict__ exp_out) {
+  pdl_launch_dependents();  // the linear's skinny GEMM may start streaming its weight meanwhile
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;

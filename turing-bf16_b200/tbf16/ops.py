@@ -27,6 +27,7 @@ _FUSED_SCALE = (15, False)
 L1_TARGET = 15
 SMALL_M = 2
 GEMV_ROWS = 8  # rows handled by the weight-streaming kernel (TBF16_GEMV_MAX_ROWS)
+SKINNY_ROWS = 256  # rows handled by the split-K skinny GEMM (kSkinnyMaxRows in the library)
 
 
 def _target_exp(K: int) -> int:
@@ -117,13 +118,14 @@ def _bias_ok(bias, N, device):
 def _materialise(M, N, K) -> bool:
     """Whether the linear should write an fp16 copy of x in its row pass (TBF16_LINEAR=fused forces
     the in-GEMM conversion, =materialise the copy). The in-GEMM conversion is redone once per 256-wide
-    N tile, so it only pays when N fits in one or two tiles."""
+    N tile, so it only pays when N fits in one or two tiles; up to 256 rows the copy is small and the
+    split-K skinny GEMM (fp16 operands only) takes the product."""
     mode = os.environ.get("TBF16_LINEAR", "")
     if mode == "fused":
         return False
     if mode == "materialise":
         return True
-    return N > 512
+    return N > 512 or M <= SKINNY_ROWS
 
 
 @torch.autocast("cuda", enabled=False)
