@@ -429,9 +429,10 @@ def dist_rank():
 def sweep_run(pk, iters=7):
     """Config 2 sweep: scaled_linear (bf16 x, weights as tbf16.convert stores them) at M = 1 .. 16384 and
     N = K in {4096, 8192}, each timed alone with CUDA events between L2 flushes (a 512 MB write, long
-    enough that the host has queued the linear's launches before the GPU reaches them). M <= 8 runs the
-    weight-streaming kernel (HBM-bound: weight GB/s against the copy peak), larger M the row pass plus
-    the tcgen05 GEMM (TFLOPS against the bf16 peak)."""
+    enough that the host has queued the linear's launches before the GPU reaches them). Up to 4 rows run
+    the weight-streaming kernel, up to 256 the split-K skinny GEMM, more the row pass plus the tcgen05 GEMM.
+    Each point's roofline is the slower of its bytes (weight + x read + y written) at the copy peak and its
+    flop at the bf16 peak; "frac" is that time over the measured one."""
     import inputs
     from tbf16 import ops
     flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
@@ -454,11 +455,12 @@ def sweep_run(pk, iters=7):
             t = statistics.median(ts)
             flop = 2.0 * M * NK * NK
             nbytes = 2.0 * NK * NK + 4.0 * M * NK  # weight + x read + y written
+            t_hbm = nbytes / (pk["hbm_gbs"] * 1e6)  # ms
+            t_tc = flop / (pk["tflops"] * 1e9)
             rows.append({"M": M, "N": NK, "K": NK, "ms": round(t, 4), "tflops": round(flop / t / 1e9, 1),
-                         "gbs": round(nbytes / t / 1e6, 1),
-                         "frac": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3) if M <= ops.GEMV_ROWS
-                         else round(flop / t / 1e9 / pk["tflops"], 3),
-                         "bound": "hbm" if M <= ops.GEMV_ROWS else "tensor"})
+                         "gbs": round(nbytes / t / 1e6, 1), "frac": round(max(t_hbm, t_tc) / t, 3),
+                         "bound": "hbm" if t_hbm >= t_tc else "tensor",
+                         "kernel": "gemv" if M <= ops.GEMV_ROWS else ("skinny" if M <= ops.SKINNY_ROWS else "gemm")})
             del x
         del w16, ws
     del flush

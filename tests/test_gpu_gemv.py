@@ -1,7 +1,8 @@
-"""Parity of the few-row linear (decode path, M <= 8) with the oracle's restatement of the reference's
-single-row kernel (small_kernels.cu:107-132): fp32 products of bf16 x and fp16 w, times ws, plus
-bias, one bf16 rounding. Elementwise within one bf16 ulp plus the fp32 summation bound
-(K * 2^-24 * sum |x w| ws). Called through tbf16.ops (ctypes -> C ABI)."""
+"""Parity of the few-row linear (decode path, tbf16_gemv, M <= 8) with the oracle's restatement of the
+reference's single-row kernel (small_kernels.cu:107-132): fp32 products of bf16 x and fp16 w, times ws,
+plus bias, one bf16 rounding. Elementwise within one bf16 ulp plus the fp32 summation bound
+(K * 2^-24 * sum |x w| ws). Up to ops.GEMV_ROWS rows through tbf16.ops, more through the C ABI directly
+(scaled_linear sends those to the skinny GEMM)."""
 import pytest
 import torch
 
@@ -29,9 +30,22 @@ def test_gemv_vs_oracle(M, K, N, bias):
     w = inputs.gemm_w(N, K, seed=N)
     b = (torch.randn(N, generator=torch.Generator().manual_seed(3)) * 0.1).bfloat16() if bias else None
     w16, ws = ops.prepare_weight(w.cuda())
-    y = ops.small_m_linear(x.cuda(), w16, ws, None if b is None else b.cuda()).cpu()
+    if M <= ops.GEMV_ROWS:
+        y = ops.small_m_linear(x.cuda(), w16, ws, None if b is None else b.cuda()).cpu()
+    else:
+        y = _gemv_direct(x.cuda(), w16, ws, None if b is None else b.cuda()).cpu()
     assert y.shape == (M, N) and y.dtype == torch.bfloat16
     _check(y, x, w16.cpu(), ws.cpu(), b)
+
+
+def _gemv_direct(x, w16, ws, b):
+    from tbf16 import _ext as E
+    M, K = x.shape
+    N = w16.shape[0]
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    E.call("tbf16_gemv", E.ptr(x), M, K, x.stride(0), E.ptr(w16), N, w16.stride(0), E.ptr(ws), E.ptr(b), E.ptr(y), N,
+           E.stream_ptr(x.device))
+    return y
 
 
 def test_gemv_strided_rows_and_3d_input():
@@ -66,7 +80,9 @@ def test_gemv_rejects_too_many_rows():
 
 def test_linear_host_matches_device_path():
     """linear_host (pinned host x and y, chunked over three streams) gives the device path's rows:
-    bit-equal where a chunk goes through the GEMM, within the GEMV bound for a final chunk of <= 8 rows."""
+    bit-equal where a chunk goes through the same GEMM, within the oracle bounds for a short final chunk
+    (skinny GEMM for 5 rows, GEMV for 3)."""
+    from helpers import assert_close_ulp, gemm_tolerance
     from tbf16 import ops
     M, K, N = 2 * 1024 + 5, 512, 768
     x = inputs.gemm_x(M, K, seed=21)
@@ -79,4 +95,10 @@ def test_linear_host_matches_device_path():
     assert y.shape == (M, N) and not y.is_cuda
     ref = ops.scaled_linear(x.cuda(), w16, ws, b.cuda()).cpu()
     assert torch.equal(y[:2048].view(torch.int16), ref[:2048].view(torch.int16))
-    _check(y[2048:], x[2048:], w16.cpu(), ws.cpu(), b)
+    xs, w16c, wsc = x[2048:].contiguous(), w16.cpu(), ws.cpu()
+    y_ref, _ = orc.linear_fused(xs, w16c, wsc, b)
+    absprod = (xs.double().abs() @ w16c.double().abs().t()) * wsc.double()[None, :]
+    assert_close_ulp(y[2048:], y_ref, gemm_tolerance(y_ref, absprod, K), what="linear_host final chunk")
+    y3 = ops.linear_host(hx[:2048 + 3].contiguous(), w16, ws, b.cuda(), chunk_rows=2048)
+    torch.cuda.synchronize()
+    _check(y3[2048:], x[2048:2051], w16c, wsc, b)

@@ -17,7 +17,8 @@ def _ext():
     return _ext
 
 
-@pytest.mark.parametrize("R,K", [(64, 64), (37, 1032), (8, 20000), (300, 4096), (1, 8)])
+@pytest.mark.parametrize("R,K", [(64, 64), (37, 1032), (8, 20000), (300, 4096), (1, 8), (16, 8192), (5, 16384),
+                                 (1024, 2056), (1025, 2056)])
 @pytest.mark.parametrize("l1", [False, True])
 def test_row_scale_fused(R, K, l1):
     E = _ext()
@@ -39,7 +40,7 @@ def test_row_scale_fused(R, K, l1):
     assert torch.equal(s2, s_inv)
 
 
-@pytest.mark.parametrize("R,K", [(64, 64), (37, 1032), (8, 20000), (257, 4096)])
+@pytest.mark.parametrize("R,K", [(64, 64), (37, 1032), (8, 20000), (257, 4096), (16, 8192), (3, 16384)])
 @pytest.mark.parametrize("t", [0, -1, 15])
 @pytest.mark.parametrize("l1", [False, True])
 def test_quantize_rows(R, K, t, l1):

@@ -555,15 +555,16 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   return tbf16_host::check_launch();
 }
 
-// The pair kernel for large products (both dimensions span several 256 tiles); TBF16_GEMM_PAIR=0 / 1
-// forces the single-CTA / pair kernel.
+// The pair kernel whenever both dimensions span two or more 256 tiles (it moves a third less data from
+// L2 per SM for the same CTA count; measured faster from M = N = 512 up), or the product fills the
+// GPU with pair tiles; TBF16_GEMM_PAIR=0 / 1 forces the single-CTA / pair kernel.
 bool use_pair(int M, int N) {
   static const int env = [] {
     const char* e = getenv("TBF16_GEMM_PAIR");
     return e ? atoi(e) : -1;
   }();
   if (env >= 0) return env != 0;
-  return (int64_t)((M + 255) / 256) * ((N + 255) / 256) >= 148;
+  return (M >= 512 && N >= 512) || (int64_t)((M + 255) / 256) * ((N + 255) / 256) >= 148;
 }
 
 bool ok8(int64_t v) { return v % 8 == 0; }

@@ -147,12 +147,96 @@ __global__ void __launch_bounds__(256) row_pass_kernel(const uint4* __restrict__
   }
 }
 
+// The same for few long rows (decode and small batches): one 256-thread block per row, thread t holding
+// the row's 16-byte chunks t, t + 256, ... in registers, so a 16-row linear input spreads over 16 SMs
+// instead of two and each thread waits for at most NCH loads. The max (or fp64 L1 sum) is reduced over
+// the warp, then over the 8 warps in a fixed order.
+template <int NCH, bool L1, bool FUSED_RULE, bool WRITE_Y>
+__global__ void __launch_bounds__(256) row_pass_block_kernel(const uint4* __restrict__ x, int K8, int64_t ldx8, int t,
+                                                             uint4* __restrict__ y, int64_t ldy8,
+                                                             float* __restrict__ s_inv, int8_t* __restrict__ exp_out) {
+  pdl_launch_dependents();
+  __shared__ float red_m[8];
+  __shared__ double red_s[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x;
+  const uint4* xr = x + row * ldx8;
+  uint4 v[NCH];
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const int i = tid + 256 * u;
+    v[u] = i < K8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
+  }
+  float m = 0.f;
+  double s = 0.0;
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = fabsf(bf16lo(w[j])), b = fabsf(bf16hi(w[j]));
+      if (L1) s += (double)a + (double)b;
+      else m = fmaxf(m, fmaxf(a, b));
+    }
+  }
+  if (L1) s = warp_sum(s);
+  else m = warp_max(m);
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_s[warp] = s;
+  }
+  __syncthreads();
+  float red;
+  if (L1) {
+    double tot = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red_s[k];
+    red = (float)tot;
+  } else {
+    red = red_m[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) red = fmaxf(red, red_m[k]);
+  }
+  const int se = FUSED_RULE ? scale_biased_exp_fused(red, t) : scale_biased_exp_small(red, t);
+  if (WRITE_Y) {
+    const float sc = pow2_from_biased(se);
+    uint4* yr = y + row * ldy8;
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int i = tid + 256 * u;
+      if (i < K8) {
+        uint4 o;
+        o.x = pack_f16(bf16lo(v[u].x) * sc, bf16hi(v[u].x) * sc);
+        o.y = pack_f16(bf16lo(v[u].y) * sc, bf16hi(v[u].y) * sc);
+        o.z = pack_f16(bf16lo(v[u].z) * sc, bf16hi(v[u].z) * sc);
+        o.w = pack_f16(bf16lo(v[u].w) * sc, bf16hi(v[u].w) * sc);
+        yr[i] = o;
+      }
+    }
+  }
+  if (tid == 0) {
+    s_inv[row] = inv_pow2_from_biased(se);
+    if (exp_out) exp_out[row] = (int8_t)(se - 127);
+  }
+}
+
+constexpr int64_t kBlockRowsMax = 1024;  // up to this many rows (8 per block would leave SMs idle)
+
 template <bool L1, bool FUSED_RULE, bool WRITE_Y>
 bool launch_row_pass_t(const void* x, int64_t rows, int K8, int64_t ldx8, int t, void* y, int64_t ldy8, float* s_inv,
                        int8_t* exp_out, cudaStream_t st) {
   const unsigned grid = (unsigned)((rows + kRowWarps - 1) / kRowWarps);
   const uint4* xp = static_cast<const uint4*>(x);
   uint4* yp = static_cast<uint4*>(y);
+  if (rows <= kBlockRowsMax && K8 > 256 && K8 <= 2048) {
+    const unsigned g = (unsigned)rows;
+#define TBF16_ROW_BLOCK(N) row_pass_block_kernel<N, L1, FUSED_RULE, WRITE_Y><<<g, 256, 0, st>>>(xp, K8, ldx8, t, yp, ldy8, s_inv, exp_out)
+    if (K8 <= 512) TBF16_ROW_BLOCK(2);
+    else if (K8 <= 1024) TBF16_ROW_BLOCK(4);
+    else TBF16_ROW_BLOCK(8);
+#undef TBF16_ROW_BLOCK
+    return true;
+  }
 #define TBF16_ROW_PASS(N) row_pass_kernel<N, L1, FUSED_RULE, WRITE_Y><<<grid, 256, 0, st>>>(xp, rows, K8, ldx8, t, yp, ldy8, s_inv, exp_out)
   if (K8 <= 32) TBF16_ROW_PASS(1);
   else if (K8 <= 64) TBF16_ROW_PASS(2);

@@ -4,8 +4,9 @@ Same public surface as the reference's tbf16/ops.py (quantize_rows, prepare_weig
 linear_q, small_m_linear, quantize_rows_shared, _target_exp), plus linear_host for activations that
 live in pinned host memory. The work runs in libtbf16_sm100.so: a row-amax -> exponent pass (which
 also writes the fp16 copy of x for large N) and a warp-specialised TMA + tcgen05 GEMM that
-accumulates in fp32 in TMEM and writes bf16 straight from the accumulator; up to 8 rows take a
-weight-streaming kernel instead (the reference's single-row GEMV, extended). The reference's Triton
+accumulates in fp32 in TMEM and writes bf16 straight from the accumulator. Up to 4 rows take a
+weight-streaming kernel instead (the reference's single-row GEMV, extended), up to 256 rows a split-K
+variant of the GEMM that keeps the whole GPU streaming the weight. The reference's Triton
 kernels and its cuBLAS small-M branch are gone, and there is no CPU fallback.
 """
 import math
@@ -26,7 +27,8 @@ _FUSED_SCALE = (15, False)
 # Rows scaled by their L1 norm for the training dX GEMM (reference tbf16/ops.py:129-130).
 L1_TARGET = 15
 SMALL_M = 2
-GEMV_ROWS = 8  # rows handled by the weight-streaming kernel (TBF16_GEMV_MAX_ROWS)
+GEMV_ROWS = 4  # rows taken by the weight-streaming kernel (it accepts up to TBF16_GEMV_MAX_ROWS = 8;
+               # from 5 rows on the skinny GEMM streams the weight faster)
 SKINNY_ROWS = 256  # rows handled by the split-K skinny GEMM (kSkinnyMaxRows in the library)
 
 
