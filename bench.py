@@ -37,6 +37,11 @@ M_DEFAULT = N_DEFAULT = K_DEFAULT = 8192
 METRIC = "scaled GEMM TFLOPS (M=N=K=8192, config 2) & % of dense fp16 tensor peak"
 
 
+# DRAM bytes (read + write) of one scaled_gemm_pair_kernel launch at M = N = K = 8192, from the ncu
+# capture summarised in profiles/scaled_gemm_pair_8192_cube.md (1.070 GB read + 0.127 GB written).
+PAIR_8192_TRAFFIC = 1.197e9
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -182,6 +187,9 @@ def main():
                     help="config-2 GEMM sweep (M = 1 .. 16384 at N = K = 4096 and 8192, L2 flushed) and the "
                          "config-4 MLP linears fwd+bwd; prints one JSON line and exits")
     ap.add_argument("--no-train-linear", action="store_true", help="skip the config-4 MLP linear fwd+bwd")
+    ap.add_argument("--profile-linear", type=int, default=0, metavar="M",
+                    help="only run tbf16.ops.scaled_linear with M rows (N, K from --N / --K) --warmup + --steps times "
+                         "and print its median time: the few-row kernels' profiling case")
     ap.add_argument("--gemm", default="materialise", choices=["materialise", "fused"],
                     help="materialise (default, what tbf16_linear does with its x16 workspace): the row pass writes "
                          "fp16(x * s) and the GEMM runs on fp16 operands; fused: bf16 x converted inside the GEMM")
@@ -196,6 +204,9 @@ def main():
     if args.only_attention:
         print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
                                                      train=args.attn_train)}))
+        return
+    if args.profile_linear:
+        print(json.dumps({"profile_linear": profile_linear_run(args.profile_linear, N, K, args.steps, args.warmup)}))
         return
     if args.sweep:
         pk = peaks()
@@ -291,7 +302,11 @@ def main():
             "data": "synthetic (config 2 distribution, seeded)", "config": config,
             "gpu_launches": 2 * args.steps,
             "roofline": {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
-                         "frac": round(gemm_tflops / pk["tflops"], 4), "traffic": None,
+                         "frac": round(gemm_tflops / pk["tflops"], 4),
+                         "traffic": (PAIR_8192_TRAFFIC if (M, N, K) == (8192, 8192, 8192) and x16 is not None
+                                     else None),
+                         "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, ncu capture "
+                                            "summarised in profiles/scaled_gemm_pair_8192_cube.md"),
                          "peak_source": f"{pk['source']} bf16 dense (burst); sustained {pk['tflops_sustained']}",
                          "kernel": ("scaled_gemm_pair_kernel<fp16 operands> (CTA pairs, tcgen05.mma.cta_group::2, TMA, "
                                     "TMEM accumulators)" if x16 is not None
@@ -465,6 +480,35 @@ def sweep_run(pk, iters=7):
         del w16, ws
     del flush
     return rows
+
+
+def profile_linear_run(M, N, K, steps, warmup, copies=4):
+    """scaled_linear at one (M, N, K) on config-2 inputs, the user-facing call (routes by M). `warmup`
+    eager calls, then a CUDA graph of one call per weight copy (4 copies of the weight: 512 MB at
+    N = K = 8192, more than L2) replayed `steps` times; the time per call is free of host overhead."""
+    import inputs
+    from tbf16 import ops
+    x = inputs.gemm_x(M, K, seed=7, device="cuda")
+    ws_list = [ops.prepare_weight(inputs.gemm_w(N, K, seed=1 + c, device="cuda")) for c in range(copies)]
+    for i in range(warmup):
+        ops.scaled_linear(x, *ws_list[i % copies])
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for w16, ws in ws_list:
+            ops.scaled_linear(x, w16, ws)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(max(1, steps)):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (max(1, steps) * copies)
+    kernel = "gemv" if M <= ops.GEMV_ROWS else ("skinny" if M <= ops.SKINNY_ROWS else "gemm")
+    return {"M": M, "N": N, "K": K, "us_per_call": round(us, 2), "weight_gbs": round(2.0 * N * K / us / 1e3, 1),
+            "kernel": kernel, "timing": f"CUDA graph of {copies} calls over {copies} weight copies"}
 
 
 def train_linear_run(pk, iters=9):
