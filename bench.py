@@ -187,6 +187,8 @@ def main():
                     help="config-2 GEMM sweep (M = 1 .. 16384 at N = K = 4096 and 8192, L2 flushed) and the "
                          "config-4 MLP linears fwd+bwd; prints one JSON line and exits")
     ap.add_argument("--no-train-linear", action="store_true", help="skip the config-4 MLP linear fwd+bwd")
+    ap.add_argument("--only-train-linear", action="store_true",
+                    help="only time the config-4 MLP linears forward + backward (their profiling case)")
     ap.add_argument("--profile-linear", type=int, default=0, metavar="M",
                     help="only run tbf16.ops.scaled_linear with M rows (N, K from --N / --K) --warmup + --steps times "
                          "and print its median time: the few-row kernels' profiling case")
@@ -204,6 +206,9 @@ def main():
     if args.only_attention:
         print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
                                                      train=args.attn_train)}))
+        return
+    if args.only_train_linear:
+        print(json.dumps({"train_linear": train_linear_run(peaks(), iters=max(1, args.steps))}))
         return
     if args.profile_linear:
         print(json.dumps({"profile_linear": profile_linear_run(args.profile_linear, N, K, args.steps, args.warmup)}))

@@ -28,7 +28,8 @@ def _linear_case(x, w, b, rows=None):
 
 @pytest.mark.parametrize("M,K,N,bias", [(256, 1024, 1024, True), (1, 4096, 4096, False), (7, 1024, 512, True),
                                         (130, 4104, 264, True), (333, 520, 1032, False), (64, 64, 256, True),
-                                        (512, 2048, 768, False), (1000, 128, 4096, True)])
+                                        (512, 2048, 768, False), (1000, 128, 4096, True), (600, 264, 1000, True),
+                                        (777, 1024, 520, False)])
 def test_linear_vs_oracle(M, K, N, bias):
     x = inputs.gemm_x(M, K, seed=M + K)
     w = inputs.gemm_w(N, K, seed=N + 1)
@@ -81,7 +82,7 @@ def test_linear_large_sampled(M, K, N):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
-@pytest.mark.parametrize("M,N,K", [(256, 512, 192), (200, 136, 1000)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 192), (200, 136, 1000), (640, 520, 192)])
 def test_gemm_f16_majors(a_mn, b_mn, M, N, K):
     from tbf16 import ops
     g = torch.Generator().manual_seed(M + N + K + 2 * a_mn + b_mn)

@@ -188,6 +188,14 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const vo
       "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// 2-D tiled store from shared memory (bulk group completion). Coordinates must be >= 0 and x * 2 bytes a
+// multiple of 16; TMA writes only the part of the box inside the tensor.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N committed bulk groups of this thread still read their shared source.
 template <int N>
@@ -483,6 +491,10 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t row
 // strides of dims 1 and 2, box {box0, box1, 1}.
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                  uint64_t stride2, uint32_t box0, uint32_t box1);
+// Output map for TMA stores of bf16 tiles: rows of box_cols = 32 elements (64 bytes, 64-byte swizzle:
+// 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3) in shared memory).
+int make_tmap_2d_out(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                     uint32_t box_rows);
 // The same for fp32 elements (box0 * 4 <= 128 bytes, the swizzle span).
 int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                      uint64_t stride2, uint32_t box0, uint32_t box1);

@@ -42,7 +42,8 @@ struct GemmParams {
   int64_t ldy;
   unsigned int* err;
   int tiles_m, tiles_n;
-  int group_m;  // M tiles per raster group
+  int group_m;    // M tiles per raster group
+  int tma_store;  // pair kernel: epilogue through shared memory and TMA stores (else direct 16-byte stores)
 };
 
 template <int BN, int STAGES, bool CONVERT>
@@ -327,21 +328,22 @@ struct PairCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int THREADS = 32 * (2 + kEpiWarps);
   static constexpr int TMEM_COLS = 512;                // two 256-column accumulators
+  static constexpr int EPI_BYTES = kEpiWarps * 2 * 32 * 64;  // per epilogue warp two 32 x 32 bf16 tiles
   static constexpr int BAR_BYTES = 8 * (2 * kPairStages + 4) + 16;
-  static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + BAR_BYTES;
+  static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     scaled_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            const GemmParams p) {
+                            const __grid_constant__ CUtensorMap tmY, const GemmParams p) {
   using C = PairCfg;
   constexpr int S = kPairStages;
   constexpr int PN = 256;  // pair tile: 256 x 256
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES);  // even CTA's are used
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES + C::EPI_BYTES);  // even CTA's are used
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;                                             // even CTA's are used
@@ -443,6 +445,11 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     // ------------------------------------------------------------ epilogue (both CTAs, own 128 rows)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
+    // TMA-store path: each warp converts 32 columns of its 32 rows into one of two 2 KB shared tiles
+    // (64-byte swizzle, conflict-free 16-byte writes) and one lane stores the tile with TMA; the buffer
+    // is rewritten only after the store issued from it two chunks earlier has read it.
+    uint8_t* ebuf = smem + S * C::STAGE_BYTES + (warp - 2) * 2 * 2048;
+    int eb = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = cid; tile < num_tiles; tile += nclusters) {
@@ -453,6 +460,51 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
       const int m = tm * 256 + (int)rank * 128 + row;
       const bool mok = m < p.M;
       const float a = mok ? __ldg(p.sa + m) : 0.f;
+      if (p.tma_store) {
+        const int row0 = tm * 256 + (int)rank * 128 + quad * 32;
+#pragma unroll 1
+        for (int c = 0; c < PN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + acc * PN + c * 32 + ((uint32_t)(quad * 32) << 16), r);
+          tmem_ld_wait();
+          const int n0 = tn * PN + c * 32;
+          if (n0 >= p.N) break;  // the rest of this tile lies past the last column
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          uint8_t* buf = ebuf + eb * 2048;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int n = n0 + 8 * j;
+            uint4 o = make_uint4(0, 0, 0, 0);
+            if (n < p.N) {  // N is a multiple of 8: the 8 columns are all inside or all outside
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float sbv = p.sb ? __ldg(p.sb + n + e) : 1.f;
+                v[e] = (__uint_as_float(r[8 * j + e]) * a) * sbv;
+                if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+              }
+              o.x = pack_bf16(v[0], v[1]);
+              o.y = pack_bf16(v[2], v[3]);
+              o.z = pack_bf16(v[4], v[5]);
+              o.w = pack_bf16(v[6], v[7]);
+            }
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) = o;
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmY, buf, n0, row0);
+            bulk_commit_group();
+          }
+          eb ^= 1;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(&tempty[acc], 0);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
       __nv_bfloat16* yrow = p.y + (int64_t)(mok ? m : 0) * p.ldy;
 #pragma unroll 1
       for (int c = 0; c < PN / 32; ++c) {
@@ -489,6 +541,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     }
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait_group<0>();  // the epilogue's TMA stores have completed
   tc_fence_before();
   __syncthreads();
   if (*abort) {  // let copies and MMAs already in flight land before the CTA's memory goes away
@@ -516,6 +569,9 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
             : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 128);
   if (rc) return rc;
+  CUtensorMap ty;
+  rc = tbf16_host::make_tmap_2d_out(&ty, y, (uint64_t)N, (uint64_t)M, (uint64_t)ldy, 32, 32);
+  if (rc) return rc;
   auto kern = scaled_gemm_pair_kernel<A_MN, B_MN>;
   static bool attr_done[64] = {false};
   if (!attr_done[d->device & 63]) {
@@ -537,6 +593,11 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
     return e ? atoi(e) : 0;
   }();
   p.group_m = group_env > 0 ? group_env : kGroupM / 2;
+  static const int epi_env = [] {  // TBF16_GEMM_EPI=0 selects the direct-store epilogue (for comparison)
+    const char* e = getenv("TBF16_GEMM_EPI");
+    return e ? atoi(e) : 1;
+  }();
+  p.tma_store = epi_env != 0 && tbf16_host::aligned16(y) ? 1 : 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int clusters = std::min(tiles, d->sms / 2);
   cudaLaunchConfig_t cfg = {};
@@ -551,7 +612,7 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return tbf16_host::check_launch();
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, p) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
 

@@ -100,6 +100,20 @@ int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, u
   return r == CUDA_SUCCESS ? TBF16_OK : TBF16_ERR_INVALID;
 }
 
+int make_tmap_2d_out(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                     uint32_t box_rows) {
+  if (!encode_fn()) return TBF16_ERR_LAUNCH;
+  if (!aligned16(base) || (ld * 2) % 16 != 0 || box_cols * 2 != 64) return TBF16_ERR_ALIGN;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TBF16_OK : TBF16_ERR_INVALID;
+}
+
 int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                      uint64_t stride2, uint32_t box0, uint32_t box1) {
   if (!encode_fn()) return TBF16_ERR_LAUNCH;
