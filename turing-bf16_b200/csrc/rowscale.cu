@@ -5,6 +5,9 @@
 // host for 16-byte alignment. Max reductions use fmaxf (NaN ignored, as the reference's kernels do);
 // L1 norms accumulate in fp64 so that the exponent does not depend on the reduction order except
 // when the sum lies within ~2^-45 (relative) of a power of two.
+#include <algorithm>
+#include <utility>
+
 #include "common.cuh"
 
 using namespace tbf16;
@@ -112,17 +115,18 @@ __global__ void __launch_bounds__(256) row_pass_kernel(const uint4* __restrict__
     v[u] = i < K8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
   }
   float m = 0.f;
-  double s = 0.0;
+  double s4[4] = {0.0, 0.0, 0.0, 0.0};  // four independent fp64 chains (a single one is latency-bound)
 #pragma unroll
   for (int u = 0; u < NCH; ++u) {
     const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float a = fabsf(bf16lo(w[j])), b = fabsf(bf16hi(w[j]));
-      if (L1) s += (double)a + (double)b;
+      if (L1) s4[j] += (double)a + (double)b;
       else m = fmaxf(m, fmaxf(a, b));
     }
   }
+  double s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
   const float red = L1 ? (float)warp_sum(s) : warp_max(m);
   const int se = FUSED_RULE ? scale_biased_exp_fused(red, t) : scale_biased_exp_small(red, t);
   if (WRITE_Y) {
@@ -168,17 +172,18 @@ __global__ void __launch_bounds__(256) row_pass_block_kernel(const uint4* __rest
     v[u] = i < K8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
   }
   float m = 0.f;
-  double s = 0.0;
+  double s4[4] = {0.0, 0.0, 0.0, 0.0};  // four independent fp64 chains (a single one is latency-bound)
 #pragma unroll
   for (int u = 0; u < NCH; ++u) {
     const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float a = fabsf(bf16lo(w[j])), b = fabsf(bf16hi(w[j]));
-      if (L1) s += (double)a + (double)b;
+      if (L1) s4[j] += (double)a + (double)b;
       else m = fmaxf(m, fmaxf(a, b));
     }
   }
+  double s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
   if (L1) s = warp_sum(s);
   else m = warp_max(m);
   if (lane == 0) {
@@ -286,58 +291,99 @@ int row_pass(const void* x, int64_t rows, int64_t K, int64_t ldx, int t, int l1,
 
 namespace {
 
-// Column amax (small_kernels.cu:136-155): 8 adjacent columns per thread over a chunk of rows,
-// merged with atomicMax on the bits of the non-negative maxima.
-__global__ void __launch_bounds__(128) col_amax_kernel(const uint4* __restrict__ x, const float* __restrict__ row_mul,
+constexpr int kColUnroll = 8;  // rows in flight per thread in the column kernels
+
+// Column amax (small_kernels.cu:136-155): a block owns 32 column vectors (256 columns, 512 contiguous
+// bytes of each row per warp) over a chunk of rows; its 8 warps take every 8th row of the chunk with
+// kColUnroll rows in flight per thread, reduce their maxima through shared memory, and one atomicMax
+// per column and block (on the bits of the non-negative maxima) merges the chunks. Same-address
+// atomics are what limits a column reduction, so there are few of them.
+__global__ void __launch_bounds__(256) col_amax_kernel(const uint4* __restrict__ x, const float* __restrict__ row_mul,
                                                        float* __restrict__ amax, int64_t R, int K8, int64_t ldx8,
                                                        int64_t rows_per_chunk) {
-  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c8 >= K8) return;
+  __shared__ float red[8][32][9];  // [warp][lane][column of the vector], padded against bank conflicts
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c8 = blockIdx.x * 32 + lane;
+  const bool cok = c8 < K8;
   const int64_t r0 = (int64_t)blockIdx.y * rows_per_chunk;
   const int64_t r1 = min(R, r0 + rows_per_chunk);
   float m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int64_t r = r0; r < r1; ++r) {
-    const uint4 v = __ldg(x + r * ldx8 + c8);
-    const float rm = row_mul ? fabsf(__ldg(row_mul + r)) : 1.f;
+  auto fold = [&](const uint4& v, float rm) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       m[2 * j] = fmaxf(m[2 * j], fabsf(bf16lo(w[j])) * rm);
       m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(bf16hi(w[j])) * rm);
     }
+  };
+  if (cok) {
+    int64_t r = r0 + warp;
+    for (; r + 8 * (kColUnroll - 1) < r1; r += 8 * kColUnroll) {
+      uint4 v[kColUnroll];
+      float rm[kColUnroll];
+#pragma unroll
+      for (int u = 0; u < kColUnroll; ++u) {
+        v[u] = __ldg(x + (r + 8 * u) * ldx8 + c8);
+        rm[u] = row_mul ? fabsf(__ldg(row_mul + r + 8 * u)) : 1.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kColUnroll; ++u) fold(v[u], rm[u]);
+    }
+    for (; r < r1; r += 8) fold(__ldg(x + r * ldx8 + c8), row_mul ? fabsf(__ldg(row_mul + r)) : 1.f);
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) atomicMax(reinterpret_cast<int*>(amax) + c8 * 8 + j, __float_as_int(m[j]));
+  for (int j = 0; j < 8; ++j) red[warp][lane][j] = m[j];
+  __syncthreads();
+  // thread (w, l) reduces column j = w of vector l over the 8 warps
+  const int j = warp;
+  float v = red[0][lane][j];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) v = fmaxf(v, red[k][lane][j]);
+  if (cok) atomicMax(reinterpret_cast<int*>(amax) + c8 * 8 + j, __float_as_int(v));
 }
 
-// Column convert (small_kernels.cu:158-184): y = fp16_rn((x * row_mul[r]) * s[c]); row 0 writes s_inv.
+// Column convert (small_kernels.cu:158-184): y = fp16_rn((x * row_mul[r]) * s[c]). Same layout as
+// col_amax_kernel: a thread's 8 column scales are built once, then kColUnroll rows are converted per
+// step; the first chunk's threads write s_inv.
 __global__ void __launch_bounds__(256) col_convert_kernel(const uint4* __restrict__ x, const float* __restrict__ row_mul,
                                                           const float* __restrict__ amax, uint4* __restrict__ y,
                                                           float* __restrict__ s_inv, int64_t R, int K8, int64_t ldx8,
-                                                          int64_t ldy8, int t) {
-  const int64_t total = R * K8;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / K8;
-    const int c8 = (int)(i - r * K8);
-    const uint4 v = __ldg(x + r * ldx8 + c8);
-    const float rm = row_mul ? __ldg(row_mul + r) : 1.f;
-    float s[8];
-    int se[8];
+                                                          int64_t ldy8, int t, int64_t rows_per_chunk) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 >= K8) return;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_chunk;
+  const int64_t r1 = min(R, r0 + rows_per_chunk);
+  float s[8];
+  int se[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      se[j] = scale_biased_exp_small(__ldg(amax + c8 * 8 + j), t);
-      s[j] = pow2_from_biased(se[j]);
-    }
+  for (int j = 0; j < 8; ++j) {
+    se[j] = scale_biased_exp_small(__ldg(amax + c8 * 8 + j), t);
+    s[j] = pow2_from_biased(se[j]);
+  }
+  if (blockIdx.y == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s_inv[c8 * 8 + j] = inv_pow2_from_biased(se[j]);
+  }
+  auto conv = [&](const uint4& v, float rm) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = pack_f16(bf16lo(w[j]) * rm * s[2 * j], bf16hi(w[j]) * rm * s[2 * j + 1]);
-    y[r * ldy8 + c8] = make_uint4(o[0], o[1], o[2], o[3]);
-    if (r == 0) {
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  int64_t r = r0;
+  for (; r + kColUnroll <= r1; r += kColUnroll) {
+    uint4 v[kColUnroll];
+    float rm[kColUnroll];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s_inv[c8 * 8 + j] = inv_pow2_from_biased(se[j]);
+    for (int u = 0; u < kColUnroll; ++u) {
+      v[u] = __ldg(x + (r + u) * ldx8 + c8);
+      rm[u] = row_mul ? __ldg(row_mul + r + u) : 1.f;
     }
+#pragma unroll
+    for (int u = 0; u < kColUnroll; ++u) y[(r + u) * ldy8 + c8] = conv(v[u], rm[u]);
   }
+  for (; r < r1; ++r) y[r * ldy8 + c8] = conv(__ldg(x + r * ldx8 + c8), row_mul ? __ldg(row_mul + r) : 1.f);
 }
 
 __global__ void fill_kernel(float* p, int64_t n, float v) {
@@ -552,15 +598,21 @@ int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   const int sms = d ? d->sms : 148;
   const int K8 = (int)(K / 8);
-  const int col_blocks = (K8 + 127) / 128;
-  const int64_t chunks =
-      std::max<int64_t>(1, std::min<int64_t>((rows + 63) / 64, ((int64_t)sms * 16 + col_blocks - 1) / col_blocks));
-  const int64_t rows_per_chunk = (rows + chunks - 1) / chunks;
-  col_amax_kernel<<<dim3(col_blocks, (unsigned)chunks), 128, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws,
-                                                                      rows, K8, ldx / 8, rows_per_chunk);
-  col_convert_kernel<<<grid_for(rows * K8, 256), 256, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws,
-                                                              static_cast<uint4*>(y16), s_inv, rows, K8, ldx / 8,
-                                                              ldy / 8, target_exp);
+  // amax: 32 column vectors per block and chunks of at least 256 rows (few same-address atomics);
+  // convert: 256 column vectors per block and chunks of at least 32 rows; both about four blocks per SM.
+  auto chunking = [&](int col_blocks, int64_t min_rows, int64_t mult) {
+    const int64_t chunks = std::max<int64_t>(
+        1, std::min<int64_t>((rows + min_rows - 1) / min_rows, ((int64_t)sms * 4 + col_blocks - 1) / col_blocks));
+    const int64_t per = ((rows + chunks - 1) / chunks + mult - 1) / mult * mult;
+    return std::make_pair(dim3(col_blocks, (unsigned)((rows + per - 1) / per)), per);
+  };
+  const auto ga = chunking((K8 + 31) / 32, 256, 8 * kColUnroll);
+  const auto gc = chunking((K8 + 255) / 256, 32, kColUnroll);
+  col_amax_kernel<<<ga.first, 256, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws, rows, K8, ldx / 8,
+                                            ga.second);
+  col_convert_kernel<<<gc.first, 256, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws,
+                                               static_cast<uint4*>(y16), s_inv, rows, K8, ldx / 8, ldy / 8, target_exp,
+                                               gc.second);
   return tbf16_host::check_launch();
 }
 
