@@ -79,9 +79,9 @@ def test_gemv_rejects_too_many_rows():
 
 
 def test_linear_host_matches_device_path():
-    """linear_host (pinned host x and y, chunked over three streams) gives the device path's rows:
-    bit-equal where a chunk goes through the same GEMM, within the oracle bounds for a short final chunk
-    (skinny GEMM for 5 rows, GEMV for 3)."""
+    """linear_host (pinned host x and y, chunked over three streams) gives the device path's rows: each
+    chunk bit-equal to scaled_linear on the same rows, and within the oracle bounds for a short final
+    chunk (GEMV for 3 rows)."""
     from helpers import assert_close_ulp, gemm_tolerance
     from tbf16 import ops
     M, K, N = 2 * 1024 + 5, 512, 768
@@ -93,12 +93,16 @@ def test_linear_host_matches_device_path():
     y = ops.linear_host(hx, w16, ws, b.cuda())
     torch.cuda.synchronize()
     assert y.shape == (M, N) and not y.is_cuda
-    ref = ops.scaled_linear(x.cuda(), w16, ws, b.cuda()).cpu()
-    assert torch.equal(y[:2048].view(torch.int16), ref[:2048].view(torch.int16))
-    xs, w16c, wsc = x[2048:].contiguous(), w16.cpu(), ws.cpu()
-    y_ref, _ = orc.linear_fused(xs, w16c, wsc, b)
-    absprod = (xs.double().abs() @ w16c.double().abs().t()) * wsc.double()[None, :]
-    assert_close_ulp(y[2048:], y_ref, gemm_tolerance(y_ref, absprod, K), what="linear_host final chunk")
+    chunks = ops._host_chunks(M, 1024)
+    assert len(chunks) > 2 and max(n for _, n in chunks) <= 1024
+    xc = x.cuda()
+    for r0, n in chunks:
+        ref = ops.scaled_linear(xc[r0:r0 + n], w16, ws, b.cuda()).cpu()
+        assert torch.equal(y[r0:r0 + n].view(torch.int16), ref.view(torch.int16)), (r0, n)
+    w16c, wsc = w16.cpu(), ws.cpu()
+    y_ref, _ = orc.linear_fused(x, w16c, wsc, b)
+    absprod = (x.double().abs() @ w16c.double().abs().t()) * wsc.double()[None, :]
+    assert_close_ulp(y, y_ref, gemm_tolerance(y_ref, absprod, K), what="linear_host")
     y3 = ops.linear_host(hx[:2048 + 3].contiguous(), w16, ws, b.cuda(), chunk_rows=2048)
     torch.cuda.synchronize()
     _check(y3[2048:], x[2048:2051], w16c, wsc, b)

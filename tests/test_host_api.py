@@ -103,3 +103,16 @@ def test_no_cpu_compute_path():
                lambda: attention.head_exp(x.view(1, 1, 8, 16))):
         with pytest.raises(RuntimeError):
             fn()
+
+
+def test_linear_host_chunks_cover_rows_once():
+    """linear_host's chunking: contiguous, covering every row once, no chunk above chunk_rows, short first
+    and last chunks when there are several."""
+    from tbf16 import ops
+    for M, rows in [(8192, 1024), (2053, 1024), (1024, 1024), (1300, 1024), (5, 1024), (1030, 1024), (9000, 512)]:
+        ch = ops._host_chunks(M, rows)
+        assert ch[0][0] == 0 and sum(n for _, n in ch) == M
+        assert all(ch[i][0] + ch[i][1] == ch[i + 1][0] for i in range(len(ch) - 1))
+        assert all(0 < n <= rows for _, n in ch)
+        if M > rows:
+            assert ch[0][1] == rows // 4

@@ -495,7 +495,7 @@ int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, u
 // 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3) in shared memory).
 int make_tmap_2d_out(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
                      uint32_t box_rows);
-// The same for fp32 elements (box0 * 4 <= 128 bytes, the swizzle span).
+// The same for fp32 elements with a 64- or 128-byte swizzle (box0 * 4 <= the swizzle span).
 int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
-                     uint64_t stride2, uint32_t box0, uint32_t box1);
+                     uint64_t stride2, uint32_t box0, uint32_t box1, int swizzle_bytes = 128);
 }  // namespace tbf16_host

@@ -115,15 +115,17 @@ int make_tmap_2d_out(CUtensorMap* map, const void* base, uint64_t cols, uint64_t
 }
 
 int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
-                     uint64_t stride2, uint32_t box0, uint32_t box1) {
+                     uint64_t stride2, uint32_t box0, uint32_t box1, int swizzle_bytes) {
   if (!encode_fn()) return TBF16_ERR_LAUNCH;
-  if (!aligned16(base) || (stride1 * 4) % 16 != 0 || (stride2 * 4) % 16 != 0 || box0 * 4 > 128) return TBF16_ERR_ALIGN;
+  if (swizzle_bytes != 64 && swizzle_bytes != 128) return TBF16_ERR_INVALID;
+  if (!aligned16(base) || (stride1 * 4) % 16 != 0 || (stride2 * 4) % 16 != 0 || box0 * 4 > (uint32_t)swizzle_bytes)
+    return TBF16_ERR_ALIGN;
   cuuint64_t gdim[3] = {d0, d1, d2};
   cuuint64_t gstride[2] = {stride1 * 4, stride2 * 4};
   cuuint32_t box[3] = {box0, box1, 1};
   cuuint32_t estride[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), gdim, gstride, box, estride,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? TBF16_OK : TBF16_ERR_INVALID;
 }

@@ -208,8 +208,8 @@ def linear_host(x_host: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, b
     start.record(cur)
     up.wait_event(start)
     down.wait_event(start)
-    for c, r0 in enumerate(range(0, M, rows)):
-        b, n = c & 1, min(rows, M - r0)
+    for c, (r0, n) in enumerate(_host_chunks(M, rows)):
+        b = c & 1
         with torch.cuda.stream(up):
             if c >= 2:
                 up.wait_event(computed[b])  # the linear of chunk c-2 has read this x buffer
@@ -229,6 +229,26 @@ def linear_host(x_host: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, b
             out[r0:r0 + n].copy_(yb[b][:n], non_blocking=True)
             downloaded[b].record(down)
     cur.wait_stream(down)
+    return out
+
+
+def _host_chunks(M, rows):
+    """(first row, rows) of linear_host's chunks: full `rows` chunks, except that the first and the last
+    are split into a quarter and three quarters, so that the first upload and the last download, which
+    nothing overlaps, are short."""
+    if M <= rows:
+        return [(0, M)]
+    q = max(8, rows // 4)
+    sizes = [q, rows - q]
+    left = M - rows
+    while left > rows + q:
+        sizes.append(rows)
+        left -= rows
+    sizes += [left - q, q] if left > q else [left]
+    out, r0 = [], 0
+    for n in sizes:
+        out.append((r0, n))
+        r0 += n
     return out
 
 
