@@ -10,14 +10,19 @@
 //
 // Main kernel: one CTA per 128-key tile of one (batch, kv head), looping over the GQA group's query
 // heads and 128-row query tiles. Everything is computed with keys as TMEM lanes, so no operand needs a
-// transpose: the same shared tiles serve as K-major or MN-major UMMA operands.
-//   warp 0     TMA: K, V once; Q_i (+ lse, delta) per query tile, 2 stages
-//   warp 10    TMA: dO_i, 1 stage
-//   warp 1     MMA: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q, dQ = dS K
-//   warps 2-9  two warps per TMEM lane quadrant, each half of the query columns: P^T (packed fp16
-//              back into TMEM), dS^T (fp16, 128B-swizzled K-major tile in shared memory), half the D
-//              columns of dQ (TMEM -> shared -> TMA reduce-add into an fp32 accumulator), and at the
-//              end half the columns of dK, dV from TMEM -> bf16
+// transpose: the same shared tiles serve as K-major or MN-major UMMA operands. Four warpgroups, their
+// registers re-split with setmaxnreg (96 for the control group, 128 for the key warps, 160 for dQ):
+//   warp 0      TMA: K, V once; Q_i (+ lse, delta) per query tile, 2 stages
+//   warp 1      MMA: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q, dQ = dS K
+//   warp 2      TMA: dO_i, 1 stage
+//   warps 4-11  key warps, two per TMEM lane quadrant, each half of the query columns: P^T (packed
+//               fp16 back into TMEM), dS^T (fp16, 128B-swizzled K-major tile in shared memory), and at
+//               the end half the columns of dK, dV from TMEM -> bf16
+//   warps 12-15 dQ warps, one per TMEM lane quadrant (queries): all D columns of dQ out of TMEM at once
+//               (which frees the columns for the next dP), then TMA reduce-adds of 32-column boxes into
+//               the fp32 accumulator from two alternating staging buffers
+// The key warps only compute P and dS, so the tile loop is dS(t) -> P(t+1) -> dS(t+1) while the tensor
+// core runs dQ(t), dK(t), dP(t+1), dV(t+1), S(t+2) and the dQ warps drain dQ(t) alongside.
 // TMEM: S^T [0,128), dP^T / dQ [128,256), dV [256,256+D), dK [256+D,256+2D). Bounded waits throughout.
 #include <algorithm>
 
@@ -29,7 +34,14 @@ namespace {
 
 constexpr int BQ = 128;   // queries per tile
 constexpr int BKV = 128;  // keys per CTA
-constexpr int kThreads = 32 * 11;
+constexpr int kThreads = 32 * 16;
+// setmaxnreg shares per warpgroup (128 threads): control 96 (the MMA issuer keeps its operand
+// descriptors in registers), key warps 128 (the launch value: no re-split), dQ warps 160 (all D = 128
+// columns of a query row at once). Their sum must not exceed the 512-thread launch's 65536 registers.
+constexpr uint32_t kRegsCtl = 96;
+constexpr uint32_t kRegsKey = 128;
+constexpr uint32_t kRegsDq = 160;
+static_assert(128 * (kRegsCtl + 2 * kRegsKey + kRegsDq) <= 65536, "register split");
 
 struct AttnBwdParams {
   int B, Hq, Hkv, Sq, Sk, group;
@@ -60,7 +72,7 @@ struct BwdCfg {
   static constexpr int Q_OFF = V_OFF + TILE;      // [2 stages]
   static constexpr int DO_OFF = Q_OFF + 2 * TILE; // one stage: its readers dP(t), dV(t) finish early
   static constexpr int DS_OFF = DO_OFF + TILE;
-  static constexpr int DQS_OFF = DS_OFF + 32768;  // dQ staging: 4 warps x (32 rows x 64 fp32)
+  static constexpr int DQS_OFF = DS_OFF + 32768;  // dQ staging: 4 warps x 2 boxes of 32 rows x 32 fp32
   static constexpr int VEC_OFF = DQS_OFF + 32768; // [2 stages] lse (natural log) and delta of the query tile
   static constexpr int BAR_OFF = VEC_OFF + 2048;
   // the dynamic shared window starts 1024-byte aligned (checked on entry), so no alignment slack
@@ -119,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_ready, 8);
     mbar_init(ds_ready, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 8);
+    mbar_init(dq_empty, 4);
     mbar_init(kv_done, 1);
     mbar_init(do_full, 1);
     mbar_init(do_empty, 1);
@@ -136,7 +148,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  // each role's code sits under its warpgroup's register re-split
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsCtl>();
+    if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer: K, V, then Q (2 stages)
     if (lane == 0 && n_t > 0) {  // no copies in flight when the CTA has no query tile
       mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
@@ -162,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_load(vec + 128, p.delta + (int64_t)bh * p.lse_ld + q0, 512, &q_full[st]);
       }
     }
-  } else if (warp == 10) {
+  } else if (warp == 2) {
     // ---------------------------------------------------------------- TMA producer: dO (one stage)
     if (lane == 0 && n_t > 0) {
       for (int t = 0; t < n_t; ++t) {
@@ -259,20 +274,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok) umma_commit(kv_done);
     }
-  } else if (warp >= 2 && warp < 10) {
-    // ---------------------------------------------------------------- compute warps
+    }
+  } else if (warp < 12) {  // key warps keep the launch's kRegsKey registers
+    // ---------------------------------------------------------------- key warps
     // Two warps per TMEM lane quadrant: warp w handles keys 32 (w % 4) .. (one key per thread, as TMEM
-    // lanes) and half h = (w - 2) / 4 of every query tile's 128 columns, i.e. queries [64 h, 64 h + 64)
-    // of P^T and dS^T, and half the D columns of dQ (there TMEM lanes are queries) and of dK, dV.
-    // Per query tile: dS(t), then dQ(t) out of TMEM (this frees the columns for dP(t+1)), then P(t+1)
-    // while dP(t+1) runs.
+    // lanes) and half h = (w - 4) / 4 of every query tile's 128 columns, i.e. queries [64 h, 64 h + 64)
+    // of P^T and dS^T, and half the D columns of dK, dV. Per query tile: dS(t), then P(t+1) (S(t+1) was
+    // issued right after dV(t)) while the tensor core runs dQ(t), dK(t) and dP(t+1).
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int r = quad * 32 + lane;  // key within the tile (P, dS, dK, dV); query within the tile (dQ)
+    const int half = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;  // key within the tile
     const int kj = k0 + r;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const int cq = half * 64;        // this warp's query columns
-    uint8_t* stage = smem + C::DQS_OFF + (warp - 2) * 4096;
     bool ok = true;
     bool bad = false;
     uint32_t pp[32];  // P of this thread's key against the warp's 64 queries, packed fp16 pairs
@@ -286,47 +300,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&q_full[t & 1], (t >> 1) & 1, abort, p.err) || !mbar_wait_warp(s_full, t & 1, abort, p.err))
         return false;
       tc_fence_after();
-      uint32_t rr[64];
-      tmem_ld32(tmem + lane_base + C::T_S + cq, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
-      tmem_ld32(tmem + lane_base + C::T_S + cq + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
-      tmem_ld_wait();
       // fully valid tiles (no user mask, keys and queries in range, whole tile below the causal
-      // diagonal) skip the per-element checks; 3 of every 8 exp2 pairs run on the FMA pipe
+      // diagonal) skip the per-element checks; 3 of every 8 exp2 pairs run on the FMA pipe. The 64
+      // columns go in two halves of 32, so only 32 logits are live at a time.
       const bool full_tile = p.mask == nullptr && k0 + BKV <= p.Sk && q0 + BQ <= p.Sq && (!p.causal || k0 + BKV - 1 <= q0);
-      if (full_tile) {
-        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2e = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
+      const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
 #pragma unroll
-        for (int e = 0; e < 64; e += 4) {
-          const float4 ls = reinterpret_cast<const float4*>(lse_s)[(cq + e) >> 2];
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t rr[32];
+        tmem_ld32(tmem + lane_base + C::T_S + cq + 32 * hh, rr);
+        tmem_ld_wait();
+        if (full_tile) {
+          const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2e = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
 #pragma unroll
-          for (int u = 0; u < 4; u += 2) {
-            float x0, x1, p0, p1;
-            const uint64_t nl = f2_mul(u == 0 ? f2_pack(ls.x, ls.y) : f2_pack(ls.z, ls.w), nl2e);
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])), c2, nl), x0, x1);
-            if ((((e + u) >> 1) & 7) >= 5) {
-              ex2_poly2(x0, x1, p0, p1);
-            } else {
-              p0 = ex2(x0);
-              p1 = ex2(x1);
+          for (int e = 0; e < 32; e += 4) {
+            const int E = 32 * hh + e;
+            const float4 ls = reinterpret_cast<const float4*>(lse_s)[(cq + E) >> 2];
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+              float x0, x1, p0, p1;
+              const uint64_t nl = f2_mul(u == 0 ? f2_pack(ls.x, ls.y) : f2_pack(ls.z, ls.w), nl2e);
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])), c2, nl), x0, x1);
+              if ((((E + u) >> 1) & 7) >= 5) {
+                ex2_poly2(x0, x1, p0, p1);
+              } else {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              }
+              pp[(E + u) >> 1] = pack_f16(p0, p1);
             }
-            pp[(e + u) >> 1] = pack_f16(p0, p1);
           }
-        }
-      } else {
-        const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
+        } else {
 #pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          float pc[2];
+          for (int e = 0; e < 32; e += 2) {
+            const int E = 32 * hh + e;
+            float pc[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = cq + e + u;
-            const int qi = q0 + col;
-            const bool valid = kj < p.Sk && qi < p.Sq && (!p.causal || kj <= qi);
-            float s = __uint_as_float(rr[e + u]) * p.scale_log2;
-            if (mrow && valid) s += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
-            pc[u] = valid ? ex2(s - lse_s[col] * 1.4426950408889634f) : 0.f;
+            for (int u = 0; u < 2; ++u) {
+              const int col = cq + E + u;
+              const int qi = q0 + col;
+              const bool valid = kj < p.Sk && qi < p.Sq && (!p.causal || kj <= qi);
+              float sv = __uint_as_float(rr[e + u]) * p.scale_log2;
+              if (mrow && valid) sv += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
+              pc[u] = valid ? ex2(sv - lse_s[col] * 1.4426950408889634f) : 0.f;
+            }
+            pp[E >> 1] = pack_f16(pc[0], pc[1]);
           }
-          pp[e >> 1] = pack_f16(pc[0], pc[1]);
         }
       }
       // dV(t-1) has read the previous P^T: it precedes S(t) in the MMA pipe
@@ -340,8 +359,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     ok = n_t > 0 && compute_p(0);
     for (int t = 0; ok && t < n_t; ++t) {
-      const int h = hk * p.group + t / n_i;
-      const int q0 = (i_first + t % n_i) * BQ;
       const float* delta_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * 1024) + 128;
       // ---- dS(t) = P (dP - delta) for this warp's 64 queries (when dP(t) completes, dK(t-1) and
       // dQ(t-1) have read dS(t-1)); masked / padded queries have P = 0 and a finite dP and delta
@@ -349,73 +366,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(dp_full, t & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
       {
-        uint32_t rr[64];
-        tmem_ld32(tmem + lane_base + C::T_DP + cq, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
-        tmem_ld32(tmem + lane_base + C::T_DP + cq + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
-        tmem_ld_wait();
-        uint32_t pk[32];
         uint32_t ovf = 0;
         const uint64_t m1 = f2_pack(-1.f, -1.f);
-#pragma unroll
-        for (int e = 0; e < 64; e += 4) {
-          const float4 dl = reinterpret_cast<const float4*>(delta_s)[(cq + e) >> 2];
-#pragma unroll
-          for (int u = 0; u < 4; u += 2) {
-            const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pp[(e + u) >> 1]));
-            const uint64_t dd = f2_fma(u == 0 ? f2_pack(dl.x, dl.y) : f2_pack(dl.z, dl.w), m1,
-                                       f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])));
-            float d0, d1;
-            f2_unpack(f2_mul(f2_pack(pf.x, pf.y), dd), d0, d1);
-            pk[(e + u) >> 1] = pack_f16(d0, d1);
-            ovf |= __vcmpeq2(pk[(e + u) >> 1] & 0x7c007c00u, 0x7c007c00u);
-          }
-        }
-        bad |= ovf != 0;
         uint8_t* dst = smem + C::DS_OFF;
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          *reinterpret_cast<uint4*>(dst + swz_off(r, half * 8 + g)) = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+        for (int hh = 0; hh < 2; ++hh) {  // two halves of 32 columns: 32 dP values live at a time
+          uint32_t rr[32];
+          tmem_ld32(tmem + lane_base + C::T_DP + cq + 32 * hh, rr);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const int E = 32 * hh + e;
+            const float4 dl = reinterpret_cast<const float4*>(delta_s)[(cq + E) >> 2];
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+              const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pp[(E + u) >> 1]));
+              const uint64_t dd = f2_fma(u == 0 ? f2_pack(dl.x, dl.y) : f2_pack(dl.z, dl.w), m1,
+                                         f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])));
+              float d0, d1;
+              f2_unpack(f2_mul(f2_pack(pf.x, pf.y), dd), d0, d1);
+              pk[(e + u) >> 1] = pack_f16(d0, d1);
+              ovf |= __vcmpeq2(pk[(e + u) >> 1] & 0x7c007c00u, 0x7c007c00u);
+            }
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+            *reinterpret_cast<uint4*>(dst + swz_off(r, half * 8 + 4 * hh + g)) =
+                make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+        }
+        bad |= ovf != 0;
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
-      // ---- dQ(t): D/2 columns of 32 queries out of TMEM at once (frees the columns for dP(t+1)), then
-      // staged in this warp's 4 KB 128B-swizzled box, 32 columns at a time, and added into the fp32
-      // accumulator with TMA reductions (rows past the sequence end are clipped). The first box goes
-      // out before P(t+1), the rest after it, so the wait for the box to be read is hidden.
-      if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) { ok = false; break; }
-      tc_fence_after();
-      constexpr int DH = D / 2;
-      uint32_t o[DH];
-#pragma unroll
-      for (int c = 0; c < DH / 32; ++c)
-        tmem_ld32(tmem + lane_base + C::T_DP + half * DH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      auto stage_box = [&](int c) {
-        if (lane == 0) bulk_wait_group_read<0>();  // the previous reduction has read the box
-        __syncwarp();
-#pragma unroll
-        for (int g = 0; g < 8; ++g)
-          *reinterpret_cast<uint4*>(stage + lane * 128 + ((g ^ (lane & 7)) << 4)) =
-              make_uint4(o[c * 32 + 4 * g], o[c * 32 + 4 * g + 1], o[c * 32 + 4 * g + 2], o[c * 32 + 4 * g + 3]);
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_reduce_add_3d(&tmDQ, stage, half * DH + c * 32, q0 + quad * 32, b * p.Hq + h);
-          bulk_commit_group();
-        }
-      };
-      stage_box(0);
-      // ---- P(t+1) while dP(t+1) runs
+      // ---- P(t+1) while the tensor core runs dQ(t), dK(t) and dP(t+1)
       if (t + 1 < n_t && !compute_p(t + 1)) { ok = false; break; }
-#pragma unroll
-      for (int c = 1; c < DH / 32; ++c) stage_box(c);
     }
-    if (lane == 0) bulk_wait_group<0>();
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.flag, kErrOverflow);
     // dK, dV epilogue: this warp's D/2 columns of its 32 keys
     if (ok && n_t > 0 && mbar_wait_warp(kv_done, 0, abort, p.err)) {
@@ -457,6 +445,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(p.dv + orow + c) = make_uint4(0, 0, 0, 0);
       }
     }
+  } else {
+    setmaxnreg_inc<kRegsDq>();
+    // ---------------------------------------------------------------- dQ warps
+    // dQ(t) = dS K lands in TMEM with queries as lanes: warp w reads all D columns of its 32 queries at
+    // once (then the columns are free for dP(t+1)) and adds them into the fp32 accumulator with TMA
+    // reductions of 32 x 32 boxes (rows past the sequence end are clipped), staged in two alternating
+    // 4 KB 128B-swizzled buffers so a box waits only for the reduction issued two boxes earlier.
+    const int quad = warp & 3;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    uint8_t* stage = smem + C::DQS_OFF + (warp - 12) * 8192;
+    int sb = 0;
+    for (int t = 0; t < n_t; ++t) {
+      const int h = hk * p.group + t / n_i;
+      const int q0 = (i_first + t % n_i) * BQ;
+      if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) break;
+      tc_fence_after();
+      uint32_t o[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c)
+        tmem_ld32(tmem + lane_base + C::T_DP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* buf = stage + sb * 4096;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          *reinterpret_cast<uint4*>(buf + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+              make_uint4(o[c * 32 + 4 * g], o[c * 32 + 4 * g + 1], o[c * 32 + 4 * g + 2], o[c * 32 + 4 * g + 3]);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tmDQ, buf, c * 32, q0 + quad * 32, b * p.Hq + h);
+          bulk_commit_group();
+        }
+        sb ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
