@@ -371,20 +371,41 @@ class _GemmaLayer(torch.nn.Module):
         self.pre_ff_norm, self.post_ff_norm = _RMSNorm(hidden), _RMSNorm(hidden)
         self.q_norm, self.k_norm = _RMSNorm(head_dim), _RMSNorm(head_dim)
 
+    fused = False  # producer fusion: norms and the GeGLU write the next linears' fp16 rows and scales
+
+    def _proj(self, x, lin):
+        from tbf16 import ops
+        if isinstance(x, tuple):  # (fp16 rows, inverse scales) from a fused producer
+            r16, s_inv = x
+            y = ops.linear_q(r16.reshape(-1, r16.shape[-1]), s_inv.reshape(-1), lin.weight16, lin.weight_scale, lin.bias)
+            return y.reshape(*r16.shape[:-1], y.shape[-1])
+        return lin(x)
+
+    def _norm_rows(self, x, norm):
+        if not self.fused:
+            return norm(x)
+        from tbf16 import ops
+        return ops.rmsnorm_rows(x, norm.weight, 1e-6, 1.0, "gemma")
+
     def forward(self, x, cos, sin):
         import torch.nn.functional as F
         B, S, _ = x.shape
-        h = self.in_norm(x)
-        q = self.q_norm(self.q_proj(h).view(B, S, self.h, self.d)).transpose(1, 2)
-        k = self.k_norm(self.k_proj(h).view(B, S, self.kv, self.d)).transpose(1, 2)
-        v = self.v_proj(h).view(B, S, self.kv, self.d).transpose(1, 2)
+        h = self._norm_rows(x, self.in_norm)
+        q = self.q_norm(self._proj(h, self.q_proj).view(B, S, self.h, self.d)).transpose(1, 2)
+        k = self.k_norm(self._proj(h, self.k_proj).view(B, S, self.kv, self.d)).transpose(1, 2)
+        v = self._proj(h, self.v_proj).view(B, S, self.kv, self.d).transpose(1, 2)
         rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
         q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         x = x + self.post_attn_norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)))
-        h = self.pre_ff_norm(x)
-        g = F.gelu(self.gate_proj(h), approximate="tanh") * self.up_proj(h)
-        return x + self.post_ff_norm(self.down_proj(g))
+        h = self._norm_rows(x, self.pre_ff_norm)
+        gate, up = self._proj(h, self.gate_proj), self._proj(h, self.up_proj)
+        if self.fused:
+            from tbf16 import ops
+            y = ops.glu_linear(gate, up, self.down_proj.weight16, self.down_proj.weight_scale, act="gelu_tanh")
+        else:
+            y = self.down_proj(F.gelu(gate, approximate="tanh") * up)
+        return x + self.post_ff_norm(y)
 
 
 def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
@@ -434,12 +455,33 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
     e.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / iters, world)
+    # the same model with producer fusion: the norms in front of linears and the GeGLU write the next
+    # linears' fp16 rows and row scales (tbf16.ops.rmsnorm_rows / glu_linear) instead of bf16 tensors
+    # that the linears read again for their row pass
+    for layer in model:
+        layer.fused = True
+    for _ in range(2):
+        logits_f = step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s.record()
+    for _ in range(iters):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms_f = max_over_ranks(s.elapsed_time(e) / iters, world)
+    for layer in model:
+        layer.fused = False
     tbf16.uninstall_sdpa()
     lin_params = layers * (hidden * (2048 + 1024 + 1024) + 2048 * hidden + 3 * hidden * 10240)
     flop = 2.0 * seq * lin_params + layers * 4.0 * 8 * seq * seq * 256 * 0.5 + 2.0 * hidden * vocab
+    drift = float((logits_f.float() - logits.float()).norm() / logits.float().norm())
     return {"config": f"Gemma-3-4B-shaped, {layers} layers, {seq} tokens per GPU, {world} GPU(s) (replicas)",
             "ms_per_prefill": round(ms, 2), "tokens_per_s_all_gpus": round(world * seq / (ms / 1e3), 1),
-            "tflops_per_gpu": round(flop / (ms / 1e3) / 1e12, 1), "finite_logits": finite}
+            "tflops_per_gpu": round(flop / (ms / 1e3) / 1e12, 1), "finite_logits": finite,
+            "fused": {"ms_per_prefill": round(ms_f, 2), "tflops_per_gpu": round(flop / (ms_f / 1e3) / 1e12, 1),
+                      "logits_rel_diff_vs_unfused": round(drift, 5),
+                      "what": "RMSNorm before q/k/v and gate/up, and GeGLU before down, fused with the row scales"}}
 
 
 def dist_rank():

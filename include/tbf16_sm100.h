@@ -158,6 +158,36 @@ int tbf16_gemm_f16(const void* a16, int a_mn, int64_t lda, const void* b16, int 
 int tbf16_gemv(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16, int64_t N, int64_t ldw,
                const float* ws, const void* bias, void* y, int64_t ldy, void* stream);
 
+/* ------------------------------------------------------------------ producer fusion */
+/* The kernels that produce a linear's input also give its row scales, so the linear needs no row pass:
+ * pass the y16 / s_inv they write to tbf16_gemm_f16 (A = y16, sa = s_inv) or tbf16_linear_scaled. The
+ * reference runs these as separate passes (torch's activation or norm, then its quantize / row_scale
+ * kernel: tbf16/ops.py:74-89, tbf16/csrc/gemm_sm75.cu:27-47); its own notes name them as the cost that
+ * dominates at small token counts. Rows up to 16384 elements (TBF16_ERR_UNSUPPORTED above). */
+#define TBF16_ACT_SILU 0
+#define TBF16_ACT_GELU_TANH 1
+#define TBF16_FUSED_MAX_ROW 16384
+
+/* Gated MLP activation: h[m, i] = bf16_rn(bf16_rn(act(g[m, i])) * u[m, i]) (act in fp32: silu
+ * x / (1 + exp(-x)), or GELU with the tanh approximation), as torch computes act(g) * u on bf16 tensors;
+ * then s_inv[m] = the fused rule's power-of-two row scale of h (row max, target target_exp, as
+ * tbf16_row_scale) and y16[m, i] = fp16_rn(h[m, i] / s_inv[m]). h is also written to h_out when non-null.
+ * g, u bf16 [M, I] (row strides ldg, ldu), y16 fp16 [M, I] (ldy), h_out bf16 (ldo). I and the strides
+ * multiples of 8, pointers 16-byte aligned. */
+int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64_t M, int64_t I, int act,
+                   int target_exp, void* y16, int64_t ldy, float* s_inv, void* h_out, int64_t ldo, void* stream);
+
+/* RMSNorm: ms[m] = mean_k x[m, k]^2 (fp32), rs = rsqrt(ms + eps) and
+ *   style TBF16_NORM_SCALE_FP32: r[m, k] = bf16_rn((x[m, k] * rs) * (w[k] + offset))   (Gemma: offset 1)
+ *   style TBF16_NORM_SCALE_BF16: r[m, k] = bf16_rn(w[k] * bf16_rn(x[m, k] * rs))        (Llama: offset unused)
+ * then s_inv and y16 of r as tbf16_glu_rows; r also written to r_out when non-null. x bf16 [M, K] (ldx),
+ * w bf16 [K]. */
+#define TBF16_NORM_SCALE_FP32 0
+#define TBF16_NORM_SCALE_BF16 1
+int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps, int style,
+                       float offset, int target_exp, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo,
+                       void* stream);
+
 /* ------------------------------------------------------------------ scaled attention (tcgen05) */
 
 /* Flash-attention forward on the fp16 copies from tbf16_prepare_qkv. Replaces the torch fp16 SDPA call of

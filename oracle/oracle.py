@@ -312,6 +312,37 @@ def linear_fused(x, w16, ws, bias=None, target_exp=15, l1=False):
     return y, s_inv
 
 
+# ----------------------------------------------------------------------------- producer fusion
+# No reference kernel exists for these (the reference runs the model's torch activation / norm and then
+# its row pass, tbf16/ops.py:74-89 and tbf16/csrc/gemm_sm75.cu:27-47); restated here as the bf16 model
+# arithmetic followed by the fused rule's row scale and fp16 rounding.
+
+def glu_rows(gate, up, act="silu", target_exp=15):
+    """h = bf16(bf16(act(g)) * u) in fp32 (act: silu g / (1 + exp(-g)), or the tanh-approximated GELU),
+    then row_scale_fused(h) and h16 = fp16(h / s_inv). Returns (h16, s_inv, h)."""
+    g, u = _cpu(gate).float(), _cpu(up).float()
+    if act == "silu":
+        a = g / (1.0 + torch.exp(-g))
+    else:
+        a = 0.5 * g * (1.0 + torch.tanh(math.sqrt(2.0 / math.pi) * (g + 0.044715 * g * g * g)))
+    h = bf16_rn(bf16_rn(a).float() * u)
+    s_inv = row_scale_fused(h, target_exp)
+    return f16_rn(h.float() / s_inv[:, None]), s_inv, h
+
+
+def rmsnorm_rows(x, weight, eps=1e-6, offset=1.0, style="gemma", target_exp=15):
+    """r = bf16((x * rsqrt(mean x^2 + eps)) * (w + offset)) ("gemma") or bf16(w * bf16(x * rsqrt(...)))
+    ("llama"), fp32 arithmetic, then row_scale_fused(r) and r16 = fp16(r / s_inv). Returns (r16, s_inv, r)."""
+    xf, w = _cpu(x).float(), _cpu(weight).float()
+    rs = torch.rsqrt((xf * xf).mean(-1, keepdim=True) + eps)
+    if style == "gemma":
+        r = bf16_rn((xf * rs) * (w + offset))
+    else:
+        r = bf16_rn(w * bf16_rn(xf * rs).float())
+    s_inv = row_scale_fused(r, target_exp)
+    return f16_rn(r.float() / s_inv[:, None]), s_inv, r
+
+
 def gemm_f16(a16, a_mn, b16, b_mn, M, N, K, sa, sb=None, bias=None):
     """y = bf16((sum_k A[m,k] B[n,k]) * sa[m] * sb[n] + bias[n]) with fp64 accumulation: the
     contraction of ops.py:167-178 (linear_q) and autograd.py:114-120 (_scaled_mm) without the fp16

@@ -1,0 +1,98 @@
+"""Producer fusion (glu_rows / rmsnorm_rows and the linears they feed): the kernel's bf16 rows within one
+bf16 ulp of the oracle's fp32 restatement (the activation / rsqrt functions of the GPU and of the host
+may differ in the last fp32 bit), its row scales and fp16 operands bit-exact for the rows it produced
+(the fused rule, as tbf16_row_scale), and glu_linear / rmsnorm_linear bit-equal to scaled_linear on
+those rows. Called through tbf16.ops (ctypes -> C ABI)."""
+import pytest
+import torch
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _within_ulp(a, b):
+    d = (a.double() - b.double()).abs()
+    return bool((d <= orc.bf16_ulp(b.double())).all())
+
+
+def _gate_up(M, I, seed):
+    g = torch.Generator().manual_seed(seed)
+    gate = (torch.randn(M, I, generator=g) * 3).bfloat16()
+    up = (torch.randn(M, I, generator=g) * torch.exp2(torch.randint(-8, 8, (M, 1), generator=g).float())).bfloat16()
+    return gate, up
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+@pytest.mark.parametrize("M,I", [(1, 8), (5, 2056), (64, 8192), (3, 10240), (17, 16384)])
+def test_glu_rows(act, M, I):
+    from tbf16 import ops
+    gate, up = _gate_up(M, I, M + I)
+    h16, s_inv, h = ops.glu_rows(gate.cuda(), up.cuda(), act, want_h=True)
+    h16, s_inv, h = h16.cpu(), s_inv.cpu(), h.cpu()
+    _, _, h_ref = orc.glu_rows(gate, up, act)
+    assert _within_ulp(h, h_ref)
+    assert (h.view(torch.int16) == h_ref.view(torch.int16)).float().mean() > 0.999
+    assert torch.equal(s_inv, orc.row_scale_fused(h, 15))  # the fused rule on the produced rows
+    assert torch.equal(h16.view(torch.int16), orc.f16_rn(h.float() / s_inv[:, None]).view(torch.int16))
+
+
+def test_glu_rows_match_torch_on_gpu():
+    """The fused rows against torch's own act(g) * u on the GPU (bf16 tensors)."""
+    import torch.nn.functional as F
+    from tbf16 import ops
+    gate, up = _gate_up(128, 4096, 7)
+    g, u = gate.cuda(), up.cuda()
+    for act, ref in (("silu", F.silu(g) * u), ("gelu_tanh", F.gelu(g, approximate="tanh") * u)):
+        _, _, h = ops.glu_rows(g, u, act, want_h=True)
+        assert _within_ulp(h.cpu(), ref.cpu())
+        assert (h.view(torch.int16) == ref.view(torch.int16)).float().mean().item() > 0.999
+
+
+@pytest.mark.parametrize("style,offset", [("gemma", 1.0), ("llama", 0.0)])
+@pytest.mark.parametrize("M,K", [(2, 64), (33, 2560), (256, 4096), (7, 16384)])
+def test_rmsnorm_rows(style, offset, M, K):
+    from tbf16 import ops
+    g = torch.Generator().manual_seed(M * 3 + K)
+    x = (torch.randn(M, K, generator=g) * torch.exp2(torch.randint(-10, 10, (M, 1), generator=g).float())).bfloat16()
+    w = (torch.randn(K, generator=g) * 0.1).bfloat16()
+    r16, s_inv, r = ops.rmsnorm_rows(x.cuda(), w.cuda(), 1e-6, offset, style, want_r=True)
+    r16, s_inv, r = r16.cpu(), s_inv.cpu(), r.cpu()
+    _, _, r_ref = orc.rmsnorm_rows(x, w, 1e-6, offset, style)
+    assert _within_ulp(r, r_ref)
+    assert torch.equal(s_inv, orc.row_scale_fused(r, 15))
+    assert torch.equal(r16.view(torch.int16), orc.f16_rn(r.float() / s_inv[:, None]).view(torch.int16))
+
+
+@pytest.mark.parametrize("M", [3, 40, 600])
+def test_fused_linears_equal_scaled_linear(M):
+    """glu_linear / rmsnorm_linear give scaled_linear's bits on the rows the producer wrote (GEMV up to 4
+    rows, the skinny GEMM up to 256, the pair GEMM above)."""
+    import inputs
+    from tbf16 import ops
+    I, H, N = 1024, 512, 768
+    gate, up = _gate_up(M, I, M)
+    w16, ws = ops.prepare_weight(inputs.gemm_w(N, I, seed=3).cuda())
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(4)) * 0.1).bfloat16().cuda()
+    g, u = gate.cuda(), up.cuda()
+    _, _, h = ops.glu_rows(g, u, "silu", want_h=True)
+    y = ops.glu_linear(g, u, w16, ws, b, act="silu")
+    assert torch.equal(y.view(torch.int16), ops.scaled_linear(h, w16, ws, b).view(torch.int16))
+    x = (torch.randn(M, H, generator=torch.Generator().manual_seed(5)) * 4).bfloat16().cuda()
+    nw = (torch.randn(H, generator=torch.Generator().manual_seed(6)) * 0.1).bfloat16().cuda()
+    w16b, wsb = ops.prepare_weight(inputs.gemm_w(N, H, seed=7).cuda())
+    _, _, r = ops.rmsnorm_rows(x, nw, 1e-6, 1.0, "gemma", want_r=True)
+    y2 = ops.rmsnorm_linear(x, nw, w16b, wsb, None, eps=1e-6, offset=1.0, style="gemma")
+    assert torch.equal(y2.view(torch.int16), ops.scaled_linear(r, w16b, wsb).view(torch.int16))
+
+
+def test_fused_rows_reject_bad_input():
+    from tbf16 import ops
+    g = torch.zeros(2, 12, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        ops.glu_rows(g, g, "silu")  # row length not a multiple of 8
+    g = torch.zeros(2, 16392, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        ops.glu_rows(g, g, "silu")  # longer than TBF16_FUSED_MAX_ROW
+    with pytest.raises(RuntimeError):
+        ops.glu_rows(g[:, :16], g[:, :16], "relu")

@@ -111,3 +111,22 @@ def test_row_reduce_l1_exact(orc):
     assert orc.row_reduce(x, l1=True)[0].item() == 1.0 + 2 ** -22
     y = torch.tensor([[float("nan"), 2.0, -3.0, 1.0]], dtype=torch.bfloat16)
     assert orc.row_reduce(y, l1=False)[0].item() == 3.0  # fmaxf ignores NaN
+
+
+def test_fused_rows_oracle_known_answers():
+    from oracle import oracle as orc
+    """The producer-fusion restatements on hand-checked rows: silu(0) = 0 and silu(g) * 1 = bf16(silu(g));
+    a constant row's RMSNorm is 1 (times weight + 1 = 1), whose row max 1 gets the fused rule's scale
+    2^14 at t = 15 (biased exponent 253 + 15 - 127 = 141)."""
+    g = torch.tensor([[0.0, 1.0, -1.0, 2.0, 0.5, -0.5, 4.0, -4.0]]).bfloat16()
+    u = torch.ones_like(g)
+    h16, s_inv, h = orc.glu_rows(g, u, "silu")
+    assert h[0, 0].item() == 0.0
+    ref = (g.float() / (1 + torch.exp(-g.float()))).bfloat16()
+    assert torch.equal(h, ref)
+    x = torch.full((1, 8), 3.0).bfloat16()
+    w = torch.zeros(8).bfloat16()
+    r16, s_inv, r = orc.rmsnorm_rows(x, w, eps=0.0, offset=1.0, style="gemma")
+    assert torch.all(r.float() == 1.0)  # x / rms(x) = 1, times (0 + 1)
+    assert s_inv.item() == 2.0 ** -14  # row max 1 -> biased 127 -> scale 2^(253 + 15 - 127 - 127)
+    assert torch.all(r16.float() == 2.0 ** 14)

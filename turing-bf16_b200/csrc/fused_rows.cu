@@ -1,0 +1,250 @@
+// Producer fusion: the kernels that produce a linear's input also compute its row exponents, so the
+// linear skips its row pass (one full read of the activation) and the producer writes fp16 operands
+// directly. The reference runs these as separate passes (torch's activation / norm, then its
+// quantize or row_scale kernel: tbf16/ops.py:74-89, tbf16/csrc/gemm_sm75.cu:27-47).
+//
+//   glu_rows_kernel      h = bf16(bf16(act(g)) * u) for a gated MLP (act = silu or tanh-gelu),
+//                        as torch computes act(g) * u on bf16 tensors
+//   rmsnorm_rows_kernel  r = RMSNorm(x) in the two common roundings (Gemma: bf16(x * rsqrt(ms + eps) *
+//                        (w + offset)); Llama: bf16(w * bf16(x * rsqrt(ms + eps))))
+// then, for the produced rows: s_inv = the fused rule's power-of-two row scale (row max, target t) and
+// y16 = fp16(row / s_inv) -- exactly what tbf16_row_scale with a y16 buffer gives on the bf16 rows.
+//
+// HBM-bound: one 256-thread block per row keeps the row in registers (up to 8 x 16 bytes per thread
+// per input, rows up to 16384 elements), so each input is read once and the fp16 operand (plus, on
+// request, the bf16 row) written once. Row maxima and sums of squares are reduced over the warp and
+// then over the 8 warps in a fixed order.
+#include "common.cuh"
+
+using namespace tbf16;
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxChunks = 8;  // 16-byte vectors per thread and input: rows up to 256 * 8 * 8 elements
+
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// GELU with the tanh approximation: 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float kKappa = 0.044715f;
+  const float x3 = x * x * x;
+  return 0.5f * x * (1.0f + tanhf(kBeta * (x + kKappa * x3)));
+}
+
+// Block-wide max (non-negative values) over the 8 warps, in a fixed order.
+__device__ __forceinline__ float block_max(float m, float* red) {
+  m = warp_max(m);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int k = 1; k < kThreads / 32; ++k) r = fmaxf(r, red[k]);
+  return r;
+}
+
+// Writes fp16(row / s_inv) from the bf16 row held in registers, s_inv, and the bf16 row if asked.
+template <int NCH>
+__device__ __forceinline__ void emit_row(const uint4 (&v)[NCH], float amax, int t, int K8, int64_t row,
+                                         uint4* __restrict__ y16, int64_t ldy8, float* __restrict__ s_inv,
+                                         uint4* __restrict__ out, int64_t ldo8) {
+  const int se = scale_biased_exp_fused(amax, t);
+  const float sc = pow2_from_biased(se);
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const int i = threadIdx.x + kThreads * u;
+    if (i < K8) {
+      uint4 o;
+      o.x = pack_f16(bf16lo(v[u].x) * sc, bf16hi(v[u].x) * sc);
+      o.y = pack_f16(bf16lo(v[u].y) * sc, bf16hi(v[u].y) * sc);
+      o.z = pack_f16(bf16lo(v[u].z) * sc, bf16hi(v[u].z) * sc);
+      o.w = pack_f16(bf16lo(v[u].w) * sc, bf16hi(v[u].w) * sc);
+      y16[row * ldy8 + i] = o;
+      if (out) out[row * ldo8 + i] = v[u];
+    }
+  }
+  if (threadIdx.x == 0) s_inv[row] = inv_pow2_from_biased(se);
+}
+
+template <int NCH, int ACT>
+__global__ void __launch_bounds__(kThreads) glu_rows_kernel(const uint4* __restrict__ g, int64_t ldg8,
+                                                            const uint4* __restrict__ u, int64_t ldu8, int I8, int t,
+                                                            uint4* __restrict__ y16, int64_t ldy8,
+                                                            float* __restrict__ s_inv, uint4* __restrict__ out,
+                                                            int64_t ldo8) {
+  pdl_launch_dependents();
+  __shared__ float red[kThreads / 32];
+  const int64_t row = blockIdx.x;
+  uint4 gv[NCH], uv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int i = threadIdx.x + kThreads * c;
+    gv[c] = i < I8 ? __ldg(g + row * ldg8 + i) : make_uint4(0, 0, 0, 0);
+    uv[c] = i < I8 ? __ldg(u + row * ldu8 + i) : make_uint4(0, 0, 0, 0);
+  }
+  float m = 0.f;
+  uint4 hv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const uint32_t gw[4] = {gv[c].x, gv[c].y, gv[c].z, gv[c].w};
+    const uint32_t uw[4] = {uv[c].x, uv[c].y, uv[c].z, uv[c].w};
+    uint32_t hw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a0 = round_bf16(ACT == TBF16_ACT_SILU ? silu(bf16lo(gw[j])) : gelu_tanh(bf16lo(gw[j])));
+      const float a1 = round_bf16(ACT == TBF16_ACT_SILU ? silu(bf16hi(gw[j])) : gelu_tanh(bf16hi(gw[j])));
+      hw[j] = pack_bf16(a0 * bf16lo(uw[j]), a1 * bf16hi(uw[j]));
+      m = fmaxf(m, fmaxf(fabsf(bf16lo(hw[j])), fabsf(bf16hi(hw[j]))));
+    }
+    hv[c] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  }
+  const float amax = block_max(m, red);
+  emit_row<NCH>(hv, amax, t, I8, row, y16, ldy8, s_inv, out, ldo8);
+}
+
+template <int NCH, int STYLE>
+__global__ void __launch_bounds__(kThreads) rmsnorm_rows_kernel(const uint4* __restrict__ x, int64_t ldx8,
+                                                                const uint4* __restrict__ w, int K8, int K,
+                                                                float eps, float offset, int t,
+                                                                uint4* __restrict__ y16, int64_t ldy8,
+                                                                float* __restrict__ s_inv, uint4* __restrict__ out,
+                                                                int64_t ldo8) {
+  pdl_launch_dependents();
+  __shared__ float red[kThreads / 32];
+  __shared__ float red_ss[kThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint4 xv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int i = threadIdx.x + kThreads * c;
+    xv[c] = i < K8 ? __ldg(x + row * ldx8 + i) : make_uint4(0, 0, 0, 0);
+  }
+  // mean of squares in fp32: per thread, then a shuffle tree, then the 8 warps in order
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const uint32_t xw[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16lo(xw[j]), b = bf16hi(xw[j]);
+      ss = fmaf(a, a, ss);
+      ss = fmaf(b, b, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red_ss[warp] = ss;
+  __syncthreads();
+  float tot = red_ss[0];
+#pragma unroll
+  for (int k = 1; k < kThreads / 32; ++k) tot += red_ss[k];
+  const float r = rsqrtf(tot / (float)K + eps);
+  float m = 0.f;
+  uint4 yv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int i = threadIdx.x + kThreads * c;
+    const uint4 wv = i < K8 ? __ldg(w + i) : make_uint4(0, 0, 0, 0);
+    const uint32_t xw[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t yw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float y0, y1;
+      if (STYLE == TBF16_NORM_SCALE_FP32) {  // (x * r) * (w + offset) in fp32, one rounding
+        y0 = (bf16lo(xw[j]) * r) * (bf16lo(ww[j]) + offset);
+        y1 = (bf16hi(xw[j]) * r) * (bf16hi(ww[j]) + offset);
+      } else {  // bf16(x * r), then the bf16 weight times it, rounded again
+        y0 = bf16lo(ww[j]) * round_bf16(bf16lo(xw[j]) * r);
+        y1 = bf16hi(ww[j]) * round_bf16(bf16hi(xw[j]) * r);
+      }
+      yw[j] = pack_bf16(y0, y1);
+      m = fmaxf(m, fmaxf(fabsf(bf16lo(yw[j])), fabsf(bf16hi(yw[j]))));
+    }
+    yv[c] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+  }
+  const float amax = block_max(m, red);
+  emit_row<NCH>(yv, amax, t, K8, row, y16, ldy8, s_inv, out, ldo8);
+}
+
+int chunks_for(int64_t K8) {
+  for (int c = 1; c <= kMaxChunks; c *= 2)
+    if (K8 <= (int64_t)kThreads * c) return c;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64_t M, int64_t I, int act,
+                   int target_exp, void* y16, int64_t ldy, float* s_inv, void* h_out, int64_t ldo, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || I < 0 || ldg < I || ldu < I || ldy < I || (h_out && ldo < I) || !s_inv || !y16 || !g || !u ||
+      target_exp < 0 || target_exp > 64 || (act != TBF16_ACT_SILU && act != TBF16_ACT_GELU_TANH))
+    return TBF16_ERR_INVALID;
+  if (I % 8 || ldg % 8 || ldu % 8 || ldy % 8 || (h_out && ldo % 8) || !tbf16_host::aligned16(g) ||
+      !tbf16_host::aligned16(u) || !tbf16_host::aligned16(y16) || (h_out && !tbf16_host::aligned16(h_out)))
+    return TBF16_ERR_ALIGN;
+  if (M == 0 || I == 0) return TBF16_OK;
+  const int64_t I8 = I / 8;
+  const int nch = chunks_for(I8);
+  if (!nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
+  auto st = static_cast<cudaStream_t>(stream);
+  const uint4 *gp = static_cast<const uint4*>(g), *up = static_cast<const uint4*>(u);
+  uint4 *yp = static_cast<uint4*>(y16), *op = static_cast<uint4*>(h_out);
+#define TBF16_GLU(N, A)                                                                                          \
+  glu_rows_kernel<N, A><<<(unsigned)M, kThreads, 0, st>>>(gp, ldg / 8, up, ldu / 8, (int)I8, target_exp, yp, ldy / 8, \
+                                                          s_inv, op, ldo / 8)
+#define TBF16_GLU_ACT(N) \
+  if (act == TBF16_ACT_SILU) TBF16_GLU(N, TBF16_ACT_SILU); else TBF16_GLU(N, TBF16_ACT_GELU_TANH)
+  switch (nch) {
+    case 1: TBF16_GLU_ACT(1); break;
+    case 2: TBF16_GLU_ACT(2); break;
+    case 4: TBF16_GLU_ACT(4); break;
+    default: TBF16_GLU_ACT(8); break;
+  }
+#undef TBF16_GLU_ACT
+#undef TBF16_GLU
+  return tbf16_host::check_launch();
+}
+
+int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps, int style,
+                       float offset, int target_exp, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo,
+                       void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || K < 0 || ldx < K || ldy < K || (r_out && ldo < K) || !s_inv || !y16 || !x || !w || !(eps >= 0.f) ||
+      target_exp < 0 || target_exp > 64 || (style != TBF16_NORM_SCALE_FP32 && style != TBF16_NORM_SCALE_BF16))
+    return TBF16_ERR_INVALID;
+  if (K % 8 || ldx % 8 || ldy % 8 || (r_out && ldo % 8) || !tbf16_host::aligned16(x) || !tbf16_host::aligned16(w) ||
+      !tbf16_host::aligned16(y16) || (r_out && !tbf16_host::aligned16(r_out)))
+    return TBF16_ERR_ALIGN;
+  if (M == 0 || K == 0) return TBF16_OK;
+  const int64_t K8 = K / 8;
+  const int nch = chunks_for(K8);
+  if (!nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
+  auto st = static_cast<cudaStream_t>(stream);
+  const uint4 *xp = static_cast<const uint4*>(x), *wp = static_cast<const uint4*>(w);
+  uint4 *yp = static_cast<uint4*>(y16), *op = static_cast<uint4*>(r_out);
+#define TBF16_NORM(N, S)                                                                                              \
+  rmsnorm_rows_kernel<N, S><<<(unsigned)M, kThreads, 0, st>>>(xp, ldx / 8, wp, (int)K8, (int)K, eps, offset,        \
+                                                              target_exp, yp, ldy / 8, s_inv, op, ldo / 8)
+#define TBF16_NORM_STYLE(N) \
+  if (style == TBF16_NORM_SCALE_FP32) TBF16_NORM(N, TBF16_NORM_SCALE_FP32); else TBF16_NORM(N, TBF16_NORM_SCALE_BF16)
+  switch (nch) {
+    case 1: TBF16_NORM_STYLE(1); break;
+    case 2: TBF16_NORM_STYLE(2); break;
+    case 4: TBF16_NORM_STYLE(4); break;
+    default: TBF16_NORM_STYLE(8); break;
+  }
+#undef TBF16_NORM_STYLE
+#undef TBF16_NORM
+  return tbf16_host::check_launch();
+}
+
+}  // extern "C"

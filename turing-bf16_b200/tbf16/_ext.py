@@ -36,6 +36,9 @@ SIGNATURES = {
     "tbf16_linear_scaled": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp],
     "tbf16_gemm_f16": [_vp, _i32, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp],
     "tbf16_gemv": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp],
+    "tbf16_glu_rows": [_vp, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp],
+    "tbf16_rmsnorm_rows": [_vp, _i64, _vp, _i64, _i64, ctypes.c_float, _i32, ctypes.c_float, _i32, _vp, _i64, _vp, _vp,
+                           _i64, _vp],
     "tbf16_attn_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64, _i64,
                        _i64, _vp, _vp, _i64, _vp, _vp],
     "tbf16_attn_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,

@@ -2,7 +2,8 @@
 
 Same public surface as the reference's tbf16/ops.py (quantize_rows, prepare_weight, scaled_linear,
 linear_q, small_m_linear, quantize_rows_shared, _target_exp), plus linear_host for activations that
-live in pinned host memory. The work runs in libtbf16_sm100.so: a row-amax -> exponent pass (which
+live in pinned host memory and the producer-fused glu_rows / rmsnorm_rows (glu_linear, rmsnorm_linear),
+which compute a linear's row scales in the kernel that produces its input. The work runs in libtbf16_sm100.so: a row-amax -> exponent pass (which
 also writes the fp16 copy of x for large N) and a warp-specialised TMA + tcgen05 GEMM that
 accumulates in fp32 in TMEM and writes bf16 straight from the accumulator. Up to 4 rows take a
 weight-streaming kernel instead (the reference's single-row GEMV, extended), up to 256 rows a split-K
@@ -327,6 +328,98 @@ def _gemv(x2, w16, w_sinv, b, N):
     return y
 
 
+_ACTS = {"silu": 0, "gelu_tanh": 1}
+_NORM_STYLES = {"gemma": 0, "llama": 1}
+
+
+def _rows2d(t, name):
+    if t.dtype != torch.bfloat16:
+        raise RuntimeError(f"tbf16.{name}: expected bf16, got {t.dtype}")
+    t2 = t.reshape(-1, t.shape[-1])
+    return t2 if _rows_ok(t2) else t2.contiguous()
+
+
+@torch.autocast("cuda", enabled=False)
+def glu_rows(gate: torch.Tensor, up: torch.Tensor, act: str = "silu", target_exp: int = 15, want_h: bool = False):
+    """Producer-fused gated activation: h = bf16(bf16(act(gate)) * up) (torch's act(g) * u on bf16 tensors)
+    with the row scales of the fused linear computed in the same pass. Returns (h16, s_inv[, h]): the fp16
+    operand fp16(h / s_inv) and the fp32 power-of-two inverse row scales, as quantize_rows / row_scale
+    give for h. act: "silu" or "gelu_tanh"."""
+    require_cuda(gate, up)
+    if act not in _ACTS:
+        raise RuntimeError(f"tbf16.glu_rows: act must be one of {sorted(_ACTS)}")
+    if gate.shape != up.shape:
+        raise RuntimeError("tbf16.glu_rows: gate and up shapes differ")
+    g2, u2 = _rows2d(gate, "glu_rows"), _rows2d(up, "glu_rows")
+    M, I = g2.shape
+    if I % 8:
+        raise RuntimeError("tbf16.glu_rows: the row length must be a multiple of 8")
+    h16 = torch.empty((M, I), device=gate.device, dtype=torch.float16)
+    s_inv = torch.empty((M,), device=gate.device, dtype=torch.float32)
+    h = torch.empty((M, I), device=gate.device, dtype=torch.bfloat16) if want_h else None
+    call("tbf16_glu_rows", ptr(g2), g2.stride(0), ptr(u2), u2.stride(0), M, I, _ACTS[act], int(target_exp), ptr(h16), I,
+         ptr(s_inv), ptr(h), I, stream_ptr(gate.device))
+    shape = gate.shape
+    out = (h16.reshape(shape), s_inv.reshape(shape[:-1]))
+    return out + (h.reshape(shape),) if want_h else out
+
+
+@torch.autocast("cuda", enabled=False)
+def rmsnorm_rows(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offset: float = 1.0, style: str = "gemma",
+                 target_exp: int = 15, want_r: bool = False):
+    """Producer-fused RMSNorm with the row scales of the linear that follows. style "gemma":
+    r = bf16((x * rsqrt(mean(x^2) + eps)) * (weight + offset)) in fp32; "llama":
+    r = bf16(weight * bf16(x * rsqrt(mean(x^2) + eps))). Returns (r16, s_inv[, r]) as glu_rows."""
+    require_cuda(x, weight)
+    if style not in _NORM_STYLES:
+        raise RuntimeError(f"tbf16.rmsnorm_rows: style must be one of {sorted(_NORM_STYLES)}")
+    x2 = _rows2d(x, "rmsnorm_rows")
+    M, K = x2.shape
+    w = weight.to(torch.bfloat16).contiguous()
+    if w.numel() != K or K % 8:
+        raise RuntimeError("tbf16.rmsnorm_rows: weight must have the row length, a multiple of 8")
+    r16 = torch.empty((M, K), device=x.device, dtype=torch.float16)
+    s_inv = torch.empty((M,), device=x.device, dtype=torch.float32)
+    r = torch.empty((M, K), device=x.device, dtype=torch.bfloat16) if want_r else None
+    call("tbf16_rmsnorm_rows", ptr(x2), x2.stride(0), ptr(w), M, K, float(eps), _NORM_STYLES[style], float(offset),
+         int(target_exp), ptr(r16), K, ptr(s_inv), ptr(r), K, stream_ptr(x.device))
+    out = (r16.reshape(x.shape), s_inv.reshape(x.shape[:-1]))
+    return out + (r.reshape(x.shape),) if want_r else out
+
+
+def _linear_from_rows(q16, s_inv, bf16_rows, w16, w_sinv, bias, lead_shape):
+    """The down projection of an already row-scaled operand: the same kernels and arithmetic as
+    scaled_linear on the bf16 rows (GEMV semantics up to GEMV_ROWS rows, which need the bf16 rows)."""
+    K = q16.shape[-1]
+    M = q16.numel() // K
+    N = w16.shape[0]
+    if M <= GEMV_ROWS:
+        return scaled_linear(bf16_rows, w16, w_sinv, bias)
+    if not _rows_ok(w16) or w16.shape[1] != K or N % 8:
+        return scaled_linear(bf16_rows, w16, w_sinv, bias)
+    y = _gemm_f16(q16.reshape(M, K), 0, w16, 0, M, N, K, s_inv.reshape(M), w_sinv.contiguous().float(),
+                  _bias_ok(bias, N, q16.device))
+    return y.reshape(*lead_shape, N)
+
+
+def glu_linear(gate: torch.Tensor, up: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None,
+               act: str = "silu"):
+    """down(act(gate) * up) for a gated MLP, equal to scaled_linear(act(gate) * up, w16, w_sinv, bias)
+    on the bf16 product, without its separate activation and row passes (glu_rows feeds the GEMM)."""
+    few = gate.numel() // gate.shape[-1] <= GEMV_ROWS
+    res = glu_rows(gate, up, act, want_h=few)
+    return _linear_from_rows(res[0], res[1], res[2] if few else None, w16, w_sinv, bias, gate.shape[:-1])
+
+
+def rmsnorm_linear(x: torch.Tensor, weight: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None,
+                   eps: float = 1e-6, offset: float = 1.0, style: str = "gemma"):
+    """linear(RMSNorm(x)) equal to scaled_linear(rmsnorm(x), ...) on the bf16 normalised rows, with the norm
+    and the linear's row pass in one kernel (rmsnorm_rows feeds the GEMM)."""
+    few = x.numel() // x.shape[-1] <= GEMV_ROWS
+    res = rmsnorm_rows(x, weight, eps, offset, style, want_r=few)
+    return _linear_from_rows(res[0], res[1], res[2] if few else None, w16, w_sinv, bias, x.shape[:-1])
+
+
 def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None):
     """The reference's small-M entry point (reference tbf16/ops.py:207-218): up to GEMV_ROWS rows go
     through the weight-streaming kernel, more through the tcgen05 GEMM (scaled_linear routes the same way)."""
@@ -334,5 +427,5 @@ def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bi
 
 
 __all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
-           "linear_host",
+           "linear_host", "glu_rows", "rmsnorm_rows", "glu_linear", "rmsnorm_linear",
            "available", "_target_exp"]
