@@ -90,7 +90,7 @@ def test_linear_host_matches_device_path():
     b = (torch.randn(N, generator=torch.Generator().manual_seed(23)) * 0.1).bfloat16()
     hx = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
     hx.copy_(x)
-    y = ops.linear_host(hx, w16, ws, b.cuda())
+    y = ops.linear_host(hx, w16, ws, b.cuda(), chunk_rows=1024)
     torch.cuda.synchronize()
     assert y.shape == (M, N) and not y.is_cuda
     chunks = ops._host_chunks(M, 1024)
