@@ -188,6 +188,34 @@ int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int
                        float offset, int target_exp, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo,
                        void* stream);
 
+/* ------------------------------------------------------------------ scaled convolutions */
+/* The reference's scaled convolutions (tbf16/conv.py:34-60): one power-of-two scale per input sample,
+ * the weight prepared as a linear's rows (tbf16_quantize_rows on [O, C kd kh kw], t = _target_exp(K)):
+ *   e[b] = frexp_exp(max |x[b]|) - t (a zero sample counts as max 1), x16 = fp16_rn(x * 2^-e[b]),
+ *   y[b, o, p] = bf16_rn((sum_k x16 w16[o, k]) * 2^e[b] * ws[o] + bias[o])   (fp32 sum, one rounding).
+ * Geometry: an array of TBF16_CONV_GEOM_LEN int64 in this order: B, C, D, H, W (input extents; 1-D and
+ * 2-D convolutions use D = H = 1 or D = 1), the input strides in elements for b, c, d, h, w (any
+ * layout), the kernel extents kd, kh, kw, the strides, the zero paddings and the dilations (each d, h,
+ * w), and the output extents Do, Ho, Wo. */
+#define TBF16_CONV_GEOM_LEN 25
+
+/* Per-sample exponents: x holds B samples of n dense elements, ld elements apart (contiguous or
+ * channels-last); writes e[b] and out_scale[b] = 2^e[b] (fp32; B floats of amax_ws as scratch). */
+int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int target_exp, float* amax_ws,
+                            int32_t* e, float* out_scale, void* stream);
+
+/* groups == 1: cols16 fp16 [B Do Ho Wo, Kp] (one row per output position, column k = ((c kd + z) kh + y)
+ * kw + x as in the weight's [O, C, kd, kh, kw] layout, zero in the padding and for K <= k < Kp) and
+ * row_scale[m] = out_scale of the row's sample; then tbf16_gemm_f16(cols16, 0, Kp, w16 [O, Kp], 0, Kp,
+ * M, O, Kp, row_scale, ws, bias, y, O) gives y channels-last [B, Do, Ho, Wo, O]. Kp: K rounded up to 8. */
+int tbf16_conv_im2col(const void* x, const int64_t* geom, int64_t K, int64_t Kp, const int32_t* e,
+                      const float* out_scale, void* cols16, float* row_scale, void* stream);
+
+/* groups > 1 (grouped and depthwise): direct convolution into y bf16 [B, O, Do, Ho, Wo] contiguous; w16
+ * fp16 [O, C / groups, kd, kh, kw] contiguous, ws fp32 [O], bias bf16 [O] nullable. */
+int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t groups, const void* w16, const float* ws,
+                       const void* bias, const int32_t* e, const float* out_scale, void* y, void* stream);
+
 /* ------------------------------------------------------------------ scaled attention (tcgen05) */
 
 /* Flash-attention forward on the fp16 copies from tbf16_prepare_qkv. Replaces the torch fp16 SDPA call of

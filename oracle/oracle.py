@@ -343,6 +343,35 @@ def rmsnorm_rows(x, weight, eps=1e-6, offset=1.0, style="gemma", target_exp=15):
     return f16_rn(r.float() / s_inv[:, None]), s_inv, r
 
 
+# ----------------------------------------------------------------------------- scaled convolutions
+
+def conv_sample_exp(x: torch.Tensor, target_exp: int) -> torch.Tensor:
+    """Per-sample exponent of tbf16/conv.py:47-48 (_pow2_exponent(amax) - t, a zero sample as max 1)."""
+    x = _cpu(x).float()
+    amax = x.abs().reshape(x.shape[0], -1).amax(1)
+    return torch.frexp(torch.where(amax > 0, amax, torch.ones_like(amax)))[1].int() - target_exp
+
+
+def conv_scaled(x, w16, ws, bias, stride, padding, dilation, groups, target_exp):
+    """tbf16/conv.py:34-60 restated with fp64 accumulation: x16 = fp16(x * 2^-e[b]) (exact power-of-two
+    scale, C rounding), the convolution of x16 with w16 in fp64, y = bf16((acc * 2^e[b]) * ws[o] + bias[o]).
+    Zero padding. Returns (y bf16, acc fp64 of |x16| * |w16| times the scales, for the tolerance)."""
+    x, w16 = _cpu(x), _cpu(w16)
+    nd = x.dim() - 2
+    conv = {1: torch.nn.functional.conv1d, 2: torch.nn.functional.conv2d, 3: torch.nn.functional.conv3d}[nd]
+    e = conv_sample_exp(x, target_exp).double()
+    bshape = (-1,) + (1,) * (nd + 1)
+    x16 = f16_rn((x.double() * torch.exp2(-e).view(bshape)).float())
+    acc = conv(x16.double(), w16.double(), None, stride, padding, dilation, groups)
+    absacc = conv(x16.double().abs(), w16.double().abs(), None, stride, padding, dilation, groups)
+    oshape = (1, -1) + (1,) * nd
+    sc = torch.exp2(e).view(bshape) * _cpu(ws).double().view(oshape)
+    y = acc * sc
+    if bias is not None:
+        y = y + _cpu(bias).double().view(oshape)
+    return bf16_rn(y), absacc * sc.abs()
+
+
 def gemm_f16(a16, a_mn, b16, b_mn, M, N, K, sa, sb=None, bias=None):
     """y = bf16((sum_k A[m,k] B[n,k]) * sa[m] * sb[n] + bias[n]) with fp64 accumulation: the
     contraction of ops.py:167-178 (linear_q) and autograd.py:114-120 (_scaled_mm) without the fp16

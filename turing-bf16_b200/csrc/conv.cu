@@ -1,0 +1,223 @@
+// Scaled bf16 convolutions (the reference's tbf16/conv.py:34-60): one exact power-of-two scale per
+// sample for the input (a convolution mixes positions, so rows cannot be scaled separately), one per
+// output channel for the weight (prepared once, as a linear's rows), fp32 accumulation, and the two
+// scales undone in the bf16 epilogue:
+//
+//   e[b]     = frexp_exp(max |x[b]|) - t      (zero samples count as max 1; t = _target_exp(K))
+//   x16      = fp16_rn(x * 2^-e[b])
+//   y[b,o,p] = bf16_rn((sum_k x16 w16[o,k]) * 2^e[b] * ws[o] + bias[o])
+//
+// groups == 1: im2col into fp16 rows (one row per output position, K = C kd kh kw columns zero-padded
+// to a multiple of 8, each row carrying its sample's output scale) and the tcgen05 GEMM against the
+// [O, K] weight rows; the output comes out channels-last. groups > 1 (depthwise and grouped convs, a few
+// input channels per output): a direct kernel, one thread per output element. The reference ends in a
+// cuDNN fp16 conv whose output is rounded to fp16 before the scales; here the fp32 sum is scaled and
+// rounded to bf16 once. Geometry is passed as an array of int64 (see TBF16_CONV_GEOM_* in the header).
+#include "common.cuh"
+
+using namespace tbf16;
+
+namespace {
+
+struct Geom {
+  int64_t B, C, D, H, W;          // input (batch, channels, depth, height, width)
+  int64_t sb, sc, sd, sh, sw;     // input strides in elements (any layout)
+  int64_t kd, kh, kw;             // kernel extent
+  int64_t std_, sth, stw;         // stride
+  int64_t pd, ph, pw;             // zero padding
+  int64_t dd, dh, dw;             // dilation
+  int64_t Do, Ho, Wo;             // output extent
+};
+
+Geom load_geom(const int64_t* g) {
+  Geom r;
+  int64_t* f = &r.B;
+  for (int i = 0; i < TBF16_CONV_GEOM_LEN; ++i) f[i] = g[i];
+  return r;
+}
+
+// x * 2^-e exactly for any e (two steps when 2^-e alone would leave fp32's normal range).
+__device__ __forceinline__ float scale_pow2(float v, int e) {
+  const int ne = -e;
+  if (ne >= -126 && ne <= 127) return v * exp2i(ne);
+  const int h = ne / 2;
+  return (v * exp2i(h)) * exp2i(ne - h);
+}
+
+// Per-sample max |x| over n dense elements of each sample (samples ld apart), merged with atomicMax.
+__global__ void __launch_bounds__(256) sample_amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, int64_t ld,
+                                                          float* __restrict__ amax) {
+  const int64_t b = blockIdx.y;
+  const __nv_bfloat16* xs = x + b * ld;
+  float m = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(__bfloat162float(xs[i])));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(amax) + b, __float_as_int(m));
+}
+
+__global__ void sample_exp_kernel(const float* __restrict__ amax, int64_t B, int t, int32_t* __restrict__ e,
+                                  float* __restrict__ out_scale) {
+  const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const float a = amax[b];
+  const int eb = frexp_exp(a > 0.f ? a : 1.0f) - t;
+  e[b] = eb;
+  out_scale[b] = exp2i(eb);
+}
+
+// cols16[m, k] = fp16(x[b, c, od*s - p + z*d, ...] * 2^-e[b]) for output position m = (b, od, oh, ow) and
+// k = ((c kd + z) kh + y) kw + x < K, 0 past K or in the padding; row_scale[m] = 2^e[b].
+__global__ void __launch_bounds__(256) im2col_kernel(const __nv_bfloat16* __restrict__ xin, const Geom g, int64_t K,
+                                                     int64_t Kp, const int32_t* __restrict__ e,
+                                                     const float* __restrict__ out_scale, uint4* __restrict__ cols,
+                                                     float* __restrict__ row_scale) {
+  const int64_t K8 = Kp / 8;
+  const int64_t M = g.B * g.Do * g.Ho * g.Wo;
+  const int64_t kvol = g.kd * g.kh * g.kw;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * K8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / K8, j = i - m * K8;
+    int64_t r = m;
+    const int64_t ow = r % g.Wo; r /= g.Wo;
+    const int64_t oh = r % g.Ho; r /= g.Ho;
+    const int64_t od = r % g.Do;
+    const int64_t b = r / g.Do;
+    const int eb = e[b];
+    const __nv_bfloat16* xb = xin + b * g.sb;
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t k = j * 8 + u;
+      float val = 0.f;
+      if (k < K) {
+        const int64_t c = k / kvol;
+        int64_t q = k - c * kvol;
+        const int64_t z = q / (g.kh * g.kw);
+        q -= z * g.kh * g.kw;
+        const int64_t yy = q / g.kw, xx = q - yy * g.kw;
+        const int64_t id = od * g.std_ - g.pd + z * g.dd;
+        const int64_t ih = oh * g.sth - g.ph + yy * g.dh;
+        const int64_t iw = ow * g.stw - g.pw + xx * g.dw;
+        if (id >= 0 && id < g.D && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
+          val = scale_pow2(__bfloat162float(xb[c * g.sc + id * g.sd + ih * g.sh + iw * g.sw]), eb);
+      }
+      v[u] = val;
+    }
+    cols[i] = make_uint4(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
+    if (j == 0) row_scale[m] = out_scale[b];
+  }
+}
+
+// Grouped / depthwise convolution, one thread per output element of y (B, O, Do, Ho, Wo) contiguous:
+// fp32 sum over the group's Cg input channels and the kernel window of fp16(x 2^-e) * w16.
+__global__ void __launch_bounds__(256) conv_grouped_kernel(const __nv_bfloat16* __restrict__ xin, const Geom g,
+                                                           int64_t O, int64_t groups,
+                                                           const __half* __restrict__ w16,
+                                                           const float* __restrict__ ws,
+                                                           const __nv_bfloat16* __restrict__ bias,
+                                                           const int32_t* __restrict__ e,
+                                                           const float* __restrict__ out_scale,
+                                                           __nv_bfloat16* __restrict__ y) {
+  const int64_t total = g.B * O * g.Do * g.Ho * g.Wo;
+  const int64_t Cg = g.C / groups, Og = O / groups;
+  const int64_t kvol = g.kd * g.kh * g.kw;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i;
+    const int64_t ow = r % g.Wo; r /= g.Wo;
+    const int64_t oh = r % g.Ho; r /= g.Ho;
+    const int64_t od = r % g.Do; r /= g.Do;
+    const int64_t o = r % O;
+    const int64_t b = r / O;
+    const int eb = e[b];
+    const int64_t c0 = (o / Og) * Cg;
+    const __nv_bfloat16* xb = xin + b * g.sb;
+    const __half* wo = w16 + o * Cg * kvol;
+    float acc = 0.f;
+    for (int64_t c = 0; c < Cg; ++c) {
+      for (int64_t z = 0; z < g.kd; ++z) {
+        const int64_t id = od * g.std_ - g.pd + z * g.dd;
+        if (id < 0 || id >= g.D) continue;
+        for (int64_t yy = 0; yy < g.kh; ++yy) {
+          const int64_t ih = oh * g.sth - g.ph + yy * g.dh;
+          if (ih < 0 || ih >= g.H) continue;
+          for (int64_t xx = 0; xx < g.kw; ++xx) {
+            const int64_t iw = ow * g.stw - g.pw + xx * g.dw;
+            if (iw < 0 || iw >= g.W) continue;
+            const float xv = __half2float(__float2half_rn(
+                scale_pow2(__bfloat162float(xb[(c0 + c) * g.sc + id * g.sd + ih * g.sh + iw * g.sw]), eb)));
+            acc = fmaf(xv, __half2float(wo[((c * g.kd + z) * g.kh + yy) * g.kw + xx]), acc);
+          }
+        }
+      }
+    }
+    float v = (acc * out_scale[b]) * ws[o];
+    if (bias) v += __bfloat162float(bias[o]);
+    y[i] = __float2bfloat16_rn(v);
+  }
+}
+
+int grid_for(int64_t work) {
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  const int64_t cap = (int64_t)(d ? d->sms : 148) * 16;
+  const int64_t g = (work + 255) / 256;
+  return (int)(g < 1 ? 1 : (g < cap ? g : cap));
+}
+
+bool geom_ok(const Geom& g) {
+  return g.B >= 0 && g.C > 0 && g.D > 0 && g.H > 0 && g.W > 0 && g.kd > 0 && g.kh > 0 && g.kw > 0 && g.std_ > 0 &&
+         g.sth > 0 && g.stw > 0 && g.pd >= 0 && g.ph >= 0 && g.pw >= 0 && g.dd > 0 && g.dh > 0 && g.dw > 0 &&
+         g.Do > 0 && g.Ho > 0 && g.Wo > 0 && g.sb >= 0 && g.sc >= 0 && g.sd >= 0 && g.sh >= 0 && g.sw >= 0 &&
+         (g.Do - 1) * g.std_ + (g.kd - 1) * g.dd < g.D + 2 * g.pd && (g.Ho - 1) * g.sth + (g.kh - 1) * g.dh < g.H + 2 * g.ph &&
+         (g.Wo - 1) * g.stw + (g.kw - 1) * g.dw < g.W + 2 * g.pw;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int target_exp, float* amax_ws,
+                            int32_t* e, float* out_scale, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (B < 0 || n < 0 || ld < n || !x || !amax_ws || !e || !out_scale || target_exp < -126 || target_exp > 126)
+    return TBF16_ERR_INVALID;
+  if (B == 0) return TBF16_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_ws, 0, sizeof(float) * B, st) != cudaSuccess) return TBF16_ERR_LAUNCH;
+  if (n > 0) {
+    const int64_t per = (n + 255) / 256;
+    const unsigned gx = (unsigned)(per < 64 ? per : 64);
+    sample_amax_kernel<<<dim3(gx, (unsigned)B), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, ld, amax_ws);
+  }
+  sample_exp_kernel<<<(unsigned)((B + 255) / 256), 256, 0, st>>>(amax_ws, B, target_exp, e, out_scale);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_conv_im2col(const void* x, const int64_t* geom, int64_t K, int64_t Kp, const int32_t* e,
+                      const float* out_scale, void* cols16, float* row_scale, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (!x || !geom || !e || !out_scale || !cols16 || !row_scale) return TBF16_ERR_INVALID;
+  const Geom g = load_geom(geom);
+  if (!geom_ok(g) || K != g.C * g.kd * g.kh * g.kw || Kp < K || Kp % 8) return TBF16_ERR_INVALID;
+  if (!tbf16_host::aligned16(cols16)) return TBF16_ERR_ALIGN;
+  const int64_t M = g.B * g.Do * g.Ho * g.Wo;
+  if (M == 0) return TBF16_OK;
+  im2col_kernel<<<grid_for(M * (Kp / 8)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), g, K, Kp, e, out_scale, static_cast<uint4*>(cols16), row_scale);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t groups, const void* w16, const float* ws,
+                       const void* bias, const int32_t* e, const float* out_scale, void* y, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (!x || !geom || !w16 || !ws || !e || !out_scale || !y || O <= 0 || groups <= 0) return TBF16_ERR_INVALID;
+  const Geom g = load_geom(geom);
+  if (!geom_ok(g) || g.C % groups || O % groups) return TBF16_ERR_INVALID;
+  const int64_t total = g.B * O * g.Do * g.Ho * g.Wo;
+  if (total == 0) return TBF16_OK;
+  conv_grouped_kernel<<<grid_for(total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), g, O, groups, static_cast<const __half*>(w16), ws,
+      static_cast<const __nv_bfloat16*>(bias), e, out_scale, static_cast<__nv_bfloat16*>(y));
+  return tbf16_host::check_launch();
+}
+
+}  // extern "C"

@@ -39,6 +39,9 @@ SIGNATURES = {
     "tbf16_glu_rows": [_vp, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp],
     "tbf16_rmsnorm_rows": [_vp, _i64, _vp, _i64, _i64, ctypes.c_float, _i32, ctypes.c_float, _i32, _vp, _i64, _vp, _vp,
                            _i64, _vp],
+    "tbf16_conv_sample_scale": [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp],
+    "tbf16_conv_im2col": [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp],
+    "tbf16_conv_grouped": [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "tbf16_attn_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64, _i64,
                        _i64, _vp, _vp, _i64, _vp, _vp],
     "tbf16_attn_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,

@@ -1,0 +1,170 @@
+"""bf16 convolutions on the B200 kernels with exact power-of-two scales (reference tbf16/conv.py).
+
+Same trick as the linear layers: the weight gets one exact power-of-two scale per output channel, the
+input one per sample (a convolution mixes positions, so rows cannot be scaled separately), the products
+accumulate in fp32 and the scales are undone in the bf16 epilogue. Same API as the reference module:
+convertible(m), convert_conv(conv) (in place, class swap so subclass forwards keep working,
+`.weight` becomes None, `.dequantized_weight()` gives it back), and convert(..., conv=True) uses them.
+
+Routing: 1x1 convolutions (stride 1, no padding, one group) are per-pixel linear layers and go through
+scaled_linear, as in the reference; other convolutions with one group become an im2col into fp16 rows
+plus the tcgen05 GEMM (output channels-last); grouped and depthwise convolutions run a direct kernel.
+The reference ends in a cuDNN fp16 convolution whose output is rounded to fp16 before the scales are
+applied; here the fp32 sum is scaled and rounded to bf16 once.
+"""
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ._ext import call, ptr, require_cuda, stream_ptr
+from .ops import _bias_ok, _gemm_f16, _target_exp, prepare_weight, scaled_linear
+
+
+def _triple(v, nd, fill):
+    """Per-dimension values of a conv attribute, as (d, h, w) with `fill` for the dimensions a 1-D or 2-D
+    convolution does not have."""
+    v = tuple(v) if isinstance(v, (tuple, list)) else (v,) * nd
+    return (fill,) * (3 - nd) + v
+
+
+def _sample_scales(x, t):
+    """(e int32 [B], 2^e fp32 [B]) for x bf16 with dense samples."""
+    B = x.shape[0]
+    n = x[0].numel()
+    ld = x.stride(0) if B > 1 else n  # a single sample's batch stride is arbitrary
+    amax = torch.empty(B, device=x.device, dtype=torch.float32)
+    e = torch.empty(B, device=x.device, dtype=torch.int32)
+    scale = torch.empty(B, device=x.device, dtype=torch.float32)
+    call("tbf16_conv_sample_scale", ptr(x), B, n, ld, int(t), ptr(amax), ptr(e), ptr(scale),
+         stream_ptr(x.device))
+    return e, scale
+
+
+def _dense(x):
+    """x itself when each sample is one dense block (contiguous or channels-last), else a contiguous copy."""
+    if x.is_contiguous():
+        return x
+    for fmt in (torch.channels_last, torch.channels_last_3d):
+        try:
+            if x.is_contiguous(memory_format=fmt):
+                return x
+        except RuntimeError:
+            pass
+    return x.contiguous()
+
+
+def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, groups, target_exp, wk16=None):
+    """The scaled convolution of a bf16 input with a prepared weight (weight16 fp16 [O, C/groups, *k],
+    weight_scale fp32 [O]); zero padding only (other padding modes are applied by the caller). wk16: the
+    weight as [O, K] rows padded to a multiple of 8 (made on the fly when None)."""
+    require_cuda(x, weight16, weight_scale)
+    nd = x.dim() - 2
+    x = _dense(x)
+    xs = x.reshape((x.shape[0], x.shape[1]) + (1,) * (3 - nd) + tuple(x.shape[2:]))
+    B, C, D, H, W = xs.shape
+    O = weight16.shape[0]
+    k = (1,) * (3 - nd) + tuple(weight16.shape[2:])
+    st, pd, dl = _triple(stride, nd, 1), _triple(padding, nd, 0), _triple(dilation, nd, 1)
+    out = tuple((n + 2 * p - d * (kk - 1) - 1) // s + 1 for n, p, d, kk, s in zip((D, H, W), pd, dl, k, st))
+    if min(out) <= 0:
+        raise RuntimeError("tbf16 conv: the kernel does not fit the padded input")
+    geom = torch.tensor([B, C, D, H, W, *xs.stride(), *k, *st, *pd, *dl, *out], dtype=torch.int64)
+    e, scale = _sample_scales(xs, target_exp)
+    b = _bias_ok(bias, O, x.device)
+    ws = weight_scale.contiguous().float()
+    out_shape = (B, O) + tuple(out[3 - nd:])
+    if groups == 1:
+        K = weight16[0].numel()
+        Kp = (K + 7) // 8 * 8
+        if wk16 is None:
+            wk16 = weight16.reshape(O, K)
+            if Kp != K:
+                wk16 = F.pad(wk16, (0, Kp - K))
+        M = B * out[0] * out[1] * out[2]
+        cols = torch.empty((M, Kp), device=x.device, dtype=torch.float16)
+        row_scale = torch.empty((M,), device=x.device, dtype=torch.float32)
+        call("tbf16_conv_im2col", ptr(xs), ptr(geom), K, Kp, ptr(e), ptr(scale), ptr(cols), ptr(row_scale),
+             stream_ptr(x.device))
+        if O % 8:  # the GEMM writes 16-byte output rows: pad the channels and slice them off
+            Op = (O + 7) // 8 * 8
+            y = _gemm_f16(cols, 0, F.pad(wk16, (0, 0, 0, Op - O)), 0, M, Op, Kp, row_scale,
+                          F.pad(ws, (0, Op - O), value=1.0), None if b is None else F.pad(b, (0, Op - O)))[:, :O]
+        else:
+            y = _gemm_f16(cols, 0, wk16, 0, M, O, Kp, row_scale, ws, b)
+        # [B, Do, Ho, Wo, O] rows -> (B, O, *spatial) with channels-last strides
+        y = y.reshape((B,) + tuple(out[3 - nd:]) + (O,))
+        return y.movedim(-1, 1)
+    y = torch.empty(out_shape, device=x.device, dtype=torch.bfloat16)
+    call("tbf16_conv_grouped", ptr(xs), ptr(geom), O, groups, ptr(weight16.contiguous()), ptr(ws), ptr(b), ptr(e),
+         ptr(scale), ptr(y), stream_ptr(x.device))
+    return y
+
+
+def _scaled_conv_forward(self, x, weight, bias):
+    # `weight` is the (removed) bf16 parameter, i.e. None; the fp16 copy lives in weight16.
+    if x.dtype != torch.bfloat16 or (torch.is_grad_enabled() and x.requires_grad):
+        bias = None if bias is None else bias.to(x.dtype)
+        return self._native_conv_forward(x, self.dequantized_weight().to(x.dtype), bias)
+    O = self.out_channels
+    if self._tbf16_pointwise:
+        return scaled_linear(x.movedim(1, -1), self.weight16.view(O, -1), self.weight_scale, bias).movedim(-1, 1)
+    if self.padding_mode != "zeros":
+        x = F.pad(x, self._reversed_padding_repeated_twice, mode=self.padding_mode)
+        padding = 0
+    else:
+        padding = self.padding
+    if isinstance(padding, str):
+        if padding == "valid":
+            padding = 0
+        else:  # "same" (stride 1): an odd total pads its extra element at the end, as torch does
+            tot = [d * (k - 1) for d, k in zip(self.dilation, self.kernel_size)]
+            if any(t % 2 for t in tot):
+                x = F.pad(x, [p for t in reversed(tot) for p in (0, t % 2)])
+            padding = tuple(t // 2 for t in tot)
+    return scaled_conv(x, self.weight16, self.weight_scale, bias, self.stride, padding, self.dilation, self.groups,
+                       self._tbf16_target_exp, getattr(self, "_tbf16_wk16", None))
+
+
+def _dequantized_weight(self):
+    w = self.weight16.float() * self.weight_scale.view((-1,) + (1,) * (self.weight16.dim() - 1))
+    return w.bfloat16()
+
+
+_classes = {}
+
+
+def _scaled_class(cls):
+    if cls not in _classes:
+        _classes[cls] = type(f"TBF16{cls.__name__}", (cls,), {
+            "_native_conv_forward": cls._conv_forward,
+            "_conv_forward": _scaled_conv_forward,
+            "dequantized_weight": _dequantized_weight,
+        })
+    return _classes[cls]
+
+
+def convertible(m: nn.Module) -> bool:
+    return (isinstance(m, (nn.Conv1d, nn.Conv2d, nn.Conv3d)) and type(m) not in _classes.values()
+            and isinstance(m.weight, torch.Tensor) and m.weight.dtype == torch.bfloat16 and m.weight.is_cuda)
+
+
+def convert_conv(conv: nn.Module):
+    """Convert one bf16 nn.Conv{1,2,3}d (or subclass) in place. Subclass forwards keep working: only
+    _conv_forward is replaced. `.weight` becomes None; use .dequantized_weight()."""
+    w = conv.weight.data
+    O = w.shape[0]
+    K = w[0].numel()
+    t = _target_exp(K)
+    w16, ws = prepare_weight(w.reshape(O, K))  # [O, K rounded up to 8]
+    del conv._parameters["weight"]
+    conv.register_parameter("weight", None)
+    conv.register_buffer("weight16", w16[:, :K].contiguous().view_as(w))
+    conv.register_buffer("weight_scale", ws)
+    if conv.groups == 1:  # the GEMM's [O, K] rows, zero-padded to a multiple of 8 (shared when K is one)
+        conv.register_buffer("_tbf16_wk16", conv.weight16.view(O, K) if K % 8 == 0 else w16, persistent=False)
+    conv._tbf16_target_exp = t
+    no_pad = conv.padding == "valid" or not isinstance(conv.padding, str) and all(p == 0 for p in conv.padding)
+    conv._tbf16_pointwise = (all(k == 1 for k in conv.kernel_size) and all(s == 1 for s in conv.stride) and no_pad
+                             and conv.groups == 1)
+    conv.__class__ = _scaled_class(type(conv))
+    return conv

@@ -11,9 +11,8 @@ nn.Linear subclass with the same parameters) whose forward and backward run on t
 Both route F.scaled_dot_product_attention to the scaled attention for bf16 inputs.
 
 Differences from the reference: the reference applies only to GPUs without bf16 tensor cores
-(Volta/Turing); this build targets B200, so is_supported_gpu() is true on sm_100. Scaled
-convolutions (the reference's conv.py) are not part of this build: conv=True leaves convolutions
-native.
+(Volta/Turing); this build targets B200, so is_supported_gpu() is true on sm_100. With conv=True,
+bf16 Conv1d/2d/3d run on the scaled convolutions of tbf16.conv (inference only), as in the reference.
 """
 import os
 import warnings
@@ -24,6 +23,7 @@ import torch.nn.functional as F
 
 from . import autograd
 from .attention import sdpa
+from .conv import convert_conv, convertible
 from .ops import prepare_weight, scaled_linear
 
 # Train mode: linear layers with in or out features below this run in fp32 (reference convert.py:27).
@@ -121,7 +121,7 @@ def is_supported_gpu(device=None) -> bool:
 def convert(model, train: bool = False, sdpa: bool = True, force: bool = False, conv: bool = True):
     """Convert in place and return the model (an nn.Module or a pipeline with a `components` dict).
     A no-op (with a warning) on GPUs this build does not target, unless force=True.
-    conv: accepted for API compatibility; convolutions stay native in this build."""
+    conv: also convert bf16 Conv1d/2d/3d (inference only)."""
     if not force and not is_supported_gpu():
         warnings.warn("tbf16.convert: this build's kernels need an sm_100 (B200) GPU; leaving the model unchanged. "
                       "Pass force=True to convert anyway.")
@@ -152,6 +152,8 @@ def convert(model, train: bool = False, sdpa: bool = True, force: bool = False, 
                     and owners[id(child.weight)] == 1):
                 setattr(mod, cname, Linear(child))
                 child.weight = None  # free the bf16 copy now, not when convert() returns
+            elif conv and convertible(child) and owners[id(child.weight)] == 1:
+                convert_conv(child)
     if torch.cuda.is_available():
         torch.cuda.empty_cache()
     if sdpa:
