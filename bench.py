@@ -187,6 +187,7 @@ def main():
                     help="config-2 GEMM sweep (M = 1 .. 16384 at N = K = 4096 and 8192, L2 flushed) and the "
                          "config-4 MLP linears fwd+bwd; prints one JSON line and exits")
     ap.add_argument("--no-train-linear", action="store_true", help="skip the config-4 MLP linear fwd+bwd")
+    ap.add_argument("--no-conv", action="store_true", help="skip the scaled-convolution timing")
     ap.add_argument("--only-train-linear", action="store_true",
                     help="only time the config-4 MLP linears forward + backward (their profiling case)")
     ap.add_argument("--profile-linear", type=int, default=0, metavar="M",
@@ -335,6 +336,8 @@ def main():
     if not args.no_prefill:
         torch.cuda.empty_cache()
         line["prefill"] = prefill_run(world)  # every rank runs its own sequence (replicas)
+    if not args.no_conv:
+        line["conv"] = conv_run(pk)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
@@ -527,6 +530,36 @@ def sweep_run(pk, iters=7):
         del w16, ws
     del flush
     return rows
+
+
+def conv_run(pk, iters=5):
+    """Scaled convolutions (tbf16.conv) on VAE-decoder-shaped layers: 3x3, 512 -> 512 channels at 128 x 128
+    and 256 -> 256 at 256 x 256 (batch 1, channels-last bf16 input), through a converted nn.Conv2d; the
+    native bf16 cuDNN convolution of the same layer beside it (informational). 2 * O * C * 9 * Ho * Wo flop."""
+    import copy
+    from tbf16.conv import convert_conv
+    res = []
+    for C, HW in ((512, 128), (256, 256)):
+        conv = torch.nn.Conv2d(C, C, 3, padding=1).cuda().bfloat16()
+        x = torch.randn(1, C, HW, HW, device="cuda").bfloat16().to(memory_format=torch.channels_last)
+        tc = convert_conv(copy.deepcopy(conv))
+        flop = 2.0 * C * C * 9 * HW * HW
+        row = {"shape": f"1x{C}x{HW}x{HW}, 3x3, {C} -> {C}"}
+        for name, mod in (("tbf16", tc), ("native_bf16_cudnn", conv)):
+            with torch.no_grad():
+                for _ in range(2):
+                    mod(x)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    mod(x)
+                e1.record()
+                torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            row[name] = {"ms": round(ms, 3), "tflops": round(flop / ms / 1e9, 1)}
+        res.append(row)
+    return res
 
 
 def profile_linear_run(M, N, K, steps, warmup, copies=4):

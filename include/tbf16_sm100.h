@@ -211,6 +211,13 @@ int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int
 int tbf16_conv_im2col(const void* x, const int64_t* geom, int64_t K, int64_t Kp, const int32_t* e,
                       const float* out_scale, void* cols16, float* row_scale, void* stream);
 
+/* The same for C a multiple of 8, in two passes of 16-byte vectors: x16cl fp16 [B, D, H, W, C]
+ * (channels-last, fp16(x * 2^-e[b])), then cols16 [B Do Ho Wo, taps C] with column tap * C + c, tap =
+ * (z kh + y) kw + x -- so the weight rows for this path are the weight permuted to [O, kd, kh, kw, C].
+ * TBF16_ERR_UNSUPPORTED when C % 8 != 0. */
+int tbf16_conv_im2col_cl(const void* x, const int64_t* geom, const int32_t* e, const float* out_scale, void* x16cl,
+                         void* cols16, float* row_scale, void* stream);
+
 /* groups > 1 (grouped and depthwise): direct convolution into y bf16 [B, O, Do, Ho, Wo] contiguous; w16
  * fp16 [O, C / groups, kd, kh, kw] contiguous, ws fp32 [O], bias bf16 [O] nullable. */
 int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t groups, const void* w16, const float* ws,

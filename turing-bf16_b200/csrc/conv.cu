@@ -9,10 +9,11 @@
 //
 // groups == 1: im2col into fp16 rows (one row per output position, K = C kd kh kw columns zero-padded
 // to a multiple of 8, each row carrying its sample's output scale) and the tcgen05 GEMM against the
-// [O, K] weight rows; the output comes out channels-last. groups > 1 (depthwise and grouped convs, a few
+// [O, K] weight rows; the output comes out channels-last. For C a multiple of 8 the rows are built from a
+// scaled channels-last fp16 copy of the input by 16-byte copies, columns in (tap, channel) order. groups > 1 (depthwise and grouped convs, a few
 // input channels per output): a direct kernel, one thread per output element. The reference ends in a
 // cuDNN fp16 conv whose output is rounded to fp16 before the scales; here the fp32 sum is scaled and
-// rounded to bf16 once. Geometry is passed as an array of int64 (see TBF16_CONV_GEOM_* in the header).
+// rounded to bf16 once. Geometry is passed as an array of int64 (TBF16_CONV_GEOM_LEN values, order in the header).
 #include "common.cuh"
 
 using namespace tbf16;
@@ -44,14 +45,39 @@ __device__ __forceinline__ float scale_pow2(float v, int e) {
   return (v * exp2i(h)) * exp2i(ne - h);
 }
 
-// Per-sample max |x| over n dense elements of each sample (samples ld apart), merged with atomicMax.
+// Per-sample max |x| over n dense elements of each sample (samples ld apart), merged with atomicMax:
+// 16-byte loads when the sample is 16-byte aligned and n a multiple of 8, four of them in flight.
 __global__ void __launch_bounds__(256) sample_amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, int64_t ld,
-                                                          float* __restrict__ amax) {
+                                                          int vec, float* __restrict__ amax) {
   const int64_t b = blockIdx.y;
   const __nv_bfloat16* xs = x + b * ld;
   float m = 0.f;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    m = fmaxf(m, fabsf(__bfloat162float(xs[i])));
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const uint4* xv = reinterpret_cast<const uint4*>(xs);
+    const int64_t n8 = n / 8;
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n8; i += 4 * stride) {
+      uint4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = __ldg(xv + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(fabsf(bf16lo(w[j])), fabsf(bf16hi(w[j]))));
+      }
+    }
+    for (; i < n8; i += stride) {
+      const uint4 q = __ldg(xv + i);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(fabsf(bf16lo(w[j])), fabsf(bf16hi(w[j]))));
+    }
+  } else {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+      m = fmaxf(m, fabsf(__bfloat162float(xs[i])));
+  }
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(amax) + b, __float_as_int(m));
 }
@@ -105,6 +131,71 @@ __global__ void __launch_bounds__(256) im2col_kernel(const __nv_bfloat16* __rest
     }
     cols[i] = make_uint4(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
     if (j == 0) row_scale[m] = out_scale[b];
+  }
+}
+
+// Fast path for C % 8 == 0, in two passes. (1) x16cl[b, d, h, w, c] = fp16(x * 2^-e[b]) channels-last,
+// 8 channels per thread (one 16-byte store). A channels-last input is read as the same flat array (one
+// 16-byte load, the sample from one division); any other layout is gathered element by element.
+__global__ void __launch_bounds__(256) scale_cl_kernel(const __nv_bfloat16* __restrict__ xin, const Geom g,
+                                                       const int32_t* __restrict__ e, uint4* __restrict__ x16cl,
+                                                       int flat) {
+  const int C8 = (int)(g.C / 8);
+  const int64_t per_sample = g.D * g.H * g.W * C8;
+  const int64_t total = g.B * per_sample;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / per_sample;
+    const int eb = e[b];
+    float v[8];
+    if (flat) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(xin + b * g.sb) + (i - b * per_sample));
+      v[0] = bf16lo(q.x); v[1] = bf16hi(q.x); v[2] = bf16lo(q.y); v[3] = bf16hi(q.y);
+      v[4] = bf16lo(q.z); v[5] = bf16hi(q.z); v[6] = bf16lo(q.w); v[7] = bf16hi(q.w);
+    } else {
+      const int c8 = (int)(i % C8);
+      int64_t r = i / C8;
+      const int64_t w = r % g.W; r /= g.W;
+      const int64_t h = r % g.H; r /= g.H;
+      const int64_t d = r % g.D;
+      const __nv_bfloat16* src = xin + b * g.sb + d * g.sd + h * g.sh + w * g.sw + (int64_t)c8 * 8 * g.sc;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __bfloat162float(src[u * g.sc]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = scale_pow2(v[u], eb);
+    x16cl[i] = make_uint4(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
+  }
+}
+
+// (2) cols16[m, tap * C + c] = x16cl at the tap's input position (zero in the padding): one warp per
+// output position (its coordinates decoded once), the lanes copying each tap's C / 8 16-byte chunks
+// (coalesced on both sides) -- taps ordered (z, y, x), channels fastest, as the weight rows prepared
+// for this path.
+__global__ void __launch_bounds__(256) im2col_cl_kernel(const uint4* __restrict__ x16cl, const Geom g,
+                                                        const float* __restrict__ out_scale, uint4* __restrict__ cols,
+                                                        float* __restrict__ row_scale) {
+  const int C8 = (int)(g.C / 8);
+  const int kh = (int)g.kh, kw = (int)g.kw, taps = (int)(g.kd * g.kh * g.kw);
+  const int lane = threadIdx.x & 31;
+  const int64_t M = g.B * g.Do * g.Ho * g.Wo;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t m = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
+    int64_t r = m;
+    const int64_t ow = r % g.Wo; r /= g.Wo;
+    const int64_t oh = r % g.Ho; r /= g.Ho;
+    const int64_t od = r % g.Do;
+    const int64_t b = r / g.Do;
+    const int64_t d0 = od * g.std_ - g.pd, h0 = oh * g.sth - g.ph, w0 = ow * g.stw - g.pw;
+    const uint4* xb = x16cl + b * g.D * g.H * g.W * C8;
+    uint4* row = cols + m * (int64_t)taps * C8;
+    for (int tap = 0; tap < taps; ++tap) {
+      const int z = tap / (kh * kw), yx = tap - z * kh * kw, yy = yx / kw, xx = yx - yy * kw;
+      const int64_t id = d0 + z * g.dd, ih = h0 + yy * g.dh, iw = w0 + xx * g.dw;
+      const bool in = id >= 0 && id < g.D && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
+      const uint4* src = xb + ((id * g.H + ih) * g.W + iw) * C8;
+      for (int c8 = lane; c8 < C8; c8 += 32) row[tap * C8 + c8] = in ? __ldg(src + c8) : make_uint4(0, 0, 0, 0);
+    }
+    if (lane == 0) row_scale[m] = out_scale[b];
   }
 }
 
@@ -184,9 +275,13 @@ int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int
   auto st = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(amax_ws, 0, sizeof(float) * B, st) != cudaSuccess) return TBF16_ERR_LAUNCH;
   if (n > 0) {
-    const int64_t per = (n + 255) / 256;
-    const unsigned gx = (unsigned)(per < 64 ? per : 64);
-    sample_amax_kernel<<<dim3(gx, (unsigned)B), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, ld, amax_ws);
+    // about four blocks per SM in all, each thread with a few 16-byte loads in flight
+    const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+    const int64_t want = ((int64_t)(d ? d->sms : 148) * 4 + B - 1) / B;
+    const int64_t per = (n / 8 + 1023) / 1024;
+    const unsigned gx = (unsigned)(per < 1 ? 1 : (per < want ? per : want));
+    const int vec = n % 8 == 0 && ld % 8 == 0 && tbf16_host::aligned16(x);
+    sample_amax_kernel<<<dim3(gx, (unsigned)B), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, ld, vec, amax_ws);
   }
   sample_exp_kernel<<<(unsigned)((B + 255) / 256), 256, 0, st>>>(amax_ws, B, target_exp, e, out_scale);
   return tbf16_host::check_launch();
@@ -203,6 +298,30 @@ int tbf16_conv_im2col(const void* x, const int64_t* geom, int64_t K, int64_t Kp,
   if (M == 0) return TBF16_OK;
   im2col_kernel<<<grid_for(M * (Kp / 8)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), g, K, Kp, e, out_scale, static_cast<uint4*>(cols16), row_scale);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_conv_im2col_cl(const void* x, const int64_t* geom, const int32_t* e, const float* out_scale, void* x16cl,
+                         void* cols16, float* row_scale, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (!x || !geom || !e || !out_scale || !x16cl || !cols16 || !row_scale) return TBF16_ERR_INVALID;
+  const Geom g = load_geom(geom);
+  if (!geom_ok(g)) return TBF16_ERR_INVALID;
+  if (g.C % 8) return TBF16_ERR_UNSUPPORTED;
+  if (!tbf16_host::aligned16(x16cl) || !tbf16_host::aligned16(cols16)) return TBF16_ERR_ALIGN;
+  const int64_t M = g.B * g.Do * g.Ho * g.Wo;
+  if (M == 0) return TBF16_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  // the input is one flat channels-last array per sample when its strides say so (and 16-byte aligned)
+  const int flat = g.sc == 1 && g.sw == g.C && g.sh == g.W * g.C && g.sd == g.H * g.W * g.C &&
+                   (g.B == 1 || g.sb % 8 == 0) && tbf16_host::aligned16(x);
+  scale_cl_kernel<<<grid_for(g.B * g.D * g.H * g.W * (g.C / 8)), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), g,
+                                                                             e, static_cast<uint4*>(x16cl), flat);
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  const int64_t want = (int64_t)(d ? d->sms : 148) * 16, need = (M + 7) / 8;  // 8 output positions per block
+  const int64_t blocks = need < want ? need : want;
+  im2col_cl_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint4*>(x16cl), g, out_scale,
+                                                     static_cast<uint4*>(cols16), row_scale);
   return tbf16_host::check_launch();
 }
 

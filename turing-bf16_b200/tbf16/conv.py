@@ -8,7 +8,9 @@ convertible(m), convert_conv(conv) (in place, class swap so subclass forwards ke
 
 Routing: 1x1 convolutions (stride 1, no padding, one group) are per-pixel linear layers and go through
 scaled_linear, as in the reference; other convolutions with one group become an im2col into fp16 rows
-plus the tcgen05 GEMM (output channels-last); grouped and depthwise convolutions run a direct kernel.
+plus the tcgen05 GEMM (output channels-last) -- for input channels in multiples of 8 through a scaled
+channels-last fp16 copy and 16-byte tap copies, with the weight rows in (taps, channels) order; grouped
+and depthwise convolutions run a direct kernel.
 The reference ends in a cuDNN fp16 convolution whose output is rounded to fp16 before the scales are
 applied; here the fp32 sum is scaled and rounded to bf16 once.
 """
@@ -53,10 +55,16 @@ def _dense(x):
     return x.contiguous()
 
 
-def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, groups, target_exp, wk16=None):
+def _taps_last(weight16):
+    """The weight as [O, taps * C] rows with the channels fastest, for the channels-last im2col."""
+    return weight16.movedim(1, -1).reshape(weight16.shape[0], -1).contiguous()
+
+
+def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, groups, target_exp, wk16=None, wcl16=None):
     """The scaled convolution of a bf16 input with a prepared weight (weight16 fp16 [O, C/groups, *k],
     weight_scale fp32 [O]); zero padding only (other padding modes are applied by the caller). wk16: the
-    weight as [O, K] rows padded to a multiple of 8 (made on the fly when None)."""
+    weight as [O, K] rows padded to a multiple of 8; wcl16: as [O, taps * C] rows (channels fastest) for
+    C a multiple of 8; each made on the fly when None."""
     require_cuda(x, weight16, weight_scale)
     nd = x.dim() - 2
     x = _dense(x)
@@ -75,16 +83,24 @@ def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, grou
     out_shape = (B, O) + tuple(out[3 - nd:])
     if groups == 1:
         K = weight16[0].numel()
-        Kp = (K + 7) // 8 * 8
-        if wk16 is None:
-            wk16 = weight16.reshape(O, K)
-            if Kp != K:
-                wk16 = F.pad(wk16, (0, Kp - K))
         M = B * out[0] * out[1] * out[2]
-        cols = torch.empty((M, Kp), device=x.device, dtype=torch.float16)
         row_scale = torch.empty((M,), device=x.device, dtype=torch.float32)
-        call("tbf16_conv_im2col", ptr(xs), ptr(geom), K, Kp, ptr(e), ptr(scale), ptr(cols), ptr(row_scale),
-             stream_ptr(x.device))
+        if C % 8 == 0:  # channels-last fp16 copy, then 16-byte tap copies (taps x channels columns)
+            Kp = K
+            wk16 = _taps_last(weight16) if wcl16 is None else wcl16
+            x16cl = torch.empty((B, D, H, W, C), device=x.device, dtype=torch.float16)
+            cols = torch.empty((M, Kp), device=x.device, dtype=torch.float16)
+            call("tbf16_conv_im2col_cl", ptr(xs), ptr(geom), ptr(e), ptr(scale), ptr(x16cl), ptr(cols), ptr(row_scale),
+                 stream_ptr(x.device))
+        else:
+            Kp = (K + 7) // 8 * 8
+            if wk16 is None:
+                wk16 = weight16.reshape(O, K)
+                if Kp != K:
+                    wk16 = F.pad(wk16, (0, Kp - K))
+            cols = torch.empty((M, Kp), device=x.device, dtype=torch.float16)
+            call("tbf16_conv_im2col", ptr(xs), ptr(geom), K, Kp, ptr(e), ptr(scale), ptr(cols), ptr(row_scale),
+                 stream_ptr(x.device))
         if O % 8:  # the GEMM writes 16-byte output rows: pad the channels and slice them off
             Op = (O + 7) // 8 * 8
             y = _gemm_f16(cols, 0, F.pad(wk16, (0, 0, 0, Op - O)), 0, M, Op, Kp, row_scale,
@@ -122,7 +138,7 @@ def _scaled_conv_forward(self, x, weight, bias):
                 x = F.pad(x, [p for t in reversed(tot) for p in (0, t % 2)])
             padding = tuple(t // 2 for t in tot)
     return scaled_conv(x, self.weight16, self.weight_scale, bias, self.stride, padding, self.dilation, self.groups,
-                       self._tbf16_target_exp, getattr(self, "_tbf16_wk16", None))
+                       self._tbf16_target_exp, getattr(self, "_tbf16_wk16", None), getattr(self, "_tbf16_wcl16", None))
 
 
 def _dequantized_weight(self):
@@ -160,7 +176,9 @@ def convert_conv(conv: nn.Module):
     conv.register_parameter("weight", None)
     conv.register_buffer("weight16", w16[:, :K].contiguous().view_as(w))
     conv.register_buffer("weight_scale", ws)
-    if conv.groups == 1:  # the GEMM's [O, K] rows, zero-padded to a multiple of 8 (shared when K is one)
+    if conv.groups == 1 and w.shape[1] % 8 == 0:  # the GEMM's rows for the channels-last im2col
+        conv.register_buffer("_tbf16_wcl16", _taps_last(conv.weight16), persistent=False)
+    elif conv.groups == 1:  # the GEMM's [O, K] rows, zero-padded to a multiple of 8 (shared when K is one)
         conv.register_buffer("_tbf16_wk16", conv.weight16.view(O, K) if K % 8 == 0 else w16, persistent=False)
     conv._tbf16_target_exp = t
     no_pad = conv.padding == "valid" or not isinstance(conv.padding, str) and all(p == 0 for p in conv.padding)
