@@ -188,6 +188,7 @@ def main():
                          "config-4 MLP linears fwd+bwd; prints one JSON line and exits")
     ap.add_argument("--no-train-linear", action="store_true", help="skip the config-4 MLP linear fwd+bwd")
     ap.add_argument("--no-conv", action="store_true", help="skip the scaled-convolution timing")
+    ap.add_argument("--only-prefill", action="store_true", help="only the config-5 Gemma-shaped prefill")
     ap.add_argument("--only-train-linear", action="store_true",
                     help="only time the config-4 MLP linears forward + backward (their profiling case)")
     ap.add_argument("--profile-linear", type=int, default=0, metavar="M",
@@ -207,6 +208,9 @@ def main():
     if args.only_attention:
         print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
                                                      train=args.attn_train)}))
+        return
+    if args.only_prefill:
+        print(json.dumps({"prefill": prefill_run(world)}))
         return
     if args.only_train_linear:
         print(json.dumps({"train_linear": train_linear_run(peaks(), iters=max(1, args.steps))}))
@@ -390,17 +394,23 @@ class _GemmaLayer(torch.nn.Module):
         from tbf16 import ops
         return ops.rmsnorm_rows(x, norm.weight, 1e-6, 1.0, "gemma")
 
+    def _norm(self, x, norm):  # norms that feed no linear
+        if not self.fused:
+            return norm(x)
+        from tbf16 import ops
+        return ops.rmsnorm(x, norm.weight, 1e-6, 1.0, "gemma")
+
     def forward(self, x, cos, sin):
         import torch.nn.functional as F
         B, S, _ = x.shape
         h = self._norm_rows(x, self.in_norm)
-        q = self.q_norm(self._proj(h, self.q_proj).view(B, S, self.h, self.d)).transpose(1, 2)
-        k = self.k_norm(self._proj(h, self.k_proj).view(B, S, self.kv, self.d)).transpose(1, 2)
+        q = self._norm(self._proj(h, self.q_proj).view(B, S, self.h, self.d), self.q_norm).transpose(1, 2)
+        k = self._norm(self._proj(h, self.k_proj).view(B, S, self.kv, self.d), self.k_norm).transpose(1, 2)
         v = self._proj(h, self.v_proj).view(B, S, self.kv, self.d).transpose(1, 2)
         rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
         q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
-        x = x + self.post_attn_norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)))
+        x = x + self._norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)), self.post_attn_norm)
         h = self._norm_rows(x, self.pre_ff_norm)
         gate, up = self._proj(h, self.gate_proj), self._proj(h, self.up_proj)
         if self.fused:
@@ -408,7 +418,7 @@ class _GemmaLayer(torch.nn.Module):
             y = ops.glu_linear(gate, up, self.down_proj.weight16, self.down_proj.weight_scale, act="gelu_tanh")
         else:
             y = self.down_proj(F.gelu(gate, approximate="tanh") * up)
-        return x + self.post_ff_norm(y)
+        return x + self._norm(y, self.post_ff_norm)
 
 
 def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
@@ -440,11 +450,14 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
 
     @torch.no_grad()
     def step():
+        torch.cuda.nvtx.range_push("prefill_fused" if model[0].fused else "prefill")  # ncu --nvtx-include
         x = embed(ids) * (hidden ** 0.5)
         x = x + outlier * 1e5
         for layer in model:
             x = layer(x, cos, sin)
-        return final_norm(x[:, -1]) @ embed.weight.t()
+        out = final_norm(x[:, -1]) @ embed.weight.t()
+        torch.cuda.nvtx.range_pop()
+        return out
 
     for _ in range(2):
         logits = step()
@@ -484,7 +497,8 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
             "tflops_per_gpu": round(flop / (ms / 1e3) / 1e12, 1), "finite_logits": finite,
             "fused": {"ms_per_prefill": round(ms_f, 2), "tflops_per_gpu": round(flop / (ms_f / 1e3) / 1e12, 1),
                       "logits_rel_diff_vs_unfused": round(drift, 5),
-                      "what": "RMSNorm before q/k/v and gate/up, and GeGLU before down, fused with the row scales"}}
+                      "what": ("RMSNorm before q/k/v and gate/up, and GeGLU before down, fused with the row "
+                               "scales; the other RMSNorms (q/k heads, after attention and MLP) on the same kernel")}}
 
 
 def dist_rank():

@@ -180,8 +180,8 @@ int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64
 /* RMSNorm: ms[m] = mean_k x[m, k]^2 (fp32), rs = rsqrt(ms + eps) and
  *   style TBF16_NORM_SCALE_FP32: r[m, k] = bf16_rn((x[m, k] * rs) * (w[k] + offset))   (Gemma: offset 1)
  *   style TBF16_NORM_SCALE_BF16: r[m, k] = bf16_rn(w[k] * bf16_rn(x[m, k] * rs))        (Llama: offset unused)
- * then s_inv and y16 of r as tbf16_glu_rows; r also written to r_out when non-null. x bf16 [M, K] (ldx),
- * w bf16 [K]. */
+ * then s_inv and y16 of r as tbf16_glu_rows; r also written to r_out when non-null. With y16 NULL (and
+ * r_out given) it is a plain RMSNorm for norms that feed no linear. x bf16 [M, K] (ldx), w bf16 [K]. */
 #define TBF16_NORM_SCALE_FP32 0
 #define TBF16_NORM_SCALE_BF16 1
 int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps, int style,

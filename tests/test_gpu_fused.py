@@ -64,6 +64,17 @@ def test_rmsnorm_rows(style, offset, M, K):
     assert torch.equal(r16.view(torch.int16), orc.f16_rn(r.float() / s_inv[:, None]).view(torch.int16))
 
 
+def test_plain_rmsnorm_matches_rmsnorm_rows():
+    """ops.rmsnorm (no fp16 operand written) gives the same bf16 rows as rmsnorm_rows."""
+    from tbf16 import ops
+    x = (torch.randn(3, 5, 256, generator=torch.Generator().manual_seed(9)) * 7).bfloat16().cuda()
+    w = (torch.randn(256, generator=torch.Generator().manual_seed(10)) * 0.1).bfloat16().cuda()
+    for style, offset in (("gemma", 1.0), ("llama", 0.0)):
+        r = ops.rmsnorm(x, w, 1e-6, offset, style)
+        _, _, r2 = ops.rmsnorm_rows(x, w, 1e-6, offset, style, want_r=True)
+        assert r.shape == x.shape and torch.equal(r.view(torch.int16), r2.view(torch.int16))
+
+
 @pytest.mark.parametrize("M", [3, 40, 600])
 def test_fused_linears_equal_scaled_linear(M):
     """glu_linear / rmsnorm_linear give scaled_linear's bits on the rows the producer wrote (GEMV up to 4

@@ -58,16 +58,18 @@ __device__ __forceinline__ void emit_row(const uint4 (&v)[NCH], float amax, int 
   for (int u = 0; u < NCH; ++u) {
     const int i = threadIdx.x + kThreads * u;
     if (i < K8) {
-      uint4 o;
-      o.x = pack_f16(bf16lo(v[u].x) * sc, bf16hi(v[u].x) * sc);
-      o.y = pack_f16(bf16lo(v[u].y) * sc, bf16hi(v[u].y) * sc);
-      o.z = pack_f16(bf16lo(v[u].z) * sc, bf16hi(v[u].z) * sc);
-      o.w = pack_f16(bf16lo(v[u].w) * sc, bf16hi(v[u].w) * sc);
-      y16[row * ldy8 + i] = o;
+      if (y16) {
+        uint4 o;
+        o.x = pack_f16(bf16lo(v[u].x) * sc, bf16hi(v[u].x) * sc);
+        o.y = pack_f16(bf16lo(v[u].y) * sc, bf16hi(v[u].y) * sc);
+        o.z = pack_f16(bf16lo(v[u].z) * sc, bf16hi(v[u].z) * sc);
+        o.w = pack_f16(bf16lo(v[u].w) * sc, bf16hi(v[u].w) * sc);
+        y16[row * ldy8 + i] = o;
+      }
       if (out) out[row * ldo8 + i] = v[u];
     }
   }
-  if (threadIdx.x == 0) s_inv[row] = inv_pow2_from_biased(se);
+  if (threadIdx.x == 0 && y16) s_inv[row] = inv_pow2_from_biased(se);
 }
 
 template <int NCH, int ACT>
@@ -218,11 +220,12 @@ int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int
                        float offset, int target_exp, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo,
                        void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
-  if (M < 0 || K < 0 || ldx < K || ldy < K || (r_out && ldo < K) || !s_inv || !y16 || !x || !w || !(eps >= 0.f) ||
+  if (M < 0 || K < 0 || ldx < K || (y16 && ldy < K) || (r_out && ldo < K) || (y16 && !s_inv) || (!y16 && !r_out) ||
+      !x || !w || !(eps >= 0.f) ||
       target_exp < 0 || target_exp > 64 || (style != TBF16_NORM_SCALE_FP32 && style != TBF16_NORM_SCALE_BF16))
     return TBF16_ERR_INVALID;
-  if (K % 8 || ldx % 8 || ldy % 8 || (r_out && ldo % 8) || !tbf16_host::aligned16(x) || !tbf16_host::aligned16(w) ||
-      !tbf16_host::aligned16(y16) || (r_out && !tbf16_host::aligned16(r_out)))
+  if (K % 8 || ldx % 8 || (y16 && ldy % 8) || (r_out && ldo % 8) || !tbf16_host::aligned16(x) ||
+      !tbf16_host::aligned16(w) || (y16 && !tbf16_host::aligned16(y16)) || (r_out && !tbf16_host::aligned16(r_out)))
     return TBF16_ERR_ALIGN;
   if (M == 0 || K == 0) return TBF16_OK;
   const int64_t K8 = K / 8;

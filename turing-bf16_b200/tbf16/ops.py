@@ -387,6 +387,24 @@ def rmsnorm_rows(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offse
     return out + (r.reshape(x.shape),) if want_r else out
 
 
+@torch.autocast("cuda", enabled=False)
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offset: float = 1.0, style: str = "gemma"):
+    """Plain RMSNorm (bf16 in and out) on the rmsnorm_rows kernel, for norms that feed no linear: one read
+    of x, one write of the result, the same roundings as rmsnorm_rows."""
+    require_cuda(x, weight)
+    if style not in _NORM_STYLES:
+        raise RuntimeError(f"tbf16.rmsnorm: style must be one of {sorted(_NORM_STYLES)}")
+    x2 = _rows2d(x, "rmsnorm")
+    M, K = x2.shape
+    w = weight.to(torch.bfloat16).contiguous()
+    if w.numel() != K or K % 8:
+        raise RuntimeError("tbf16.rmsnorm: weight must have the row length, a multiple of 8")
+    r = torch.empty((M, K), device=x.device, dtype=torch.bfloat16)
+    call("tbf16_rmsnorm_rows", ptr(x2), x2.stride(0), ptr(w), M, K, float(eps), _NORM_STYLES[style], float(offset), 15,
+         None, 0, None, ptr(r), K, stream_ptr(x.device))
+    return r.reshape(x.shape)
+
+
 def _linear_from_rows(q16, s_inv, bf16_rows, w16, w_sinv, bias, lead_shape):
     """The down projection of an already row-scaled operand: the same kernels and arithmetic as
     scaled_linear on the bf16 rows (GEMV semantics up to GEMV_ROWS rows, which need the bf16 rows)."""
@@ -427,5 +445,5 @@ def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bi
 
 
 __all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
-           "linear_host", "glu_rows", "rmsnorm_rows", "glu_linear", "rmsnorm_linear",
+           "linear_host", "glu_rows", "rmsnorm_rows", "glu_linear", "rmsnorm_linear", "rmsnorm",
            "available", "_target_exp"]
