@@ -189,6 +189,7 @@ def main():
     ap.add_argument("--no-train-linear", action="store_true", help="skip the config-4 MLP linear fwd+bwd")
     ap.add_argument("--no-conv", action="store_true", help="skip the scaled-convolution timing")
     ap.add_argument("--only-prefill", action="store_true", help="only the config-5 Gemma-shaped prefill")
+    ap.add_argument("--only-conv", action="store_true", help="only the scaled-convolution timing")
     ap.add_argument("--only-train-linear", action="store_true",
                     help="only time the config-4 MLP linears forward + backward (their profiling case)")
     ap.add_argument("--profile-linear", type=int, default=0, metavar="M",
@@ -214,6 +215,9 @@ def main():
         return
     if args.only_train_linear:
         print(json.dumps({"train_linear": train_linear_run(peaks(), iters=max(1, args.steps))}))
+        return
+    if args.only_conv:
+        print(json.dumps({"conv": conv_run(peaks(), iters=max(1, args.steps))}))
         return
     if args.profile_linear:
         print(json.dumps({"profile_linear": profile_linear_run(args.profile_linear, N, K, args.steps, args.warmup)}))
@@ -548,10 +552,12 @@ def sweep_run(pk, iters=7):
 
 def conv_run(pk, iters=5):
     """Scaled convolutions (tbf16.conv) on VAE-decoder-shaped layers: 3x3, 512 -> 512 channels at 128 x 128
-    and 256 -> 256 at 256 x 256 (batch 1, channels-last bf16 input), through a converted nn.Conv2d; the
-    native bf16 cuDNN convolution of the same layer beside it (informational). 2 * O * C * 9 * Ho * Wo flop."""
+    and 256 -> 256 at 256 x 256 (batch 1, channels-last bf16 input), through a converted nn.Conv2d (the
+    implicit GEMM); the same layer on the im2col path and the native bf16 cuDNN convolution beside it
+    (informational). 2 * O * C * 9 * Ho * Wo flop. `ms` from CUDA-graph replays (device time), `eager_ms`
+    from back-to-back eager calls (includes the host's launch overhead)."""
     import copy
-    from tbf16.conv import convert_conv
+    from tbf16.conv import convert_conv, scaled_conv
     res = []
     for C, HW in ((512, 128), (256, 256)):
         conv = torch.nn.Conv2d(C, C, 3, padding=1).cuda().bfloat16()
@@ -559,19 +565,37 @@ def conv_run(pk, iters=5):
         tc = convert_conv(copy.deepcopy(conv))
         flop = 2.0 * C * C * 9 * HW * HW
         row = {"shape": f"1x{C}x{HW}x{HW}, 3x3, {C} -> {C}"}
-        for name, mod in (("tbf16", tc), ("native_bf16_cudnn", conv)):
+
+        def im2col(x, tc=tc):
+            return scaled_conv(x, tc.weight16, tc.weight_scale, tc.bias, tc.stride, tc.padding, tc.dilation,
+                               tc.groups, tc._tbf16_target_exp, wcl16=tc._tbf16_wcl16, implicit=False)
+
+        for name, fn in (("tbf16", tc), ("tbf16_im2col", im2col), ("native_bf16_cudnn", conv)):
             with torch.no_grad():
                 for _ in range(2):
-                    mod(x)
+                    fn(x)
                 torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 for _ in range(iters):
-                    mod(x)
+                    fn(x)
                 e1.record()
                 torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / iters
-            row[name] = {"ms": round(ms, 3), "tflops": round(flop / ms / 1e9, 1)}
+                eager = e0.elapsed_time(e1) / iters
+                # the same call replayed from a CUDA graph: device time without the host's launch overhead
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn(x)
+                g.replay()
+                torch.cuda.synchronize()
+                e0.record()
+                for _ in range(iters):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / iters
+                del g
+            row[name] = {"ms": round(ms, 3), "tflops": round(flop / ms / 1e9, 1), "eager_ms": round(eager, 3)}
         res.append(row)
     return res
 

@@ -218,6 +218,23 @@ int tbf16_conv_im2col(const void* x, const int64_t* geom, int64_t K, int64_t Kp,
 int tbf16_conv_im2col_cl(const void* x, const int64_t* geom, const int32_t* e, const float* out_scale, void* x16cl,
                          void* cols16, float* row_scale, void* stream);
 
+/* Implicit-GEMM convolution (one group): the whole scaled convolution in one call, without im2col rows.
+ * Per-sample amax into amax_ws (B floats, overwritten) and the exponents e / output scales out_scale
+ * (B each, as tbf16_conv_sample_scale with this target_exp); x16cl receives the scaled channels-last fp16
+ * copy [B, D, H, W, C] (as in tbf16_conv_im2col_cl); the GEMM's TMA then loads each (tap, 64-channel)
+ * block of 128 output positions straight from it, the padding as zero fill. wtap16: fp16 [O, taps * C]
+ * rows, taps (z, y, x) outer and channels fastest (the rows of the im2col_cl path). y: bf16
+ * [B * Do * Ho * Wo, O] (channels-last output, row stride O) =
+ * bf16_rn((sum x16cl w16) * out_scale[b] * ws[o] + bias[o]). Replaces the same reference call as the
+ * im2col path (tbf16/conv.py:34-60). TBF16_ERR_UNSUPPORTED unless tbf16_conv_implicit_supported says so:
+ * C % 64 == 0, O % 8 == 0, stride 1, Wo a power-of-two divisor of 128 or a multiple of 128, and
+ * Ho * Wo a multiple of 128 (other convs take the im2col path); also unless each sample of x is one
+ * dense block (contiguous or channels-last). */
+int tbf16_conv_implicit_supported(const int64_t* geom, int64_t O);
+int tbf16_conv_implicit(const void* x, const int64_t* geom, int target_exp, float* amax_ws, int32_t* e,
+                        float* out_scale, void* x16cl, const void* wtap16, int64_t O, const float* ws, const void* bias,
+                        void* y, void* stream);
+
 /* groups > 1 (grouped and depthwise): direct convolution into y bf16 [B, O, Do, Ho, Wo] contiguous; w16
  * fp16 [O, C / groups, kd, kh, kw] contiguous, ws fp32 [O], bias bf16 [O] nullable. */
 int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t groups, const void* w16, const float* ws,

@@ -127,3 +127,60 @@ def test_convert_reaches_nested_and_subclassed_convs():
         tbf16.convert(wrapped, sdpa=False, force=True)
         assert type(wrapped[0]).__name__ == "TBF16CausalConv3d"
         assert rel_err(wrapped(x3), r3) < 3e-3
+
+
+# Stride-1 convolutions with C % 64 == 0 and output rows that tile into 128-position boxes take the
+# implicit GEMM (TMA loads of each tap's block straight from the scaled channels-last copy): output
+# widths below, at and above 128, dilation, valid padding, 3-D, 192 channels (three 64-channel blocks per
+# tap), 25 taps, and a pair tile whose second half lies past the last sample (M = 384).
+IMPLICIT = [
+    ("2d 3x3 Wo=64", lambda: nn.Conv2d(64, 96, 3, padding=1), (2, 64, 32, 64), False),
+    ("2d 3x3 Wo=256 channels_last", lambda: nn.Conv2d(128, 128, 3, padding=1), (1, 128, 16, 256), True),
+    ("2d 3x3 dilation 2", lambda: nn.Conv2d(64, 64, 3, padding=2, dilation=2, bias=False), (1, 64, 32, 32), False),
+    ("2d 3x3 valid", lambda: nn.Conv2d(64, 72, 3), (1, 64, 34, 34), False),
+    ("2d 5x5 C=192", lambda: nn.Conv2d(192, 64, 5, padding=2), (2, 192, 16, 16), False),
+    ("2d 3x3 M=384", lambda: nn.Conv2d(64, 64, 3, padding=1), (3, 64, 8, 16), False),
+    ("3d 3x3x3", lambda: nn.Conv3d(64, 64, 3, padding=1), (1, 64, 4, 16, 32), False),
+]
+
+
+@pytest.mark.parametrize("name,make,shape,cl", IMPLICIT, ids=[c[0] for c in IMPLICIT])
+def test_conv_implicit_vs_oracle(name, make, shape, cl):
+    from tbf16 import _ext
+    from tbf16.conv import scaled_conv
+    tc, x, y = _run(make(), shape, channels_last=cl)
+    nd = x.dim() - 2
+    # the case takes the implicit GEMM
+    k = (1,) * (3 - nd) + tuple(tc.weight16.shape[2:])
+    xs = x.reshape((x.shape[0], x.shape[1]) + (1,) * (3 - nd) + tuple(x.shape[2:]))
+    pad = (0,) * (3 - nd) + tuple(tc.padding)
+    dil = (1,) * (3 - nd) + tuple(tc.dilation)
+    out = tuple((n + 2 * p - d * (kk - 1) - 1) + 1 for n, p, d, kk in zip(xs.shape[2:], pad, dil, k))
+    geom = torch.tensor([*xs.shape, *xs.stride(), *k, 1, 1, 1, *pad, *dil, *out], dtype=torch.int64)
+    assert _ext.lib().tbf16_conv_implicit_supported(_ext.ptr(geom), tc.out_channels) == 0
+    y_ref, absacc = orc.conv_scaled(x.contiguous(), tc.weight16, tc.weight_scale, tc.bias, tc.stride, tc.padding,
+                                    tc.dilation, tc.groups, tc._tbf16_target_exp)
+    assert y.shape == y_ref.shape
+    K = tc.weight16[0].numel()
+    tol = gemm_tolerance(y_ref, absacc, K)
+    assert_close_ulp(y.contiguous(), y_ref, tol, what=name)
+    assert rel_err(y, _fp64_ref(tc, x)) < 3e-3
+    # the im2col path: the same products, so the same result within the fp32 summation bound
+    with torch.no_grad():
+        y2 = scaled_conv(x, tc.weight16, tc.weight_scale, tc.bias, tc.stride, tc.padding, tc.dilation, tc.groups,
+                         tc._tbf16_target_exp, implicit=False)
+    assert_close_ulp(y.contiguous(), y2.contiguous().cpu(), 2 * tol, what=name + " vs im2col")
+
+
+def test_conv_implicit_scales():
+    """Samples of very different magnitude in one batch keep their own scale through the implicit GEMM."""
+    tc, x, y = _run(nn.Conv2d(64, 64, 3, padding=1), (2, 64, 16, 32))
+    x2 = x.clone()
+    x2[0] *= 2.0 ** 40
+    x2[1] *= 2.0 ** -40
+    with torch.no_grad():
+        y2 = tc(x2)
+    assert torch.isfinite(y2.float()).all()
+    r = _fp64_ref(tc, x2)
+    for b in range(2):
+        assert rel_err(y2[b], r[b]) < 3e-3

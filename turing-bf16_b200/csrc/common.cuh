@@ -364,6 +364,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(m)), "r"(mbar), "r"(x), "r"(y)
       : "memory");
 }
+// 5-D tiled load for a CTA pair (no multicast), completing on the even CTA's barrier like tma_load_2d_pair.
+__device__ __forceinline__ void tma_load_5d_pair(void* dst, const CUtensorMap* m, uint64_t* bar_local, int c0, int c1,
+                                                 int c2, int c3, int c4) {
+  const uint32_t mbar = smem_u32(bar_local) & 0xFEFFFFFFu;
+  asm volatile(
+      "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
 // TMEM allocation / release for a CTA pair: one warp with the same warp index in each CTA.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols));
@@ -454,6 +464,20 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c) {
 }  // namespace tbf16
 
 // Host helpers shared by the .cu files.
+// Implicit convolution (the pair kernel's CONV form): A is not a matrix but the scaled channels-last
+// fp16 input [B, D, H, W, C] seen through a 5-D tensor map. Row m of the product is output position
+// (b, z, y, x) of a stride-1 convolution, K block kb is (tap = kb / cb, 64-channel block kb % cb), and a
+// 128-row A tile -- bx x by output positions of one (b, z) slice -- is one box load at the tap's input
+// offset: padding and the channels past C arrive as the load's zero fill.
+struct ConvGemm {
+  int Wo, Ho, Do;     // output extent
+  int cb;             // 64-channel blocks per tap
+  int kh, kw;         // kernel extent (kd = taps / (kh kw))
+  int pw, ph, pd;     // zero padding
+  int dw, dh, dd;     // dilation
+  int sa_div;         // rows per sample: the row scale of row m is sa[m / sa_div]
+};
+
 namespace tbf16_host {
 struct DeviceInfo {
   int device = -1;
@@ -466,6 +490,16 @@ struct DeviceInfo {
 const DeviceInfo* device_info();
 // TBF16_OK, or TBF16_ERR_DEVICE when the current device is not sm_100.
 int require_sm100();
+// 5-D tensor map of a channels-last fp16 tensor [B, D, H, W, C] (C % 8 == 0, 16-byte aligned) for the
+// implicit convolution: box of 64 channels x bx x by positions x 1 x 1, 128-byte swizzle, zero fill.
+int make_tmap_conv_in(CUtensorMap* map, const void* base, int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                      int bx, int by);
+// Implicit-GEMM convolution on the pair kernel (gemm.cu): y[M, N] (rows = output positions (b, z, y, x)
+// of a stride-1 conv, M = B Do Ho Wo) = scaled products of x16cl [B, D, H, W, C] and w16 [N, taps x cb x 64]
+// (row stride ldw = taps x cb x 64, channels zero-padded per tap); sa per sample. Validated by the caller.
+int conv_gemm_pair(const void* x16cl, int64_t B, int64_t D, int64_t H, int64_t W, int64_t C, const ConvGemm& cv,
+                   const void* w16, int64_t ldw, int M, int N, const float* sa, const float* sb, const void* bias,
+                   void* y, int64_t ldy, cudaStream_t st);
 // Maps the last CUDA error to a status (clears it).
 int check_launch();
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

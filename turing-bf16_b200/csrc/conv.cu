@@ -14,6 +14,8 @@
 // input channels per output): a direct kernel, one thread per output element. The reference ends in a
 // cuDNN fp16 conv whose output is rounded to fp16 before the scales; here the fp32 sum is scaled and
 // rounded to bf16 once. Geometry is passed as an array of int64 (TBF16_CONV_GEOM_LEN values, order in the header).
+#include <utility>
+
 #include "common.cuh"
 
 using namespace tbf16;
@@ -137,15 +139,28 @@ __global__ void __launch_bounds__(256) im2col_kernel(const __nv_bfloat16* __rest
 // Fast path for C % 8 == 0, in two passes. (1) x16cl[b, d, h, w, c] = fp16(x * 2^-e[b]) channels-last,
 // 8 channels per thread (one 16-byte store). A channels-last input is read as the same flat array (one
 // 16-byte load, the sample from one division); any other layout is gathered element by element.
+// With amax non-null the exponents come from the sample maxima here (the rule of sample_exp_kernel), and
+// the thread that converts a sample's first 8 channels also writes its e and output scale.
 __global__ void __launch_bounds__(256) scale_cl_kernel(const __nv_bfloat16* __restrict__ xin, const Geom g,
-                                                       const int32_t* __restrict__ e, uint4* __restrict__ x16cl,
-                                                       int flat) {
+                                                       int32_t* __restrict__ e, uint4* __restrict__ x16cl,
+                                                       int flat, const float* __restrict__ amax = nullptr,
+                                                       int t = 0, float* __restrict__ out_scale = nullptr) {
   const int C8 = (int)(g.C / 8);
   const int64_t per_sample = g.D * g.H * g.W * C8;
   const int64_t total = g.B * per_sample;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = i / per_sample;
-    const int eb = e[b];
+    int eb;
+    if (amax) {
+      const float a = __ldg(amax + b);
+      eb = frexp_exp(a > 0.f ? a : 1.0f) - t;
+      if (i == b * per_sample) {
+        e[b] = eb;
+        out_scale[b] = exp2i(eb);
+      }
+    } else {
+      eb = e[b];
+    }
     float v[8];
     if (flat) {
       const uint4 q = __ldg(reinterpret_cast<const uint4*>(xin + b * g.sb) + (i - b * per_sample));
@@ -247,6 +262,18 @@ __global__ void __launch_bounds__(256) conv_grouped_kernel(const __nv_bfloat16* 
   }
 }
 
+// The implicit GEMM's conditions: one group (checked by the caller), channels a multiple of 64 (a K
+// block is one tap's 64 channels; the weight rows are then the (tap, channel) rows of the im2col path),
+// stride 1, and output rows that tile into 128-position boxes inside one (sample, depth) slice: Wo a
+// power-of-two divisor of 128 or a multiple of 128, and Ho Wo a multiple of 128.
+bool implicit_ok(const Geom& g, int64_t O) {
+  if (g.C % 64 || O % 8 || g.std_ != 1 || g.sth != 1 || g.stw != 1) return false;
+  const int64_t bx = g.Wo < 128 ? g.Wo : 128;
+  if (bx <= 0 || g.Wo % bx || 128 % bx || (g.Ho * g.Wo) % 128) return false;
+  const int64_t M = g.B * g.Do * g.Ho * g.Wo, K = g.kd * g.kh * g.kw * g.C;
+  return M <= INT32_MAX && K <= INT32_MAX && O <= INT32_MAX && g.B * g.D * g.H * g.W <= INT32_MAX;
+}
+
 int grid_for(int64_t work) {
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   const int64_t cap = (int64_t)(d ? d->sms : 148) * 16;
@@ -264,15 +291,9 @@ bool geom_ok(const Geom& g) {
 
 }  // namespace
 
-extern "C" {
-
-int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int target_exp, float* amax_ws,
-                            int32_t* e, float* out_scale, void* stream) {
-  if (int st = tbf16_host::require_sm100()) return st;
-  if (B < 0 || n < 0 || ld < n || !x || !amax_ws || !e || !out_scale || target_exp < -126 || target_exp > 126)
-    return TBF16_ERR_INVALID;
-  if (B == 0) return TBF16_OK;
-  auto st = static_cast<cudaStream_t>(stream);
+namespace {
+// amax_ws[b] = max |x| over sample b's n dense elements (samples ld apart).
+int launch_sample_amax(const void* x, int64_t B, int64_t n, int64_t ld, float* amax_ws, cudaStream_t st) {
   if (cudaMemsetAsync(amax_ws, 0, sizeof(float) * B, st) != cudaSuccess) return TBF16_ERR_LAUNCH;
   if (n > 0) {
     // about four blocks per SM in all, each thread with a few 16-byte loads in flight
@@ -283,6 +304,38 @@ int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int
     const int vec = n % 8 == 0 && ld % 8 == 0 && tbf16_host::aligned16(x);
     sample_amax_kernel<<<dim3(gx, (unsigned)B), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, ld, vec, amax_ws);
   }
+  return TBF16_OK;
+}
+
+// The input's samples are dense blocks of C D H W elements (any order of the four strides).
+bool dense_samples(const Geom& g) {
+  int64_t sz[4] = {g.C, g.D, g.H, g.W}, sd[4] = {g.sc, g.sd, g.sh, g.sw};
+  for (int i = 0; i < 4; ++i)  // sort the dimensions by stride (size-1 dimensions last)
+    for (int j = i + 1; j < 4; ++j)
+      if ((sz[j] > 1 && (sz[i] == 1 || sd[j] < sd[i]))) {
+        std::swap(sz[i], sz[j]);
+        std::swap(sd[i], sd[j]);
+      }
+  int64_t expect = 1;
+  for (int i = 0; i < 4 && sz[i] > 1; ++i) {
+    if (sd[i] != expect) return false;
+    expect *= sz[i];
+  }
+  return g.B == 1 || g.sb >= expect;
+}
+}  // namespace
+
+extern "C" {
+
+
+int tbf16_conv_sample_scale(const void* x, int64_t B, int64_t n, int64_t ld, int target_exp, float* amax_ws,
+                            int32_t* e, float* out_scale, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (B < 0 || n < 0 || ld < n || !x || !amax_ws || !e || !out_scale || target_exp < -126 || target_exp > 126)
+    return TBF16_ERR_INVALID;
+  if (B == 0) return TBF16_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (int rc = launch_sample_amax(x, B, n, ld, amax_ws, st)) return rc;
   sample_exp_kernel<<<(unsigned)((B + 255) / 256), 256, 0, st>>>(amax_ws, B, target_exp, e, out_scale);
   return tbf16_host::check_launch();
 }
@@ -315,14 +368,62 @@ int tbf16_conv_im2col_cl(const void* x, const int64_t* geom, const int32_t* e, c
   // the input is one flat channels-last array per sample when its strides say so (and 16-byte aligned)
   const int flat = g.sc == 1 && g.sw == g.C && g.sh == g.W * g.C && g.sd == g.H * g.W * g.C &&
                    (g.B == 1 || g.sb % 8 == 0) && tbf16_host::aligned16(x);
-  scale_cl_kernel<<<grid_for(g.B * g.D * g.H * g.W * (g.C / 8)), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), g,
-                                                                             e, static_cast<uint4*>(x16cl), flat);
+  scale_cl_kernel<<<grid_for(g.B * g.D * g.H * g.W * (g.C / 8)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), g, const_cast<int32_t*>(e), static_cast<uint4*>(x16cl), flat);
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   const int64_t want = (int64_t)(d ? d->sms : 148) * 16, need = (M + 7) / 8;  // 8 output positions per block
   const int64_t blocks = need < want ? need : want;
   im2col_cl_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint4*>(x16cl), g, out_scale,
                                                      static_cast<uint4*>(cols16), row_scale);
   return tbf16_host::check_launch();
+}
+
+int tbf16_conv_implicit_supported(const int64_t* geom, int64_t O) {
+  if (!geom) return TBF16_ERR_INVALID;
+  const Geom g = load_geom(geom);
+  if (!geom_ok(g) || O <= 0) return TBF16_ERR_INVALID;
+  return implicit_ok(g, O) ? TBF16_OK : TBF16_ERR_UNSUPPORTED;
+}
+
+int tbf16_conv_implicit(const void* x, const int64_t* geom, int target_exp, float* amax_ws, int32_t* e,
+                        float* out_scale, void* x16cl, const void* wtap16, int64_t O, const float* ws, const void* bias,
+                        void* y, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (!x || !geom || !amax_ws || !e || !out_scale || !x16cl || !wtap16 || !ws || !y || O <= 0 || target_exp < -126 ||
+      target_exp > 126)
+    return TBF16_ERR_INVALID;
+  const Geom g = load_geom(geom);
+  if (!geom_ok(g)) return TBF16_ERR_INVALID;
+  if (!implicit_ok(g, O) || !dense_samples(g)) return TBF16_ERR_UNSUPPORTED;
+  if (!tbf16_host::aligned16(x16cl) || !tbf16_host::aligned16(wtap16) || !tbf16_host::aligned16(y))
+    return TBF16_ERR_ALIGN;
+  const int64_t M = g.B * g.Do * g.Ho * g.Wo;
+  if (M == 0) return TBF16_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int64_t n = g.C * g.D * g.H * g.W;
+  if (int rc = launch_sample_amax(x, g.B, n, g.B > 1 ? g.sb : n, amax_ws, st)) return rc;
+  const int flat = g.sc == 1 && g.sw == g.C && g.sh == g.W * g.C && g.sd == g.H * g.W * g.C &&
+                   (g.B == 1 || g.sb % 8 == 0) && tbf16_host::aligned16(x);
+  scale_cl_kernel<<<grid_for(g.B * g.D * g.H * g.W * (g.C / 8)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), g, e, static_cast<uint4*>(x16cl), flat, amax_ws, target_exp, out_scale);
+  if (int rc = tbf16_host::check_launch()) return rc;
+  ConvGemm cv;
+  cv.Wo = (int)g.Wo;
+  cv.Ho = (int)g.Ho;
+  cv.Do = (int)g.Do;
+  cv.cb = (int)((g.C + 63) / 64);
+  cv.kh = (int)g.kh;
+  cv.kw = (int)g.kw;
+  cv.pw = (int)g.pw;
+  cv.ph = (int)g.ph;
+  cv.pd = (int)g.pd;
+  cv.dw = (int)g.dw;
+  cv.dh = (int)g.dh;
+  cv.dd = (int)g.dd;
+  cv.sa_div = (int)(g.Do * g.Ho * g.Wo);
+  const int64_t K = g.kd * g.kh * g.kw * cv.cb * 64;
+  return tbf16_host::conv_gemm_pair(x16cl, g.B, g.D, g.H, g.W, g.C, cv, wtap16, K, (int)M, (int)O, out_scale, ws, bias,
+                                    y, O, st);
 }
 
 int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t groups, const void* w16, const float* ws,

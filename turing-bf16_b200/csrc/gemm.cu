@@ -44,6 +44,7 @@ struct GemmParams {
   int tiles_m, tiles_n;
   int group_m;    // M tiles per raster group
   int tma_store;  // pair kernel: epilogue through shared memory and TMA stores (else direct 16-byte stores)
+  ConvGemm cv;    // pair kernel, implicit convolution only
 };
 
 template <int BN, int STAGES, bool CONVERT>
@@ -334,7 +335,7 @@ struct PairCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool CONV>
 __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     scaled_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmY, const GemmParams p) {
@@ -386,12 +387,39 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
         int tm, tn;
         tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
         const int m0 = tm * 256 + (int)rank * 128, n0 = tn * PN + (int)rank * 128;
+        int cx = 0, cy = 0, cz = 0, cbat = 0;  // CONV: input coordinates of the A box at tap (0, 0, 0)
+        if (CONV) {
+          int r = m0;
+          const int xo = r % p.cv.Wo;
+          r /= p.cv.Wo;
+          const int yo = r % p.cv.Ho;
+          r /= p.cv.Ho;
+          const int zo = r % p.cv.Do;
+          cbat = r / p.cv.Do;  // past the last sample for the second half of a ragged last pair: zero fill
+          cx = xo - p.cv.pw;
+          cy = yo - p.cv.ph;
+          cz = zo - p.cv.pd;
+        }
+        int cblk = 0, kx = 0, ky = 0, kz = 0;  // CONV: K block kb = ((kz kh + ky) kw + kx) cb + cblk
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both CTAs' bytes
-          if (!A_MN) {
+          if (CONV) {
+            tma_load_5d_pair(sA, &tmA, &full[stage], cblk * BK, cx + kx * p.cv.dw, cy + ky * p.cv.dh,
+                             cz + kz * p.cv.dd, cbat);
+            if (++cblk == p.cv.cb) {
+              cblk = 0;
+              if (++kx == p.cv.kw) {
+                kx = 0;
+                if (++ky == p.cv.kh) {
+                  ky = 0;
+                  ++kz;
+                }
+              }
+            }
+          } else if (!A_MN) {
             tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, m0);
           } else {
 #pragma unroll
@@ -459,7 +487,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
       tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
       const int m = tm * 256 + (int)rank * 128 + row;
       const bool mok = m < p.M;
-      const float a = mok ? __ldg(p.sa + m) : 0.f;
+      const float a = mok ? __ldg(p.sa + (CONV ? m / p.cv.sa_div : m)) : 0.f;
       if (p.tma_store) {
         const int row0 = tm * 256 + (int)rank * 128 + quad * 32;
 #pragma unroll 1
@@ -556,23 +584,21 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
   }
 }
 
-template <bool A_MN, bool B_MN>
-int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
-                     const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
+// The pair kernel with A's tensor map already built (a matrix, or the conv input for CONV).
+template <bool A_MN, bool B_MN, bool CONV>
+int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
+                     const float* sb, const void* bias, void* y, int64_t ldy, const ConvGemm* cv, cudaStream_t st) {
   using C = PairCfg;
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   if (!d) return TBF16_ERR_DEVICE;
-  CUtensorMap ta, tb;
-  int rc = A_MN ? tbf16_host::make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64)
-                : tbf16_host::make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, BM);
-  if (rc) return rc;
-  rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
-            : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 128);
+  CUtensorMap tb;
+  int rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
+                : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 128);
   if (rc) return rc;
   CUtensorMap ty;
   rc = tbf16_host::make_tmap_2d_out(&ty, y, (uint64_t)N, (uint64_t)M, (uint64_t)ldy, 32, 32);
   if (rc) return rc;
-  auto kern = scaled_gemm_pair_kernel<A_MN, B_MN>;
+  auto kern = scaled_gemm_pair_kernel<A_MN, B_MN, CONV>;
   static bool attr_done[64] = {false};
   if (!attr_done[d->device & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
@@ -598,6 +624,7 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
     return e ? atoi(e) : 1;
   }();
   p.tma_store = epi_env != 0 && tbf16_host::aligned16(y) ? 1 : 0;
+  if (cv) p.cv = *cv;
   const int tiles = p.tiles_m * p.tiles_n;
   const int clusters = std::min(tiles, d->sms / 2);
   cudaLaunchConfig_t cfg = {};
@@ -616,6 +643,16 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   return tbf16_host::check_launch();
 }
 
+template <bool A_MN, bool B_MN>
+int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
+                     const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
+  CUtensorMap ta;
+  int rc = A_MN ? tbf16_host::make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64)
+                : tbf16_host::make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, BM);
+  if (rc) return rc;
+  return launch_pair_core<A_MN, B_MN, false>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+}
+
 // The pair kernel whenever both dimensions span two or more 256 tiles (it moves a third less data from
 // L2 per SM for the same CTA count; measured faster from M = N = 512 up), or the product fills the
 // GPU with pair tiles; TBF16_GEMM_PAIR=0 / 1 forces the single-CTA / pair kernel.
@@ -631,6 +668,20 @@ bool use_pair(int M, int N) {
 bool ok8(int64_t v) { return v % 8 == 0; }
 
 }  // namespace
+
+namespace tbf16_host {
+
+int conv_gemm_pair(const void* x16cl, int64_t B, int64_t D, int64_t H, int64_t W, int64_t C, const ConvGemm& cv,
+                   const void* w16, int64_t ldw, int M, int N, const float* sa, const float* sb, const void* bias,
+                   void* y, int64_t ldy, cudaStream_t st) {
+  const int bx = cv.Wo < 128 ? cv.Wo : 128;
+  CUtensorMap ta;
+  if (int rc = make_tmap_conv_in(&ta, x16cl, B, D, H, W, C, bx, 128 / bx)) return rc;
+  // K = taps x cb x 64: the weight rows are exactly one K long
+  return launch_pair_core<false, false, true>(ta, w16, ldw, M, N, (int)ldw, sa, sb, bias, y, ldy, &cv, st);
+}
+
+}  // namespace tbf16_host
 
 extern "C" {
 

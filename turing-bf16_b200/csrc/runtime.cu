@@ -86,6 +86,21 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t row
   return r == CUDA_SUCCESS ? TBF16_OK : TBF16_ERR_INVALID;
 }
 
+int make_tmap_conv_in(CUtensorMap* map, const void* base, int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                      int bx, int by) {
+  if (!encode_fn()) return TBF16_ERR_LAUNCH;
+  if (!aligned16(base) || C % 8 != 0) return TBF16_ERR_ALIGN;
+  cuuint64_t gdim[5] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)B};
+  cuuint64_t gstride[4] = {(cuuint64_t)(C * 2), (cuuint64_t)(W * C * 2), (cuuint64_t)(H * W * C * 2),
+                           (cuuint64_t)(D * H * W * C * 2)};
+  cuuint32_t box[5] = {64, (cuuint32_t)bx, (cuuint32_t)by, 1, 1};
+  cuuint32_t estride[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TBF16_OK : TBF16_ERR_INVALID;
+}
+
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                  uint64_t stride2, uint32_t box0, uint32_t box1) {
   if (!encode_fn()) return TBF16_ERR_LAUNCH;

@@ -7,10 +7,12 @@ convertible(m), convert_conv(conv) (in place, class swap so subclass forwards ke
 `.weight` becomes None, `.dequantized_weight()` gives it back), and convert(..., conv=True) uses them.
 
 Routing: 1x1 convolutions (stride 1, no padding, one group) are per-pixel linear layers and go through
-scaled_linear, as in the reference; other convolutions with one group become an im2col into fp16 rows
-plus the tcgen05 GEMM (output channels-last) -- for input channels in multiples of 8 through a scaled
-channels-last fp16 copy and 16-byte tap copies, with the weight rows in (taps, channels) order; grouped
-and depthwise convolutions run a direct kernel.
+scaled_linear, as in the reference. Other convolutions with one group run the tcgen05 GEMM against the
+weight rows in (taps, channels) order, output channels-last: stride-1 convolutions with channels in
+multiples of 64 and output rows that tile into 128-position boxes as an implicit GEMM (the GEMM's TMA
+loads each tap's input block from a scaled channels-last fp16 copy, padding as zero fill); the rest
+through im2col rows (16-byte tap copies from that copy for channels in multiples of 8, else a generic
+im2col). Grouped and depthwise convolutions run a direct kernel.
 The reference ends in a cuDNN fp16 convolution whose output is rounded to fp16 before the scales are
 applied; here the fp32 sum is scaled and rounded to bf16 once.
 """
@@ -18,7 +20,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from ._ext import call, ptr, require_cuda, stream_ptr
+from ._ext import call, lib, ptr, require_cuda, stream_ptr
 from .ops import _bias_ok, _gemm_f16, _target_exp, prepare_weight, scaled_linear
 
 
@@ -60,11 +62,13 @@ def _taps_last(weight16):
     return weight16.movedim(1, -1).reshape(weight16.shape[0], -1).contiguous()
 
 
-def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, groups, target_exp, wk16=None, wcl16=None):
+def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, groups, target_exp, wk16=None, wcl16=None,
+                implicit=True):
     """The scaled convolution of a bf16 input with a prepared weight (weight16 fp16 [O, C/groups, *k],
     weight_scale fp32 [O]); zero padding only (other padding modes are applied by the caller). wk16: the
     weight as [O, K] rows padded to a multiple of 8; wcl16: as [O, taps * C] rows (channels fastest) for
-    C a multiple of 8; each made on the fly when None."""
+    C a multiple of 8; each made on the fly when None. implicit=False keeps a convolution the implicit GEMM
+    supports on the im2col path (same result up to the fp32 summation order)."""
     require_cuda(x, weight16, weight_scale)
     nd = x.dim() - 2
     x = _dense(x)
@@ -77,13 +81,23 @@ def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, grou
     if min(out) <= 0:
         raise RuntimeError("tbf16 conv: the kernel does not fit the padded input")
     geom = torch.tensor([B, C, D, H, W, *xs.stride(), *k, *st, *pd, *dl, *out], dtype=torch.int64)
-    e, scale = _sample_scales(xs, target_exp)
     b = _bias_ok(bias, O, x.device)
     ws = weight_scale.contiguous().float()
     out_shape = (B, O) + tuple(out[3 - nd:])
+    M = B * out[0] * out[1] * out[2]
+    if groups == 1 and implicit and lib().tbf16_conv_implicit_supported(ptr(geom), O) == 0:
+        wk16 = _taps_last(weight16) if wcl16 is None else wcl16
+        amax = torch.empty(B, device=x.device, dtype=torch.float32)
+        e = torch.empty(B, device=x.device, dtype=torch.int32)
+        scale = torch.empty(B, device=x.device, dtype=torch.float32)
+        x16cl = torch.empty((B, D, H, W, C), device=x.device, dtype=torch.float16)
+        y = torch.empty((M, O), device=x.device, dtype=torch.bfloat16)
+        call("tbf16_conv_implicit", ptr(xs), ptr(geom), int(target_exp), ptr(amax), ptr(e), ptr(scale), ptr(x16cl),
+             ptr(wk16), O, ptr(ws), ptr(b), ptr(y), stream_ptr(x.device))
+        return y.reshape((B,) + tuple(out[3 - nd:]) + (O,)).movedim(-1, 1)
+    e, scale = _sample_scales(xs, target_exp)
     if groups == 1:
         K = weight16[0].numel()
-        M = B * out[0] * out[1] * out[2]
         row_scale = torch.empty((M,), device=x.device, dtype=torch.float32)
         if C % 8 == 0:  # channels-last fp16 copy, then 16-byte tap copies (taps x channels columns)
             Kp = K
