@@ -24,7 +24,9 @@ def _gate_up(M, I, seed):
 
 
 @pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
-@pytest.mark.parametrize("M,I", [(1, 8), (5, 2056), (64, 8192), (3, 10240), (17, 16384)])
+# one warp per row up to 1024 elements (1, 2 or 4 vectors a lane; row counts not a multiple of the 8 rows
+# of a block), one right-sized block per row above (one or two vectors a thread)
+@pytest.mark.parametrize("M,I", [(1, 8), (9, 384), (13, 1000), (5, 2056), (64, 8192), (3, 10240), (17, 16384)])
 def test_glu_rows(act, M, I):
     from tbf16 import ops
     gate, up = _gate_up(M, I, M + I)
@@ -50,7 +52,8 @@ def test_glu_rows_match_torch_on_gpu():
 
 
 @pytest.mark.parametrize("style,offset", [("gemma", 1.0), ("llama", 0.0)])
-@pytest.mark.parametrize("M,K", [(2, 64), (33, 2560), (256, 4096), (7, 16384)])
+@pytest.mark.parametrize("M,K", [(2, 64), (33, 256), (17, 512), (11, 1024), (5, 1032), (33, 2560), (256, 4096),
+                                 (7, 16384)])
 def test_rmsnorm_rows(style, offset, M, K):
     from tbf16 import ops
     g = torch.Generator().manual_seed(M * 3 + K)

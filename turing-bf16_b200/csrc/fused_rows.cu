@@ -10,18 +10,22 @@
 // then, for the produced rows: s_inv = the fused rule's power-of-two row scale (row max, target t) and
 // y16 = fp16(row / s_inv) -- exactly what tbf16_row_scale with a y16 buffer gives on the bf16 rows.
 //
-// HBM-bound: one 256-thread block per row keeps the row in registers (up to 8 x 16 bytes per thread
-// per input, rows up to 16384 elements), so each input is read once and the fp16 operand (plus, on
-// request, the bf16 row) written once. Row maxima and sums of squares are reduced over the warp and
-// then over the 8 warps in a fixed order.
+// HBM-bound: the threads that own a row keep it in registers, so each input is read once and the fp16
+// operand (plus, on request, the bf16 row) written once -- one warp per row for rows up to 1024
+// elements (up to 4 x 16 bytes a lane), else one block per row with the fewest warps that hold it at one
+// or two 16-byte vectors a thread (rows up to 16384 elements), which keeps registers per thread low and
+// several blocks on each SM. Row maxima and sums of squares are reduced over the lanes and then over
+// the warps in a fixed order.
 #include "common.cuh"
 
 using namespace tbf16;
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMaxChunks = 8;  // 16-byte vectors per thread and input: rows up to 256 * 8 * 8 elements
+constexpr int kMaxThreads = 1024;
+constexpr int kMaxChunks = 2;       // 16-byte vectors per thread and input in the block-per-row kernels
+constexpr int kWarpRowsMaxK8 = 128;  // rows up to 1024 elements: one warp per row (up to 4 vectors a lane)
+constexpr int kWarpRowsPerBlock = 8;
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -35,28 +39,53 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(kBeta * (x + kKappa * x3)));
 }
 
-// Block-wide max (non-negative values) over the 8 warps, in a fixed order.
-__device__ __forceinline__ float block_max(float m, float* red) {
-  m = warp_max(m);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  float r = red[0];
+// The threads that own one row: a warp (WARP, short rows, 8 rows per block) or the whole block (one row
+// per block, up to 1024 threads). Reductions go over the lanes by a shuffle tree and then, for a block,
+// over its warps in index order, so a row's result does not depend on scheduling.
+template <bool WARP>
+struct RowGroup {
+  int tid, nthr;
+  int64_t row;
+  float* red;  // block: one float per warp
+  __device__ RowGroup(float* red_) : red(red_) {
+    if (WARP) {
+      tid = threadIdx.x & 31;
+      nthr = 32;
+      row = (int64_t)blockIdx.x * kWarpRowsPerBlock + (threadIdx.x >> 5);
+    } else {
+      tid = threadIdx.x;
+      nthr = blockDim.x;
+      row = blockIdx.x;
+    }
+  }
+  template <bool MAX>
+  __device__ float reduce(float v) {
 #pragma unroll
-  for (int k = 1; k < kThreads / 32; ++k) r = fmaxf(r, red[k]);
-  return r;
-}
+    for (int o = 16; o > 0; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = MAX ? fmaxf(v, w) : v + w;
+    }
+    if (WARP) return v;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();  // red is free (an earlier reduction's readers are done)
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int k = 1; k < nw; ++k) r = MAX ? fmaxf(r, red[k]) : r + red[k];
+    return r;
+  }
+};
 
 // Writes fp16(row / s_inv) from the bf16 row held in registers, s_inv, and the bf16 row if asked.
-template <int NCH>
-__device__ __forceinline__ void emit_row(const uint4 (&v)[NCH], float amax, int t, int K8, int64_t row,
+template <int NCH, bool WARP>
+__device__ __forceinline__ void emit_row(const RowGroup<WARP>& rg, const uint4 (&v)[NCH], float amax, int t, int K8,
                                          uint4* __restrict__ y16, int64_t ldy8, float* __restrict__ s_inv,
                                          uint4* __restrict__ out, int64_t ldo8) {
   const int se = scale_biased_exp_fused(amax, t);
   const float sc = pow2_from_biased(se);
 #pragma unroll
   for (int u = 0; u < NCH; ++u) {
-    const int i = threadIdx.x + kThreads * u;
+    const int i = rg.tid + rg.nthr * u;
     if (i < K8) {
       if (y16) {
         uint4 o;
@@ -64,29 +93,30 @@ __device__ __forceinline__ void emit_row(const uint4 (&v)[NCH], float amax, int 
         o.y = pack_f16(bf16lo(v[u].y) * sc, bf16hi(v[u].y) * sc);
         o.z = pack_f16(bf16lo(v[u].z) * sc, bf16hi(v[u].z) * sc);
         o.w = pack_f16(bf16lo(v[u].w) * sc, bf16hi(v[u].w) * sc);
-        y16[row * ldy8 + i] = o;
+        y16[rg.row * ldy8 + i] = o;
       }
-      if (out) out[row * ldo8 + i] = v[u];
+      if (out) out[rg.row * ldo8 + i] = v[u];
     }
   }
-  if (threadIdx.x == 0 && y16) s_inv[row] = inv_pow2_from_biased(se);
+  if (rg.tid == 0 && y16) s_inv[rg.row] = inv_pow2_from_biased(se);
 }
 
-template <int NCH, int ACT>
-__global__ void __launch_bounds__(kThreads) glu_rows_kernel(const uint4* __restrict__ g, int64_t ldg8,
-                                                            const uint4* __restrict__ u, int64_t ldu8, int I8, int t,
-                                                            uint4* __restrict__ y16, int64_t ldy8,
-                                                            float* __restrict__ s_inv, uint4* __restrict__ out,
-                                                            int64_t ldo8) {
+template <int NCH, int ACT, bool WARP>
+__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) glu_rows_kernel(const uint4* __restrict__ g, int64_t ldg8,
+                                                               const uint4* __restrict__ u, int64_t ldu8, int64_t M,
+                                                               int I8, int t, uint4* __restrict__ y16, int64_t ldy8,
+                                                               float* __restrict__ s_inv, uint4* __restrict__ out,
+                                                               int64_t ldo8) {
   pdl_launch_dependents();
-  __shared__ float red[kThreads / 32];
-  const int64_t row = blockIdx.x;
+  __shared__ float red[kMaxThreads / 32];
+  RowGroup<WARP> rg(red);
+  if (WARP && rg.row >= M) return;
   uint4 gv[NCH], uv[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int i = threadIdx.x + kThreads * c;
-    gv[c] = i < I8 ? __ldg(g + row * ldg8 + i) : make_uint4(0, 0, 0, 0);
-    uv[c] = i < I8 ? __ldg(u + row * ldu8 + i) : make_uint4(0, 0, 0, 0);
+    const int i = rg.tid + rg.nthr * c;
+    gv[c] = i < I8 ? __ldg(g + rg.row * ldg8 + i) : make_uint4(0, 0, 0, 0);
+    uv[c] = i < I8 ? __ldg(u + rg.row * ldu8 + i) : make_uint4(0, 0, 0, 0);
   }
   float m = 0.f;
   uint4 hv[NCH];
@@ -104,29 +134,28 @@ __global__ void __launch_bounds__(kThreads) glu_rows_kernel(const uint4* __restr
     }
     hv[c] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
   }
-  const float amax = block_max(m, red);
-  emit_row<NCH>(hv, amax, t, I8, row, y16, ldy8, s_inv, out, ldo8);
+  const float amax = rg.template reduce<true>(m);
+  emit_row<NCH, WARP>(rg, hv, amax, t, I8, y16, ldy8, s_inv, out, ldo8);
 }
 
-template <int NCH, int STYLE>
-__global__ void __launch_bounds__(kThreads) rmsnorm_rows_kernel(const uint4* __restrict__ x, int64_t ldx8,
-                                                                const uint4* __restrict__ w, int K8, int K,
-                                                                float eps, float offset, int t,
-                                                                uint4* __restrict__ y16, int64_t ldy8,
-                                                                float* __restrict__ s_inv, uint4* __restrict__ out,
-                                                                int64_t ldo8) {
+template <int NCH, int STYLE, bool WARP>
+__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) rmsnorm_rows_kernel(const uint4* __restrict__ x, int64_t ldx8,
+                                                                   const uint4* __restrict__ w, int64_t M, int K8,
+                                                                   int K, float eps, float offset, int t,
+                                                                   uint4* __restrict__ y16, int64_t ldy8,
+                                                                   float* __restrict__ s_inv, uint4* __restrict__ out,
+                                                                   int64_t ldo8) {
   pdl_launch_dependents();
-  __shared__ float red[kThreads / 32];
-  __shared__ float red_ss[kThreads / 32];
-  const int64_t row = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ float red[kMaxThreads / 32];
+  RowGroup<WARP> rg(red);
+  if (WARP && rg.row >= M) return;
   uint4 xv[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int i = threadIdx.x + kThreads * c;
-    xv[c] = i < K8 ? __ldg(x + row * ldx8 + i) : make_uint4(0, 0, 0, 0);
+    const int i = rg.tid + rg.nthr * c;
+    xv[c] = i < K8 ? __ldg(x + rg.row * ldx8 + i) : make_uint4(0, 0, 0, 0);
   }
-  // mean of squares in fp32: per thread, then a shuffle tree, then the 8 warps in order
+  // mean of squares in fp32: per thread, then the group's fixed-order reduction
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
@@ -138,19 +167,13 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_rows_kernel(const uint4* __r
       ss = fmaf(b, b, ss);
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) red_ss[warp] = ss;
-  __syncthreads();
-  float tot = red_ss[0];
-#pragma unroll
-  for (int k = 1; k < kThreads / 32; ++k) tot += red_ss[k];
+  const float tot = rg.template reduce<false>(ss);
   const float r = rsqrtf(tot / (float)K + eps);
   float m = 0.f;
   uint4 yv[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int i = threadIdx.x + kThreads * c;
+    const int i = rg.tid + rg.nthr * c;
     const uint4 wv = i < K8 ? __ldg(w + i) : make_uint4(0, 0, 0, 0);
     const uint32_t xw[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -170,14 +193,25 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_rows_kernel(const uint4* __r
     }
     yv[c] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
   }
-  const float amax = block_max(m, red);
-  emit_row<NCH>(yv, amax, t, K8, row, y16, ldy8, s_inv, out, ldo8);
+  const float amax = rg.template reduce<true>(m);
+  emit_row<NCH, WARP>(rg, yv, amax, t, K8, y16, ldy8, s_inv, out, ldo8);
 }
 
-int chunks_for(int64_t K8) {
+// Launch shape for rows of K8 16-byte vectors: short rows one warp each (vectors per lane nch of 1, 2, 4);
+// longer rows one block each, nch (1 or 2) vectors per thread and the fewest warps that cover the row, so
+// that each thread holds little and many blocks fit an SM. nch = 0: the row is too long.
+struct RowLaunch {
+  bool warp;
+  int nch, threads;
+};
+RowLaunch row_launch(int64_t K8) {
+  if (K8 <= kWarpRowsMaxK8) return {true, K8 <= 32 ? 1 : (K8 <= 64 ? 2 : 4), 32 * kWarpRowsPerBlock};
   for (int c = 1; c <= kMaxChunks; c *= 2)
-    if (K8 <= (int64_t)kThreads * c) return c;
-  return 0;
+    if (K8 <= (int64_t)kMaxThreads * c) {
+      const int64_t per = (K8 + c - 1) / c;
+      return {false, c, (int)((per + 31) / 32 * 32)};
+    }
+  return {false, 0, 0};
 }
 
 }  // namespace
@@ -195,21 +229,24 @@ int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64
     return TBF16_ERR_ALIGN;
   if (M == 0 || I == 0) return TBF16_OK;
   const int64_t I8 = I / 8;
-  const int nch = chunks_for(I8);
-  if (!nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
+  const RowLaunch L = row_launch(I8);
+  if (!L.nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
   auto st = static_cast<cudaStream_t>(stream);
   const uint4 *gp = static_cast<const uint4*>(g), *up = static_cast<const uint4*>(u);
   uint4 *yp = static_cast<uint4*>(y16), *op = static_cast<uint4*>(h_out);
-#define TBF16_GLU(N, A)                                                                                          \
-  glu_rows_kernel<N, A><<<(unsigned)M, kThreads, 0, st>>>(gp, ldg / 8, up, ldu / 8, (int)I8, target_exp, yp, ldy / 8, \
-                                                          s_inv, op, ldo / 8)
-#define TBF16_GLU_ACT(N) \
-  if (act == TBF16_ACT_SILU) TBF16_GLU(N, TBF16_ACT_SILU); else TBF16_GLU(N, TBF16_ACT_GELU_TANH)
-  switch (nch) {
-    case 1: TBF16_GLU_ACT(1); break;
-    case 2: TBF16_GLU_ACT(2); break;
-    case 4: TBF16_GLU_ACT(4); break;
-    default: TBF16_GLU_ACT(8); break;
+  const unsigned blocks = (unsigned)(L.warp ? (M + kWarpRowsPerBlock - 1) / kWarpRowsPerBlock : M);
+#define TBF16_GLU(N, A, W)                                                                                 \
+  glu_rows_kernel<N, A, W><<<blocks, L.threads, 0, st>>>(gp, ldg / 8, up, ldu / 8, M, (int)I8, target_exp, yp, \
+                                                         ldy / 8, s_inv, op, ldo / 8)
+#define TBF16_GLU_ACT(N, W) \
+  if (act == TBF16_ACT_SILU) TBF16_GLU(N, TBF16_ACT_SILU, W); else TBF16_GLU(N, TBF16_ACT_GELU_TANH, W)
+  if (L.warp) {
+    if (L.nch == 1) TBF16_GLU_ACT(1, true);
+    else if (L.nch == 2) TBF16_GLU_ACT(2, true);
+    else TBF16_GLU_ACT(4, true);
+  } else {
+    if (L.nch == 1) TBF16_GLU_ACT(1, false);
+    else TBF16_GLU_ACT(2, false);
   }
 #undef TBF16_GLU_ACT
 #undef TBF16_GLU
@@ -229,21 +266,24 @@ int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int
     return TBF16_ERR_ALIGN;
   if (M == 0 || K == 0) return TBF16_OK;
   const int64_t K8 = K / 8;
-  const int nch = chunks_for(K8);
-  if (!nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
+  const RowLaunch L = row_launch(K8);
+  if (!L.nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
   auto st = static_cast<cudaStream_t>(stream);
   const uint4 *xp = static_cast<const uint4*>(x), *wp = static_cast<const uint4*>(w);
   uint4 *yp = static_cast<uint4*>(y16), *op = static_cast<uint4*>(r_out);
-#define TBF16_NORM(N, S)                                                                                              \
-  rmsnorm_rows_kernel<N, S><<<(unsigned)M, kThreads, 0, st>>>(xp, ldx / 8, wp, (int)K8, (int)K, eps, offset,        \
-                                                              target_exp, yp, ldy / 8, s_inv, op, ldo / 8)
-#define TBF16_NORM_STYLE(N) \
-  if (style == TBF16_NORM_SCALE_FP32) TBF16_NORM(N, TBF16_NORM_SCALE_FP32); else TBF16_NORM(N, TBF16_NORM_SCALE_BF16)
-  switch (nch) {
-    case 1: TBF16_NORM_STYLE(1); break;
-    case 2: TBF16_NORM_STYLE(2); break;
-    case 4: TBF16_NORM_STYLE(4); break;
-    default: TBF16_NORM_STYLE(8); break;
+  const unsigned blocks = (unsigned)(L.warp ? (M + kWarpRowsPerBlock - 1) / kWarpRowsPerBlock : M);
+#define TBF16_NORM(N, S, W)                                                                                       \
+  rmsnorm_rows_kernel<N, S, W><<<blocks, L.threads, 0, st>>>(xp, ldx / 8, wp, M, (int)K8, (int)K, eps, offset,   \
+                                                             target_exp, yp, ldy / 8, s_inv, op, ldo / 8)
+#define TBF16_NORM_STYLE(N, W) \
+  if (style == TBF16_NORM_SCALE_FP32) TBF16_NORM(N, TBF16_NORM_SCALE_FP32, W); else TBF16_NORM(N, TBF16_NORM_SCALE_BF16, W)
+  if (L.warp) {
+    if (L.nch == 1) TBF16_NORM_STYLE(1, true);
+    else if (L.nch == 2) TBF16_NORM_STYLE(2, true);
+    else TBF16_NORM_STYLE(4, true);
+  } else {
+    if (L.nch == 1) TBF16_NORM_STYLE(1, false);
+    else TBF16_NORM_STYLE(2, false);
   }
 #undef TBF16_NORM_STYLE
 #undef TBF16_NORM
