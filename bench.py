@@ -647,20 +647,30 @@ def train_linear_run(pk, iters=9):
         h = torch.nn.functional.silu(autograd.linear(x, wg)) * autograd.linear(x, wu)
         autograd.linear(h, wd).backward(dy)
 
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize()
-    ts = []
-    for _ in range(iters):  # median of per-step times: robust to a host hiccup in one step
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        step()
-        e1.record()
+    def step_fused():  # the SiLU-gate fused into the down linear's input pass and its backward
+        autograd.glu_linear(autograd.linear(x, wg), autograd.linear(x, wu), wd).backward(dy)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
         torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1))
-    t = statistics.median(ts)
+        ts = []
+        for _ in range(iters):  # median of per-step times: robust to a host hiccup in one step
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    t = timed(step)
+    tf = timed(step_fused)
+    tfl = lambda ms: round(flop / (ms / 1e3) / 1e12, 1)
     return {"config": f"M={M} h={Hd} i={I} (gate, up, down) fwd+bwd", "ms": round(t, 3),
-            "tflops": round(flop / (t / 1e3) / 1e12, 1), "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 3)}
+            "tflops": tfl(t), "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 3),
+            "fused": {"ms": round(tf, 3), "tflops": tfl(tf), "frac": round(flop / (tf / 1e3) / 1e12 / pk["tflops"], 3),
+                      "what": "autograd.glu_linear: SiLU(gate) * up fused into the down linear's row pass and its backward"}}
 
 
 def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):

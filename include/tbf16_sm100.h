@@ -168,14 +168,24 @@ int tbf16_gemv(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w16
 #define TBF16_ACT_GELU_TANH 1
 #define TBF16_FUSED_MAX_ROW 16384
 
-/* Gated MLP activation: h[m, i] = bf16_rn(bf16_rn(act(g[m, i])) * u[m, i]) (act in fp32: silu
- * x / (1 + exp(-x)), or GELU with the tanh approximation), as torch computes act(g) * u on bf16 tensors;
+/* Gated MLP activation: h[m, i] = bf16_rn(bf16_rn(act(g[m, i])) * u[m, i]) (act in fp32 with the fast
+ * exp and division: silu x / (1 + exp(-x)), or GELU with the tanh approximation), torch's act(g) * u on
+ * bf16 tensors to within one bf16 ulp (identical in all but ~1e-4 of the elements);
  * then s_inv[m] = the fused rule's power-of-two row scale of h (row max, target target_exp, as
  * tbf16_row_scale) and y16[m, i] = fp16_rn(h[m, i] / s_inv[m]). h is also written to h_out when non-null.
  * g, u bf16 [M, I] (row strides ldg, ldu), y16 fp16 [M, I] (ldy), h_out bf16 (ldo). I and the strides
  * multiples of 8, pointers 16-byte aligned. */
 int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64_t M, int64_t I, int act,
                    int target_exp, void* y16, int64_t ldy, float* s_inv, void* h_out, int64_t ldo, void* stream);
+
+/* Backward of the gated activation for training, as torch's autograd differentiates act(g) * u on bf16
+ * tensors: with a = bf16_rn(act(g)) recomputed, du = bf16_rn(dh * a), da = bf16_rn(dh * u) and
+ * dg = bf16_rn(da * act'(g)) (act' in fp32: silu s (1 + g (1 - s)), s = 1 / (1 + exp(-g)); tanh-GELU
+ * 0.5 (1 + t) + 0.5 g (1 - t^2) sqrt(2/pi) (1 + 3 * 0.044715 g^2)). One read of dh, g, u and one write of
+ * dg, du instead of torch's four elementwise passes. No reference counterpart (the reference leaves the
+ * activation to torch). All bf16 [M, I], strides and I multiples of 8, pointers 16-byte aligned. */
+int tbf16_glu_bwd(const void* dh, int64_t ldh, const void* g, int64_t ldg, const void* u, int64_t ldu, int64_t M,
+                  int64_t I, int act, void* dg, int64_t lddg, void* du, int64_t lddu, void* stream);
 
 /* RMSNorm: ms[m] = mean_k x[m, k]^2 (fp32), rs = rsqrt(ms + eps) and
  *   style TBF16_NORM_SCALE_FP32: r[m, k] = bf16_rn((x[m, k] * rs) * (w[k] + offset))   (Gemma: offset 1)

@@ -110,3 +110,49 @@ def test_fused_rows_reject_bad_input():
         ops.glu_rows(g, g, "silu")  # longer than TBF16_FUSED_MAX_ROW
     with pytest.raises(RuntimeError):
         ops.glu_rows(g[:, :16], g[:, :16], "relu")
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+@pytest.mark.parametrize("M,I", [(7, 8), (64, 4096), (3, 10248)])
+def test_glu_bwd_matches_torch_autograd(act, M, I):
+    """d_gate, d_up in one pass against torch's autograd of act(g) * u on bf16 tensors on the GPU."""
+    import torch.nn.functional as F
+    from tbf16 import ops
+    gate, up = _gate_up(M, I, 3 * M + I)
+    g, u = gate.cuda().requires_grad_(), up.cuda().requires_grad_()
+    dh = (torch.randn(M, I, generator=torch.Generator().manual_seed(M)) * 0.01).bfloat16().cuda()
+    h = (F.silu(g) if act == "silu" else F.gelu(g, approximate="tanh")) * u
+    h.backward(dh)
+    dg, du = ops.glu_bwd(dh, g.detach(), u.detach(), act)
+    for ours, ref in ((dg, g.grad), (du, u.grad)):
+        assert _within_ulp(ours.cpu(), ref.cpu())
+        assert (ours.view(torch.int16) == ref.view(torch.int16)).float().mean().item() > 0.999
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+def test_glu_linear_training_matches_unfused(act):
+    """GLULinearFn (fused rows forward, fused activation backward) against the unfused composition
+    act(gate) * up -> autograd.linear: the same scaled GEMMs on operands scaled by the fused and the
+    small-kernel rule respectively, so outputs and gradients agree to the fp16 operand rounding."""
+    import torch.nn.functional as F
+    from helpers import rel_err
+    from tbf16 import autograd
+    torch.manual_seed(0)
+    M, H, I = 512, 256, 1024
+    gate = (torch.randn(M, I, device="cuda") * 2).bfloat16().requires_grad_()
+    up = torch.randn(M, I, device="cuda").bfloat16().requires_grad_()
+    w = (torch.randn(H, I, device="cuda") * 0.03).bfloat16().requires_grad_()
+    b = torch.randn(H, device="cuda").bfloat16().requires_grad_()
+    dy = torch.randn(M, H, device="cuda").bfloat16()
+    y = autograd.glu_linear(gate, up, w, b, act)
+    y.backward(dy)
+    got = [y.detach(), gate.grad, up.grad, w.grad, b.grad]
+    for t in (gate, up, w, b):
+        t.grad = None
+    a = F.silu(gate) if act == "silu" else F.gelu(gate, approximate="tanh")
+    y2 = autograd.linear(a * up, w, b)
+    y2.backward(dy)
+    ref = [y2.detach(), gate.grad, up.grad, w.grad, b.grad]
+    for name, x, r in zip(("y", "d_gate", "d_up", "dW", "db"), got, ref):
+        assert torch.isfinite(x.float()).all(), name
+        assert rel_err(x, r) < 5e-3, (name, rel_err(x, r))

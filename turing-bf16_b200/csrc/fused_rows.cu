@@ -4,7 +4,7 @@
 // quantize or row_scale kernel: tbf16/ops.py:74-89, tbf16/csrc/gemm_sm75.cu:27-47).
 //
 //   glu_rows_kernel      h = bf16(bf16(act(g)) * u) for a gated MLP (act = silu or tanh-gelu),
-//                        as torch computes act(g) * u on bf16 tensors
+//                        as torch computes act(g) * u on bf16 tensors (to within one bf16 ulp: fast exp)
 //   rmsnorm_rows_kernel  r = RMSNorm(x) in the two common roundings (Gemma: bf16(x * rsqrt(ms + eps) *
 //                        (w + offset)); Llama: bf16(w * bf16(x * rsqrt(ms + eps))))
 // then, for the produced rows: s_inv = the fused rule's power-of-two row scale (row max, target t) and
@@ -29,15 +29,27 @@ constexpr int kWarpRowsPerBlock = 8;
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// The activations use the hardware's fast exp and division (__expf, __fdividef): a few fp32 ulps from
+// the correctly rounded expf / division / tanhf that torch's kernels call, so act(g) rounds to the same
+// bf16 in all but about 1e-4 of the elements and never lands more than one bf16 ulp away. With the
+// accurate library calls these kernels were bound by arithmetic, at about half the HBM rate.
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// GELU with the tanh approximation: 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))).
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float kKappa = 0.044715f;
+__device__ __forceinline__ float sigmoid_fast(float z) { return __fdividef(1.0f, 1.0f + __expf(-z)); }
+
+constexpr float kGeluBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+constexpr float kGeluKappa = 0.044715f;
+
+// tanh(y) for the tanh-GELU's y = sqrt(2 / pi) (x + 0.044715 x^3), as 2 sigmoid(2y) - 1 rounded to fp32:
+// within a few fp32 ulps of tanhf(y) for every y (no cancellation near -1, where 1 + tanh(y) takes the
+// same 2^-24 steps as torch's 1 + tanhf(y), so tiny negative outputs match too).
+__device__ __forceinline__ float gelu_t(float x) {
   const float x3 = x * x * x;
-  return 0.5f * x * (1.0f + tanhf(kBeta * (x + kKappa * x3)));
+  return 2.0f * sigmoid_fast(2.0f * (kGeluBeta * (x + kGeluKappa * x3))) - 1.0f;
 }
+
+// GELU with the tanh approximation: 0.5 x (1 + tanh(y)).
+__device__ __forceinline__ float gelu_tanh(float x) { return 0.5f * x * (1.0f + gelu_t(x)); }
 
 // The threads that own one row: a warp (WARP, short rows, 8 rows per block) or the whole block (one row
 // per block, up to 1024 threads). Reductions go over the lanes by a shuffle tree and then, for a block,
@@ -197,6 +209,55 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) r
   emit_row<NCH, WARP>(rg, yv, amax, t, K8, y16, ldy8, s_inv, out, ldo8);
 }
 
+// Backward of h = bf16(act(g)) * u as torch's autograd takes it on bf16 tensors: a = bf16(act(g)) again,
+// du = bf16(dh a), da = bf16(dh u), dg = bf16(da act'(g)) with act' in fp32, in the order torch's
+// silu backward evaluates it (da s (1 + g (1 - s)), s = 1 / (1 + e^-g)); tanh-GELU: da (0.5 (1 + t) +
+// 0.5 g (1 - t^2) sqrt(2/pi) (1 + 3 0.044715 g^2)), t = tanh(sqrt(2/pi) (g + 0.044715 g^3)) as the
+// forward's gelu_t.
+// One block per row, 16-byte vectors.
+template <int ACT>
+__global__ void __launch_bounds__(256) glu_bwd_kernel(const uint4* __restrict__ dh, int64_t ldh8,
+                                                      const uint4* __restrict__ g, int64_t ldg8,
+                                                      const uint4* __restrict__ u, int64_t ldu8, int I8,
+                                                      uint4* __restrict__ dg, int64_t lddg8, uint4* __restrict__ du,
+                                                      int64_t lddu8) {
+  const int64_t row = blockIdx.x;
+  for (int i = threadIdx.x; i < I8; i += blockDim.x) {
+    const uint4 hv = __ldg(dh + row * ldh8 + i), gv = __ldg(g + row * ldg8 + i), uv = __ldg(u + row * ldu8 + i);
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t go[4], uo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float dgv[2], duv[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float x = k ? bf16hi(gw[j]) : bf16lo(gw[j]);
+        const float d = k ? bf16hi(hw[j]) : bf16lo(hw[j]);
+        const float up = k ? bf16hi(uw[j]) : bf16lo(uw[j]);
+        const float da = round_bf16(d * up);
+        float a;
+        if (ACT == TBF16_ACT_SILU) {
+          const float e1 = 1.0f + __expf(-x);
+          const float sg = __fdividef(1.0f, e1);
+          a = __fdividef(x, e1);
+          dgv[k] = da * sg * (1.0f + x * (1.0f - sg));
+        } else {
+          const float t = gelu_t(x);
+          a = 0.5f * x * (1.0f + t);
+          const float left = 0.5f * x, right = 1.0f + t;
+          const float right_d = left * (1.0f - t * t) * (kGeluBeta * (1.0f + 3.0f * kGeluKappa * (x * x)));
+          dgv[k] = da * (0.5f * right + right_d);
+        }
+        duv[k] = d * round_bf16(a);
+      }
+      go[j] = pack_bf16(dgv[0], dgv[1]);
+      uo[j] = pack_bf16(duv[0], duv[1]);
+    }
+    dg[row * lddg8 + i] = make_uint4(go[0], go[1], go[2], go[3]);
+    du[row * lddu8 + i] = make_uint4(uo[0], uo[1], uo[2], uo[3]);
+  }
+}
+
 // Launch shape for rows of K8 16-byte vectors: short rows one warp each (vectors per lane nch of 1, 2, 4);
 // longer rows one block each, nch (1 or 2) vectors per thread and the fewest warps that cover the row, so
 // that each thread holds little and many blocks fit an SM. nch = 0: the row is too long.
@@ -250,6 +311,31 @@ int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64
   }
 #undef TBF16_GLU_ACT
 #undef TBF16_GLU
+  return tbf16_host::check_launch();
+}
+
+int tbf16_glu_bwd(const void* dh, int64_t ldh, const void* g, int64_t ldg, const void* u, int64_t ldu, int64_t M,
+                  int64_t I, int act, void* dg, int64_t lddg, void* du, int64_t lddu, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || I < 0 || ldh < I || ldg < I || ldu < I || lddg < I || lddu < I || !dh || !g || !u || !dg || !du ||
+      (act != TBF16_ACT_SILU && act != TBF16_ACT_GELU_TANH))
+    return TBF16_ERR_INVALID;
+  if (I % 8 || ldh % 8 || ldg % 8 || ldu % 8 || lddg % 8 || lddu % 8 || !tbf16_host::aligned16(dh) ||
+      !tbf16_host::aligned16(g) || !tbf16_host::aligned16(u) || !tbf16_host::aligned16(dg) || !tbf16_host::aligned16(du))
+    return TBF16_ERR_ALIGN;
+  if (M == 0 || I == 0) return TBF16_OK;
+  if (M > INT32_MAX || I / 8 > INT32_MAX) return TBF16_ERR_UNSUPPORTED;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int I8 = (int)(I / 8);
+  const int threads = I8 >= 256 ? 256 : (I8 + 31) / 32 * 32;
+  const uint4 *hp = static_cast<const uint4*>(dh), *gp = static_cast<const uint4*>(g), *up = static_cast<const uint4*>(u);
+  uint4 *gop = static_cast<uint4*>(dg), *uop = static_cast<uint4*>(du);
+  if (act == TBF16_ACT_SILU)
+    glu_bwd_kernel<TBF16_ACT_SILU><<<(unsigned)M, threads, 0, st>>>(hp, ldh / 8, gp, ldg / 8, up, ldu / 8, I8, gop,
+                                                                     lddg / 8, uop, lddu / 8);
+  else
+    glu_bwd_kernel<TBF16_ACT_GELU_TANH><<<(unsigned)M, threads, 0, st>>>(hp, ldh / 8, gp, ldg / 8, up, ldu / 8, I8, gop,
+                                                                          lddg / 8, uop, lddu / 8);
   return tbf16_host::check_launch();
 }
 

@@ -598,16 +598,22 @@ int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   const int sms = d ? d->sms : 148;
   const int K8 = (int)(K / 8);
-  // amax: 32 column vectors per block and chunks of at least 256 rows (few same-address atomics);
-  // convert: 256 column vectors per block and chunks of at least 32 rows; both about four blocks per SM.
+  // amax: 32 column vectors per block and chunks of at least 128 rows (few same-address atomics);
+  // convert: 256 column vectors per block and chunks of at least 16 rows; both up to 16 blocks per SM.
+  // blocks per SM, amax / convert minimum rows per chunk (measured on 8192 x 2048, 2048 x 8192 and
+  // 8192 x 8192; TBF16_COL_* override them for tuning)
+  static const int knobs[3] = {
+      getenv("TBF16_COL_BLOCKS_PER_SM") ? atoi(getenv("TBF16_COL_BLOCKS_PER_SM")) : 16,
+      getenv("TBF16_COL_AMAX_MINROWS") ? atoi(getenv("TBF16_COL_AMAX_MINROWS")) : 128,
+      getenv("TBF16_COL_CONV_MINROWS") ? atoi(getenv("TBF16_COL_CONV_MINROWS")) : 16};
   auto chunking = [&](int col_blocks, int64_t min_rows, int64_t mult) {
     const int64_t chunks = std::max<int64_t>(
-        1, std::min<int64_t>((rows + min_rows - 1) / min_rows, ((int64_t)sms * 4 + col_blocks - 1) / col_blocks));
+        1, std::min<int64_t>((rows + min_rows - 1) / min_rows, ((int64_t)sms * knobs[0] + col_blocks - 1) / col_blocks));
     const int64_t per = ((rows + chunks - 1) / chunks + mult - 1) / mult * mult;
     return std::make_pair(dim3(col_blocks, (unsigned)((rows + per - 1) / per)), per);
   };
-  const auto ga = chunking((K8 + 31) / 32, 256, 8 * kColUnroll);
-  const auto gc = chunking((K8 + 255) / 256, 32, kColUnroll);
+  const auto ga = chunking((K8 + 31) / 32, std::max(knobs[1], 8 * kColUnroll), 8 * kColUnroll);
+  const auto gc = chunking((K8 + 255) / 256, std::max(knobs[2], kColUnroll), kColUnroll);
   col_amax_kernel<<<ga.first, 256, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws, rows, K8, ldx / 8,
                                             ga.second);
   col_convert_kernel<<<gc.first, 256, 0, st>>>(static_cast<const uint4*>(x), row_mul, amax_ws,

@@ -86,33 +86,83 @@ class ScaledLinearFn(torch.autograd.Function):
     @torch.autocast("cuda", enabled=False)
     def backward(ctx, dy):
         x16, sx, w = ctx.saved_tensors
-        N, K = w.shape
-        dy2 = dy.reshape(-1, N).contiguous()
-        if dy2.dtype != torch.bfloat16:
-            dy2 = dy2.bfloat16()
-        M = dy2.shape[0]
-        dx = dw = db = None
-        pad = N % 8 or K % 8
-        if ctx.needs_input_grad[0]:  # contraction over N: dY rows (L1, t=15) x W columns (t = _target_exp(N))
-            t = ops._target_exp(N)
-            dy16, sdy = ops.quantize_rows(dy2, ops.L1_TARGET, l1=True)
-            w16c, swc = quantize_cols(w.contiguous(), t)
-            if pad:
-                dx = _padded_mm(dy16, sdy, w16c, swc, M, N, K, kind="dx")
-            else:
-                dx = _scaled_mm(dy16, sdy, w16c, swc, a_mn=False, b_mn=True)  # B[k, n] = w16c[n, k]
-            dx = dx.reshape(ctx.x_shape)
-        if ctx.needs_input_grad[1]:  # contraction over M: dW[n, k] = sum_m dy[m, n] sx[m] x16[m, k]
-            # |x16| < 1, so |dW16| < M * 2^t; keep that under fp16's max (reference autograd.py:84-87).
-            t = min(0, 15 - math.ceil(math.log2(max(M, 1))))
-            dy16c, sdyc = quantize_cols(dy2, t, sx)
-            if pad:
-                dw = _padded_mm(dy16c, sdyc, x16, None, M, N, K, kind="dw")
-            else:
-                dw = _scaled_mm(dy16c, sdyc, x16, _ones(K, x16.device), a_mn=True, b_mn=True)
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            db = dy2.float().sum(0).to(dy.dtype)
-        return dx, dw, db
+        return _linear_backward(dy, x16, sx, w, ctx.needs_input_grad[0], ctx.needs_input_grad[1],
+                                ctx.has_bias and ctx.needs_input_grad[2], ctx.x_shape)
+
+
+def _linear_backward(dy, x16, sx, w, want_dx, want_dw, want_db, x_shape):
+    """dX, dW, db of y = x W^T + b from the forward's fp16 rows x16 and inverse row scales sx."""
+    N, K = w.shape
+    dy2 = dy.reshape(-1, N).contiguous()
+    if dy2.dtype != torch.bfloat16:
+        dy2 = dy2.bfloat16()
+    M = dy2.shape[0]
+    dx = dw = db = None
+    pad = N % 8 or K % 8
+    if want_dx:  # contraction over N: dY rows (L1, t=15) x W columns (t = _target_exp(N))
+        t = ops._target_exp(N)
+        dy16, sdy = ops.quantize_rows(dy2, ops.L1_TARGET, l1=True)
+        w16c, swc = quantize_cols(w.contiguous(), t)
+        if pad:
+            dx = _padded_mm(dy16, sdy, w16c, swc, M, N, K, kind="dx")
+        else:
+            dx = _scaled_mm(dy16, sdy, w16c, swc, a_mn=False, b_mn=True)  # B[k, n] = w16c[n, k]
+        dx = dx.reshape(x_shape)
+    if want_dw:  # contraction over M: dW[n, k] = sum_m dy[m, n] sx[m] x16[m, k]
+        # |x16| < 1, so |dW16| < M * 2^t; keep that under fp16's max (reference autograd.py:84-87).
+        t = min(0, 15 - math.ceil(math.log2(max(M, 1))))
+        dy16c, sdyc = quantize_cols(dy2, t, sx.reshape(-1))
+        x16 = x16.reshape(M, K)
+        if pad:
+            dw = _padded_mm(dy16c, sdyc, x16, None, M, N, K, kind="dw")
+        else:
+            dw = _scaled_mm(dy16c, sdyc, x16, _ones(K, x16.device), a_mn=True, b_mn=True)
+    if want_db:
+        db = dy2.float().sum(0).to(dy.dtype)
+    return dx, dw, db
+
+
+class GLULinearFn(torch.autograd.Function):
+    """y = (act(gate) * up) W^T + b for training, with the gated activation fused: forward, the
+    producer-fused rows (tbf16_glu_rows: h's fp16 operand and row scales in one pass, no row pass in the
+    linear); backward, the linear's dX and dW as ScaledLinearFn's (h's fp16 rows stand in for x16) and
+    d_gate, d_up in one pass (tbf16_glu_bwd, torch's autograd arithmetic for act(g) * u on bf16).
+    Needs I (gate's last dimension) a multiple of 8."""
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def forward(ctx, gate, up, w, bias, act):
+        N, I = w.shape
+        h16, s_inv = ops.glu_rows(gate, up, act)
+        w16, sw = ops.prepare_weight(w)
+        ctx.save_for_backward(gate, up, h16, s_inv, w)
+        ctx.act, ctx.has_bias = act, bias is not None
+        return ops.linear_q(h16.reshape(-1, I), s_inv.reshape(-1), w16, sw, bias).reshape(*gate.shape[:-1], N)
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def backward(ctx, dy):
+        gate, up, h16, s_inv, w = ctx.saved_tensors
+        want_gu = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        dh, dw, db = _linear_backward(dy, h16, s_inv, w, want_gu, ctx.needs_input_grad[2],
+                                      ctx.has_bias and ctx.needs_input_grad[3], gate.shape)
+        dg = du = None
+        if want_gu:
+            dg, du = ops.glu_bwd(dh.to(torch.bfloat16), gate, up, ctx.act)
+        return dg, du, dw, db, None
+
+
+def glu_linear(gate, up, w, bias=None, act="silu"):
+    """Training form of linear(act(gate) * up, w, bias) with the activation fused into the linear's
+    input pass and its backward (GLULinearFn); act: "silu" or "gelu_tanh". Falls back to the unfused
+    composition for inputs the fused kernels do not take (row length not a multiple of 8 or above
+    16384, non-bf16)."""
+    I = gate.shape[-1]
+    if (gate.dtype == up.dtype == torch.bfloat16 and I % 8 == 0 and I <= 16384 and w.shape[1] == I
+            and gate.is_cuda):
+        return GLULinearFn.apply(gate, up, w, bias, act)
+    a = F.silu(gate) if act == "silu" else F.gelu(gate, approximate="tanh")
+    return linear(a * up, w, bias)
 
 
 def _padded_mm(a16, sa, b16, sb, M, N, K, kind):

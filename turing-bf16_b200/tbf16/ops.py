@@ -341,7 +341,8 @@ def _rows2d(t, name):
 
 @torch.autocast("cuda", enabled=False)
 def glu_rows(gate: torch.Tensor, up: torch.Tensor, act: str = "silu", target_exp: int = 15, want_h: bool = False):
-    """Producer-fused gated activation: h = bf16(bf16(act(gate)) * up) (torch's act(g) * u on bf16 tensors)
+    """Producer-fused gated activation: h = bf16(bf16(act(gate)) * up) (torch's act(g) * u on bf16 tensors,
+    to within one bf16 ulp)
     with the row scales of the fused linear computed in the same pass. Returns (h16, s_inv[, h]): the fp16
     operand fp16(h / s_inv) and the fp32 power-of-two inverse row scales, as quantize_rows / row_scale
     give for h. act: "silu" or "gelu_tanh"."""
@@ -362,6 +363,26 @@ def glu_rows(gate: torch.Tensor, up: torch.Tensor, act: str = "silu", target_exp
     shape = gate.shape
     out = (h16.reshape(shape), s_inv.reshape(shape[:-1]))
     return out + (h.reshape(shape),) if want_h else out
+
+
+def glu_bwd(dh: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, act: str = "silu"):
+    """Gradients of h = bf16(act(gate)) * up as torch's autograd gives them on bf16 tensors (to within one
+    bf16 ulp), in one pass:
+    returns (d_gate, d_up), bf16 of gate's shape."""
+    require_cuda(dh, gate, up)
+    if act not in _ACTS:
+        raise RuntimeError(f"tbf16.glu_bwd: act must be one of {sorted(_ACTS)}")
+    if not (dh.shape == gate.shape == up.shape):
+        raise RuntimeError("tbf16.glu_bwd: dh, gate and up shapes differ")
+    h2, g2, u2 = (_rows2d(t, "glu_bwd") for t in (dh, gate, up))
+    M, I = g2.shape
+    if I % 8:
+        raise RuntimeError("tbf16.glu_bwd: the row length must be a multiple of 8")
+    dg = torch.empty((M, I), device=gate.device, dtype=torch.bfloat16)
+    du = torch.empty((M, I), device=gate.device, dtype=torch.bfloat16)
+    call("tbf16_glu_bwd", ptr(h2), h2.stride(0), ptr(g2), g2.stride(0), ptr(u2), u2.stride(0), M, I, _ACTS[act],
+         ptr(dg), I, ptr(du), I, stream_ptr(gate.device))
+    return dg.reshape(gate.shape), du.reshape(gate.shape)
 
 
 @torch.autocast("cuda", enabled=False)
@@ -445,5 +466,5 @@ def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bi
 
 
 __all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
-           "linear_host", "glu_rows", "rmsnorm_rows", "glu_linear", "rmsnorm_linear", "rmsnorm",
+           "linear_host", "glu_rows", "glu_bwd", "rmsnorm_rows", "glu_linear", "rmsnorm_linear", "rmsnorm",
            "available", "_target_exp"]
