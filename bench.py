@@ -408,11 +408,17 @@ class _GemmaLayer(torch.nn.Module):
         import torch.nn.functional as F
         B, S, _ = x.shape
         h = self._norm_rows(x, self.in_norm)
-        q = self._norm(self._proj(h, self.q_proj).view(B, S, self.h, self.d), self.q_norm).transpose(1, 2)
-        k = self._norm(self._proj(h, self.k_proj).view(B, S, self.kv, self.d), self.k_norm).transpose(1, 2)
+        q = self._proj(h, self.q_proj).view(B, S, self.h, self.d)
+        k = self._proj(h, self.k_proj).view(B, S, self.kv, self.d)
         v = self._proj(h, self.v_proj).view(B, S, self.kv, self.d).transpose(1, 2)
-        rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
-        q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
+        if self.fused:  # QK-norm and RoPE in one pass per tensor
+            from tbf16 import ops
+            q = ops.rmsnorm_rope(q, self.q_norm.weight, cos, sin, 1e-6, 1.0, "gemma").transpose(1, 2)
+            k = ops.rmsnorm_rope(k, self.k_norm.weight, cos, sin, 1e-6, 1.0, "gemma").transpose(1, 2)
+        else:
+            q, k = self.q_norm(q).transpose(1, 2), self.k_norm(k).transpose(1, 2)
+            rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
+            q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         x = x + self._norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)), self.post_attn_norm)
         h = self._norm_rows(x, self.pre_ff_norm)
@@ -502,7 +508,8 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
             "fused": {"ms_per_prefill": round(ms_f, 2), "tflops_per_gpu": round(flop / (ms_f / 1e3) / 1e12, 1),
                       "logits_rel_diff_vs_unfused": round(drift, 5),
                       "what": ("RMSNorm before q/k/v and gate/up, and GeGLU before down, fused with the row "
-                               "scales; the other RMSNorms (q/k heads, after attention and MLP) on the same kernel")}}
+                               "scales; the q/k head RMSNorms fused with RoPE (one pass per tensor); the "
+                               "RMSNorms after attention and MLP on the norm kernel")}}
 
 
 def dist_rank():

@@ -187,6 +187,18 @@ int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64
 int tbf16_glu_bwd(const void* dh, int64_t ldh, const void* g, int64_t ldg, const void* u, int64_t ldu, int64_t M,
                   int64_t I, int act, void* dg, int64_t lddg, void* du, int64_t lddu, void* stream);
 
+/* Attention operands: per-head RMSNorm (optional) and rotary embedding in one pass, as a model computes
+ * them on bf16 tensors. x: bf16 rows of D values (one head of one token; M rows, row stride ldx), row r at
+ * position (r / H) % S -- a contiguous (B, S, H, D) tensor. With w non-null, y = rmsnorm over the row as
+ * tbf16_rmsnorm_rows (style, offset, eps); else y = x. Then out = bf16_rn(bf16_rn(y * cos) + bf16_rn(rot(y) *
+ * sin)), rot(y) = (-y[D/2:], y[:D/2]) (rotate-half), cos / sin bf16 [S, D] rows (row stride ldc). Replaces
+ * the norm + five elementwise passes (mul, neg, cat, mul, add) before the attention's scale passes; no
+ * reference counterpart (the reference leaves both to the model). D = 64, 128, 256 or 512
+ * (TBF16_ERR_UNSUPPORTED otherwise); strides multiples of 8, pointers 16-byte aligned. */
+int tbf16_rmsnorm_rope(const void* x, int64_t ldx, const void* w, int64_t M, int64_t D, float eps, int style,
+                       float offset, const void* cos, const void* sin, int64_t ldc, int64_t S, int64_t H, void* out,
+                       int64_t ldo, void* stream);
+
 /* RMSNorm: ms[m] = mean_k x[m, k]^2 (fp32), rs = rsqrt(ms + eps) and
  *   style TBF16_NORM_SCALE_FP32: r[m, k] = bf16_rn((x[m, k] * rs) * (w[k] + offset))   (Gemma: offset 1)
  *   style TBF16_NORM_SCALE_BF16: r[m, k] = bf16_rn(w[k] * bf16_rn(x[m, k] * rs))        (Llama: offset unused)

@@ -156,3 +156,43 @@ def test_glu_linear_training_matches_unfused(act):
     for name, x, r in zip(("y", "d_gate", "d_up", "dW", "db"), got, ref):
         assert torch.isfinite(x.float()).all(), name
         assert rel_err(x, r) < 5e-3, (name, rel_err(x, r))
+
+
+def _rope_ref(y, cos, sin):
+    """The model-side rotary embedding on bf16 tensors (rotate-half)."""
+    D = y.shape[-1]
+    rot = torch.cat([-y[..., D // 2:], y[..., :D // 2]], -1)
+    return y * cos + rot * sin
+
+
+@pytest.mark.parametrize("D", [64, 128, 256, 512])
+@pytest.mark.parametrize("norm", [True, False])
+def test_rmsnorm_rope_matches_torch(D, norm):
+    """QK-norm + RoPE in one pass: bit-equal to torch's bf16 ops on the same normed rows (the norm itself
+    is rmsnorm_rows' arithmetic, checked against the oracle above)."""
+    from tbf16 import ops
+    g = torch.Generator().manual_seed(D + norm)
+    B, S, H = 2, 37, 3
+    x = (torch.randn(B, S, H, D, generator=g) * torch.exp2(torch.randint(-6, 6, (B, S, H, 1), generator=g).float()))
+    x = x.bfloat16().cuda()
+    w = (torch.randn(D, generator=g) * 0.2).bfloat16().cuda() if norm else None
+    pos = torch.arange(S, dtype=torch.float32)
+    inv = 1.0 / (1e4 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    ang = torch.outer(pos, inv)
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16().cuda()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16().cuda()
+    out = ops.rmsnorm_rope(x, w, cos[None, None], sin[None, None], 1e-6, 1.0, "gemma")
+    y = ops.rmsnorm(x, w, 1e-6, 1.0, "gemma") if norm else x
+    ref = _rope_ref(y.transpose(1, 2), cos, sin).transpose(1, 2)  # the model applies it on (B, H, S, D)
+    assert out.shape == x.shape
+    assert torch.equal(out.view(torch.int16), ref.contiguous().view(torch.int16))
+
+
+def test_rmsnorm_rope_rejects():
+    from tbf16 import ops
+    x = torch.zeros(1, 4, 2, 96, dtype=torch.bfloat16, device="cuda")
+    c = torch.zeros(4, 96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError):
+        ops.rmsnorm_rope(x, None, c, c)  # D = 96 is not one of 64, 128, 256, 512
+    with pytest.raises(RuntimeError):
+        ops.rmsnorm_rope(x[..., :64], None, c[:3, :64], c[:3, :64])  # cos / sin for the wrong S

@@ -209,6 +209,94 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) r
   emit_row<NCH, WARP>(rg, yv, amax, t, K8, y16, ldy8, s_inv, out, ldo8);
 }
 
+// Attention operands: RMSNorm over each head's D values (optional; the QK-norm of Gemma 3 / Qwen 3) and
+// rotary embedding with the rotate-half convention, as a model computes them on bf16 tensors:
+// y = the norm's bf16 output (rmsnorm_rows' arithmetic), out = bf16(bf16(y cos) + bf16(rot(y) sin)) with
+// rot(y) = (-y[D/2:], y[:D/2]) and cos, sin the bf16 rows of the token's position. One warp per row of
+// D = 64, 128, 256 or 512 (a lane holds 1 or 2 16-byte vectors); row r is position (r / H) % S.
+template <int NCH, int STYLE, bool NORM>
+__global__ void __launch_bounds__(32 * kWarpRowsPerBlock) norm_rope_kernel(
+    const uint4* __restrict__ x, int64_t ldx8, const uint4* __restrict__ w, int64_t M, int D8, float eps, float offset,
+    const uint4* __restrict__ cosv, const uint4* __restrict__ sinv, int64_t ldc8, int64_t S, int64_t H,
+    uint4* __restrict__ out, int64_t ldo8) {
+  __shared__ float red[1];
+  RowGroup<true> rg(red);
+  if (rg.row >= M) return;
+  const int half = D8 / 2;  // vectors in half a row: the rotation partner of vector c is c ^ half
+  uint4 yv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int i = rg.tid + 32 * c;
+    yv[c] = i < D8 ? __ldg(x + rg.row * ldx8 + i) : make_uint4(0, 0, 0, 0);
+  }
+  if (NORM) {
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t xw[4] = {yv[c].x, yv[c].y, yv[c].z, yv[c].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = bf16lo(xw[j]), b = bf16hi(xw[j]);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(b, b, ss);
+      }
+    }
+    const float r = rsqrtf(rg.template reduce<false>(ss) / (float)(D8 * 8) + eps);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = rg.tid + 32 * c;
+      const uint4 wv = i < D8 ? __ldg(w + i) : make_uint4(0, 0, 0, 0);
+      const uint32_t xw[4] = {yv[c].x, yv[c].y, yv[c].z, yv[c].w};
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float y0, y1;
+        if (STYLE == TBF16_NORM_SCALE_FP32) {
+          y0 = (bf16lo(xw[j]) * r) * (bf16lo(ww[j]) + offset);
+          y1 = (bf16hi(xw[j]) * r) * (bf16hi(ww[j]) + offset);
+        } else {
+          y0 = bf16lo(ww[j]) * round_bf16(bf16lo(xw[j]) * r);
+          y1 = bf16hi(ww[j]) * round_bf16(bf16hi(xw[j]) * r);
+        }
+        o[j] = pack_bf16(y0, y1);
+      }
+      yv[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // the partner vectors: another lane's (half < 32) or this lane's other vector (half = 32)
+  uint4 pv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    if (half < 32) {
+      pv[c].x = __shfl_xor_sync(0xffffffffu, yv[c].x, half);
+      pv[c].y = __shfl_xor_sync(0xffffffffu, yv[c].y, half);
+      pv[c].z = __shfl_xor_sync(0xffffffffu, yv[c].z, half);
+      pv[c].w = __shfl_xor_sync(0xffffffffu, yv[c].w, half);
+    } else {
+      pv[c] = yv[c ^ 1];
+    }
+  }
+  const int64_t pos = (rg.row / H) % S;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int i = rg.tid + 32 * c;
+    if (i >= D8) continue;
+    const float sign = i < half ? -1.f : 1.f;
+    const uint4 cv = __ldg(cosv + pos * ldc8 + i), sv = __ldg(sinv + pos * ldc8 + i);
+    const uint32_t yw[4] = {yv[c].x, yv[c].y, yv[c].z, yv[c].w}, pw[4] = {pv[c].x, pv[c].y, pv[c].z, pv[c].w};
+    const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = round_bf16(bf16lo(yw[j]) * bf16lo(cw[j])) + round_bf16(sign * bf16lo(pw[j]) * bf16lo(sw[j]));
+      const float hi = round_bf16(bf16hi(yw[j]) * bf16hi(cw[j])) + round_bf16(sign * bf16hi(pw[j]) * bf16hi(sw[j]));
+      o[j] = pack_bf16(lo, hi);
+    }
+    out[rg.row * ldo8 + i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // Backward of h = bf16(act(g)) * u as torch's autograd takes it on bf16 tensors: a = bf16(act(g)) again,
 // du = bf16(dh a), da = bf16(dh u), dg = bf16(da act'(g)) with act' in fp32, in the order torch's
 // silu backward evaluates it (da s (1 + g (1 - s)), s = 1 / (1 + e^-g)); tanh-GELU: da (0.5 (1 + t) +
@@ -336,6 +424,41 @@ int tbf16_glu_bwd(const void* dh, int64_t ldh, const void* g, int64_t ldg, const
   else
     glu_bwd_kernel<TBF16_ACT_GELU_TANH><<<(unsigned)M, threads, 0, st>>>(hp, ldh / 8, gp, ldg / 8, up, ldu / 8, I8, gop,
                                                                           lddg / 8, uop, lddu / 8);
+  return tbf16_host::check_launch();
+}
+
+int tbf16_rmsnorm_rope(const void* x, int64_t ldx, const void* w, int64_t M, int64_t D, float eps, int style,
+                       float offset, const void* cos, const void* sin, int64_t ldc, int64_t S, int64_t H, void* out,
+                       int64_t ldo, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (M < 0 || S <= 0 || H <= 0 || ldx < D || ldc < D || ldo < D || !x || !cos || !sin || !out || !(eps >= 0.f) ||
+      (style != TBF16_NORM_SCALE_FP32 && style != TBF16_NORM_SCALE_BF16))
+    return TBF16_ERR_INVALID;
+  if (D != 64 && D != 128 && D != 256 && D != 512) return TBF16_ERR_UNSUPPORTED;
+  if (ldx % 8 || ldc % 8 || ldo % 8 || !tbf16_host::aligned16(x) || (w && !tbf16_host::aligned16(w)) ||
+      !tbf16_host::aligned16(cos) || !tbf16_host::aligned16(sin) || !tbf16_host::aligned16(out))
+    return TBF16_ERR_ALIGN;
+  if (M == 0) return TBF16_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)((M + kWarpRowsPerBlock - 1) / kWarpRowsPerBlock);
+  const uint4 *xp = static_cast<const uint4*>(x), *wp = static_cast<const uint4*>(w);
+  const uint4 *cp = static_cast<const uint4*>(cos), *sp = static_cast<const uint4*>(sin);
+  uint4* op = static_cast<uint4*>(out);
+  const int D8 = (int)(D / 8);
+#define TBF16_ROPE(N, S_, NORM)                                                                                     \
+  norm_rope_kernel<N, S_, NORM><<<blocks, 32 * kWarpRowsPerBlock, 0, st>>>(xp, ldx / 8, wp, M, D8, eps, offset, cp, sp, \
+                                                                          ldc / 8, S, H, op, ldo / 8)
+#define TBF16_ROPE_N(N)                                                                  \
+  if (!w) TBF16_ROPE(N, TBF16_NORM_SCALE_FP32, false);                                   \
+  else if (style == TBF16_NORM_SCALE_FP32) TBF16_ROPE(N, TBF16_NORM_SCALE_FP32, true);   \
+  else TBF16_ROPE(N, TBF16_NORM_SCALE_BF16, true)
+  if (D8 <= 32) {
+    TBF16_ROPE_N(1);
+  } else {
+    TBF16_ROPE_N(2);
+  }
+#undef TBF16_ROPE_N
+#undef TBF16_ROPE
   return tbf16_host::check_launch();
 }
 

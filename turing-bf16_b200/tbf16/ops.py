@@ -426,6 +426,31 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offset: fl
     return r.reshape(x.shape)
 
 
+@torch.autocast("cuda", enabled=False)
+def rmsnorm_rope(x: torch.Tensor, weight, cos: torch.Tensor, sin: torch.Tensor, eps: float = 1e-6, offset: float = 1.0,
+                 style: str = "gemma"):
+    """Per-head RMSNorm (weight None: none) and rotate-half rotary embedding of x (..., S, H, D) bf16 in one
+    pass: rmsnorm(x) * cos + rot(rmsnorm(x)) * sin with torch's bf16 roundings, rot(y) = cat(-y[..., D/2:],
+    y[..., :D/2]); cos, sin bf16 holding S x D values (e.g. (S, D) or (1, 1, S, D)). D = 64, 128, 256 or 512.
+    Returns a tensor of x's shape (contiguous)."""
+    require_cuda(x, cos, sin)
+    if x.dtype != torch.bfloat16 or cos.dtype != torch.bfloat16 or sin.dtype != torch.bfloat16 or x.dim() < 3:
+        raise RuntimeError("tbf16.rmsnorm_rope: bf16 x (..., S, H, D), cos and sin expected")
+    S, H, D = x.shape[-3:]
+    if cos.numel() != S * D or sin.numel() != S * D:
+        raise RuntimeError("tbf16.rmsnorm_rope: cos / sin must hold S x D values")
+    if style not in _NORM_STYLES:
+        raise RuntimeError(f"tbf16.rmsnorm_rope: style must be one of {sorted(_NORM_STYLES)}")
+    xc = x.contiguous()
+    c2, s2 = cos.reshape(S, D).contiguous(), sin.reshape(S, D).contiguous()
+    w = None if weight is None else weight.to(torch.bfloat16).contiguous()
+    out = torch.empty_like(xc)
+    M = xc.numel() // D
+    call("tbf16_rmsnorm_rope", ptr(xc), D, ptr(w), M, D, float(eps), _NORM_STYLES[style], float(offset), ptr(c2),
+         ptr(s2), D, S, H, ptr(out), D, stream_ptr(x.device))
+    return out
+
+
 def _linear_from_rows(q16, s_inv, bf16_rows, w16, w_sinv, bias, lead_shape):
     """The down projection of an already row-scaled operand: the same kernels and arithmetic as
     scaled_linear on the bf16 rows (GEMV semantics up to GEMV_ROWS rows, which need the bf16 rows)."""
@@ -467,4 +492,5 @@ def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bi
 
 __all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
            "linear_host", "glu_rows", "glu_bwd", "rmsnorm_rows", "glu_linear", "rmsnorm_linear", "rmsnorm",
+           "rmsnorm_rope",
            "available", "_target_exp"]
