@@ -384,6 +384,20 @@ class _GemmaLayer(torch.nn.Module):
 
     fused = False  # producer fusion: norms and the GeGLU write the next linears' fp16 rows and scales
 
+    def fuse_projections(self):
+        """The prepared weight rows of q/k/v and of gate/up stacked, so each group is one GEMM (as
+        fused-QKV / fused-gate-up checkpoints store them): the same products, fewer partly filled waves."""
+        cat = lambda *ls: (torch.cat([l.weight16 for l in ls]), torch.cat([l.weight_scale for l in ls]))
+        self.qkv_rows = cat(self.q_proj, self.k_proj, self.v_proj)
+        self.gu_rows = cat(self.gate_proj, self.up_proj)
+        self.fused = True
+
+    def _proj_rows(self, rows, wrows):
+        from tbf16 import ops
+        r16, s_inv = rows
+        y = ops.linear_q(r16.reshape(-1, r16.shape[-1]), s_inv.reshape(-1), *wrows)
+        return y.reshape(*r16.shape[:-1], y.shape[-1])
+
     def _proj(self, x, lin):
         from tbf16 import ops
         if isinstance(x, tuple):  # (fp16 rows, inverse scales) from a fused producer
@@ -408,25 +422,33 @@ class _GemmaLayer(torch.nn.Module):
         import torch.nn.functional as F
         B, S, _ = x.shape
         h = self._norm_rows(x, self.in_norm)
-        q = self._proj(h, self.q_proj).view(B, S, self.h, self.d)
-        k = self._proj(h, self.k_proj).view(B, S, self.kv, self.d)
-        v = self._proj(h, self.v_proj).view(B, S, self.kv, self.d).transpose(1, 2)
-        if self.fused:  # QK-norm and RoPE in one pass per tensor
+        if self.fused:  # one q/k/v GEMM; QK-norm and RoPE in one pass per tensor, read from its column slices
             from tbf16 import ops
+            qkv = self._proj_rows(h, self.qkv_rows)
+            nq, nk = self.h * self.d, self.kv * self.d
+            q = qkv[..., :nq].view(B, S, self.h, self.d)
+            k = qkv[..., nq:nq + nk].view(B, S, self.kv, self.d)
+            v = qkv[..., nq + nk:].view(B, S, self.kv, self.d).transpose(1, 2)
             q = ops.rmsnorm_rope(q, self.q_norm.weight, cos, sin, 1e-6, 1.0, "gemma").transpose(1, 2)
             k = ops.rmsnorm_rope(k, self.k_norm.weight, cos, sin, 1e-6, 1.0, "gemma").transpose(1, 2)
         else:
+            q = self._proj(h, self.q_proj).view(B, S, self.h, self.d)
+            k = self._proj(h, self.k_proj).view(B, S, self.kv, self.d)
+            v = self._proj(h, self.v_proj).view(B, S, self.kv, self.d).transpose(1, 2)
             q, k = self.q_norm(q).transpose(1, 2), self.k_norm(k).transpose(1, 2)
             rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
             q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         x = x + self._norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)), self.post_attn_norm)
         h = self._norm_rows(x, self.pre_ff_norm)
-        gate, up = self._proj(h, self.gate_proj), self._proj(h, self.up_proj)
-        if self.fused:
+        if self.fused:  # one gate/up GEMM; the GeGLU reads its two column halves in place
             from tbf16 import ops
-            y = ops.glu_linear(gate, up, self.down_proj.weight16, self.down_proj.weight_scale, act="gelu_tanh")
+            gu = self._proj_rows(h, self.gu_rows)
+            inter = self.gate_proj.weight16.shape[0]
+            y = ops.glu_linear(gu[..., :inter], gu[..., inter:], self.down_proj.weight16, self.down_proj.weight_scale,
+                               act="gelu_tanh")
         else:
+            gate, up = self._proj(h, self.gate_proj), self._proj(h, self.up_proj)
             y = self.down_proj(F.gelu(gate, approximate="tanh") * up)
         return x + self._norm(y, self.post_ff_norm)
 
@@ -485,7 +507,7 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
     # linears' fp16 rows and row scales (tbf16.ops.rmsnorm_rows / glu_linear) instead of bf16 tensors
     # that the linears read again for their row pass
     for layer in model:
-        layer.fused = True
+        layer.fuse_projections()
     for _ in range(2):
         logits_f = step()
     torch.cuda.synchronize()
@@ -508,8 +530,9 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
             "fused": {"ms_per_prefill": round(ms_f, 2), "tflops_per_gpu": round(flop / (ms_f / 1e3) / 1e12, 1),
                       "logits_rel_diff_vs_unfused": round(drift, 5),
                       "what": ("RMSNorm before q/k/v and gate/up, and GeGLU before down, fused with the row "
-                               "scales; the q/k head RMSNorms fused with RoPE (one pass per tensor); the "
-                               "RMSNorms after attention and MLP on the norm kernel")}}
+                               "scales; q/k/v and gate/up each one GEMM over the stacked weight rows; the q/k "
+                               "head RMSNorms fused with RoPE (one pass per tensor, read from the QKV output's "
+                               "column slices); the RMSNorms after attention and MLP on the norm kernel")}}
 
 
 def dist_rank():

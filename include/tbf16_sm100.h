@@ -188,14 +188,16 @@ int tbf16_glu_bwd(const void* dh, int64_t ldh, const void* g, int64_t ldg, const
                   int64_t I, int act, void* dg, int64_t lddg, void* du, int64_t lddu, void* stream);
 
 /* Attention operands: per-head RMSNorm (optional) and rotary embedding in one pass, as a model computes
- * them on bf16 tensors. x: bf16 rows of D values (one head of one token; M rows, row stride ldx), row r at
- * position (r / H) % S -- a contiguous (B, S, H, D) tensor. With w non-null, y = rmsnorm over the row as
+ * them on bf16 tensors. x: bf16 rows of D values, one per head of a token: row r is head r % H of token
+ * r / H, at x + (r / H) * ldtok + (r % H) * D, position (r / H) % S -- a (B, S, H, D) tensor whose heads
+ * are contiguous and whose tokens are ldtok >= H * D elements apart (a column slice of a fused QKV
+ * projection, or contiguous with ldtok = H * D). M a multiple of H. out: rows ldo apart. With w non-null, y = rmsnorm over the row as
  * tbf16_rmsnorm_rows (style, offset, eps); else y = x. Then out = bf16_rn(bf16_rn(y * cos) + bf16_rn(rot(y) *
  * sin)), rot(y) = (-y[D/2:], y[:D/2]) (rotate-half), cos / sin bf16 [S, D] rows (row stride ldc). Replaces
  * the norm + five elementwise passes (mul, neg, cat, mul, add) before the attention's scale passes; no
  * reference counterpart (the reference leaves both to the model). D = 64, 128, 256 or 512
  * (TBF16_ERR_UNSUPPORTED otherwise); strides multiples of 8, pointers 16-byte aligned. */
-int tbf16_rmsnorm_rope(const void* x, int64_t ldx, const void* w, int64_t M, int64_t D, float eps, int style,
+int tbf16_rmsnorm_rope(const void* x, int64_t ldtok, const void* w, int64_t M, int64_t D, float eps, int style,
                        float offset, const void* cos, const void* sin, int64_t ldc, int64_t S, int64_t H, void* out,
                        int64_t ldo, void* stream);
 

@@ -196,3 +196,23 @@ def test_rmsnorm_rope_rejects():
         ops.rmsnorm_rope(x, None, c, c)  # D = 96 is not one of 64, 128, 256, 512
     with pytest.raises(RuntimeError):
         ops.rmsnorm_rope(x[..., :64], None, c[:3, :64], c[:3, :64])  # cos / sin for the wrong S
+
+
+def test_rmsnorm_rope_column_slices_of_fused_qkv():
+    """q and k read in place as column slices of one [tokens, (Hq + 2 Hkv) D] projection output."""
+    from tbf16 import ops
+    g = torch.Generator().manual_seed(5)
+    B, S, Hq, Hk, D = 2, 19, 4, 2, 128
+    qkv = (torch.randn(B, S, (Hq + 2 * Hk) * D, generator=g) * 3).bfloat16().cuda()
+    q = qkv[..., :Hq * D].view(B, S, Hq, D)
+    k = qkv[..., Hq * D:(Hq + Hk) * D].view(B, S, Hk, D)
+    ang = torch.outer(torch.arange(S, dtype=torch.float32), 1.0 / (1e4 ** (torch.arange(0, D, 2) / D)))
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16().cuda()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16().cuda()
+    for t, seed in ((q, 1), (k, 2)):
+        w = (torch.randn(D, generator=torch.Generator().manual_seed(seed)) * 0.2).bfloat16().cuda()
+        out = ops.rmsnorm_rope(t, w, cos, sin)
+        ref = ops.rmsnorm_rope(t.contiguous(), w, cos, sin)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        ref2 = _rope_ref(ops.rmsnorm(t.contiguous(), w, 1e-6, 1.0, "gemma").transpose(1, 2), cos, sin).transpose(1, 2)
+        assert torch.equal(out.view(torch.int16), ref2.contiguous().view(torch.int16))

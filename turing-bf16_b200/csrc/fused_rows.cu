@@ -213,21 +213,24 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) r
 // rotary embedding with the rotate-half convention, as a model computes them on bf16 tensors:
 // y = the norm's bf16 output (rmsnorm_rows' arithmetic), out = bf16(bf16(y cos) + bf16(rot(y) sin)) with
 // rot(y) = (-y[D/2:], y[:D/2]) and cos, sin the bf16 rows of the token's position. One warp per row of
-// D = 64, 128, 256 or 512 (a lane holds 1 or 2 16-byte vectors); row r is position (r / H) % S.
+// D = 64, 128, 256 or 512 (a lane holds 1 or 2 16-byte vectors); row r is head r % H of token r / H (tokens
+// ldtok apart in x, so q and k can be column slices of one fused projection), at position (r / H) % S.
 template <int NCH, int STYLE, bool NORM>
 __global__ void __launch_bounds__(32 * kWarpRowsPerBlock) norm_rope_kernel(
-    const uint4* __restrict__ x, int64_t ldx8, const uint4* __restrict__ w, int64_t M, int D8, float eps, float offset,
+    const uint4* __restrict__ x, int64_t ldtok8, const uint4* __restrict__ w, int64_t M, int D8, float eps, float offset,
     const uint4* __restrict__ cosv, const uint4* __restrict__ sinv, int64_t ldc8, int64_t S, int64_t H,
     uint4* __restrict__ out, int64_t ldo8) {
   __shared__ float red[1];
   RowGroup<true> rg(red);
   if (rg.row >= M) return;
   const int half = D8 / 2;  // vectors in half a row: the rotation partner of vector c is c ^ half
+  const int64_t tok = rg.row / H;
+  const uint4* xr = x + tok * ldtok8 + (rg.row - tok * H) * D8;
   uint4 yv[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int i = rg.tid + 32 * c;
-    yv[c] = i < D8 ? __ldg(x + rg.row * ldx8 + i) : make_uint4(0, 0, 0, 0);
+    yv[c] = i < D8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
   }
   if (NORM) {
     float ss = 0.f;
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(32 * kWarpRowsPerBlock) norm_rope_kernel(
       pv[c] = yv[c ^ 1];
     }
   }
-  const int64_t pos = (rg.row / H) % S;
+  const int64_t pos = tok % S;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int i = rg.tid + 32 * c;
@@ -427,15 +430,16 @@ int tbf16_glu_bwd(const void* dh, int64_t ldh, const void* g, int64_t ldg, const
   return tbf16_host::check_launch();
 }
 
-int tbf16_rmsnorm_rope(const void* x, int64_t ldx, const void* w, int64_t M, int64_t D, float eps, int style,
+int tbf16_rmsnorm_rope(const void* x, int64_t ldtok, const void* w, int64_t M, int64_t D, float eps, int style,
                        float offset, const void* cos, const void* sin, int64_t ldc, int64_t S, int64_t H, void* out,
                        int64_t ldo, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
-  if (M < 0 || S <= 0 || H <= 0 || ldx < D || ldc < D || ldo < D || !x || !cos || !sin || !out || !(eps >= 0.f) ||
+  if (M < 0 || S <= 0 || H <= 0 || M % H || ldtok < H * D || ldc < D || ldo < D || !x || !cos || !sin || !out ||
+      !(eps >= 0.f) ||
       (style != TBF16_NORM_SCALE_FP32 && style != TBF16_NORM_SCALE_BF16))
     return TBF16_ERR_INVALID;
   if (D != 64 && D != 128 && D != 256 && D != 512) return TBF16_ERR_UNSUPPORTED;
-  if (ldx % 8 || ldc % 8 || ldo % 8 || !tbf16_host::aligned16(x) || (w && !tbf16_host::aligned16(w)) ||
+  if (ldtok % 8 || ldc % 8 || ldo % 8 || !tbf16_host::aligned16(x) || (w && !tbf16_host::aligned16(w)) ||
       !tbf16_host::aligned16(cos) || !tbf16_host::aligned16(sin) || !tbf16_host::aligned16(out))
     return TBF16_ERR_ALIGN;
   if (M == 0) return TBF16_OK;
@@ -446,7 +450,7 @@ int tbf16_rmsnorm_rope(const void* x, int64_t ldx, const void* w, int64_t M, int
   uint4* op = static_cast<uint4*>(out);
   const int D8 = (int)(D / 8);
 #define TBF16_ROPE(N, S_, NORM)                                                                                     \
-  norm_rope_kernel<N, S_, NORM><<<blocks, 32 * kWarpRowsPerBlock, 0, st>>>(xp, ldx / 8, wp, M, D8, eps, offset, cp, sp, \
+  norm_rope_kernel<N, S_, NORM><<<blocks, 32 * kWarpRowsPerBlock, 0, st>>>(xp, ldtok / 8, wp, M, D8, eps, offset, cp, sp, \
                                                                           ldc / 8, S, H, op, ldo / 8)
 #define TBF16_ROPE_N(N)                                                                  \
   if (!w) TBF16_ROPE(N, TBF16_NORM_SCALE_FP32, false);                                   \

@@ -441,12 +441,19 @@ def rmsnorm_rope(x: torch.Tensor, weight, cos: torch.Tensor, sin: torch.Tensor, 
         raise RuntimeError("tbf16.rmsnorm_rope: cos / sin must hold S x D values")
     if style not in _NORM_STYLES:
         raise RuntimeError(f"tbf16.rmsnorm_rope: style must be one of {sorted(_NORM_STYLES)}")
-    xc = x.contiguous()
+    # heads contiguous, tokens a uniform stride apart (e.g. a column slice of a fused QKV output): read in place
+    lead = x.shape[:-2]
+    tok = x.stride(-3)
+    uniform = all(x.stride(i) == tok * math.prod(lead[i + 1:]) for i in range(len(lead)) if lead[i] > 1)
+    xc = x if (x.stride(-1) == 1 and x.stride(-2) == D and uniform and tok % 8 == 0 and x.data_ptr() % 16 == 0) \
+        else x.contiguous()
+    if xc is not x:
+        tok = H * D
     c2, s2 = cos.reshape(S, D).contiguous(), sin.reshape(S, D).contiguous()
     w = None if weight is None else weight.to(torch.bfloat16).contiguous()
-    out = torch.empty_like(xc)
-    M = xc.numel() // D
-    call("tbf16_rmsnorm_rope", ptr(xc), D, ptr(w), M, D, float(eps), _NORM_STYLES[style], float(offset), ptr(c2),
+    out = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+    M = x.numel() // D
+    call("tbf16_rmsnorm_rope", ptr(xc), tok, ptr(w), M, D, float(eps), _NORM_STYLES[style], float(offset), ptr(c2),
          ptr(s2), D, S, H, ptr(out), D, stream_ptr(x.device))
     return out
 
