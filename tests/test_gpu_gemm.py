@@ -127,3 +127,19 @@ def test_skinny_linear_vs_oracle(M, K, N, bias):
     w16, ws = ops.prepare_weight(w.cuda())
     y2 = ops.scaled_linear(x.cuda(), w16, ws, None if b is None else b.cuda()).cpu()
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+# Products whose last wave of 256-wide pair tiles would leave most CTA pairs idle take narrower pair
+# tiles: 2048 x 3072 -> 192 columns, 2048 x 2560 -> 160, 600 x 1000 and 520 x 520 -> 128 (M and N tails,
+# the last tile partly past N).
+@pytest.mark.parametrize("M,K,N,bias,rows", [(2048, 1024, 3072, True, 64), (2048, 2048, 2560, False, 64),
+                                             (600, 1032, 1000, True, None), (520, 256, 520, False, None)])
+def test_narrow_pair_tiles_vs_oracle(M, K, N, bias, rows):
+    x = inputs.gemm_x(M, K, seed=M + N)
+    w = inputs.gemm_w(N, K, seed=K + 3)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(2)) * 0.1).bfloat16() if bias else None
+    sel = None if rows is None else torch.randperm(M, generator=torch.Generator().manual_seed(4))[:rows]
+    y, y_ref, absprod, xs, w16, ws = _linear_case(x, w, b, sel)
+    assert_close_ulp(y, y_ref, gemm_tolerance(y_ref, absprod, K), what=f"narrow tiles {M}x{K}x{N}")
+    exact = xs.double() @ w.double().t() + (b.double() if bias else 0)
+    assert rel_err(y, exact) < 2e-3

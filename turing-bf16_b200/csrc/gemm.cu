@@ -323,25 +323,29 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, i
 // MMA completion is multicast to both CTAs' empty / accumulator-full barriers; both CTAs' epilogue
 // warps release an accumulator on the even CTA's barrier. No multicast loads.
 constexpr int kPairStages = 6;
+// PN: the pair tile's width (256 x PN outputs; 256 for the headline shapes, 192 / 160 / 128 for products
+// whose last wave of 256-wide tiles would leave most pairs idle).
+template <int PN>
 struct PairCfg {
+  static_assert(PN % 32 == 0 && PN >= 128 && PN <= 256, "pair tile width");
   static constexpr int A_BYTES = BM * BK * 2;          // this CTA's 128 rows
-  static constexpr int B_BYTES = 128 * BK * 2;         // this CTA's half of the 256 B rows
+  static constexpr int B_BYTES = (PN / 2) * BK * 2;    // this CTA's half of the PN B rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int THREADS = 32 * (2 + kEpiWarps);
-  static constexpr int TMEM_COLS = 512;                // two 256-column accumulators
+  static constexpr int TMEM_COLS = 512;                // two PN-column accumulators
   static constexpr int EPI_BYTES = kEpiWarps * 2 * 32 * 64;  // per epilogue warp two 32 x 32 bf16 tiles
   static constexpr int BAR_BYTES = 8 * (2 * kPairStages + 4) + 16;
   static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-template <bool A_MN, bool B_MN, bool CONV>
-__global__ void __launch_bounds__(PairCfg::THREADS, 1)
+template <bool A_MN, bool B_MN, bool CONV, int PN>
+__global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
     scaled_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmY, const GemmParams p) {
-  using C = PairCfg;
+  using C = PairCfg<PN>;
+  static_assert(PN == 256 || (!B_MN && !CONV), "narrow pair tiles take K-major B only");
   constexpr int S = kPairStages;
-  constexpr int PN = 256;  // pair tile: 256 x 256
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES + C::EPI_BYTES);  // even CTA's are used
@@ -386,7 +390,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
       for (int tile = cid; tile < num_tiles && !*abort; tile += nclusters) {
         int tm, tn;
         tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-        const int m0 = tm * 256 + (int)rank * 128, n0 = tn * PN + (int)rank * 128;
+        const int m0 = tm * 256 + (int)rank * 128, n0 = tn * PN + (int)rank * (PN / 2);
         int cx = 0, cy = 0, cz = 0, cbat = 0;  // CONV: input coordinates of the A box at tap (0, 0, 0)
         if (CONV) {
           int r = m0;
@@ -585,20 +589,20 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
 }
 
 // The pair kernel with A's tensor map already built (a matrix, or the conv input for CONV).
-template <bool A_MN, bool B_MN, bool CONV>
+template <bool A_MN, bool B_MN, bool CONV, int PN>
 int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
                      const float* sb, const void* bias, void* y, int64_t ldy, const ConvGemm* cv, cudaStream_t st) {
-  using C = PairCfg;
+  using C = PairCfg<PN>;
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   if (!d) return TBF16_ERR_DEVICE;
   CUtensorMap tb;
   int rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
-                : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 128);
+                : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, PN / 2);
   if (rc) return rc;
   CUtensorMap ty;
   rc = tbf16_host::make_tmap_2d_out(&ty, y, (uint64_t)N, (uint64_t)M, (uint64_t)ldy, 32, 32);
   if (rc) return rc;
-  auto kern = scaled_gemm_pair_kernel<A_MN, B_MN, CONV>;
+  auto kern = scaled_gemm_pair_kernel<A_MN, B_MN, CONV, PN>;
   static bool attr_done[64] = {false};
   if (!attr_done[d->device & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
@@ -613,7 +617,7 @@ int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, i
   p.ldy = ldy;
   p.err = d->err;
   p.tiles_m = (M + 255) / 256;
-  p.tiles_n = (N + 255) / 256;
+  p.tiles_n = (N + PN - 1) / PN;
   static const int group_env = [] {
     const char* e = getenv("TBF16_GEMM_GROUP");
     return e ? atoi(e) : 0;
@@ -643,6 +647,36 @@ int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, i
   return tbf16_host::check_launch();
 }
 
+// Pair tile width for a product with K-major B: the one with the least work per SM counted as waves of
+// tiles x (tile width + a fixed 32-column share for its prologue / epilogue). Measured (linear_q, CUDA
+// graph): 600 x 1000 x 1024 16.7 -> 13.1 us at 128; 2048 x 2560 x 2048 33.1 -> 31.4 us and x 10240
+// 109.7 -> 107.5 us at 160 -- far less than the waves suggest, because a narrow tile moves more operand
+// bytes per flop and the kernel is close to the L2 -> shared-memory rate with every SM loading (4096^3:
+// 101.6 us at 256, 128 us at 160). TBF16_GEMM_PN = 256 / 192 / 160 / 128 forces one.
+int pair_width(int M, int N, int pairs) {
+  static const int env = [] {
+    const char* e = getenv("TBF16_GEMM_PN");
+    return e ? atoi(e) : 0;
+  }();
+  if (env == 256 || env == 192 || env == 160 || env == 128) return env;
+  const int64_t tm = (M + 255) / 256;
+  auto cost = [&](int pn) {
+    const int64_t tiles = tm * ((N + pn - 1) / pn);
+    return (tiles + pairs - 1) / pairs * (pn + 32);
+  };
+  // a narrower tile moves more operand bytes per flop (at 160, 30 % more per SM), so it has to save at
+  // least a tenth of the waves' time to be taken
+  int best = 256;
+  int64_t best_cost = cost(256) * 9 / 10;
+  for (int pn : {192, 160, 128}) {
+    if (cost(pn) < best_cost) {
+      best_cost = cost(pn);
+      best = pn;
+    }
+  }
+  return best;
+}
+
 template <bool A_MN, bool B_MN>
 int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
                      const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
@@ -650,7 +684,16 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   int rc = A_MN ? tbf16_host::make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64)
                 : tbf16_host::make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, BM);
   if (rc) return rc;
-  return launch_pair_core<A_MN, B_MN, false>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+  if (!B_MN) {
+    const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+    switch (pair_width(M, N, d ? d->sms / 2 : 74)) {
+      case 192: return launch_pair_core<A_MN, false, false, 192>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+      case 160: return launch_pair_core<A_MN, false, false, 160>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+      case 128: return launch_pair_core<A_MN, false, false, 128>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+      default: break;
+    }
+  }
+  return launch_pair_core<A_MN, B_MN, false, 256>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
 }
 
 // The pair kernel whenever both dimensions span two or more 256 tiles (it moves a third less data from
@@ -678,7 +721,7 @@ int conv_gemm_pair(const void* x16cl, int64_t B, int64_t D, int64_t H, int64_t W
   CUtensorMap ta;
   if (int rc = make_tmap_conv_in(&ta, x16cl, B, D, H, W, C, bx, 128 / bx)) return rc;
   // K = taps x cb x 64: the weight rows are exactly one K long
-  return launch_pair_core<false, false, true>(ta, w16, ldw, M, N, (int)ldw, sa, sb, bias, y, ldy, &cv, st);
+  return launch_pair_core<false, false, true, 256>(ta, w16, ldw, M, N, (int)ldw, sa, sb, bias, y, ldy, &cv, st);
 }
 
 }  // namespace tbf16_host
