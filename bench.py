@@ -439,17 +439,22 @@ class _GemmaLayer(torch.nn.Module):
             rot = lambda t: torch.cat([-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]], -1)
             q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
-        x = x + self._norm(self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d)), self.post_attn_norm)
-        h = self._norm_rows(x, self.pre_ff_norm)
-        if self.fused:  # one gate/up GEMM; the GeGLU reads its two column halves in place
+        o = self.o_proj(a.transpose(1, 2).reshape(B, S, self.h * self.d))
+        if self.fused:  # post-attention norm, residual add and pre-FF norm rows in one pass
             from tbf16 import ops
+            x, h16, h_inv = ops.add_rmsnorm_rows(o, x, self.pre_ff_norm.weight, post_weight=self.post_attn_norm.weight)
+            h = (h16, h_inv)
+        else:
+            x = x + self._norm(o, self.post_attn_norm)
+            h = self._norm_rows(x, self.pre_ff_norm)
+        if self.fused:  # one gate/up GEMM; the GeGLU reads its two column halves in place
             gu = self._proj_rows(h, self.gu_rows)
             inter = self.gate_proj.weight16.shape[0]
             y = ops.glu_linear(gu[..., :inter], gu[..., inter:], self.down_proj.weight16, self.down_proj.weight_scale,
                                act="gelu_tanh")
-        else:
-            gate, up = self._proj(h, self.gate_proj), self._proj(h, self.up_proj)
-            y = self.down_proj(F.gelu(gate, approximate="tanh") * up)
+            return ops.rmsnorm(y, self.post_ff_norm.weight, 1e-6, 1.0, "gemma", residual=x)
+        gate, up = self._proj(h, self.gate_proj), self._proj(h, self.up_proj)
+        y = self.down_proj(F.gelu(gate, approximate="tanh") * up)
         return x + self._norm(y, self.post_ff_norm)
 
 
@@ -532,7 +537,8 @@ def prefill_run(world, seq=2048, layers=34, vocab=262144, hidden=2560, iters=3):
                       "what": ("RMSNorm before q/k/v and gate/up, and GeGLU before down, fused with the row "
                                "scales; q/k/v and gate/up each one GEMM over the stacked weight rows; the q/k "
                                "head RMSNorms fused with RoPE (one pass per tensor, read from the QKV output's "
-                               "column slices); the RMSNorms after attention and MLP on the norm kernel")}}
+                               "column slices); the post-norms with their residual adds, the post-attention one "
+                               "with the pre-FF norm rows, in one pass")}}
 
 
 def dist_rank():

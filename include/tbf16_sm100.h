@@ -212,6 +212,17 @@ int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int
                        float offset, int target_exp, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo,
                        void* stream);
 
+/* The norm with a layer's residual add folded in, each step optional: a = RMSNorm_wa(x) (skipped when wa
+ * is NULL), a = bf16_rn(res + a) (skipped when res is NULL), a written to a_out (nullable); then
+ * r = RMSNorm_wb(a) (skipped when wb is NULL) with y16 / s_inv / r_out as tbf16_rmsnorm_rows. Both
+ * norms use style, offset and eps. Covers x + norm(y) (wa, res, a_out: Gemma's post-norms), the
+ * pre-norm rows of a residual sum (res, wb, y16: Llama), and both at once (Gemma's post-attention norm,
+ * residual and pre-feed-forward norm in one pass). tbf16_rmsnorm_rows is this call with wb only. All
+ * rows [M, K] bf16 (fp16 for y16), strides multiples of 8, pointers 16-byte aligned. */
+int tbf16_add_rmsnorm_rows(const void* x, int64_t ldx, const void* res, int64_t ldr, const void* wa, const void* wb,
+                           int64_t M, int64_t K, float eps, int style, float offset, int target_exp, void* a_out,
+                           int64_t lda, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo, void* stream);
+
 /* ------------------------------------------------------------------ scaled convolutions */
 /* The reference's scaled convolutions (tbf16/conv.py:34-60): one power-of-two scale per input sample,
  * the weight prepared as a linear's rows (tbf16_quantize_rows on [O, C kd kh kw], t = _target_exp(K)):

@@ -216,3 +216,22 @@ def test_rmsnorm_rope_column_slices_of_fused_qkv():
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
         ref2 = _rope_ref(ops.rmsnorm(t.contiguous(), w, 1e-6, 1.0, "gemma").transpose(1, 2), cos, sin).transpose(1, 2)
         assert torch.equal(out.view(torch.int16), ref2.contiguous().view(torch.int16))
+
+
+@pytest.mark.parametrize("M,K", [(5, 256), (2048, 2560), (1100, 4096), (3, 10240)])
+def test_residual_norm_forms(M, K):
+    """x + rmsnorm(y) and (s = residual + [rmsnorm](x), rmsnorm_rows(s)) in one pass each: bit-equal to the
+    unfused sequence of ops.rmsnorm / torch's bf16 add / rmsnorm_rows (warp-per-row and block shapes)."""
+    from tbf16 import ops
+    g = torch.Generator().manual_seed(M + K)
+    x = (torch.randn(M, K, generator=g) * 4).bfloat16().cuda()
+    res = (torch.randn(M, K, generator=g) * 30).bfloat16().cuda()
+    w = (torch.randn(K, generator=g) * 0.1).bfloat16().cuda()
+    pw = (torch.randn(K, generator=g) * 0.1).bfloat16().cuda()
+    eq = lambda a, b: torch.equal(a.contiguous().view(torch.int16), b.contiguous().view(torch.int16))
+    assert eq(ops.rmsnorm(x, pw, residual=res), res + ops.rmsnorm(x, pw))
+    for post in (pw, None):
+        s, r16, s_inv = ops.add_rmsnorm_rows(x, res, w, post_weight=post)
+        s_ref = res + (ops.rmsnorm(x, post) if post is not None else x)
+        r16_ref, s_inv_ref = ops.rmsnorm_rows(s_ref, w)
+        assert eq(s, s_ref) and eq(r16, r16_ref) and torch.equal(s_inv, s_inv_ref)

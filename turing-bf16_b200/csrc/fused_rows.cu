@@ -150,28 +150,39 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) g
   emit_row<NCH, WARP>(rg, hv, amax, t, I8, y16, ldy8, s_inv, out, ldo8);
 }
 
+// A chain of row operations on one register-resident row (each step optional): a = RMSNorm_a(x) (bf16),
+// a = bf16(res + a) (a residual add, the way a model adds two bf16 tensors), a written out; then
+// r = RMSNorm_b(a) and the linear's fp16 operand fp16(r / s_inv) with its row scale, and/or r in bf16.
+// rmsnorm_rows is the chain with only the second norm; the other uses fold a layer's residual adds into
+// the norms around them (x + norm(y), and the next block's norm rows of that sum).
+struct NormRows {
+  const uint4* x;
+  int64_t ldx8;
+  const uint4* res;  // nullable
+  int64_t ldr8;
+  const uint4* wa;   // nullable: the first norm
+  const uint4* wb;   // nullable: the second norm
+  uint4* a_out;      // nullable
+  int64_t lda8;
+  uint4* y16;        // nullable (then s_inv is unused)
+  int64_t ldy8;
+  float* s_inv;
+  uint4* r_out;      // nullable
+  int64_t ldo8;
+  int64_t M;
+  int K8, K, t;
+  float eps, offset;
+};
+
+// v = RMSNorm(v) with weight w, in place: mean of squares in fp32 (per thread, then the group's
+// fixed-order reduction), then the style's rounding.
 template <int NCH, int STYLE, bool WARP>
-__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) rmsnorm_rows_kernel(const uint4* __restrict__ x, int64_t ldx8,
-                                                                   const uint4* __restrict__ w, int64_t M, int K8,
-                                                                   int K, float eps, float offset, int t,
-                                                                   uint4* __restrict__ y16, int64_t ldy8,
-                                                                   float* __restrict__ s_inv, uint4* __restrict__ out,
-                                                                   int64_t ldo8) {
-  pdl_launch_dependents();
-  __shared__ float red[kMaxThreads / 32];
-  RowGroup<WARP> rg(red);
-  if (WARP && rg.row >= M) return;
-  uint4 xv[NCH];
-#pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int i = rg.tid + rg.nthr * c;
-    xv[c] = i < K8 ? __ldg(x + rg.row * ldx8 + i) : make_uint4(0, 0, 0, 0);
-  }
-  // mean of squares in fp32: per thread, then the group's fixed-order reduction
+__device__ __forceinline__ void norm_in_place(RowGroup<WARP>& rg, uint4 (&v)[NCH], const uint4* __restrict__ w, int K8,
+                                              int K, float eps, float offset) {
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const uint32_t xw[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+    const uint32_t xw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float a = bf16lo(xw[j]), b = bf16hi(xw[j]);
@@ -179,15 +190,12 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) r
       ss = fmaf(b, b, ss);
     }
   }
-  const float tot = rg.template reduce<false>(ss);
-  const float r = rsqrtf(tot / (float)K + eps);
-  float m = 0.f;
-  uint4 yv[NCH];
+  const float r = rsqrtf(rg.template reduce<false>(ss) / (float)K + eps);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int i = rg.tid + rg.nthr * c;
     const uint4 wv = i < K8 ? __ldg(w + i) : make_uint4(0, 0, 0, 0);
-    const uint32_t xw[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+    const uint32_t xw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
     uint32_t yw[4];
 #pragma unroll
@@ -201,12 +209,57 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) r
         y1 = bf16hi(ww[j]) * round_bf16(bf16hi(xw[j]) * r);
       }
       yw[j] = pack_bf16(y0, y1);
-      m = fmaxf(m, fmaxf(fabsf(bf16lo(yw[j])), fabsf(bf16hi(yw[j]))));
     }
-    yv[c] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+    v[c] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
   }
-  const float amax = rg.template reduce<true>(m);
-  emit_row<NCH, WARP>(rg, yv, amax, t, K8, y16, ldy8, s_inv, out, ldo8);
+}
+
+template <int NCH, int STYLE, bool WARP>
+__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) norm_rows_kernel(const NormRows p) {
+  pdl_launch_dependents();
+  __shared__ float red[kMaxThreads / 32];
+  RowGroup<WARP> rg(red);
+  if (WARP && rg.row >= p.M) return;
+  uint4 v[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int i = rg.tid + rg.nthr * c;
+    v[c] = i < p.K8 ? __ldg(p.x + rg.row * p.ldx8 + i) : make_uint4(0, 0, 0, 0);
+  }
+  if (p.wa) norm_in_place<NCH, STYLE, WARP>(rg, v, p.wa, p.K8, p.K, p.eps, p.offset);
+  if (p.res) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = rg.tid + rg.nthr * c;
+      if (i < p.K8) {
+        const uint4 rv = __ldg(p.res + rg.row * p.ldr8 + i);
+        v[c] = make_uint4(pack_bf16(bf16lo(rv.x) + bf16lo(v[c].x), bf16hi(rv.x) + bf16hi(v[c].x)),
+                          pack_bf16(bf16lo(rv.y) + bf16lo(v[c].y), bf16hi(rv.y) + bf16hi(v[c].y)),
+                          pack_bf16(bf16lo(rv.z) + bf16lo(v[c].z), bf16hi(rv.z) + bf16hi(v[c].z)),
+                          pack_bf16(bf16lo(rv.w) + bf16lo(v[c].w), bf16hi(rv.w) + bf16hi(v[c].w)));
+      }
+    }
+  }
+  if (p.a_out) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = rg.tid + rg.nthr * c;
+      if (i < p.K8) p.a_out[rg.row * p.lda8 + i] = v[c];
+    }
+  }
+  if (p.wb) norm_in_place<NCH, STYLE, WARP>(rg, v, p.wb, p.K8, p.K, p.eps, p.offset);
+  float amax = 0.f;
+  if (p.y16) {
+    float m = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t yw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(fabsf(bf16lo(yw[j])), fabsf(bf16hi(yw[j]))));
+    }
+    amax = rg.template reduce<true>(m);
+  }
+  if (p.y16 || p.r_out) emit_row<NCH, WARP>(rg, v, amax, p.t, p.K8, p.y16, p.ldy8, p.s_inv, p.r_out, p.ldo8);
 }
 
 // Attention operands: RMSNorm over each head's D values (optional; the QK-norm of Gemma 3 / Qwen 3) and
@@ -356,14 +409,46 @@ struct RowLaunch {
   bool warp;
   int nch, threads;
 };
-RowLaunch row_launch(int64_t K8) {
+RowLaunch row_launch(int64_t K8, int64_t M, int64_t warp_max_k8) {
   if (K8 <= kWarpRowsMaxK8) return {true, K8 <= 32 ? 1 : (K8 <= 64 ? 2 : 4), 32 * kWarpRowsPerBlock};
+  // enough rows to fill the GPU with warps: a warp per row, 8 or 16 vectors a lane (no block barriers,
+  // many loads in flight per thread)
+  if (K8 <= warp_max_k8 && M >= 1024) return {true, K8 <= 256 ? 8 : (K8 <= 384 ? 12 : 16), 32 * kWarpRowsPerBlock};
   for (int c = 1; c <= kMaxChunks; c *= 2)
     if (K8 <= (int64_t)kMaxThreads * c) {
       const int64_t per = (K8 + c - 1) / c;
       return {false, c, (int)((per + 31) / 32 * 32)};
     }
   return {false, 0, 0};
+}
+
+int launch_norm_rows(const NormRows& p, int style, cudaStream_t st) {
+  static const int warp_max = [] {  // rows (in 16-byte vectors) up to which many-row norms take a warp per row
+    const char* e = getenv("TBF16_NORM_WARP_MAX_K8");
+    return e ? atoi(e) : 512;
+  }();
+  const RowLaunch L = row_launch(p.K8, p.M, warp_max);
+  if (!L.nch || p.M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
+  const unsigned blocks = (unsigned)(L.warp ? (p.M + kWarpRowsPerBlock - 1) / kWarpRowsPerBlock : p.M);
+#define TBF16_NORM(N, S, W) norm_rows_kernel<N, S, W><<<blocks, L.threads, 0, st>>>(p)
+#define TBF16_NORM_STYLE(N, W) \
+  if (style == TBF16_NORM_SCALE_FP32) TBF16_NORM(N, TBF16_NORM_SCALE_FP32, W); else TBF16_NORM(N, TBF16_NORM_SCALE_BF16, W)
+  if (L.warp) {
+    switch (L.nch) {
+      case 1: TBF16_NORM_STYLE(1, true); break;
+      case 2: TBF16_NORM_STYLE(2, true); break;
+      case 4: TBF16_NORM_STYLE(4, true); break;
+      case 8: TBF16_NORM_STYLE(8, true); break;
+      case 12: TBF16_NORM_STYLE(12, true); break;
+      default: TBF16_NORM_STYLE(16, true); break;
+    }
+  } else {
+    if (L.nch == 1) TBF16_NORM_STYLE(1, false);
+    else TBF16_NORM_STYLE(2, false);
+  }
+#undef TBF16_NORM_STYLE
+#undef TBF16_NORM
+  return tbf16_host::check_launch();
 }
 
 }  // namespace
@@ -381,7 +466,7 @@ int tbf16_glu_rows(const void* g, int64_t ldg, const void* u, int64_t ldu, int64
     return TBF16_ERR_ALIGN;
   if (M == 0 || I == 0) return TBF16_OK;
   const int64_t I8 = I / 8;
-  const RowLaunch L = row_launch(I8);
+  const RowLaunch L = row_launch(I8, M, kWarpRowsMaxK8);
   if (!L.nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
   auto st = static_cast<cudaStream_t>(stream);
   const uint4 *gp = static_cast<const uint4*>(g), *up = static_cast<const uint4*>(u);
@@ -466,41 +551,49 @@ int tbf16_rmsnorm_rope(const void* x, int64_t ldtok, const void* w, int64_t M, i
   return tbf16_host::check_launch();
 }
 
+
 int tbf16_rmsnorm_rows(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps, int style,
                        float offset, int target_exp, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo,
                        void* stream) {
+  if (!w) return TBF16_ERR_INVALID;
+  return tbf16_add_rmsnorm_rows(x, ldx, nullptr, 0, nullptr, w, M, K, eps, style, offset, target_exp, nullptr, 0, y16,
+                                ldy, s_inv, r_out, ldo, stream);
+}
+
+int tbf16_add_rmsnorm_rows(const void* x, int64_t ldx, const void* res, int64_t ldr, const void* wa, const void* wb,
+                           int64_t M, int64_t K, float eps, int style, float offset, int target_exp, void* a_out,
+                           int64_t lda, void* y16, int64_t ldy, float* s_inv, void* r_out, int64_t ldo, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
-  if (M < 0 || K < 0 || ldx < K || (y16 && ldy < K) || (r_out && ldo < K) || (y16 && !s_inv) || (!y16 && !r_out) ||
-      !x || !w || !(eps >= 0.f) ||
+  if (M < 0 || K < 0 || ldx < K || (res && ldr < K) || (a_out && lda < K) || (y16 && ldy < K) || (r_out && ldo < K) ||
+      (y16 && !s_inv) || (!y16 && !r_out && !a_out) || (r_out && !wb && !wa && !res) || !x || !(eps >= 0.f) ||
       target_exp < 0 || target_exp > 64 || (style != TBF16_NORM_SCALE_FP32 && style != TBF16_NORM_SCALE_BF16))
     return TBF16_ERR_INVALID;
-  if (K % 8 || ldx % 8 || (y16 && ldy % 8) || (r_out && ldo % 8) || !tbf16_host::aligned16(x) ||
-      !tbf16_host::aligned16(w) || (y16 && !tbf16_host::aligned16(y16)) || (r_out && !tbf16_host::aligned16(r_out)))
+  auto a16 = [](const void* q) { return !q || tbf16_host::aligned16(q); };
+  if (K % 8 || ldx % 8 || (res && ldr % 8) || (a_out && lda % 8) || (y16 && ldy % 8) || (r_out && ldo % 8) ||
+      !tbf16_host::aligned16(x) || !a16(res) || !a16(wa) || !a16(wb) || !a16(a_out) || !a16(y16) || !a16(r_out))
     return TBF16_ERR_ALIGN;
   if (M == 0 || K == 0) return TBF16_OK;
-  const int64_t K8 = K / 8;
-  const RowLaunch L = row_launch(K8);
-  if (!L.nch || M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
-  auto st = static_cast<cudaStream_t>(stream);
-  const uint4 *xp = static_cast<const uint4*>(x), *wp = static_cast<const uint4*>(w);
-  uint4 *yp = static_cast<uint4*>(y16), *op = static_cast<uint4*>(r_out);
-  const unsigned blocks = (unsigned)(L.warp ? (M + kWarpRowsPerBlock - 1) / kWarpRowsPerBlock : M);
-#define TBF16_NORM(N, S, W)                                                                                       \
-  rmsnorm_rows_kernel<N, S, W><<<blocks, L.threads, 0, st>>>(xp, ldx / 8, wp, M, (int)K8, (int)K, eps, offset,   \
-                                                             target_exp, yp, ldy / 8, s_inv, op, ldo / 8)
-#define TBF16_NORM_STYLE(N, W) \
-  if (style == TBF16_NORM_SCALE_FP32) TBF16_NORM(N, TBF16_NORM_SCALE_FP32, W); else TBF16_NORM(N, TBF16_NORM_SCALE_BF16, W)
-  if (L.warp) {
-    if (L.nch == 1) TBF16_NORM_STYLE(1, true);
-    else if (L.nch == 2) TBF16_NORM_STYLE(2, true);
-    else TBF16_NORM_STYLE(4, true);
-  } else {
-    if (L.nch == 1) TBF16_NORM_STYLE(1, false);
-    else TBF16_NORM_STYLE(2, false);
-  }
-#undef TBF16_NORM_STYLE
-#undef TBF16_NORM
-  return tbf16_host::check_launch();
+  NormRows p;
+  p.x = static_cast<const uint4*>(x);
+  p.ldx8 = ldx / 8;
+  p.res = static_cast<const uint4*>(res);
+  p.ldr8 = ldr / 8;
+  p.wa = static_cast<const uint4*>(wa);
+  p.wb = static_cast<const uint4*>(wb);
+  p.a_out = static_cast<uint4*>(a_out);
+  p.lda8 = lda / 8;
+  p.y16 = static_cast<uint4*>(y16);
+  p.ldy8 = ldy / 8;
+  p.s_inv = s_inv;
+  p.r_out = static_cast<uint4*>(r_out);
+  p.ldo8 = ldo / 8;
+  p.M = M;
+  p.K8 = (int)(K / 8);
+  p.K = (int)K;
+  p.t = target_exp;
+  p.eps = eps;
+  p.offset = offset;
+  return launch_norm_rows(p, style, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -37,6 +37,8 @@ SIGNATURES = {
     "tbf16_gemm_f16": [_vp, _i32, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp],
     "tbf16_gemv": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp],
     "tbf16_glu_rows": [_vp, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp],
+    "tbf16_add_rmsnorm_rows": [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, ctypes.c_float, _i32, ctypes.c_float, _i32,
+                               _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp],
     "tbf16_glu_bwd": [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i32, _vp, _i64, _vp, _i64, _vp],
     "tbf16_rmsnorm_rope": [_vp, _i64, _vp, _i64, _i64, ctypes.c_float, _i32, ctypes.c_float, _vp, _vp, _i64, _i64,
                            _i64, _vp, _i64, _vp],

@@ -409,9 +409,11 @@ def rmsnorm_rows(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offse
 
 
 @torch.autocast("cuda", enabled=False)
-def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offset: float = 1.0, style: str = "gemma"):
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offset: float = 1.0, style: str = "gemma",
+            residual=None):
     """Plain RMSNorm (bf16 in and out) on the rmsnorm_rows kernel, for norms that feed no linear: one read
-    of x, one write of the result, the same roundings as rmsnorm_rows."""
+    of x, one write of the result, the same roundings as rmsnorm_rows. With `residual` (x's shape, bf16):
+    residual + rmsnorm(x) in the same pass, as a model adds the two bf16 tensors."""
     require_cuda(x, weight)
     if style not in _NORM_STYLES:
         raise RuntimeError(f"tbf16.rmsnorm: style must be one of {sorted(_NORM_STYLES)}")
@@ -421,9 +423,43 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, offset: fl
     if w.numel() != K or K % 8:
         raise RuntimeError("tbf16.rmsnorm: weight must have the row length, a multiple of 8")
     r = torch.empty((M, K), device=x.device, dtype=torch.bfloat16)
-    call("tbf16_rmsnorm_rows", ptr(x2), x2.stride(0), ptr(w), M, K, float(eps), _NORM_STYLES[style], float(offset), 15,
-         None, 0, None, ptr(r), K, stream_ptr(x.device))
+    if residual is None:
+        call("tbf16_rmsnorm_rows", ptr(x2), x2.stride(0), ptr(w), M, K, float(eps), _NORM_STYLES[style], float(offset),
+             15, None, 0, None, ptr(r), K, stream_ptr(x.device))
+    else:
+        if residual.shape != x.shape:
+            raise RuntimeError("tbf16.rmsnorm: residual must have x's shape")
+        r2 = _rows2d(residual, "rmsnorm")
+        call("tbf16_add_rmsnorm_rows", ptr(x2), x2.stride(0), ptr(r2), r2.stride(0), ptr(w), None, M, K, float(eps),
+             _NORM_STYLES[style], float(offset), 15, ptr(r), K, None, 0, None, None, 0, stream_ptr(x.device))
     return r.reshape(x.shape)
+
+
+@torch.autocast("cuda", enabled=False)
+def add_rmsnorm_rows(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, post_weight=None,
+                     eps: float = 1e-6, offset: float = 1.0, style: str = "gemma", target_exp: int = 15):
+    """A residual block's end and the next block's producer-fused norm in one pass:
+    s = residual + (rmsnorm(x, post_weight) if post_weight is given else x)  (bf16, the new residual stream),
+    then rmsnorm_rows(s, weight). Returns (s, r16, s_inv) -- s for the next residual add, (r16, s_inv) the
+    next linear's fp16 operand and row scales, as rmsnorm_rows."""
+    require_cuda(x, residual, weight)
+    if style not in _NORM_STYLES:
+        raise RuntimeError(f"tbf16.add_rmsnorm_rows: style must be one of {sorted(_NORM_STYLES)}")
+    if residual.shape != x.shape:
+        raise RuntimeError("tbf16.add_rmsnorm_rows: residual must have x's shape")
+    x2, r2 = _rows2d(x, "add_rmsnorm_rows"), _rows2d(residual, "add_rmsnorm_rows")
+    M, K = x2.shape
+    w = weight.to(torch.bfloat16).contiguous()
+    pw = None if post_weight is None else post_weight.to(torch.bfloat16).contiguous()
+    if w.numel() != K or K % 8 or (pw is not None and pw.numel() != K):
+        raise RuntimeError("tbf16.add_rmsnorm_rows: weights must have the row length, a multiple of 8")
+    s = torch.empty((M, K), device=x.device, dtype=torch.bfloat16)
+    r16 = torch.empty((M, K), device=x.device, dtype=torch.float16)
+    s_inv = torch.empty((M,), device=x.device, dtype=torch.float32)
+    call("tbf16_add_rmsnorm_rows", ptr(x2), x2.stride(0), ptr(r2), r2.stride(0), ptr(pw), ptr(w), M, K, float(eps),
+         _NORM_STYLES[style], float(offset), int(target_exp), ptr(s), K, ptr(r16), K, ptr(s_inv), None, 0,
+         stream_ptr(x.device))
+    return s.reshape(x.shape), r16.reshape(x.shape), s_inv.reshape(x.shape[:-1])
 
 
 @torch.autocast("cuda", enabled=False)
@@ -499,5 +535,5 @@ def small_m_linear(x2: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bi
 
 __all__ = ["quantize_rows", "quantize_rows_shared", "prepare_weight", "scaled_linear", "linear_q", "small_m_linear",
            "linear_host", "glu_rows", "glu_bwd", "rmsnorm_rows", "glu_linear", "rmsnorm_linear", "rmsnorm",
-           "rmsnorm_rope",
+           "rmsnorm_rope", "add_rmsnorm_rows",
            "available", "_target_exp"]
