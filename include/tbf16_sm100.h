@@ -289,6 +289,14 @@ int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t gr
 int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev, const void* mask, int64_t mask_sb,
                    int64_t mask_sh, int64_t mask_sq, void* out, float* lse, int64_t lse_ld, void* o16, void* stream);
+/* tbf16_attn_fwd with the output's element strides given: out element (b, h, i, d) at
+ * b * out_sb + h * out_sh + i * out_ss + d (D contiguous; strides multiples of 8). out_sb = Sq Hq D,
+ * out_sh = D, out_ss = Hq D writes (B, Sq, Hq, D) order, the rows the output projection reads, so the
+ * transpose + reshape a model does next is free. tbf16_attn_fwd is this call with contiguous strides. */
+int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
+                       int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev, const void* mask,
+                       int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh,
+                       int64_t out_ss, float* lse, int64_t lse_ld, void* o16, void* stream);
 
 /* Bytes of workspace tbf16_attn_bwd needs (fp32 dQ accumulator, fp16 dO16, delta, head maxima). */
 int64_t tbf16_attn_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D);

@@ -123,3 +123,22 @@ def test_lse_output():
     f = orc.sdpa_fwd(q, k, v, is_causal=True, v_exp=0)
     assert lse.shape[-1] % 128 == 0  # padded row stride for the backward's bulk copies
     assert torch.allclose(lse[..., :256].cpu().double(), f["lse"], rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("D", [128, 256])
+def test_sdpa_output_in_token_major_order(D):
+    """Inference output is (B, H, S, D) over (B, S, H, D) memory (as torch's own SDPA returns it), so the
+    model's transpose + reshape for the output projection is a view; values equal the contiguous call."""
+    from tbf16 import attention, _ext
+    torch.manual_seed(0)
+    B, H, Hkv, S = 2, 4, 2, 300
+    q = torch.randn(B, H, S, D, device="cuda").bfloat16()
+    k = torch.randn(B, Hkv, S, D, device="cuda").bfloat16()
+    v = torch.randn(B, Hkv, S, D, device="cuda").bfloat16()
+    out = attention.sdpa(q, k, v, is_causal=True, enable_gqa=True)
+    assert out.shape == (B, H, S, D) and out.transpose(1, 2).is_contiguous()
+    q16, k16, v16, _, ev = attention.prepare_qkv(q, k, v, v_exp=13)
+    ref = torch.empty(B, H, S, D, device="cuda", dtype=torch.bfloat16)
+    _ext.call("tbf16_attn_fwd", _ext.ptr(q16), _ext.ptr(k16), _ext.ptr(v16), B, H, Hkv, S, S, D, 1.0 / D ** 0.5, 1,
+              _ext.ptr(ev.contiguous()), None, 0, 0, 0, _ext.ptr(ref), None, 0, None, _ext.stream_ptr(q.device))
+    assert torch.equal(out.contiguous().view(torch.int16), ref.view(torch.int16))

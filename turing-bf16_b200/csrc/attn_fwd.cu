@@ -36,7 +36,8 @@ struct AttnFwdParams {
   float scale_log2;   // softmax scale * log2(e)
   int causal;         // keys j <= query i (top-left aligned, as torch's is_causal)
   const int32_t* ev;  // [B * Hkv]: output multiplied by 2^ev
-  __nv_bfloat16* out; // [B, Hq, Sq, D] contiguous
+  __nv_bfloat16* out; // (B, Hq, Sq, D) with element strides osb, osh, oss (D contiguous)
+  int64_t osb, osh, oss;
   float* lse;         // [B * Hq, lse_ld] natural-log logsumexp, nullable
   int64_t lse_ld;
   __half* o16;        // [B, Hq, Sq, D] fp16 O before the 2^ev scale (training), nullable
@@ -280,7 +281,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
-      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D;
+      __nv_bfloat16* orow = p.out + (int64_t)(bh / p.Hq) * p.osb + (int64_t)(bh % p.Hq) * p.osh +
+                            (int64_t)min(qi, p.Sq - 1) * p.oss;
       __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -620,7 +622,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
-      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D;
+      __nv_bfloat16* orow = p.out + (int64_t)(bh / p.Hq) * p.osb + (int64_t)(bh % p.Hq) * p.osh +
+                            (int64_t)min(qi, p.Sq - 1) * p.oss;
       __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -707,6 +710,15 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
                               int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
                               const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, float* lse,
                               int64_t lse_ld, void* o16, void* stream) {
+  return tbf16_attn_fwd_out(q16, k16, v16, B, Hq, Hkv, Sq, Sk, D, scale, causal, ev, mask, mask_sb, mask_sh, mask_sq, out,
+                            Hq * Sq * D, Sq * D, D, lse, lse_ld, o16, stream);
+}
+
+extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,
+                                  int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
+                                  const int32_t* ev, const void* mask, int64_t mask_sb, int64_t mask_sh,
+                                  int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh, int64_t out_ss,
+                                  float* lse, int64_t lse_ld, void* o16, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq < 0 || Sk < 0 || !ev || !out || B * Hq > 65535 ||
       Sq > INT32_MAX || Sk > INT32_MAX)
@@ -715,6 +727,7 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
   if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16) ||
       !tbf16_host::aligned16(out) || !tbf16_host::aligned16(o16))
     return TBF16_ERR_ALIGN;
+  if (out_sb < 0 || out_sh < 0 || out_ss < 0 || out_sb % 8 || out_sh % 8 || out_ss % 8) return TBF16_ERR_ALIGN;
   if (B == 0 || Sq == 0) return TBF16_OK;
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
   AttnFwdParams prm;
@@ -724,6 +737,9 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
   prm.causal = causal;
   prm.ev = ev;
   prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.osb = out_sb;
+  prm.osh = out_sh;
+  prm.oss = out_ss;
   prm.lse = lse;
   prm.lse_ld = lse_ld;
   if (lse && lse_ld < Sq) return TBF16_ERR_INVALID;

@@ -52,6 +52,8 @@ SIGNATURES = {
     "tbf16_conv_implicit": [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp],
     "tbf16_attn_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64, _i64,
                        _i64, _vp, _vp, _i64, _vp, _vp],
+    "tbf16_attn_fwd_out": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64,
+                           _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp],
     "tbf16_attn_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                        _i64,
                        ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],

@@ -121,14 +121,18 @@ def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None,
         pad = (0, Dk - D)
         q16, k16, v16 = (torch.nn.functional.pad(t, pad) for t in (q16, k16, v16))
     dev = q16.device
-    out = torch.empty((B, Hq, Sq, Dk), device=dev, dtype=torch.bfloat16)
+    if need_o16 or Dk != D:
+        out = torch.empty((B, Hq, Sq, Dk), device=dev, dtype=torch.bfloat16)
+    else:  # (B, Sq, Hq, D) in memory, as torch's own SDPA returns it: the model's transpose + reshape to
+        # (B, Sq, Hq D) rows for the output projection is then a view
+        out = torch.empty((B, Sq, Hq, Dk), device=dev, dtype=torch.bfloat16).transpose(1, 2)
     lse_ld = (Sq + 127) // 128 * 128  # row stride the backward's bulk copies need
     lse = torch.empty((B, Hq, lse_ld), device=dev, dtype=torch.float32) if need_lse else None
     o16 = torch.empty((B, Hq, Sq, Dk), device=dev, dtype=torch.float16) if need_o16 else None
     m = additive_mask(attn_mask, B, Hq, Sq, Sk, dev)
     ms = m.stride()[:3] if m is not None else (0, 0, 0)
-    call("tbf16_attn_fwd", ptr(q16), ptr(k16), ptr(v16), B, Hq, Hkv, Sq, Sk, Dk, sc, int(bool(is_causal)),
-         ptr(ev.contiguous()), ptr(m), *ms, ptr(out), ptr(lse), lse_ld, ptr(o16), stream_ptr(dev))
+    call("tbf16_attn_fwd_out", ptr(q16), ptr(k16), ptr(v16), B, Hq, Hkv, Sq, Sk, Dk, sc, int(bool(is_causal)),
+         ptr(ev.contiguous()), ptr(m), *ms, ptr(out), *out.stride()[:3], ptr(lse), lse_ld, ptr(o16), stream_ptr(dev))
     if need_o16:
         return out, lse, o16
     if Dk != D:
