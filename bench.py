@@ -182,6 +182,7 @@ def main():
     ap.add_argument("--only-attention", action="store_true",
                     help="time only the config-3 attention forward (S from --attn-S) and print its JSON; for profiling")
     ap.add_argument("--attn-S", type=int, default=16384)
+    ap.add_argument("--attn-D", type=int, default=128, help="with --only-attention: head dim (64, 128, 256)")
     ap.add_argument("--attn-train", action="store_true", help="with --only-attention: also time fwd+bwd (config 4)")
     ap.add_argument("--sweep", action="store_true",
                     help="config-2 GEMM sweep (M = 1 .. 16384 at N = K = 4096 and 8192, L2 flushed) and the "
@@ -207,7 +208,7 @@ def main():
               "l2": "inputs larger than L2 (384 MB per step)"}
 
     if args.only_attention:
-        print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, iters=max(1, args.steps),
+        print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, D=args.attn_D, iters=max(1, args.steps),
                                                      train=args.attn_train)}))
         return
     if args.only_prefill:

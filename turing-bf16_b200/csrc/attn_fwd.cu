@@ -86,10 +86,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
+  // causal: the grid is (heads, query tiles) so that CTAs start in order of their key count -- every
+  // head's last (heaviest) query tile first -- and the light tiles fill in behind them
+  const int bh = p.causal ? (int)blockIdx.x : (int)blockIdx.y;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int bhk = b * p.Hkv + h / p.group;
-  const int m_tile = p.causal ? (p.m_tiles - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy tiles first
+  const int m_tile = p.causal ? (p.m_tiles - 1 - (int)blockIdx.y) : (int)blockIdx.x;
   const int m0 = m_tile * BM;
   const int kv_end = p.causal ? min(p.Sk, m0 + BM) : p.Sk;
   const int n_kv = (kv_end + BN - 1) / BN;
@@ -699,7 +701,7 @@ int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdP
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
-  dim3 grid(prm.m_tiles, (unsigned)BHq);
+  const dim3 grid = prm.causal ? dim3((unsigned)BHq, prm.m_tiles) : dim3(prm.m_tiles, (unsigned)BHq);
   attn_fwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
   return tbf16_host::check_launch();
 }
