@@ -384,9 +384,12 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
+    // Launched as a programmatic dependent of the kernel that writes A and its row scales (the row pass
+    // or a fused producer): the first stages' weight tiles load before griddepcontrol.wait, A only after.
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      bool first = true;
       for (int tile = cid; tile < num_tiles && !*abort; tile += nclusters) {
         int tm, tn;
         tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
@@ -405,14 +408,9 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
           cz = zo - p.cv.pd;
         }
         int cblk = 0, kx = 0, ky = 0, kz = 0;  // CONV: K block kb = ((kz kh + ky) kw + kx) cb + cblk
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
-          uint8_t* sA = smem + stage * C::STAGE_BYTES;
-          uint8_t* sB = sA + C::A_BYTES;
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both CTAs' bytes
+        auto load_a = [&](uint8_t* sA, uint64_t* bar, int kb) {  // K blocks in order (CONV steps its counters)
           if (CONV) {
-            tma_load_5d_pair(sA, &tmA, &full[stage], cblk * BK, cx + kx * p.cv.dw, cy + ky * p.cv.dh,
-                             cz + kz * p.cv.dd, cbat);
+            tma_load_5d_pair(sA, &tmA, bar, cblk * BK, cx + kx * p.cv.dw, cy + ky * p.cv.dh, cz + kz * p.cv.dd, cbat);
             if (++cblk == p.cv.cb) {
               cblk = 0;
               if (++kx == p.cv.kw) {
@@ -424,17 +422,40 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
               }
             }
           } else if (!A_MN) {
-            tma_load_2d_pair(sA, &tmA, &full[stage], kb * BK, m0);
+            tma_load_2d_pair(sA, &tmA, bar, kb * BK, m0);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(sA + j * 64 * BK * 2, &tmA, &full[stage], m0 + j * 64, kb * BK);
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(sA + j * 64 * BK * 2, &tmA, bar, m0 + j * 64, kb * BK);
           }
+        };
+        auto load_b = [&](uint8_t* sB, uint64_t* bar, int kb) {
           if (!B_MN) {
-            tma_load_2d_pair(sB, &tmB, &full[stage], kb * BK, n0);
+            tma_load_2d_pair(sB, &tmB, bar, kb * BK, n0);
           } else {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) tma_load_2d_pair(sB + j * 64 * BK * 2, &tmB, &full[stage], n0 + j * 64, kb * BK);
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(sB + j * 64 * BK * 2, &tmB, bar, n0 + j * 64, kb * BK);
           }
+        };
+        int kb0 = 0;
+        if (first) {  // every stage is free: weight tiles first, then (after the wait) the A tiles
+          first = false;
+          const int pre = KB < S ? KB : S;
+          for (int kb = 0; kb < pre; ++kb) {
+            if (leader) mbar_arrive_expect_tx(&full[kb], 2 * C::STAGE_BYTES);  // both CTAs' bytes
+            load_b(smem + kb * C::STAGE_BYTES + C::A_BYTES, &full[kb], kb);
+          }
+          pdl_wait();
+          for (int kb = 0; kb < pre; ++kb) load_a(smem + kb * C::STAGE_BYTES, &full[kb], kb);
+          stage = pre == S ? 0 : pre;
+          phase = pre == S ? 1u : 0u;
+          kb0 = pre;
+        }
+        for (int kb = kb0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);  // both CTAs' bytes
+          load_a(sA, &full[stage], kb);
+          load_b(sA + C::A_BYTES, &full[stage], kb);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
@@ -636,13 +657,17 @@ int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, i
   cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // may start while the kernel before it runs, if that kernel allows it (the row pass and the fused
+  // producers do, right away); the producer waits (griddepcontrol.wait) before it loads A
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, p) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
