@@ -115,30 +115,52 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    // A programmatic dependent of the kernel that writes A's row scales (and, for fp16 A, A itself):
+    // the first stages' weight tiles load before griddepcontrol.wait, A only after.
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      bool first = true;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
         int tm, tn;
         tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
         const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < KB; ++kb) {
+        auto load_a = [&](uint8_t* sA, uint64_t* bar, int kb) {
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, bar, kb * BK, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sA + j * 64 * BK * 2, &tmA, bar, m0 + j * 64, kb * BK);
+          }
+        };
+        auto load_b = [&](uint8_t* sB, uint64_t* bar, int kb) {
+          if (!B_MN) {
+            tma_load_2d(sB, &tmB, bar, kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * 64 * BK * 2, &tmB, bar, n0 + j * 64, kb * BK);
+          }
+        };
+        int kb0 = 0;
+        if (first) {  // every stage is free: weight tiles first, then (after the wait) the A tiles
+          first = false;
+          const int pre = KB < STAGES ? KB : STAGES;
+          for (int kb = 0; kb < pre; ++kb) {
+            mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+            load_b(smem + kb * C::STAGE_BYTES + C::A_BYTES, &full[kb], kb);
+          }
+          pdl_wait();
+          for (int kb = 0; kb < pre; ++kb) load_a(smem + kb * C::STAGE_BYTES, &full[kb], kb);
+          stage = pre == STAGES ? 0 : pre;
+          phase = pre == STAGES ? 1u : 0u;
+          kb0 = pre;
+        }
+        for (int kb = kb0; kb < KB; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.err)) break;
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
-          uint8_t* sB = sA + C::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          if (!A_MN) {
-            tma_load_2d(sA, &tmA, &full[stage], kb * BK, m0);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sA + j * 64 * BK * 2, &tmA, &full[stage], m0 + j * 64, kb * BK);
-          }
-          if (!B_MN) {
-            tma_load_2d(sB, &tmB, &full[stage], kb * BK, n0);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * 64 * BK * 2, &tmB, &full[stage], n0 + j * 64, kb * BK);
-          }
+          load_a(sA, &full[stage], kb);
+          load_b(sA + C::A_BYTES, &full[stage], kb);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -309,8 +331,17 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, i
   p.group_m = group_env > 0 ? group_env : kGroupM;
   p.tiles_n = (N + BN - 1) / BN;
   const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = std::min(tiles, d->sms);
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(tiles, d->sms));
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see the producer
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
 
