@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(256) scale_cl_kernel(const __nv_bfloat16* __re
                                                        int32_t* __restrict__ e, uint4* __restrict__ x16cl,
                                                        int flat, const float* __restrict__ amax = nullptr,
                                                        int t = 0, float* __restrict__ out_scale = nullptr) {
+  pdl_launch_dependents();  // the implicit GEMM may start its prologue and weight loads meanwhile
   const int C8 = (int)(g.C / 8);
   const int64_t per_sample = g.D * g.H * g.W * C8;
   const int64_t total = g.B * per_sample;
