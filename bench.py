@@ -21,7 +21,6 @@ import json
 import os
 import pathlib
 import statistics
-import subprocess
 import sys
 import threading
 import time

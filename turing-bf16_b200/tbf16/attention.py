@@ -13,7 +13,6 @@ import math
 
 import torch
 
-from . import _ext
 from ._ext import BF16, F16, call, ptr, require_cuda, stream_ptr
 
 _DTYPE = {torch.bfloat16: BF16, torch.float16: F16}

@@ -16,8 +16,7 @@ import weakref
 
 import torch
 
-from . import _ext
-from ._ext import BF16, F16, available, call, ptr, require_cuda, stream_ptr
+from ._ext import available, call, ptr, require_cuda, stream_ptr
 
 # Kept for callers that set them (reference tbf16/ops.py:19-23); this build has one path for every M.
 _USE_CUDA = os.environ.get("TBF16_BACKEND", "cuda") == "cuda"
