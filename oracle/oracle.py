@@ -343,6 +343,48 @@ def rmsnorm_rows(x, weight, eps=1e-6, offset=1.0, style="gemma", target_exp=15):
     return f16_rn(r.float() / s_inv[:, None]), s_inv, r
 
 
+def add_rmsnorm_rows(x, residual, weight, post_weight=None, eps=1e-6, offset=1.0, style="gemma", target_exp=15):
+    """s = bf16(residual + (rmsnorm_rows(x, post_weight)'s bf16 rows if post_weight is given else x)) -- a
+    model's bf16 residual add -- then rmsnorm_rows(s, weight). Returns (s, r16, s_inv)."""
+    a = _cpu(x)
+    if post_weight is not None:
+        a = rmsnorm_rows(a, post_weight, eps, offset, style, target_exp)[2]
+    s_ = bf16_rn(_cpu(residual).float() + a.float())
+    r16, s_inv, _ = rmsnorm_rows(s_, weight, eps, offset, style, target_exp)
+    return s_, r16, s_inv
+
+
+def rope(y, cos, sin):
+    """Rotate-half rotary embedding on bf16 tensors, a model's three roundings:
+    bf16(bf16(y cos) + bf16(rot(y) sin)), rot(y) = (-y[..., D/2:], y[..., :D/2]); y (..., S, H, D) with
+    cos / sin (S, D) broadcast over the heads."""
+    y = _cpu(y).float()
+    D = y.shape[-1]
+    rot = torch.cat([-y[..., D // 2:], y[..., :D // 2]], -1)
+    c, s_ = _cpu(cos).float()[:, None, :], _cpu(sin).float()[:, None, :]
+    return bf16_rn(bf16_rn(y * c).float() + bf16_rn(rot * s_).float())
+
+
+def glu_bwd(dh, gate, up, act="silu"):
+    """Gradients of h = bf16(act(g)) * u as torch's autograd takes them on bf16 tensors, fp32 arithmetic:
+    a = bf16(act(g)), du = bf16(dh a), da = bf16(dh u), dg = bf16(da act'(g)) (silu: s (1 + g (1 - s)),
+    s = 1 / (1 + e^-g); tanh-GELU: 0.5 (1 + t) + 0.5 g (1 - t^2) sqrt(2/pi) (1 + 3 0.044715 g^2)).
+    Returns (dg, du)."""
+    d, g, u = _cpu(dh).float(), _cpu(gate).float(), _cpu(up).float()
+    if act == "silu":
+        sg = 1.0 / (1.0 + torch.exp(-g))
+        a = g / (1.0 + torch.exp(-g))
+        dact = sg * (1.0 + g * (1.0 - sg))
+    else:
+        kb = math.sqrt(2.0 / math.pi)
+        t = torch.tanh(kb * (g + 0.044715 * g * g * g))
+        a = 0.5 * g * (1.0 + t)
+        dact = 0.5 * (1.0 + t) + 0.5 * g * (1.0 - t * t) * kb * (1.0 + 3.0 * 0.044715 * g * g)
+    du = bf16_rn(d * bf16_rn(a).float())
+    da = bf16_rn(d * u)
+    return bf16_rn(da.float() * dact), du
+
+
 # ----------------------------------------------------------------------------- scaled convolutions
 
 def conv_sample_exp(x: torch.Tensor, target_exp: int) -> torch.Tensor:

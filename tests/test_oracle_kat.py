@@ -130,3 +130,40 @@ def test_fused_rows_oracle_known_answers():
     assert torch.all(r.float() == 1.0)  # x / rms(x) = 1, times (0 + 1)
     assert s_inv.item() == 2.0 ** -14  # row max 1 -> biased 127 -> scale 2^(253 + 15 - 127 - 127)
     assert torch.all(r16.float() == 2.0 ** 14)
+
+
+def test_fused_op_restatements_match_torch_cpu():
+    """The oracle's restatements of the fused model-side ops against torch's own bf16 ops on the CPU:
+    rotary embedding and the residual add bit-equal; the gated activation's backward within one bf16
+    ulp of torch's autograd (its CPU exp / tanh may differ from the oracle's in the last fp32 bit)."""
+    import torch.nn.functional as F
+    from oracle import oracle as orc
+    g = torch.Generator().manual_seed(3)
+    S, H, D = 9, 2, 64
+    y = (torch.randn(2, S, H, D, generator=g) * 3).bfloat16()
+    ang = torch.outer(torch.arange(S, dtype=torch.float32), 1.0 / (1e4 ** (torch.arange(0, D, 2) / D)))
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16()
+    rot = torch.cat([-y[..., D // 2:], y[..., :D // 2]], -1)
+    ref = y * cos[:, None, :] + rot * sin[:, None, :]
+    assert torch.equal(orc.rope(y, cos, sin).view(torch.int16), ref.view(torch.int16))
+    x = torch.randn(5, 64, generator=g).bfloat16()
+    res = (torch.randn(5, 64, generator=g) * 10).bfloat16()
+    w = (torch.randn(64, generator=g) * 0.1).bfloat16()
+    s, r16, s_inv = orc.add_rmsnorm_rows(x, res, w)
+    assert torch.equal(s.view(torch.int16), (res + x).view(torch.int16))
+    r16b, s_invb, _ = orc.rmsnorm_rows(res + x, w)
+    assert torch.equal(r16.view(torch.int16), r16b.view(torch.int16)) and torch.equal(s_inv, s_invb)
+    for act in ("silu", "gelu_tanh"):
+        gt = (torch.randn(7, 256, generator=g) * 3).bfloat16().requires_grad_()
+        ut = torch.randn(7, 256, generator=g).bfloat16().requires_grad_()
+        dh = (torch.randn(7, 256, generator=g) * 0.01).bfloat16()
+        h = (F.silu(gt) if act == "silu" else F.gelu(gt, approximate="tanh")) * ut
+        h.backward(dh)
+        dg, du = orc.glu_bwd(dh, gt.detach(), ut.detach(), act)
+        # where tanh saturates (g < -5) torch's CPU kernel rounds tanh to exactly -1, giving 0 where the
+        # restatement keeps a value below 1e-7: an absolute floor of 2^-18 max|dh| covers that
+        floor = 2.0 ** -18 * dh.abs().max().item()
+        for ours, theirs in ((dg, gt.grad), (du, ut.grad)):
+            d = (ours.double() - theirs.double()).abs()
+            assert bool((d <= orc.bf16_ulp(theirs.double()) + floor).all()), act
