@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
 
 template <int BN, int STAGES, bool CONVERT, bool A_MN, bool B_MN>
 int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
-                const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
+                const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st, bool pdl = false) {
   using C = Cfg<BN, STAGES, CONVERT>;
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   if (!d) return TBF16_ERR_DEVICE;
@@ -336,11 +336,15 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, i
   cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
+  // pdl: the kernel before it is this call's own row pass, which writes only A's operand and row scales,
+  // so the GEMM may start early and load its first weight tiles before griddepcontrol.wait (see the
+  // producer). Any other predecessor may write the weights (prepare_weight's pass does), so other
+  // launches are plain: the wait is then a no-op and every load follows the predecessor's completion.
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see the producer
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
@@ -643,7 +647,8 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
 // The pair kernel with A's tensor map already built (a matrix, or the conv input for CONV).
 template <bool A_MN, bool B_MN, bool CONV, int PN>
 int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
-                     const float* sb, const void* bias, void* y, int64_t ldy, const ConvGemm* cv, cudaStream_t st) {
+                     const float* sb, const void* bias, void* y, int64_t ldy, const ConvGemm* cv, cudaStream_t st,
+                     bool pdl) {
   using C = PairCfg<PN>;
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   if (!d) return TBF16_ERR_DEVICE;
@@ -693,12 +698,13 @@ int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, i
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  // may start while the kernel before it runs, if that kernel allows it (the row pass and the fused
-  // producers do, right away); the producer waits (griddepcontrol.wait) before it loads A
+  // pdl: may start while the kernel before it runs -- only when that kernel is known to write just A and
+  // its row scales (this call's own row pass, the conv's scale pass): the producer loads the first
+  // weight tiles before griddepcontrol.wait. Other launches are plain (see launch_gemm).
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, p) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
@@ -735,7 +741,7 @@ int pair_width(int M, int N, int pairs) {
 
 template <bool A_MN, bool B_MN>
 int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* sa,
-                     const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st) {
+                     const float* sb, const void* bias, void* y, int64_t ldy, cudaStream_t st, bool pdl = false) {
   CUtensorMap ta;
   int rc = A_MN ? tbf16_host::make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64)
                 : tbf16_host::make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, BM);
@@ -743,13 +749,13 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   if (!B_MN) {
     const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
     switch (pair_width(M, N, d ? d->sms / 2 : 74)) {
-      case 192: return launch_pair_core<A_MN, false, false, 192>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
-      case 160: return launch_pair_core<A_MN, false, false, 160>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
-      case 128: return launch_pair_core<A_MN, false, false, 128>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+      case 192: return launch_pair_core<A_MN, false, false, 192>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
+      case 160: return launch_pair_core<A_MN, false, false, 160>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
+      case 128: return launch_pair_core<A_MN, false, false, 128>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
       default: break;
     }
   }
-  return launch_pair_core<A_MN, B_MN, false, 256>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st);
+  return launch_pair_core<A_MN, B_MN, false, 256>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
 }
 
 // The pair kernel whenever both dimensions span two or more 256 tiles (it moves a third less data from
@@ -777,7 +783,7 @@ int conv_gemm_pair(const void* x16cl, int64_t B, int64_t D, int64_t H, int64_t W
   CUtensorMap ta;
   if (int rc = make_tmap_conv_in(&ta, x16cl, B, D, H, W, C, bx, 128 / bx)) return rc;
   // K = taps x cb x 64: the weight rows are exactly one K long
-  return launch_pair_core<false, false, true, 256>(ta, w16, ldw, M, N, (int)ldw, sa, sb, bias, y, ldy, &cv, st);
+  return launch_pair_core<false, false, true, 256>(ta, w16, ldw, M, N, (int)ldw, sa, sb, bias, y, ldy, &cv, st, true);
 }
 
 }  // namespace tbf16_host
@@ -808,9 +814,10 @@ int tbf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w
       return tbf16_host::skinny_gemm(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy, st,
                                        true);
     if (use_pair((int)M, (int)N))
-      return launch_gemm_pair<false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy, st);
+      return launch_gemm_pair<false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y, ldy, st,
+                                            true);
     return launch_gemm<256, 4, false, false, false>(x16_ws, K, w16, ldw, (int)M, (int)N, (int)K, x_sinv, ws, bias, y,
-                                                    ldy, st);
+                                                    ldy, st, true);
   }
   if (int st = tbf16_row_scale(x, M, K, ldx, target_exp, l1, x_sinv, nullptr, nullptr, 0, stream)) return st;
   return tbf16_linear_scaled(x, M, K, ldx, w16, N, ldw, ws, bias, y, ldy, x_sinv, stream);
