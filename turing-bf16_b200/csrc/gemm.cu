@@ -19,6 +19,12 @@
 //               in place in the A stage, then fence.proxy.async and arrive on the stage's conv barrier.
 // Every mbarrier wait is bounded (2 s); on timeout the kernel records it in the device error word,
 // every role leaves its loop, and the CTA drains and frees its TMEM before returning.
+//
+// The CTA-pair kernel (scaled_gemm_pair_kernel, further down) is the one large products use: clusters
+// of two CTAs compute 256 x PN tiles with tcgen05.mma.cta_group::2 (PN = 256, or 192 / 160 / 128 when
+// the last wave of 256-wide tiles would leave most pairs idle), and its CONV form reads A as an implicit
+// convolution through a 5-D tensor map. Inside tbf16_linear both kernels launch as programmatic
+// dependents of the call's own row pass (first weight tiles before griddepcontrol.wait, A after).
 #include <algorithm>
 
 #include "common.cuh"
