@@ -5,17 +5,20 @@
 //
 //   glu_rows_kernel      h = bf16(bf16(act(g)) * u) for a gated MLP (act = silu or tanh-gelu),
 //                        as torch computes act(g) * u on bf16 tensors (to within one bf16 ulp: fast exp)
-//   rmsnorm_rows_kernel  r = RMSNorm(x) in the two common roundings (Gemma: bf16(x * rsqrt(ms + eps) *
-//                        (w + offset)); Llama: bf16(w * bf16(x * rsqrt(ms + eps))))
+//   norm_rows_kernel     r = RMSNorm(x) in the two common roundings (Gemma: bf16(x * rsqrt(ms + eps) *
+//                        (w + offset)); Llama: bf16(w * bf16(x * rsqrt(ms + eps)))), optionally after a
+//                        first norm and a residual add (x + norm(y), and the next block's norm rows)
 // then, for the produced rows: s_inv = the fused rule's power-of-two row scale (row max, target t) and
 // y16 = fp16(row / s_inv) -- exactly what tbf16_row_scale with a y16 buffer gives on the bf16 rows.
+// Also here, for the attention's operands and for training: norm_rope_kernel (per-head RMSNorm + rotary
+// embedding in one pass) and glu_bwd_kernel (the gated activation's backward).
 //
 // HBM-bound: the threads that own a row keep it in registers, so each input is read once and the fp16
 // operand (plus, on request, the bf16 row) written once -- one warp per row for rows up to 1024
-// elements (up to 4 x 16 bytes a lane), else one block per row with the fewest warps that hold it at one
-// or two 16-byte vectors a thread (rows up to 16384 elements), which keeps registers per thread low and
-// several blocks on each SM. Row maxima and sums of squares are reduced over the lanes and then over
-// the warps in a fixed order.
+// elements (up to 4 x 16 bytes a lane), and for norms of up to 4096 over many rows (8-16 a lane); else
+// one block per row with the fewest warps that hold it at one or two 16-byte vectors a thread (rows up
+// to 16384 elements), which keeps registers per thread low and several blocks on each SM. Row maxima
+// and sums of squares are reduced over the lanes and then over the warps in a fixed order.
 #include "common.cuh"
 
 using namespace tbf16;
