@@ -2,8 +2,11 @@
 
 Same public surface as the reference's tbf16/ops.py (quantize_rows, prepare_weight, scaled_linear,
 linear_q, small_m_linear, quantize_rows_shared, _target_exp), plus linear_host for activations that
-live in pinned host memory and the producer-fused glu_rows / rmsnorm_rows (glu_linear, rmsnorm_linear),
-which compute a linear's row scales in the kernel that produces its input. The work runs in libtbf16_sm100.so: a row-amax -> exponent pass (which
+live in pinned host memory and the producer-fused glu_rows / rmsnorm_rows / add_rmsnorm_rows
+(glu_linear, rmsnorm_linear), which compute a linear's row scales in the kernel that produces its input,
+rmsnorm (with an optional residual add), rmsnorm_rope (QK-norm + rotary embedding in one pass) and
+glu_bwd (the gated activation's backward for training). The work runs in libtbf16_sm100.so: a
+row-amax -> exponent pass (which
 also writes the fp16 copy of x for large N) and a warp-specialised TMA + tcgen05 GEMM that
 accumulates in fp32 in TMEM and writes bf16 straight from the accumulator. Up to 4 rows take a
 weight-streaming kernel instead (the reference's single-row GEMV, extended), up to 256 rows a split-K
