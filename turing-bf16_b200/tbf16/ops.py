@@ -483,8 +483,8 @@ def rmsnorm_rope(x: torch.Tensor, weight, cos: torch.Tensor, sin: torch.Tensor, 
     lead = x.shape[:-2]
     tok = x.stride(-3)
     uniform = all(x.stride(i) == tok * math.prod(lead[i + 1:]) for i in range(len(lead)) if lead[i] > 1)
-    xc = x if (x.stride(-1) == 1 and x.stride(-2) == D and uniform and tok % 8 == 0 and x.data_ptr() % 16 == 0) \
-        else x.contiguous()
+    xc = x if (x.stride(-1) == 1 and x.stride(-2) == D and uniform and tok >= H * D and tok % 8 == 0
+               and x.data_ptr() % 16 == 0) else x.contiguous()
     if xc is not x:
         tok = H * D
     c2, s2 = cos.reshape(S, D).contiguous(), sin.reshape(S, D).contiguous()
