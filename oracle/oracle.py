@@ -231,21 +231,46 @@ def _logit_mask(attn_mask, is_causal, Sq, Sk):
     return m
 
 
-def sdpa_fwd(q, k, v, attn_mask=None, is_causal=False, scale=None, v_exp=13):
+def _select_kv_heads(t, kv_heads, group):
+    """Stacks the (b, hkv) head groups of t (B, H, S, D) along a new batch axis: query tensors give
+    (n, group, S, D), key / value tensors (group = 1) give (n, 1, S, D)."""
+    return torch.stack([t[b, h * group:(h + 1) * group] for b, h in kv_heads])
+
+
+def _select_mask(m, kv_heads, group):
+    if m is None or m.dim() < 4:
+        return m
+    return torch.stack([m[b if m.shape[0] > 1 else 0, h * group:(h + 1) * group] if m.shape[1] > 1
+                        else m[b if m.shape[0] > 1 else 0] for b, h in kv_heads])
+
+
+def sdpa_fwd(q, k, v, attn_mask=None, is_causal=False, scale=None, v_exp=13, kv_heads=None):
     """Scaled attention forward, tbf16/attention.py:56-65 (v_exp=13, inference) and
     tbf16/autograd.py:153-164 (v_exp=0, training), computed in fp64 from the exact fp16 copies.
 
     Returns a dict: out (bf16 of O * 2^ev rounded once, this build's epilogue), out_ref (the
     reference's fp16 out16 rounded again to bf16 by head_scale, attention.py:65), lse (natural-log
     logsumexp of the scaled logits, fp64), o16 (fp64 O before the 2^ev rescale), p, and the
-    integer exponents a, ev."""
+    integer exponents a, ev.
+
+    kv_heads: optional list of (b, h_kv) pairs. The exponents a and ev are still taken over every
+    head (they are global maxima in the reference), but the fp64 attention is computed only for
+    those KV heads and their query heads, stacked along the batch axis: every returned tensor then
+    has shape (len(kv_heads), group, ...) for query-side values and (len(kv_heads), 1, ...) for ev."""
     q16, k16, v16, a, ev = prepare_qkv(q, k, v, v_exp)
     B, Hq, Sq, D = q16.shape
     Sk = k16.shape[2]
     sc = scale if scale is not None else 1.0 / math.sqrt(D)
+    m = _logit_mask(attn_mask, is_causal, Sq, Sk)
+    if kv_heads is not None:
+        group = Hq // k16.shape[1]
+        q16, k16, v16 = (_select_kv_heads(q16, kv_heads, group), _select_kv_heads(k16, kv_heads, 1),
+                         _select_kv_heads(v16, kv_heads, 1))
+        ev = torch.stack([ev[b, h:h + 1] for b, h in kv_heads])
+        m = _select_mask(m, kv_heads, group)
+        Hq = group
     kk, vv = _expand_kv(k16, Hq).double(), _expand_kv(v16, Hq).double()
     s = (q16.double() @ kk.transpose(-1, -2)) * sc
-    m = _logit_mask(attn_mask, is_causal, Sq, Sk)
     if m is not None:
         s = s + m
     lse = torch.logsumexp(s, -1)
@@ -260,20 +285,31 @@ def sdpa_fwd(q, k, v, attn_mask=None, is_causal=False, scale=None, v_exp=13):
             "k16": k16, "v16": v16, "scale": sc, "zmax": zmax, "pv_abs": p @ vv.abs()}
 
 
-def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None):
+def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None, kv_heads=None):
     """Scaled attention backward, tbf16/autograd.py:166-193, in fp64 from the exact fp16 operands:
     G = (12 - ceil(log2 D)) - max_{b,h}(head_exp(dout) + ev_q); dO16 = fp16(dout * 2^(ev_q + G));
     dq = dq16 * 2^(a - G), dk = reduce_kv(dk16) * 2^(-a - G), dv = reduce_kv(dv16) * 2^(-ev - G),
     each rounded once to bf16 (the reference rounds dq16/dk16/dv16 to fp16 first). The retry loop
-    (:177-189) never triggers here because nothing is rounded to fp16 after dO16."""
-    f = sdpa_fwd(q, k, v, attn_mask, is_causal, scale, v_exp=0)
+    (:177-189) never triggers here because nothing is rounded to fp16 after dO16.
+
+    Also returned for error bounds: abs_dq, abs_dk (the dQ / dK contractions over P (|dP| + sum |dO16| |O|),
+    the magnitudes that the rounding of P, delta and dS scale with, scaled like the gradients), abs_dv
+    (over P |dO16|), and dq16 / dk16 / dv16 before their power-of-two scales (the reference rounds
+    these to fp16). kv_heads: as in sdpa_fwd (G stays global)."""
+    f = sdpa_fwd(q, k, v, attn_mask, is_causal, scale, v_exp=0, kv_heads=kv_heads)
     q16, k16, v16, a, ev, p, o = f["q16"], f["k16"], f["v16"], f["a"], f["ev"], f["p"], f["o16"]
-    B, Hq, Sq, D = q16.shape
-    Hkv = k16.shape[1]
-    ev_q = expand_heads(ev, Hq)
-    e = (head_exp(dout) + ev_q).max()
+    Hq = q16.shape[1]
+    B_all, Hq_all = q.shape[0], q.shape[1]
+    ev_full = prepare_exponents(q, k, v, 0)[1]
+    e = (head_exp(dout) + expand_heads(ev_full, Hq_all)).max()
+    D = q16.shape[-1]
     t_do = 12 - math.ceil(math.log2(D))
     G = int(t_do - e)
+    if kv_heads is not None:
+        dout = _select_kv_heads(_cpu(dout), kv_heads, Hq_all // k.shape[1])
+    B = q16.shape[0]
+    Hkv = k16.shape[1]
+    ev_q = expand_heads(ev, Hq)
     do16 = head_scale(dout, ev_q + G, torch.float16).double()
     kk, vv = _expand_kv(k16, Hq).double(), _expand_kv(v16, Hq).double()
     dv16 = p.transpose(-1, -2) @ do16
@@ -288,11 +324,16 @@ def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None):
         return g if Hkv == Hq else g.view(B, Hkv, Hq // Hkv, *g.shape[2:]).sum(2)
 
     two = lambda ex: torch.ldexp(torch.ones(()), ex.double())[..., None, None]
+    # |dS| with the magnitudes its rounding errors scale with: P times (|dP| + sum_d |dO16| |O|)
+    dsa = p * (dp.abs() + (do16.abs() * o.abs()).sum(-1, keepdim=True))
     dq = bf16_rn(dq16 * two(a - G))
     dk = bf16_rn(reduce_kv(dk16) * two(-a - G))
     dv = bf16_rn(reduce_kv(dv16) * two(-ev - G))
     return {"dq": dq, "dk": dk, "dv": dv, "G": G, "a": a, "ev": ev, "out": f["out"], "lse": f["lse"],
-            "do16": do16, "delta": delta}
+            "do16": do16, "delta": delta, "dq16": dq16, "dk16": reduce_kv(dk16), "dv16": reduce_kv(dv16),
+            "abs_dq": (dsa @ kk.abs()) * f["scale"] * two(a - G),
+            "abs_dk": reduce_kv(dsa.transpose(-1, -2) @ q16.double().abs()) * f["scale"] * two(-a - G),
+            "abs_dv": reduce_kv(p.transpose(-1, -2) @ do16.abs()) * two(-ev - G)}
 
 
 # ----------------------------------------------------------------------------- GEMMs
@@ -459,30 +500,36 @@ def gemv_ref(x, w16, ws, bias=None):
     return bf16_rn(v.float())
 
 
-def linear_train(x, w, bias, dy):
+def linear_train(x, w, bias, dy, rows=None, dw_rows=None):
     """tbf16/autograd.py:58-90 (ScaledLinearFn) with this build's GEMM semantics (fp32/fp64
     accumulation, one bf16 rounding). Exponent conventions kept from the reference:
       forward: x rows max t=_target_exp(K) (ops.py:133-137), w rows t=_target_exp(K) (ops.py:140-142)
       dX:      dy rows L1 t=15 (autograd.py:79), w columns t=_target_exp(N) (autograd.py:80)
       dW:      dy columns t=min(0, 15 - ceil(log2 M)) with row_mul = sx (autograd.py:85-87)
       db:      fp32 column sum of dy (autograd.py:88-89), here summed in fp64.
-    x (M, K), w (N, K), bias (N,) or None, dy (M, N), all bf16."""
+    x (M, K), w (N, K), bias (N,) or None, dy (M, N), all bf16.
+
+    rows / dw_rows (optional index tensors): the scales are always computed from the full operands,
+    but y and dx are returned only for rows `rows` of M and dw only for rows `dw_rows` of N, so that
+    full-size layers can be checked on a sample of their outputs."""
     x2, w, dy2 = _cpu(x).reshape(-1, x.shape[-1]).contiguous(), _cpu(w).contiguous(), _cpu(dy).reshape(-1, w.shape[0]).contiguous()
     M, K = x2.shape
     N = w.shape[0]
+    rows = torch.arange(M) if rows is None else _cpu(rows).long()
+    dw_rows = torch.arange(N) if dw_rows is None else _cpu(dw_rows).long()
     t = target_exp(K)
     x16, sx = quantize_rows(x2, t)
     w16, sw = quantize_rows(w, t)
-    y = gemm_f16(x16, 0, w16, 0, M, N, K, sx, sw, bias)
+    y = gemm_f16(x16[rows], 0, w16, 0, len(rows), N, K, sx[rows], sw, bias)
     dy16, sdy = quantize_rows(dy2, 15, l1=True)
     w16c, swc = quantize_cols(w, target_exp(N))
-    dx = gemm_f16(dy16, 0, w16c, 1, M, K, N, sdy, swc)
+    dx = gemm_f16(dy16[rows], 0, w16c, 1, len(rows), K, N, sdy[rows], swc)
     t2 = min(0, 15 - math.ceil(math.log2(max(M, 1))))
     dy16c, sdyc = quantize_cols(dy2, t2, row_mul=sx)
-    dw = gemm_f16(dy16c, 1, x16, 1, N, K, M, sdyc, None)
+    dw = gemm_f16(dy16c[:, dw_rows], 1, x16, 1, len(dw_rows), K, M, sdyc[dw_rows], None)
     db = None if bias is None else bf16_rn(dy2.double().sum(0))
     return {"y": y, "dx": dx, "dw": dw, "db": db, "x16": x16, "sx": sx, "w16": w16, "sw": sw, "dy16": dy16,
-            "sdy": sdy, "w16c": w16c, "swc": swc, "dy16c": dy16c, "sdyc": sdyc}
+            "sdy": sdy, "w16c": w16c, "swc": swc, "dy16c": dy16c, "sdyc": sdyc, "rows": rows, "dw_rows": dw_rows}
 
 
 def rel_err(y, ref):

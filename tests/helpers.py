@@ -29,7 +29,9 @@ def assert_close_ulp(y, ref, tol, frac_exact=0.95, what=""):
 
 
 def rel_err(y, ref):
-    y, ref = y.detach().double().cpu(), ref.detach().double().cpu()
+    """||y - ref|| / ||ref|| in fp64, on the GPU when both tensors are there."""
+    dev = ref.device if (y.is_cuda and ref.is_cuda) else "cpu"
+    y, ref = y.detach().to(dev).double(), ref.detach().to(dev).double()
     return ((y - ref).norm() / ref.norm()).item()
 
 
@@ -60,3 +62,18 @@ def bits_equal(a: torch.Tensor, b: torch.Tensor) -> bool:
         return False
     both_nan = torch.isnan(a.float()) & torch.isnan(b.float())
     return bool(((a.view(torch.int16) == b.view(torch.int16)) | both_nan).all())
+
+
+def ulp_distance(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Number of bf16 values between a and b (both bf16): the distance of their bit patterns on the
+    ordered integer line (negative values mirrored, so -0 and +0 are one point)."""
+    def ordered(t):
+        v = t.detach().cpu().contiguous().view(torch.int16).int()
+        return torch.where(v < 0, -(v & 0x7FFF), v)
+    return (ordered(a) - ordered(b)).abs()
+
+
+def report(name: str, **values):
+    """One greppable line per parity measurement (shown with pytest -s)."""
+    parts = " ".join(f"{k}={v:.3e}" if isinstance(v, float) else f"{k}={v}" for k, v in values.items())
+    print(f"\nPARITY {name} {parts}")

@@ -5,13 +5,16 @@ run on the same inputs on the same GPU as this build's kernels.
 Known reference behaviour excluded here (and documented): with --use_fast_math the reference's fused
 GEMM flushes s_inv = 2^-127 to zero for rows whose max is zero or below 2^-113, then multiplies by
 1/0 and returns NaN for those rows; this build keeps the exact subnormal and returns the bias."""
+import math
 import pathlib
 
 import pytest
 import torch
+import torch.nn.functional as F
 
 import inputs
-from helpers import assert_close_ulp, bits_equal, edge_rows, gemm_tolerance, rel_err
+from helpers import (assert_close_ulp, bf16_ulp, bits_equal, edge_rows, gemm_tolerance, rel_err, report,
+                     ulp_distance)
 
 pytestmark = pytest.mark.gpu
 
@@ -39,7 +42,17 @@ def test_linear_vs_reference_fused_kernel(M, K, N):
     # both sides accumulate in fp32 (different orders): twice the accumulation bound
     tol = gemm_tolerance(y_ref.cpu(), 2 * absprod.cpu(), K)
     assert_close_ulp(y.cpu(), y_ref.cpu(), tol, frac_exact=0.9, what=f"vs reference fused {M}x{K}x{N}")
+    # within one bf16 ulp of the reference's output wherever the two fp32 accumulations (different
+    # orders) cannot move the value by half an ulp; elsewhere the tolerance above applies
+    dist = ulp_distance(y, y_ref)
+    acc_bound = 2 * 8.0 * math.sqrt(K) * 2.0 ** -24 * absprod.cpu()
+    tight = acc_bound < 0.5 * bf16_ulp(y_ref.cpu())
+    assert int(dist[tight].max()) <= 1, f"{int((dist[tight] > 1).sum())} well-conditioned elements beyond 1 ulp"
     exact = x.double() @ w.double().t() + b.double()
+    report(f"linear vs reference fused kernel {M}x{K}x{N}", bit_equal=float((dist == 0).double().mean()),
+           within_1ulp=float((dist <= 1).double().mean()), max_ulp=int(dist.max()),
+           max_ulp_well_conditioned=int(dist[tight].max()), well_conditioned=float(tight.double().mean()),
+           err_fp64=rel_err(y, exact), ref_err_fp64=rel_err(y_ref, exact))
     assert rel_err(y, exact) < 2e-3 and rel_err(y_ref, exact) < 2e-3
 
 
@@ -118,3 +131,74 @@ def test_head_amax_and_scale_vs_reference_kernel():
     E.call("tbf16_head_scale_cast", E.ptr(v), E.BF16, 2, 4, 256, 64, *v.stride()[:3], E.ptr(e), 4, 1, E.ptr(y), E.F16,
            E.stream_ptr())
     assert bits_equal(y, y_ref)
+
+
+def _reference_sdpa(small, q, k, v, causal):
+    """The reference's inference attention (tbf16/attention.py:38-65) on the GPU: its own head_amax and
+    head_scale_cast kernels for the exponents and the fp16 copies (v_exp = 13), torch's fp16 attention on
+    the memory-efficient backend, and its head_scale_cast of the fp16 output back to bf16."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    B, H = q.shape[:2]
+    Hkv = k.shape[1]
+    eq = torch.frexp(small.head_amax(q))[1].amax()
+    ek = torch.frexp(small.head_amax(k))[1].amax()
+    a = torch.div(ek - eq, 2, rounding_mode="floor")
+    a = torch.maximum(torch.minimum(a, 14 - eq), ek - 14).to(torch.int32)
+    ev = (torch.frexp(small.head_amax(v))[1] - 13).to(torch.int32)
+    q16 = small.head_scale_cast(q, a.expand(B, H).contiguous(), torch.float16)
+    k16 = small.head_scale_cast(k, (-a).expand(B, Hkv).contiguous(), torch.float16)
+    v16 = small.head_scale_cast(v, (-ev).contiguous(), torch.float16)
+    with sdpa_kernel(SDPBackend.EFFICIENT_ATTENTION):
+        out16 = F.scaled_dot_product_attention(q16, k16, v16, is_causal=causal, enable_gqa=H != Hkv)
+    ev_q = ev if H == Hkv else ev.repeat_interleave(H // Hkv, 1)
+    return small.head_scale_cast(out16, ev_q.contiguous(), torch.bfloat16), q16, k16, v16, ev_q
+
+
+def _attention_tolerance(q16, k16, v16, ev_q, out_ref, causal, rows_per_chunk=2048):
+    """Per-element bound between two fp16 attention pipelines, computed on the GPU in fp64: one bf16 ulp,
+    the fp16 rounding of P in each (2^-10 of the head's V scale), and the fp32 rounding of the logits in
+    each (4 ulp of the row's largest |logit| times the weights' spread, which matters for config 3's
+    logits that overflow fp16)."""
+    B, H, S, D = q16.shape
+    grp = H // k16.shape[1]
+    scale = 1.0 / math.sqrt(D)
+    two_ev = torch.ldexp(torch.ones((), device=q16.device, dtype=torch.float64), ev_q.double())
+    tol = torch.empty(out_ref.shape, dtype=torch.float64, device=q16.device)
+    for b in range(B):
+        for h in range(H):
+            kh, vh = k16[b, h // grp].double(), v16[b, h // grp].double()
+            vmax = vh.abs().amax()
+            for r0 in range(0, S, rows_per_chunk):
+                r1 = min(S, r0 + rows_per_chunk)
+                s = (q16[b, h, r0:r1].double() @ kh.t()) * scale
+                if causal:
+                    s.masked_fill_(torch.arange(S, device=s.device)[None, :] > torch.arange(r0, r1, device=s.device)[:, None],
+                                   float("-inf"))
+                zmax = torch.where(torch.isfinite(s), s.abs(), torch.zeros_like(s)).amax(-1, keepdim=True)
+                p = torch.softmax(s, -1)
+                spread = p @ vh.abs() + (p @ vh).abs()
+                tol[b, h, r0:r1] = (2.0 ** -10 * vmax + 2.0 ** -20 * zmax * spread) * two_ev[b, h]
+    return tol + bf16_ulp(out_ref).to(tol.device)
+
+
+@pytest.mark.parametrize("S", [4096, 16384])
+@pytest.mark.parametrize("causal", [False, True])
+def test_sdpa_vs_reference_pipeline_config3(S, causal):
+    """Config 3 (B=1, H=16, D=128, Q/K x 2^8 so raw logits overflow fp16, V x 2^h per head) at full size:
+    every output element against the reference's own pipeline run on the same GPU."""
+    from tbf16 import attention
+    small = _ref("tbf16_ref_small")
+    q, k, v = inputs.attention_qkv(1, 16, S, 128, seed=S + int(causal), device="cuda")
+    out = attention.sdpa(q, k, v, is_causal=causal)
+    out_ref, q16, k16, v16, ev_q = _reference_sdpa(small, q, k, v, causal)
+    q16m, k16m, v16m, _, _ = attention.prepare_qkv(q, k, v, v_exp=13)
+    assert bits_equal(q16m, q16) and bits_equal(k16m, k16) and bits_equal(v16m, v16)
+    tol = _attention_tolerance(q16, k16, v16, ev_q, out_ref, causal)
+    d = (out.double() - out_ref.double()).abs()
+    dist = ulp_distance(out, out_ref)
+    report(f"sdpa vs reference pipeline S={S} causal={causal}", bit_equal=float((dist == 0).double().mean()),
+           within_1ulp=float((dist <= 1).double().mean()), max_ulp=int(dist.max()),
+           worst_over_tol=float((d / tol).max()))
+    assert torch.isfinite(out.float()).all()
+    assert (d <= tol).all(), f"{int((d > tol).sum())} elements outside tolerance"
+    assert float((dist <= 1).double().mean()) > 0.99
