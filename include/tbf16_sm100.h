@@ -49,6 +49,11 @@ int tbf16_device_check(int device);
  * 2 = attention backward produced a non-finite value, 4 = a kernel found its dynamic shared memory
  * window not 1024-byte aligned and did nothing). Synchronises the device; reset != 0 clears. */
 int tbf16_device_status(unsigned int* bits, int reset);
+/* Failure-path self-test (no counterpart in the reference): one warp waits on an mbarrier that nothing
+ * arrives on, through the bounded-wait helper the pipelined kernels use, with the limit timeout_ns
+ * (1 ns .. 1 s) instead of their 2 s. The wait gives up, sets bit 1 of the device status word and the
+ * kernel returns, leaving the context usable; read and clear the bit with tbf16_device_status. */
+int tbf16_selftest_bounded_wait(uint64_t timeout_ns, void* stream);
 
 /* ------------------------------------------------------------------ row / column power-of-two scales */
 

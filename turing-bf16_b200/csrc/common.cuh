@@ -144,9 +144,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Warp-wide bounded wait: lane 0 polls (so 32 lanes do not hammer the barrier word), then every lane
 // takes its own acquire of the completed phase. Safe when the barrier cannot complete its next phase
 // before this warp has consumed the current one (true for every ring below).
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned int* err) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned int* err,
+                                               uint64_t timeout_ns = 2000000000ull) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err);
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err, timeout_ns);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   if (ok) (void)mbar_try_wait(bar, parity);
   return ok;

@@ -147,6 +147,26 @@ int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d
 
 }  // namespace tbf16_host
 
+namespace {
+using namespace tbf16;
+
+// One warp waits, through the same bounded-wait helper every pipelined kernel uses, on an mbarrier that
+// nothing arrives on. The wait gives up after timeout_ns, records kErrWaitTimeout in the device error
+// word and the kernel returns: the failure path of a stalled pipeline, exercised without stalling one.
+__global__ void bounded_wait_selftest_kernel(unsigned int* err, uint64_t timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  mbar_wait_warp(&bar, 0, &abort, err, timeout_ns);
+}
+
+}  // namespace
+
 extern "C" {
 
 int tbf16_abi_version(void) { return 100; }
@@ -172,6 +192,14 @@ int tbf16_device_check(int device) {
   int st = tbf16_host::require_sm100();
   cudaSetDevice(prev);
   return st;
+}
+
+int tbf16_selftest_bounded_wait(uint64_t timeout_ns, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (timeout_ns == 0 || timeout_ns > 1000000000ull) return TBF16_ERR_INVALID;
+  const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+  bounded_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(d->err, timeout_ns);
+  return tbf16_host::check_launch();
 }
 
 int tbf16_device_status(unsigned int* bits, int reset) {

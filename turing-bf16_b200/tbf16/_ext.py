@@ -59,6 +59,7 @@ SIGNATURES = {
                        ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
     "tbf16_device_check": [_i32],
     "tbf16_device_status": [_vp, _i32],
+    "tbf16_selftest_bounded_wait": [ctypes.c_uint64, _vp],
 }
 
 # entry points returning a size (int64) rather than a status
