@@ -1,17 +1,19 @@
-"""Training: backward passes on fp16 tensor cores, B200 kernels.
+"""Differentiable scaled ops for training on the B200 kernels.
 
-Same public surface as the reference's tbf16/autograd.py (quantize_cols, ScaledLinearFn,
-FP32LinearFn, linear, ScaledSDPAFn, sdpa, CHECK_OVERFLOW).
+Public names as in the reference's tbf16/autograd.py: quantize_cols, ScaledLinearFn, FP32LinearFn,
+linear, ScaledSDPAFn, sdpa, CHECK_OVERFLOW.
 
-Linear: dX = dY @ W and dW = dY^T @ X are fp16 GEMMs too. The contraction dimension changes, so
-dY, W and X are scaled per column (exact powers of two, the reference's exponent conventions) where
-the forward scaled per row. All three GEMMs are this build's tcgen05 kernel, which reads MN-major
-operands directly (no transposed copies) and writes bf16 from the fp32 accumulator.
+Linear backward: dX = dY W contracts over N and dW = dY^T X over M, so the operands whose contraction
+axis changed are given power-of-two scales per column instead of per row (the reference's exponent
+conventions for each operand, autograd.py:71-90 there). The three products run on the tcgen05 GEMM,
+which reads the column-scaled operands MN-major from their row-major storage and writes bf16 from
+its fp32 accumulator.
 
-Attention: the tcgen05 flash-attention forward and backward, with dO multiplied by a power of two
-2^G picked per call so the internal dS stays in fp16's normal range. If the kernel reports a
-non-finite value the backward is redone with a smaller G (the reference's retry, autograd.py:177-189);
-with gradients written from fp32 accumulators this practically never triggers.
+Attention: the tcgen05 flash-attention forward and backward. The backward multiplies dO by 2^G, G
+chosen per call from the head exponents so that dS stays inside fp16's normal range; a kernel that
+still meets a non-finite value raises a device flag and the call is repeated with G lowered by 8, at
+most six times (the reference's retry, autograd.py:177-189). Gradients leave the kernel from fp32
+accumulators, so the retry is a safety net rather than a regular path.
 """
 import math
 import os
@@ -22,8 +24,8 @@ import torch.nn.functional as F
 from . import attention, ops
 from ._ext import call, lib, ptr, require_cuda, stream_ptr
 
-# Check attention gradients for fp16 overflow and redo them at a smaller scale if needed.
-# Costs one host sync per attention backward; TBF16_ATTN_CHECK=0 turns it off.
+# Whether the attention backward reads the kernel's non-finite flag (one host synchronisation per call) and
+# retries at a smaller dO scale; TBF16_ATTN_CHECK=0 skips the read and the retry.
 CHECK_OVERFLOW = os.environ.get("TBF16_ATTN_CHECK", "1") != "0"
 
 
@@ -45,16 +47,6 @@ def quantize_cols(x: torch.Tensor, target_exp: int = 0, row_mul=None):
     return y, s_inv
 
 
-_ONES = {}
-
-
-def _ones(n, device):
-    key = (n, device)
-    if key not in _ONES:
-        _ONES[key] = torch.ones(n, device=device)
-    return _ONES[key]
-
-
 @torch.autocast("cuda", enabled=False)
 def _scaled_mm(a16, sa, b16, sb, a_mn=False, b_mn=False):
     """(A @ B^T) * sa[:, None] * sb[None, :] as bf16, with A = a16 (M, K) or a16 (K, M) if a_mn, and
@@ -70,17 +62,18 @@ def _aligned(*ts):
 
 
 class ScaledLinearFn(torch.autograd.Function):
+    """y = x W^T + b for bf16 x and W. What the backward needs is kept in the forward's own form: x's
+    fp16 rows and inverse row scales (as many bytes as x; dW folds the scales into dY's columns) and W,
+    which the backward scales by columns."""
+
     @staticmethod
     @torch.autocast("cuda", enabled=False)
     def forward(ctx, x, w, bias):
-        N, K = w.shape
-        x16, sx = ops.quantize_rows_shared(x)  # Q/K/V (and gate/up) share one fp16 copy of x
-        w16, sw = ops.prepare_weight(w)
-        # Saved instead of x (same size). dW reuses it with the row scales folded into dY.
-        ctx.save_for_backward(x16, sx, w)
-        ctx.has_bias = bias is not None
-        ctx.x_shape = x.shape
-        return ops.linear_q(x16, sx, w16, sw, bias).reshape(*x.shape[:-1], N)
+        rows16, rows_sinv = ops.quantize_rows_shared(x)  # one fp16 copy for sibling layers reading x
+        y = ops.linear_q(rows16, rows_sinv, *ops.prepare_weight(w), bias)
+        ctx.save_for_backward(rows16, rows_sinv, w)
+        ctx.x_shape, ctx.has_bias = x.shape, bias is not None
+        return y.reshape(*x.shape[:-1], w.shape[0])
 
     @staticmethod
     @torch.autocast("cuda", enabled=False)
@@ -116,7 +109,7 @@ def _linear_backward(dy, x16, sx, w, want_dx, want_dw, want_db, x_shape):
         if pad:
             dw = _padded_mm(dy16c, sdyc, x16, None, M, N, K, kind="dw")
         else:
-            dw = _scaled_mm(dy16c, sdyc, x16, _ones(K, x16.device), a_mn=True, b_mn=True)
+            dw = _scaled_mm(dy16c, sdyc, x16, None, a_mn=True, b_mn=True)
     if want_db:
         db = dy2.float().sum(0).to(dy.dtype)
     return dx, dw, db
@@ -189,30 +182,32 @@ def _padded_mm(a16, sa, b16, sb, M, N, K, kind):
 
 
 class FP32LinearFn(torch.autograd.Function):
-    """bf16 in/out, fp32 math. Saves the bf16 input (shared with sibling layers), not an fp32 copy
-    (reference autograd.py:93-112; used for skinny layers such as LoRA adapters)."""
+    """Layers with a dimension below convert.MIN_DIM (LoRA adapters and the like; the reference's
+    autograd.py:93-112 role): fp32 GEMMs over the bf16 tensors with bf16 results. The saved x is the
+    caller's bf16 tensor itself, so adapters that read the same input share it."""
 
     @staticmethod
     @torch.autocast("cuda", enabled=False)
     def forward(ctx, x, w, bias):
         ctx.save_for_backward(x, w)
-        ctx.has_bias = bias is not None
-        return F.linear(x.float(), w.float(), None if bias is None else bias.float()).to(x.dtype)
+        ctx.with_bias = bias is not None
+        y = torch.matmul(x.float(), w.float().t())
+        return (y if bias is None else y + bias.float()).to(x.dtype)
 
     @staticmethod
     @torch.autocast("cuda", enabled=False)
     def backward(ctx, dy):
         x, w = ctx.saved_tensors
-        dyf = dy.float()
-        dx = (dyf @ w.float()).to(x.dtype) if ctx.needs_input_grad[0] else None
-        dw = (dyf.reshape(-1, dy.shape[-1]).t() @ x.reshape(-1, x.shape[-1]).float()).to(w.dtype) \
-            if ctx.needs_input_grad[1] else None
-        db = dyf.reshape(-1, dy.shape[-1]).sum(0).to(dy.dtype) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        need_x, need_w, need_b = ctx.needs_input_grad
+        g = dy.float().reshape(-1, w.shape[0])
+        dx = (g @ w.float()).reshape(x.shape).to(x.dtype) if need_x else None
+        dw = (g.t() @ x.reshape(-1, w.shape[1]).float()).to(w.dtype) if need_w else None
+        db = g.sum(0).to(dy.dtype) if need_b and ctx.with_bias else None
         return dx, dw, db
 
 
 def linear(x, w, bias=None):
-    """Differentiable F.linear for bf16 x and w on fp16 tensor cores."""
+    """F.linear(x, w, bias) with gradients, for bf16 x and w, on the scaled kernels (ScaledLinearFn)."""
     return ScaledLinearFn.apply(x, w, bias)
 
 

@@ -130,73 +130,87 @@ def scaled_conv(x, weight16, weight_scale, bias, stride, padding, dilation, grou
     return y
 
 
-def _scaled_conv_forward(self, x, weight, bias):
-    # `weight` is the (removed) bf16 parameter, i.e. None; the fp16 copy lives in weight16.
-    if x.dtype != torch.bfloat16 or (torch.is_grad_enabled() and x.requires_grad):
-        bias = None if bias is None else bias.to(x.dtype)
-        return self._native_conv_forward(x, self.dequantized_weight().to(x.dtype), bias)
-    O = self.out_channels
-    if self._tbf16_pointwise:
-        return scaled_linear(x.movedim(1, -1), self.weight16.view(O, -1), self.weight_scale, bias).movedim(-1, 1)
-    if self.padding_mode != "zeros":
-        x = F.pad(x, self._reversed_padding_repeated_twice, mode=self.padding_mode)
-        padding = 0
-    else:
-        padding = self.padding
-    if isinstance(padding, str):
-        if padding == "valid":
-            padding = 0
-        else:  # "same" (stride 1): an odd total pads its extra element at the end, as torch does
-            tot = [d * (k - 1) for d, k in zip(self.dilation, self.kernel_size)]
-            if any(t % 2 for t in tot):
-                x = F.pad(x, [p for t in reversed(tot) for p in (0, t % 2)])
-            padding = tuple(t // 2 for t in tot)
-    return scaled_conv(x, self.weight16, self.weight_scale, bias, self.stride, padding, self.dilation, self.groups,
-                       self._tbf16_target_exp, getattr(self, "_tbf16_wk16", None), getattr(self, "_tbf16_wcl16", None))
+def _zero_padding(conv, x):
+    """(x, padding) with the convolution's padding expressed as zeros around x for scaled_conv: non-zero
+    padding modes are applied to x here; "valid" is 0; "same" (stride 1) splits the total padding as
+    torch does, an odd total putting its extra element at the end."""
+    if conv.padding_mode != "zeros":
+        return F.pad(x, conv._reversed_padding_repeated_twice, mode=conv.padding_mode), 0
+    if not isinstance(conv.padding, str):
+        return x, conv.padding
+    if conv.padding == "valid":
+        return x, 0
+    total = [d * (k - 1) for d, k in zip(conv.dilation, conv.kernel_size)]
+    if any(t % 2 for t in total):
+        x = F.pad(x, [p for t in reversed(total) for p in (0, t % 2)])
+    return x, tuple(t // 2 for t in total)
 
 
-def _dequantized_weight(self):
-    w = self.weight16.float() * self.weight_scale.view((-1,) + (1,) * (self.weight16.dim() - 1))
-    return w.bfloat16()
+class _ScaledConv:
+    """Mixed in ahead of a bf16 convolution's own class by convert_conv, so that class's forward (and any
+    subclass logic around it) still runs and only the innermost `_conv_forward` changes: bf16 inputs
+    outside autograd take scaled_conv on the fp16 weight rows; anything else the class's own convolution
+    on the rebuilt bf16 weight."""
+
+    def dequantized_weight(self):
+        """The bf16 weight rebuilt from `weight16` and `weight_scale` (exact)."""
+        scale = self.weight_scale.view((-1,) + (1,) * (self.weight16.dim() - 1))
+        return (self.weight16.float() * scale).bfloat16()
+
+    def _conv_forward(self, x, weight, bias):
+        # `weight` is the removed bf16 parameter (None): the layer's weight lives in weight16 / weight_scale
+        if x.dtype != torch.bfloat16 or (torch.is_grad_enabled() and x.requires_grad):
+            b = None if bias is None else bias.to(x.dtype)
+            return super()._conv_forward(x, self.dequantized_weight().to(x.dtype), b)
+        if self._tbf16_pointwise:  # a per-pixel linear layer
+            rows = self.weight16.view(self.out_channels, -1)
+            return scaled_linear(x.movedim(1, -1), rows, self.weight_scale, bias).movedim(-1, 1)
+        x, padding = _zero_padding(self, x)
+        return scaled_conv(x, self.weight16, self.weight_scale, bias, self.stride, padding, self.dilation,
+                           self.groups, self._tbf16_target_exp, getattr(self, "_tbf16_wk16", None),
+                           getattr(self, "_tbf16_wcl16", None))
 
 
-_classes = {}
+_SCALED_CLASSES = {}
 
 
-def _scaled_class(cls):
-    if cls not in _classes:
-        _classes[cls] = type(f"TBF16{cls.__name__}", (cls,), {
-            "_native_conv_forward": cls._conv_forward,
-            "_conv_forward": _scaled_conv_forward,
-            "dequantized_weight": _dequantized_weight,
-        })
-    return _classes[cls]
+def _scaled_class_for(cls):
+    """The class a converted `cls` instance takes: _ScaledConv ahead of cls, made once per class."""
+    if cls not in _SCALED_CLASSES:
+        _SCALED_CLASSES[cls] = type(f"TBF16{cls.__name__}", (_ScaledConv, cls), {})
+    return _SCALED_CLASSES[cls]
 
 
 def convertible(m: nn.Module) -> bool:
-    return (isinstance(m, (nn.Conv1d, nn.Conv2d, nn.Conv3d)) and type(m) not in _classes.values()
+    """A Conv1d/2d/3d (or subclass) with a bf16 CUDA weight that has not been converted yet."""
+    return (isinstance(m, (nn.Conv1d, nn.Conv2d, nn.Conv3d)) and not isinstance(m, _ScaledConv)
             and isinstance(m.weight, torch.Tensor) and m.weight.dtype == torch.bfloat16 and m.weight.is_cuda)
 
 
+def _is_pointwise(conv) -> bool:
+    unpadded = conv.padding == "valid" or (not isinstance(conv.padding, str) and not any(conv.padding))
+    return (conv.groups == 1 and unpadded and all(k == 1 for k in conv.kernel_size)
+            and all(s == 1 for s in conv.stride))
+
+
 def convert_conv(conv: nn.Module):
-    """Convert one bf16 nn.Conv{1,2,3}d (or subclass) in place. Subclass forwards keep working: only
-    _conv_forward is replaced. `.weight` becomes None; use .dequantized_weight()."""
+    """Convert one bf16 convolution in place (reference conv.py:86-103 behaviour): the bf16 weight
+    parameter is replaced by `weight16` (fp16, the weight's shape) and `weight_scale` (fp32 [O], inverse
+    power-of-two scales of the output channels' rows), plus the GEMM's row layouts of the weight, and the
+    instance is re-classed (_scaled_class_for). `.weight` becomes None; `.dequantized_weight()` rebuilds it."""
     w = conv.weight.data
-    O = w.shape[0]
-    K = w[0].numel()
-    t = _target_exp(K)
-    w16, ws = prepare_weight(w.reshape(O, K))  # [O, K rounded up to 8]
+    O, K = w.shape[0], w[0].numel()
+    rows16, w_sinv = prepare_weight(w.reshape(O, K))  # [O, K rounded up to a multiple of 8]
     del conv._parameters["weight"]
     conv.register_parameter("weight", None)
-    conv.register_buffer("weight16", w16[:, :K].contiguous().view_as(w))
-    conv.register_buffer("weight_scale", ws)
-    if conv.groups == 1 and w.shape[1] % 8 == 0:  # the GEMM's rows for the channels-last im2col
-        conv.register_buffer("_tbf16_wcl16", _taps_last(conv.weight16), persistent=False)
-    elif conv.groups == 1:  # the GEMM's [O, K] rows, zero-padded to a multiple of 8 (shared when K is one)
-        conv.register_buffer("_tbf16_wk16", conv.weight16.view(O, K) if K % 8 == 0 else w16, persistent=False)
-    conv._tbf16_target_exp = t
-    no_pad = conv.padding == "valid" or not isinstance(conv.padding, str) and all(p == 0 for p in conv.padding)
-    conv._tbf16_pointwise = (all(k == 1 for k in conv.kernel_size) and all(s == 1 for s in conv.stride) and no_pad
-                             and conv.groups == 1)
-    conv.__class__ = _scaled_class(type(conv))
+    conv.register_buffer("weight16", rows16[:, :K].contiguous().view_as(w))
+    conv.register_buffer("weight_scale", w_sinv)
+    if conv.groups == 1:
+        if w.shape[1] % 8 == 0:  # rows in (taps, channels) order for the channels-last im2col / implicit GEMM
+            conv.register_buffer("_tbf16_wcl16", _taps_last(conv.weight16), persistent=False)
+        else:  # [O, K] rows padded to a multiple of 8 (a view of weight16 when K already is one)
+            conv.register_buffer("_tbf16_wk16", conv.weight16.view(O, K) if K % 8 == 0 else rows16, persistent=False)
+    conv._tbf16_target_exp = _target_exp(K)
+    conv._tbf16_pointwise = _is_pointwise(conv)
+    conv.__class__ = _scaled_class_for(type(conv))
     return conv
