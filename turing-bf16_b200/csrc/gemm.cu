@@ -210,6 +210,9 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
+    // sa may be written by the grid this one was launched early behind: wait for it here too rather
+    // than rely on the producer's wait being ordered before these loads (a no-op for plain launches).
+    pdl_wait();
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -257,6 +260,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, CONVERT>::THREADS, 1)
   } else if (CONVERT) {
     // ------------------------------------------------------------ converters: bf16 -> fp16(x * s) in place
     const int row = (warp - 2 - kEpiWarps) * 32 + lane;  // 0..127, one row of the A tile per thread
+    pdl_wait();  // sa comes from the row pass (a no-op for plain launches)
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -543,6 +547,7 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
     // (64-byte swizzle, conflict-free 16-byte writes) and one lane stores the tile with TMA; the buffer
     // is rewritten only after the store issued from it two chunks earlier has read it.
     uint8_t* ebuf = smem + S * C::STAGE_BYTES + (warp - 2) * 2 * 2048;
+    pdl_wait();  // sa (and the conv's sample scales) come from the pass this GEMM may launch behind
     int eb = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
