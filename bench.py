@@ -346,6 +346,8 @@ def main():
         line["prefill"] = prefill_run(world)  # every rank runs its own sequence (replicas)
     if not args.no_conv:
         line["conv"] = conv_run(pk)
+    if world > 1:
+        line["collectives"] = collectives_run(pk, world, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
@@ -757,6 +759,82 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
     t = s0.elapsed_time(s1) / iters
     res["train_fwd_bwd_causal"] = {"config": f"B={B2} H={H} S={S2} D={D}, dY x2^-20", "ms": round(t, 3),
                                    "tflops": round(flop / (t / 1e3) / 1e12, 1)}
+    return res
+
+
+def collectives_run(pk, world, rank, iters=5):
+    """The partitions that exchange data, timed on N ranks (max over ranks, CUDA events):
+      column_parallel  config 2's 8192^3 linear with W's rows split over the ranks (each computes
+                       y[:, its N / world columns]) and y reassembled by NCCL all_gather_into_tensor
+                       (shard.linear_column_parallel); 2 M N K flop per step for the whole job
+      attention_heads  config 3 (H = 16, S = 16k, D = 128) with the heads split over the ranks and eq, ek
+                       made global by one all_reduce(MAX) (shard.sdpa_heads); 4 H S^2 D flop (half causal)
+      train_attention_heads  config 4's attention (B = 2, H = 16, S = 4096, causal) forward + backward on
+                       split heads, with the backward's dO exponent exchange (shard.sdpa_heads_train)
+    Each entry gives the collective's own time and share of the step (events around it inside the step)."""
+    import torch.distributed as dist
+    import inputs
+    from tbf16 import ops, shard
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = {}
+
+    def timed(step, iters=iters):
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / iters, world)
+
+    # column-parallel linear
+    M = N = K = 8192
+    x = inputs.gemm_x(M, K, seed=100, device=dev)
+    w16, ws = ops.prepare_weight(inputs.gemm_w(N, K, seed=1, device=dev))
+    w_sh, ws_sh, _ = shard.shard_weight(w16, ws, None, rank, world)
+    del w16, ws
+    y_local = ops.scaled_linear(x, w_sh, ws_sh)
+    gathered = torch.empty((world, *y_local.shape), device=dev, dtype=y_local.dtype)
+    ms = timed(lambda: shard.linear_column_parallel(x, w_sh, ws_sh))
+    ms_gather = timed(lambda: dist.all_gather_into_tensor(gathered, y_local))
+    res["column_parallel"] = {"config": f"M={M} N={N} K={K}, W rows split {world} ways, NCCL all_gather of y",
+                              "ms": round(ms, 4), "tflops": round(2.0 * M * N * K / (ms / 1e3) / 1e12, 1),
+                              "all_gather_ms": round(ms_gather, 4), "all_gather_share": round(ms_gather / ms, 3),
+                              "gathered_bytes": 2 * M * N}
+    del x, w_sh, ws_sh, y_local, gathered
+    torch.cuda.empty_cache()
+    # head-sharded inference attention (config 3)
+    H, S, D = 16, 16384, 128
+    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device=dev)
+    h0, h1 = shard.shard_range(H, rank, world)
+    qs, ks, vs = (t[:, h0:h1].contiguous() for t in (q, k, v))
+    del q, k, v
+    e = torch.zeros(2, device=dev, dtype=torch.int32)
+    ms_ar = timed(lambda: dist.all_reduce(e, op=dist.ReduceOp.MAX))
+    att = {"config": f"B=1 H={H} S={S} D={D}, heads split {world} ways, all_reduce(MAX) of eq, ek",
+           "all_reduce_ms": round(ms_ar, 4)}
+    for causal in (False, True):
+        ms = timed(lambda: shard.sdpa_heads(qs, ks, vs, is_causal=causal))
+        flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)
+        att["causal" if causal else "noncausal"] = {"ms": round(ms, 3), "tflops": round(flop / (ms / 1e3) / 1e12, 1),
+                                                    "all_reduce_share": round(ms_ar / ms, 4)}
+    res["attention_heads"] = att
+    del qs, ks, vs
+    # head-sharded training attention (config 4's attention)
+    B2, S2 = 2, 4096
+    q, k, v = inputs.attention_qkv(B2, H, S2, D, seed=4, device=dev, qk_exp=0)
+    qs, ks, vs = (t[:, h0:h1].contiguous().requires_grad_() for t in (q, k, v))
+    do = (torch.randn(B2, h1 - h0, S2, D, device=dev) * 2.0 ** -20).bfloat16()
+    ms = timed(lambda: shard.sdpa_heads_train(qs, ks, vs, is_causal=True).backward(do))
+    flop = 3.5 * 4.0 * B2 * H * S2 * S2 * D * 0.5
+    res["train_attention_heads"] = {"config": f"B={B2} H={H} S={S2} D={D} causal, heads split {world} ways, "
+                                              "all_reduce(MAX) of eq, ek and of the dO exponent",
+                                    "ms": round(ms, 3), "tflops": round(flop / (ms / 1e3) / 1e12, 1),
+                                    "collectives_ms": round(2 * ms_ar, 4), "collectives_share": round(2 * ms_ar / ms, 4)}
     return res
 
 

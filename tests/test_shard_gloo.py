@@ -1,7 +1,8 @@
 """Host logic of the multi-GPU partitions, on CPU with 2 gloo ranks: the column-parallel all-gather
-reassembles exactly the unsharded linear, and the head-sharded exponent exchange gives every rank the
-unsharded call's (a, ev, fp16 operands). The compute ops are the CPU oracle's (the GPU kernels are
-covered by the -m gpu tests); only the exchange and partition logic is under test here."""
+reassembles exactly the unsharded linear, the head-sharded exponent exchange gives every rank the
+unsharded call's (a, ev, fp16 operands), and the backward's dO exponent exchange gives the unsharded
+G. The compute ops are the CPU oracle's (the GPU kernels are covered by the -m gpu tests); only the
+exchange and partition logic is under test here."""
 import os
 import socket
 
@@ -64,7 +65,20 @@ def _worker(rank, world, port, results):
                   and torch.equal(v16.view(torch.int16), rv[:, h0:h1].view(torch.int16)))
         # without the exchange, rank 0 alone would pick a different a
         local_a = orc.prepare_qkv(q[:, h0:h1], k[:, h0:h1], v[:, h0:h1], 13)[3]
-        results[rank] = (col_ok, rows_ok, att_ok, int(local_a) != int(ra) or rank == 1)
+
+        # training backward: the dO exponent G of the sharded call equals the unsharded call's
+        # (reference autograd.py:173-178); rank 1's heads carry the larger dO, so rank 0 needs the exchange
+        do = torch.randn(1, 4, 64, 64, generator=torch.Generator().manual_seed(12)).bfloat16()
+        do[:, 2:] *= 2.0 ** 9
+        _, _, _, _, ev_t = orc.prepare_qkv(q, k, v, 0)
+        e_local, e_global = shard.global_dout_exponent(do[:, h0:h1], ev_t[:, h0:h1], head_exp=orc.head_exp)
+        t_do = 12 - 6  # 12 - ceil(log2 64)
+        G_full = orc.sdpa_bwd(q, k, v, do)["G"]
+        offset = int(e_global) - int(e_local)
+        # the kernel derives G from its own heads with the lowered target: (t_do - offset) - e_local
+        g_ok = (t_do - int(e_global) == G_full) and ((t_do - offset) - int(e_local) == G_full)
+        g_mattered = offset > 0 if rank == 0 else offset == 0
+        results[rank] = (col_ok, rows_ok, att_ok, int(local_a) != int(ra) or rank == 1, g_ok, g_mattered)
     finally:
         dist.destroy_process_group()
 
@@ -77,11 +91,13 @@ def test_shard_exchange_gloo_world2():
     mp.start_processes(_worker, args=(world, port, results), nprocs=world, start_method="spawn", join=True)
     assert len(results) == world
     for rank in range(world):
-        col_ok, rows_ok, att_ok, exchange_mattered = results[rank]
+        col_ok, rows_ok, att_ok, exchange_mattered, g_ok, g_mattered = results[rank]
         assert col_ok, f"column-parallel gather differs on rank {rank}"
         assert rows_ok, f"row-sharded linear differs on rank {rank}"
         assert att_ok, f"head-sharded exponents differ on rank {rank}"
         assert exchange_mattered
+        assert g_ok, f"head-sharded backward exponent G differs on rank {rank}"
+        assert g_mattered
 
 
 def test_shard_range_partitions():

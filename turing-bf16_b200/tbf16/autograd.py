@@ -211,9 +211,11 @@ def linear(x, w, bias=None):
     return ScaledLinearFn.apply(x, w, bias)
 
 
-def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale, d_orig):
+def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale, d_orig, t_do_offset=0):
     """Runs tbf16_attn_bwd with the reference's retry loop: t_do = 12 - ceil(log2 d), lowered by 8 and
-    redone while the kernel reports a non-finite value (at most 6 attempts)."""
+    redone while the kernel reports a non-finite value (at most 6 attempts). t_do_offset (>= 0) lowers
+    the target further: a head-sharded call passes how far the global dO exponent exceeds its own heads'
+    maximum, so G comes out as the unsharded call's."""
     B, Hq, Sq, Dk = q16.shape
     Hkv, Sk = k16.shape[1], k16.shape[2]
     dev = q16.device
@@ -229,7 +231,7 @@ def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale
     nbytes = lib().tbf16_attn_bwd_workspace_size(B, Hq, Hkv, Sq, Sk, Dk)
     ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
     ms = mask16.stride()[:3] if mask16 is not None else (0, 0, 0)
-    t_do = 12 - math.ceil(math.log2(d_orig))
+    t_do = 12 - math.ceil(math.log2(d_orig)) - int(t_do_offset)
     for _attempt in range(6):
         flag.zero_()
         call("tbf16_attn_bwd", ptr(q16), ptr(k16), ptr(v16), ptr(o16), ptr(lse), lse.shape[-1], ptr(dout),

@@ -10,12 +10,17 @@ The path shards without changing any result:
     the exponents that place q and k, as maxima over ALL (b, h) (attention.py:41), so the sharded call
     makes them global with one all_reduce(MAX) of two int32 and then scales exactly as the unsharded
     call would (prepare_qkv_sharded, sdpa_heads).
+  - training attention over heads: the backward's dO exponent e = max_{b,h}(head_exp(dO) + ev_q) is
+    also a global maximum (autograd.py:175), exchanged with one more all_reduce(MAX) of one int32
+    before the backward kernel runs (global_dout_exponent, sdpa_heads_train).
 The compute ops are parameters so the exchange logic can be checked on CPU with gloo.
 """
+import math
+
 import torch
 import torch.distributed as dist
 
-from . import attention
+from . import attention, autograd
 from .ops import scaled_linear
 
 
@@ -81,3 +86,60 @@ def sdpa_heads(q, k, v, attn_mask=None, is_causal=False, scale=None, enable_gqa=
     q16, k16, v16, _, ev = prepare_qkv_sharded(q, k, v, v_exp=13, group=group)
     out, _ = attention.attn_forward(q16, k16, v16, ev, attn_mask, is_causal, scale, d_orig=D0)
     return out[..., :D0] if out.shape[-1] != D0 else out
+
+
+def global_dout_exponent(dout, ev, group=None, head_exp=attention.head_exp):
+    """(e_local, e_global) as int32 tensors: max over this rank's (b, h) and over every rank's of
+    head_exp(dout) + ev_q, the exponent that fixes the backward's dO scale 2^G, G = t_do - e
+    (reference autograd.py:173-178). ev: this rank's per-(b, h_kv) V exponents."""
+    ev_q = attention.expand_heads(ev, dout.shape[1])
+    e_local = (head_exp(dout) + ev_q).amax().to(torch.int32).reshape(1)
+    e_global = e_local.clone()
+    dist.all_reduce(e_global, op=dist.ReduceOp.MAX, group=group)
+    return e_local[0], e_global[0]
+
+
+class _ShardedSDPAFn(torch.autograd.Function):
+    """Training attention on this rank's heads with the unsharded call's scales: the forward's a from the
+    global eq, ek (prepare_qkv_sharded); the backward's G from the global dO exponent. The backward kernel
+    derives G from its own heads' maximum, so its target t_do is lowered by (e_global - e_local), read on
+    the host: one synchronisation per call, as the overflow check already costs."""
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def forward(ctx, q, k, v, attn_mask, is_causal, scale, group):
+        D0 = q.shape[-1]
+        if D0 > 128:
+            raise NotImplementedError("tbf16 sharded training attention: head dims up to 128")
+        q16, k16, v16, a, ev = prepare_qkv_sharded(q, k, v, v_exp=0, group=group)
+        Dk = 64 if D0 <= 64 else 128
+        if Dk != D0:
+            q16, k16, v16 = (torch.nn.functional.pad(t, (0, Dk - D0)) for t in (q16, k16, v16))
+        sc = 1.0 / math.sqrt(D0) if scale is None else float(scale)
+        B, Hq, Sq, _ = q16.shape
+        mask16 = attention.additive_mask(attn_mask, B, Hq, Sq, k.shape[2], q.device)
+        out, lse, o16 = attention.attn_forward(q16, k16, v16, ev, mask16, is_causal, sc, need_lse=True, need_o16=True)
+        ctx.save_for_backward(q16, k16, v16, o16, lse, a, ev, mask16)
+        ctx.args = (is_causal, sc, D0, group)
+        return out[..., :D0].contiguous() if Dk != D0 else out
+
+    @staticmethod
+    @torch.autocast("cuda", enabled=False)
+    def backward(ctx, dout):
+        q16, k16, v16, o16, lse, a, ev, mask16 = ctx.saved_tensors
+        is_causal, sc, D0, group = ctx.args
+        if D0 % 8:
+            dout = torch.nn.functional.pad(dout, (0, 8 - D0 % 8))
+        e_local, e_global = global_dout_exponent(dout, ev, group)
+        offset = int(e_global) - int(e_local)
+        dq, dk, dv, _ = autograd.attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, sc, D0,
+                                               t_do_offset=offset)
+        if q16.shape[-1] != D0:
+            dq, dk, dv = (t[..., :D0].contiguous() for t in (dq, dk, dv))
+        return dq, dk, dv, None, None, None, None
+
+
+def sdpa_heads_train(q, k, v, attn_mask=None, is_causal=False, scale=None, group=None):
+    """Differentiable scaled attention on this rank's heads (q, k, v sliced by head, GQA groups whole on
+    one rank): forward and gradients equal the matching heads of tbf16.autograd.sdpa on the full tensors."""
+    return _ShardedSDPAFn.apply(q, k, v, attn_mask, is_causal, scale, group)
