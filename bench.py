@@ -36,8 +36,8 @@ M_DEFAULT = N_DEFAULT = K_DEFAULT = 8192
 METRIC = "scaled GEMM TFLOPS (M=N=K=8192, config 2) & % of dense fp16 tensor peak"
 
 
-# DRAM bytes (read + write) of one scaled_gemm_pair_kernel launch at M = N = K = 8192, from the ncu
-# capture summarised in profiles/scaled_gemm_pair_8192_cube.md (1.070 GB read + 0.127 GB written).
+# DRAM bytes (read + write) of one scaled_gemm_pair_kernel launch at M = N = K = 8192: dram__bytes_read.sum
+# + dram__bytes_write.sum of one launch captured with ncu (1.070 GB read + 0.127 GB written).
 PAIR_8192_TRAFFIC = 1.197e9
 
 
@@ -144,6 +144,45 @@ def cpu_linear_sample(x, w16, ws, rows):
     return ((c.float() * sx[:, None]) * ws[None, :]).bfloat16()
 
 
+def host_info():
+    """The host the CPU legs ran on: logical CPUs, torch's intra-op threads and the CPU model."""
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "cpu_model": model}
+
+
+def cpu_attention_sample(H=16, S=16384, D=128, rows=1024, causal=False, steps=2):
+    """The reference's inference attention (tbf16/attention.py:38-65) on the host cores: exponents and fp16
+    copies by the oracle's C restatement of its head_amax / head_scale_cast, torch's CPU fp16
+    scaled_dot_product_attention (what the reference calls with ops._USE_CUDA = False), the output scaled
+    back to bf16. Sample: the first `rows` query rows of every head against all S keys (config 3's
+    distribution). Returns (TFLOPS, sample text)."""
+    import inputs
+    from oracle import oracle as orc
+    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0)
+    q = q[:, :, :rows].contiguous()
+
+    def run():
+        q16, k16, v16, _, ev = orc.prepare_qkv(q, k, v, 13)
+        out16 = torch.nn.functional.scaled_dot_product_attention(q16, k16, v16, is_causal=causal)
+        return orc.head_scale(out16, orc.expand_heads(ev, H), torch.bfloat16)
+
+    run()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run()
+    dt = (time.perf_counter() - t0) / steps
+    flop = 4.0 * H * rows * S * D
+    return flop / dt / 1e12, (f"{rows} query rows x {S} keys x {H} heads (D={D}) per step, {steps} steps "
+                              f"({dt * steps:.1f} s), torch CPU fp16 SDPA")
+
+
 def run_cpu_reference(M, N, K, steps, warmup, rows=256):
     """Time the CPU implementation on `rows`-row samples of the workload; returns (TFLOPS, sample text)."""
     import inputs
@@ -176,6 +215,7 @@ def main():
     ap.add_argument("--K", type=int, default=K_DEFAULT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the 2-second back-to-back GEMM leg")
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-5 Gemma-shaped prefill")
     ap.add_argument("--only-attention", action="store_true",
@@ -236,7 +276,7 @@ def main():
                 "vs_baseline": None, "dtype": "fp16 operands, fp32 accumulation", "data": "synthetic (config 2 distribution)",
                 "config": config, "impl": "reference",
                 "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
-                                 "sample": sample},
+                                 "sample": sample, "host": host_info()},
                 "e2e": {"value": round(tflops, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
@@ -319,8 +359,8 @@ def main():
                          "frac": round(gemm_tflops / pk["tflops"], 4),
                          "traffic": (PAIR_8192_TRAFFIC if (M, N, K) == (8192, 8192, 8192) and x16 is not None
                                      else None),
-                         "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, ncu capture "
-                                            "summarised in profiles/scaled_gemm_pair_8192_cube.md"),
+                         "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                            "kernel at M = N = K = 8192, from an ncu capture"),
                          "peak_source": f"{pk['source']} bf16 dense (burst); sustained {pk['tflops_sustained']}",
                          "kernel": ("scaled_gemm_pair_kernel<fp16 operands> (CTA pairs, tcgen05.mma.cta_group::2, TMA, "
                                     "TMEM accumulators)" if x16 is not None
@@ -330,8 +370,12 @@ def main():
                                 "frac": round(rs_gbs / pk["hbm_gbs"], 4), "bytes": rs_bytes,
                                 "writes_fp16_copy": x16 is not None},
             "clocks": clocks.summary()}
+    if not args.no_sustained and x16 is not None:
+        line["sustained"] = sustained_run(step, M, N, K, pk, stream, local, world)
     if not args.no_e2e:
         line["e2e"] = e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16)
+    if rank == 0 and (M, N, K) == (8192, 8192, 8192):
+        line["cublas_bf16_linear"] = cublas_linear_run(x, M, N, K, pk)
     if not args.no_train_linear:
         line["train_linear"] = train_linear_run(pk)
     if not args.no_attention:
@@ -351,7 +395,12 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
-                                "sample": sample}
+                                "sample": sample, "host": host_info()}
+        if not args.no_attention:
+            atf, asample = cpu_attention_sample()
+            line["cpu_baseline"]["attention"] = {
+                "value": round(atf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": asample,
+                "gpu_kernel_tflops": line.get("attention", {}).get("noncausal", {}).get("kernel_tflops")}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
@@ -716,8 +765,36 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
     + tcgen05 flash attention) in TFLOPS, causal and not; kernel-only time against the bf16 peak."""
     import inputs
     from tbf16 import attention
-    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda")
     res = {"config": f"B=1 H={H} S={S} D={D}, Q,K x2^8, V x2^h"}
+    if S == 16384 and D == 128:  # config 3's other lengths, and torch's native bf16 SDPA (informational)
+        res["by_S"] = {}
+        for S2 in (4096, 8192, 16384):
+            q, k, v = inputs.attention_qkv(1, H, S2, D, seed=0, device="cuda")
+            q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
+            row = {}
+            for causal in (False, True):
+                flop = 4.0 * H * S2 * S2 * D * (0.5 if causal else 1.0)
+                for name, fn in (("kernel", lambda: attention.attn_forward(q16, k16, v16, ev, is_causal=causal)),
+                                 ("torch_bf16_sdpa", lambda: torch.nn.functional.scaled_dot_product_attention(
+                                     q, k, v, is_causal=causal))):
+                    for _ in range(2):
+                        fn()
+                    torch.cuda.synchronize()
+                    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s0.record()
+                    for _ in range(iters):
+                        fn()
+                    s1.record()
+                    torch.cuda.synchronize()
+                    t = s0.elapsed_time(s1) / iters
+                    row[f"{'causal' if causal else 'noncausal'}_{name}"] = {
+                        "ms": round(t, 3), "tflops": round(flop / (t / 1e3) / 1e12, 1),
+                        "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
+            res["by_S"][S2] = row
+            del q, k, v, q16, k16, v16
+        res["torch_bf16_sdpa_note"] = ("torch's native bf16 F.scaled_dot_product_attention on the same inputs "
+                                       "(no fp16 scaling): informational")
+    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda")
     for causal in (False, True):
         flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)
         q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
@@ -760,6 +837,53 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
     res["train_fwd_bwd_causal"] = {"config": f"B={B2} H={H} S={S2} D={D}, dY x2^-20", "ms": round(t, 3),
                                    "tflops": round(flop / (t / 1e3) / 1e12, 1)}
     return res
+
+
+def sustained_run(step, M, N, K, pk, stream, local, world, seconds=2.0):
+    """The headline step (row pass + GEMM) back to back for about `seconds`, as a long training or serving
+    loop runs it: under the 1 kW power cap the SM clock settles below its burst value, so this number is
+    set against the measured sustained bf16 peak, with the SM clock sampled during the loop."""
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    n = max(10, int(seconds * 1e3 / max(e0.elapsed_time(e1), 1e-3)))
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(n):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    tflops = 2.0 * M * N * K * world * n / (ms / 1e3) / 1e12
+    peak = pk.get("tflops_sustained") or pk["tflops"]
+    return {"steps": n, "seconds": round(ms / 1e3, 2), "tflops": round(tflops, 1), "peak_sustained": peak,
+            "frac_of_sustained": round(tflops / world / peak, 4), "clocks": clocks.summary()}
+
+
+def cublas_linear_run(x, M, N, K, pk, iters=10):
+    """Informational: torch's native bf16 F.linear (cuBLAS) on the same bf16 activations and an N(0, 1/K)
+    bf16 weight; no fp16 scaling, so no overflow handling: the library ceiling this path is set beside."""
+    import inputs
+    w = inputs.gemm_w(N, K, seed=1, device=x.device)
+    for _ in range(3):
+        torch.nn.functional.linear(x, w)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        torch.nn.functional.linear(x, w)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    return {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / pk["tflops"], 4),
+            "what": "torch.nn.functional.linear in bf16 (cuBLAS), back to back, informational"}
 
 
 def collectives_run(pk, world, rank, iters=5):

@@ -87,7 +87,10 @@ int tbf16_quantize_cols(const void* x, int64_t rows, int64_t K, int64_t ldx, int
  * floats (256 KB) that every GPU loading the library holds until exit. K > TBF16_NOALLOC_MAX_COLS
  * returns TBF16_ERR_INVALID. No cudaMalloc / cudaFree. All calls on a GPU share the array: calls that
  * overlap on the GPU race. The first call on each device resolves the array's address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * (cudaGetSymbolAddress); make that first call before any stream capture. The address is kept for the
+ * life of the process: after cudaDeviceReset (or anything else that destroys and re-creates the
+ * device's primary context) the library's module is loaded again and the array may move, so do not
+ * call this entry point on that device afterwards.
  * No counterpart in the reference (its extension allocates every workspace with torch::empty). */
 #define TBF16_NOALLOC_MAX_COLS 65536
 int tbf16_quantize_cols_noalloc(const void* x, int64_t rows, int64_t K, int64_t ldx, int target_exp,

@@ -137,8 +137,13 @@ def _materialise(M, N, K) -> bool:
 def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None):
     """y = x @ W^T + b for bf16 x, with W given by prepare_weight. Returns bf16.
 
-    One fused launch pair for every M: the row-scale kernel, then the tcgen05 GEMM whose converter
-    warps turn x into fp16(x * 2^s) in shared memory (reference fused path, gemm_sm75.cu:257-284)."""
+    Routed by the number of rows M (reference fused path, gemm_sm75.cu:257-284, for every M): up to
+    GEMV_ROWS rows, one weight-streaming pass (tbf16_gemv); otherwise tbf16_linear: the row pass
+    computes each row's power-of-two scale and, when _materialise says so (N above 512 or at most
+    SKINNY_ROWS rows), also writes fp16(x * 2^s) in the same read of x, and the tcgen05 GEMM then
+    runs on fp16 operands (split-K skinny GEMM up to SKINNY_ROWS rows, CTA-pair or single-CTA GEMM
+    above); for narrow N the GEMM's converter warps build the fp16 tile from bf16 x in shared memory
+    instead. The product leaves the fp32 accumulator as bf16 once."""
     require_cuda(x, w16, w_sinv)
     if x.dtype != torch.bfloat16:
         raise RuntimeError(f"tbf16.scaled_linear: x must be bf16, got {x.dtype}")
