@@ -9,7 +9,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from helpers import assert_close_ulp, gemm_tolerance, rel_err
+from helpers import assert_close_ulp, gemm_tolerance, rel_err, report
 from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -43,9 +43,13 @@ def test_linear_train(name, M, K, N, xs, gs):
                      what="dw")
     # and against plain fp64 autograd
     e_y, e_dx, e_dw, e_db = _grads(F.linear, [x.double(), w.double(), b.double()], dy.double())
+    errs = {}
     for got, exact, what in ((y, e_y, "y"), (dx, e_dx, "dx"), (dw, e_dw, "dw"), (db, e_db, "db")):
         assert torch.isfinite(got.float()).all(), what
-        assert rel_err(got, exact) < 3e-3, (what, rel_err(got, exact))
+        errs[what] = rel_err(got, exact)
+    report(f"linear_train {name} vs fp64", **errs)
+    for what, e in errs.items():
+        assert e < 3e-3, (what, e)
 
 
 def _ref_attn(q, k, v, causal, allowed=None):
@@ -69,7 +73,12 @@ def _ref_attn(q, k, v, causal, allowed=None):
     ("dO x1e-10", 8, 8, 1024, 64, True, 1.0, 1e-10, 1.0),
     ("dO x1e6, v x1e4", 8, 8, 1024, 64, True, 1.0, 1e6, 1e4),
     ("peaky q,k x8", 8, 8, 1024, 64, True, 8.0, 1.0, 1.0),
-    ("odd length", 4, 2, 333, 64, True, 1.0, 1.0, 1.0)])
+    ("odd length", 4, 2, 333, 64, True, 1.0, 1.0, 1.0),
+    ("D=256 GQA 8/4 causal", 8, 4, 1024, 256, True, 1.0, 1.0, 1.0),
+    ("D=256 non-causal", 4, 4, 512, 256, False, 1.0, 1.0, 1.0),
+    ("D=256 dO x1e-10, v x1e4", 4, 2, 512, 256, True, 1.0, 1e-10, 1e4),
+    ("D=256 odd length", 4, 2, 333, 256, True, 1.0, 1.0, 1.0),
+    ("D=200 padded to 256", 2, 2, 256, 200, True, 1.0, 1.0, 1.0)])
 def test_sdpa_train(name, Hq, Hkv, S, D, causal, qs, gs, vs):
     from tbf16 import autograd as ag
     g = torch.Generator().manual_seed(Hq * S + D)
@@ -82,11 +91,16 @@ def test_sdpa_train(name, Hq, Hkv, S, D, causal, qs, gs, vs):
                            [q.cuda(), k.cuda(), v.cuda()], do.cuda())
     ref = orc.sdpa_bwd(q, k, v, do, is_causal=causal)
     exact = _grads(lambda q, k, v: _ref_attn(q, k, v, causal), [q.double(), k.double(), v.double()], do.double())
+    errs, errs_orc = {}, {}
     for got, orc_v, ex, what in ((o, ref["out"], exact[0], "o"), (dq, ref["dq"], exact[1], "dq"),
                                  (dk, ref["dk"], exact[2], "dk"), (dv, ref["dv"], exact[3], "dv")):
         assert torch.isfinite(got.float()).all(), what
-        assert rel_err(got, orc_v) < 4e-3, (what, rel_err(got, orc_v))
-        assert rel_err(got, ex) < 6e-3, (what, rel_err(got, ex))
+        errs[what], errs_orc[what] = rel_err(got, ex), rel_err(got, orc_v)
+    report(f"sdpa_train {name} vs fp64", **errs)
+    report(f"sdpa_train {name} vs oracle", **errs_orc)
+    for what in errs:
+        assert errs_orc[what] < 4e-3, (what, errs_orc[what])
+        assert errs[what] < 6e-3, (what, errs[what])
 
 
 def test_sdpa_train_exponent_G_bit_exact():
@@ -102,11 +116,11 @@ def test_sdpa_train_exponent_G_bit_exact():
         assert int(G) == orc.sdpa_bwd(q, k, v, do)["G"]
 
 
-@pytest.mark.parametrize("kind", ["bool", "float"])
-def test_sdpa_train_masks(kind):
+@pytest.mark.parametrize("kind,D", [("bool", 64), ("float", 64), ("bool", 256)])
+def test_sdpa_train_masks(kind, D):
     """Sliding window + padding (reference tests/test_autograd.py:45-64)."""
     from tbf16 import autograd as ag
-    Hq, Hkv, S, D = 8, 4, 1000, 64
+    Hq, Hkv, S = 8, 4, 1000
     g = torch.Generator().manual_seed(7)
     q = torch.randn(2, Hq, S, D, generator=g).bfloat16()
     k, v = (torch.randn(2, Hkv, S, D, generator=g).bfloat16() for _ in range(2))
@@ -120,6 +134,10 @@ def test_sdpa_train_masks(kind):
     o, dq, dk, dv = _grads(lambda q, k, v: ag.sdpa(q, k, v, attn_mask=mask.cuda(), enable_gqa=True),
                            [q.cuda(), k.cuda(), v.cuda()], do.cuda())
     exact = _grads(lambda q, k, v: _ref_attn(q, k, v, False, allowed), [q.double(), k.double(), v.double()], do.double())
+    errs = {}
     for got, ex, what in zip((o, dq, dk, dv), exact, ("o", "dq", "dk", "dv")):
         assert torch.isfinite(got.float()).all(), what
-        assert rel_err(got, ex) < 6e-3, (what, rel_err(got, ex))
+        errs[what] = rel_err(got, ex)
+    report(f"sdpa_train masks {kind} D={D} vs fp64", **errs)
+    for what, e in errs.items():
+        assert e < 6e-3, (what, e)

@@ -18,9 +18,12 @@
 //   warps 4-11  key warps, two per TMEM lane quadrant, each half of the query columns: P^T (packed
 //               fp16 back into TMEM), dS^T (fp16, 128B-swizzled K-major tile in shared memory), and at
 //               the end half the columns of dK, dV from TMEM -> bf16
-//   warps 12-15 dQ warps, one per TMEM lane quadrant (queries): all D columns of dQ out of TMEM at once
-//               (which frees the columns for the next dP), then TMA reduce-adds of 32-column boxes into
-//               the fp32 accumulator from two alternating staging buffers
+//   warps 12-15 dQ warps, one per TMEM lane quadrant. D = 128: the tensor core computes dQ^T = K^T dS^T
+//               (head dims as lanes), each thread reads its d's 128 query columns at once (which frees
+//               them for the next dP) and adds them into the fp32 accumulator with red.global.add, the
+//               warp's 32 consecutive d making each instruction one 128-byte segment (no shared-memory
+//               staging). D = 64: dQ = dS K with queries as lanes, TMA reduce-adds of 32-column boxes
+//               from two alternating staging buffers.
 // The key warps only compute P and dS, so the tile loop is dS(t) -> P(t+1) -> dS(t+1) while the tensor
 // core runs dQ(t), dK(t), dP(t+1), dV(t+1), S(t+2) and the dQ warps drain dQ(t) alongside.
 // TMEM: S^T [0,128), dP^T / dQ [128,256), dV [256,256+D), dK [256+D,256+2D). Bounded waits throughout.
@@ -72,8 +75,12 @@ struct BwdCfg {
   static constexpr int Q_OFF = V_OFF + TILE;      // [2 stages]
   static constexpr int DO_OFF = Q_OFF + 2 * TILE; // one stage: its readers dP(t), dV(t) finish early
   static constexpr int DS_OFF = DO_OFF + TILE;
-  static constexpr int DQS_OFF = DS_OFF + 32768;  // dQ staging: 4 warps x 2 boxes of 32 rows x 32 fp32
-  static constexpr int VEC_OFF = DQS_OFF + 32768; // [2 stages] lse (natural log) and delta of the query tile
+  // D = 128: dQ is computed transposed (head dims as TMEM lanes) and added into the fp32 accumulator with
+  // coalesced reductions straight from registers; D = 64 keeps queries as lanes and stages 32 x 32 boxes
+  // for TMA reduce-adds (4 warps x 2 boxes of 4 KB)
+  static constexpr bool DQ_T = D == 128;
+  static constexpr int DQS_OFF = DS_OFF + 32768;
+  static constexpr int VEC_OFF = DQS_OFF + (DQ_T ? 0 : 32768); // [2 stages] lse (natural log) and delta
   static constexpr int BAR_OFF = VEC_OFF + 2048;
   // the dynamic shared window starts 1024-byte aligned (checked on entry), so no alignment slack
   static constexpr int SMEM = BAR_OFF + 256;
@@ -199,7 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && n_t > 0) {
       constexpr uint32_t id_sq = idesc_f16_f32(128, 128, false, false);  // S^T, dP^T
       constexpr uint32_t id_kd = idesc_f16_f32(128, D, false, true);     // dV, dK
-      constexpr uint32_t id_q = idesc_f16_f32(128, D, true, true);       // dQ
+      // dQ (M = queries, N = D) or, with DQ_T, dQ^T (M = D, N = queries): both operands MN-major
+      constexpr uint32_t id_q = C::DQ_T ? idesc_f16_f32(D, 128, true, true) : idesc_f16_f32(128, D, true, true);
       // a k16 step adds its byte offset / 16 to the 14-bit start-address field (no carry: < 2^18 bytes)
       const uint64_t kd = smem_desc_sw128(smem_u32(smem + C::K_OFF), 16, 1024);
       const uint64_t vd = smem_desc_sw128(smem_u32(smem + C::V_OFF), 16, 1024);
@@ -256,9 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(ds_ready, t & 1, abort, p.err)) break;
         tc_fence_after();
         // dQ first: its extraction (the dQ warps) gates dP(t+1)
+        if constexpr (C::DQ_T) {
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)  // dQ = dS K   (dS^T read MN-major, K MN-major)
-          umma_f16_ss(tmem + C::T_DP, dsd_mn + (kk * 2048 >> 4), kd_mn + (kk * 2048 >> 4), id_q, kk > 0);
+          for (int kk = 0; kk < BKV / 16; ++kk)  // dQ^T = K^T dS^T   (K MN-major as A: m = d; dS^T MN-major as B)
+            umma_f16_ss(tmem + C::T_DP, kd_mn + (kk * 2048 >> 4), dsd_mn + (kk * 2048 >> 4), id_q, kk > 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)  // dQ = dS K   (dS^T read MN-major, K MN-major)
+            umma_f16_ss(tmem + C::T_DP, dsd_mn + (kk * 2048 >> 4), kd_mn + (kk * 2048 >> 4), id_q, kk > 0);
+        }
         umma_commit(dq_full);
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q   (Q MN-major)
@@ -454,6 +468,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 4 KB 128B-swizzled buffers so a box waits only for the reduction issued two boxes earlier.
     const int quad = warp & 3;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    if constexpr (C::DQ_T) {
+      // dQ^T(t) = K^T dS^T: lanes are head dims, columns queries. Thread d reads its 128 query columns at
+      // once (freeing the columns for dP(t+1)), then adds each into dq_acc[q][d]: the warp's 32 lanes are
+      // 32 consecutive d, so every reduction instruction covers one contiguous 128-byte segment.
+      const int d = quad * 32 + lane;
+      for (int t = 0; t < n_t; ++t) {
+        const int h = hk * p.group + t / n_i;
+        const int q0 = (i_first + t % n_i) * BQ;
+        if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) break;
+        tc_fence_after();
+        uint32_t o[BQ];
+#pragma unroll
+        for (int c = 0; c < BQ / 32; ++c)
+          tmem_ld32(tmem + lane_base + C::T_DP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        float* dst = p.dq_acc + ((int64_t)(b * p.Hq + h) * p.Sq + q0) * D + d;
+        const int nq = min(BQ, p.Sq - q0);
+#pragma unroll
+        for (int c = 0; c < BQ; ++c)
+          if (c < nq) red_add_f32(dst + (int64_t)c * D, __uint_as_float(o[c]));
+      }
+    } else {
     uint8_t* stage = smem + C::DQS_OFF + (warp - 12) * 8192;
     int sb = 0;
     for (int t = 0; t < n_t; ++t) {
@@ -488,6 +527,358 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_group<0>();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------
+// Head dim 256. The key-stationary design above keeps dK and dV of all D columns in TMEM (2 D columns per
+// key); at D = 256 that is all 512 columns, so here each 128-key tile is split over two CTAs by OUTPUT
+// columns: CTA dh (blockIdx.z) accumulates dK, dV and dQ for head dims [128 dh, 128 dh + 128). Both CTAs
+// compute the full-D contractions S^T = K Q^T and dP^T = V dO^T (the softmax needs all of D), so those
+// two products are done twice; everything downstream is split. Query tiles are 64 rows, so that K, V
+// (64 KB each, resident) plus one 32 KB stage of Q and of dO fit in shared memory.
+//   warp 0      TMA: K, V once; per query tile Q (4 atoms of 64 rows x 64 dims), lse and delta, one stage
+//   warp 1      MMA, per query tile t (all 128-row M):
+//                 S^T  = K Q^T          (N = 64 queries, K = 256)      -> TMEM [0, 64)
+//                 dP^T = V dO^T         (N = 64, K = 256)              -> TMEM [64, 128)
+//                 dV  += P^T dO_dh      (TS: P^T from TMEM; N = 128)   -> TMEM [256, 384)
+//                 dK  += dS^T Q_dh      (dS^T from shared memory)      -> TMEM [384, 512)
+//                 dQ^T = K_dh^T dS^T    (M = 128 head dims, N = 64)    -> TMEM [128, 192)
+//               issued as dV(t) | dK(t) dQ^T(t) dP(t+1) S(t+1) | dV(t+1) ...: Q's stage is released by
+//               dK(t) and reloaded while dQ^T(t) and dP(t+1) run
+//   warp 2      TMA: dO per query tile, one stage (released by dV(t))
+//   warps 4-11  key warps, two per TMEM lane quadrant, each 32 of the 64 query columns: P^T (packed fp16
+//               back over its S^T columns), dS^T (fp16 into a 128B-swizzled 128 x 64 tile), and at the
+//               end 64 of the 128 dK / dV columns
+//   warps 12-15 dQ warps: dQ^T rows are head dims, so each thread adds its 64 query values into the fp32
+//               accumulator with red.global.add, 32 consecutive head dims per warp instruction
+namespace d256 {
+constexpr int QROWS = 64;
+constexpr int KROWS = 128;
+constexpr int D = 256;
+constexpr int K_OFF = 0;                    // 4 atoms x 128 rows x 128 B
+constexpr int V_OFF = K_OFF + 65536;
+constexpr int Q_OFF = V_OFF + 65536;        // 4 atoms x 64 rows x 128 B
+constexpr int DO_OFF = Q_OFF + 32768;
+constexpr int DS_OFF = DO_OFF + 32768;      // dS^T: 128 keys x 64 queries fp16, one atom
+constexpr int VEC_OFF = DS_OFF + 16384;     // lse[64], delta[64]
+constexpr int BAR_OFF = VEC_OFF + 512;
+constexpr int SMEM = BAR_OFF + 256;
+constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_DV = 256, T_DK = 384;
+static_assert(SMEM <= 227 * 1024, "shared memory");
+}  // namespace d256
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_d256_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                         const AttnBwdParams p) {
+  using namespace d256;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) atomicOr(p.err, kErrSmemAlign);
+    return;
+  }
+  uint8_t* smem = smem_raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* do_full = bars + 3;
+  uint64_t* do_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* dp_full = bars + 6;
+  uint64_t* p_ready = bars + 7;
+  uint64_t* ds_ready = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_empty = bars + 10;
+  uint64_t* kv_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bhk = blockIdx.x;
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int k0 = blockIdx.y * KROWS;
+  const int dh = blockIdx.z;  // this CTA's half of the head dims for dK, dV and dQ
+  const int i_first = p.causal ? k0 / QROWS : 0;
+  const int n_i = max(0, p.q_tiles - i_first);
+  const int n_t = p.group * n_i;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_ready, 8);
+    mbar_init(ds_ready, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(kv_done, 1);
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA: K, V, then Q + lse + delta
+    if (lane == 0 && n_t > 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * 65536);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        tma_load_3d(smem + K_OFF + a * 16384, &tmK, kv_full, a * 64, k0, bhk);
+        tma_load_3d(smem + V_OFF + a * 16384, &tmV, kv_full, a * 64, k0, bhk);
+      }
+      for (int t = 0; t < n_t; ++t) {
+        const int h = hk * p.group + t / n_i;
+        const int q0 = (i_first + t % n_i) * QROWS;
+        const int bh = b * p.Hq + h;
+        if (!mbar_wait(q_empty, (t & 1) ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(q_full, 32768 + 512);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) tma_load_3d(smem + Q_OFF + a * 8192, &tmQ, q_full, a * 64, q0, bh);
+        float* vec = reinterpret_cast<float*>(smem + VEC_OFF);
+        bulk_load(vec, p.lse + (int64_t)bh * p.lse_ld + q0, 256, q_full);
+        bulk_load(vec + 64, p.delta + (int64_t)bh * p.lse_ld + q0, 256, q_full);
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- TMA: dO
+    if (lane == 0 && n_t > 0) {
+      for (int t = 0; t < n_t; ++t) {
+        const int h = hk * p.group + t / n_i;
+        const int q0 = (i_first + t % n_i) * QROWS;
+        if (!mbar_wait(do_empty, (t & 1) ^ 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(do_full, 32768);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) tma_load_3d(smem + DO_OFF + a * 8192, &tmDO, do_full, a * 64, q0, b * p.Hq + h);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n_t > 0) {
+      constexpr uint32_t id_s = idesc_f16_f32(128, QROWS, false, false);   // S^T, dP^T
+      constexpr uint32_t id_kv = idesc_f16_f32(128, 128, false, true);  // dV, dK
+      constexpr uint32_t id_qt = idesc_f16_f32(128, QROWS, true, true);    // dQ^T
+      const uint32_t k_addr = smem_u32(smem + K_OFF), v_addr = smem_u32(smem + V_OFF);
+      const uint32_t q_addr = smem_u32(smem + Q_OFF), do_addr = smem_u32(smem + DO_OFF);
+      const uint32_t ds_addr = smem_u32(smem + DS_OFF);
+      auto issue_full_d = [&](uint32_t a_addr, uint32_t b_addr, uint32_t d_col) {  // K = 256 head dims
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t in_atom = (kk & 3) * 32;
+          umma_f16_ss(tmem + d_col, smem_desc_sw128(a_addr + (kk >> 2) * 16384 + in_atom, 16, 1024),
+                      smem_desc_sw128(b_addr + (kk >> 2) * 8192 + in_atom, 16, 1024), id_s, kk > 0);
+        }
+      };
+      bool ok = mbar_wait(kv_full, 0, abort, p.err) && mbar_wait(q_full, 0, abort, p.err);
+      if (ok) {
+        tc_fence_after();
+        issue_full_d(k_addr, q_addr, T_S);
+        umma_commit(s_full);
+        ok = mbar_wait(do_full, 0, abort, p.err);
+        if (ok) {
+          tc_fence_after();
+          issue_full_d(v_addr, do_addr, T_DP);
+          umma_commit(dp_full);
+        }
+      }
+      for (int t = 0; ok && t < n_t; ++t) {
+        const bool next = t + 1 < n_t;
+        if (!mbar_wait(p_ready, t & 1, abort, p.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < QROWS / 16; ++kk)  // dV += P^T dO_dh   (P^T: queries 32 w.. in packed columns 32 w..)
+          umma_f16_ts(tmem + T_DV, tmem + T_S + (kk >> 1) * 32 + (kk & 1) * 8,
+                      smem_desc_sw128(do_addr + dh * 16384 + kk * 2048, 8192, 1024), id_kv, (t > 0 || kk > 0));
+        umma_commit(do_empty);  // dP(t) and dV(t) were dO(t)'s readers
+        if (!mbar_wait(ds_ready, t & 1, abort, p.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < QROWS / 16; ++kk)  // dK += dS^T Q_dh
+          umma_f16_ss(tmem + T_DK, smem_desc_sw128(ds_addr + kk * 32, 16, 1024),
+                      smem_desc_sw128(q_addr + dh * 16384 + kk * 2048, 8192, 1024), id_kv, (t > 0 || kk > 0));
+        umma_commit(q_empty);  // S(t) and dK(t) were Q(t)'s readers
+        if (t > 0 && !mbar_wait(dq_empty, (t - 1) & 1, abort, p.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < KROWS / 16; ++kk)  // dQ^T = K_dh^T dS^T   (both MN-major)
+          umma_f16_ss(tmem + T_DQ, smem_desc_sw128(k_addr + dh * 32768 + kk * 2048, 16384, 1024),
+                      smem_desc_sw128(ds_addr + kk * 2048, 16384, 1024), id_qt, kk > 0);
+        umma_commit(dq_full);
+        if (next) {
+          if (!mbar_wait(do_full, (t + 1) & 1, abort, p.err)) break;
+          tc_fence_after();
+          issue_full_d(v_addr, do_addr, T_DP);
+          umma_commit(dp_full);
+          if (!mbar_wait(q_full, (t + 1) & 1, abort, p.err)) break;
+          tc_fence_after();
+          issue_full_d(k_addr, q_addr, T_S);
+          umma_commit(s_full);
+        }
+      }
+      if (ok) umma_commit(kv_done);
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------------------------------------------------------- key warps
+    const int quad = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;  // key within the tile
+    const int kj = k0 + r;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int cq = half * 32;        // this warp's 32 query columns
+    const float* vec = reinterpret_cast<const float*>(smem + VEC_OFF);
+    bool ok = true, bad = false;
+    uint32_t pp[16];  // P of this thread's key against the warp's 32 queries, packed fp16 pairs
+
+    auto compute_p = [&](int t) -> bool {
+      const int h = hk * p.group + t / n_i;
+      const int q0 = (i_first + t % n_i) * QROWS;
+      if (!mbar_wait_warp(q_full, t & 1, abort, p.err) || !mbar_wait_warp(s_full, t & 1, abort, p.err)) return false;
+      tc_fence_after();
+      uint32_t rr[32];
+      tmem_ld32(tmem + lane_base + T_S + cq, rr);
+      tmem_ld_wait();
+      const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float pc[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int col = cq + e + u;
+          const int qi = q0 + col;
+          const bool valid = kj < p.Sk && qi < p.Sq && (!p.causal || kj <= qi);
+          float sv = __uint_as_float(rr[e + u]) * p.scale_log2;
+          if (mrow && valid) sv += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
+          pc[u] = valid ? ex2(sv - vec[col] * 1.4426950408889634f) : 0.f;
+        }
+        pp[e >> 1] = pack_f16(pc[0], pc[1]);
+      }
+      tmem_st16(tmem + lane_base + T_S + cq, pp);  // P^T over this warp's own S^T columns
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      return true;
+    };
+
+    ok = n_t > 0 && compute_p(0);
+    for (int t = 0; ok && t < n_t; ++t) {
+      if (!mbar_wait_warp(dp_full, t & 1, abort, p.err)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t rr[32];
+        tmem_ld32(tmem + lane_base + T_DP + cq, rr);
+        tmem_ld_wait();
+        uint32_t pk[16];
+        uint32_t ovf = 0;
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pp[e >> 1]));
+          const float d0 = pf.x * (__uint_as_float(rr[e]) - vec[64 + cq + e]);
+          const float d1 = pf.y * (__uint_as_float(rr[e + 1]) - vec[64 + cq + e + 1]);
+          pk[e >> 1] = pack_f16(d0, d1);
+          ovf |= __vcmpeq2(pk[e >> 1] & 0x7c007c00u, 0x7c007c00u);
+        }
+        bad |= ovf != 0;
+        // dS^T row r, queries [cq, cq + 32): 16-byte chunks 4 half .. 4 half + 3 of the 128-byte row
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          *reinterpret_cast<uint4*>(smem + DS_OFF + swz_off(r, half * 4 + g)) =
+              make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_ready);
+      if (t + 1 < n_t && !compute_p(t + 1)) { ok = false; break; }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.flag, kErrOverflow);
+    // dK, dV: this warp's 64 of the CTA's 128 head-dim columns for its 32 keys
+    const int64_t orow = ((int64_t)bhk * p.Sk + min(kj, p.Sk - 1)) * D + dh * 128 + half * 64;
+    if (ok && n_t > 0 && mbar_wait_warp(kv_done, 0, abort, p.err)) {
+      tc_fence_after();
+      const float sk = p.scale * exp2i(-__ldg(p.a) - __ldg(p.G));
+      const float sv = exp2i(-__ldg(p.ev + bhk) - __ldg(p.G));
+      bool nf = false;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        __nv_bfloat16* dst = (which ? p.dk : p.dv) + orow;
+        const float f = which ? sk : sv;
+        const uint32_t col0 = (which ? T_DK : T_DV) + half * 64;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + col0 + c * 32, o);
+          tmem_ld_wait();
+          if (kj < p.Sk) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                v[e] = __uint_as_float(o[8 * g + e]) * f;
+                nf |= !isfinite(v[e]);
+              }
+              *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) =
+                  make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+            }
+          }
+        }
+      }
+      if (__any_sync(0xffffffffu, nf) && lane == 0) atomicOr(p.flag, kErrOverflow);
+    } else if (n_t == 0 && kj < p.Sk) {  // keys no query sees: zero gradients
+      for (int c = 0; c < 64; c += 8) {
+        *reinterpret_cast<uint4*>(p.dk + orow + c) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(p.dv + orow + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  } else if (warp >= 12) {
+    // ---------------------------------------------------------------- dQ warps
+    const int quad = warp & 3;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int d = dh * 128 + quad * 32 + lane;
+    for (int t = 0; t < n_t; ++t) {
+      const int h = hk * p.group + t / n_i;
+      const int q0 = (i_first + t % n_i) * QROWS;
+      if (!mbar_wait_warp(dq_full, t & 1, abort, p.err)) break;
+      tc_fence_after();
+      uint32_t o[QROWS];
+      tmem_ld32(tmem + lane_base + T_DQ, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+      tmem_ld32(tmem + lane_base + T_DQ + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      float* dst = p.dq_acc + ((int64_t)(b * p.Hq + h) * p.Sq + q0) * D + d;
+      const int nq = min(QROWS, p.Sq - q0);
+#pragma unroll
+      for (int c = 0; c < QROWS; ++c)
+        if (c < nq) red_add_f32(dst + (int64_t)c * D, __uint_as_float(o[c]));
+    }
   }
 
   tc_fence_before();
@@ -631,6 +1022,28 @@ int launch_bwd(const void* q16, const void* k16, const void* v16, const void* do
   return tbf16_host::check_launch();
 }
 
+int launch_bwd_d256(const void* q16, const void* k16, const void* v16, const void* do16, AttnBwdParams prm, int64_t Sk,
+                    cudaStream_t st) {
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  constexpr int D = 256;
+  CUtensorMap tq, tk, tv, tdo;
+  const int64_t BHq = (int64_t)prm.B * prm.Hq, BHk = (int64_t)prm.B * prm.Hkv;
+  if (int rc = tbf16_host::make_tmap_3d(&tq, q16, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 64, d256::QROWS)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tdo, do16, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 64, d256::QROWS)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tk, k16, D, Sk, BHk, D, (uint64_t)Sk * D, 64, d256::KROWS)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, Sk, BHk, D, (uint64_t)Sk * D, 64, d256::KROWS)) return rc;
+  static bool attr_done[64] = {false};
+  if (!attr_done[dev->device & 63]) {
+    if (cudaFuncSetAttribute(attn_bwd_d256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d256::SMEM) != cudaSuccess)
+      return tbf16_host::check_launch();
+    attr_done[dev->device & 63] = true;
+  }
+  prm.q_tiles = (int)((prm.Sq + d256::QROWS - 1) / d256::QROWS);
+  dim3 grid((unsigned)BHk, (unsigned)((Sk + d256::KROWS - 1) / d256::KROWS), 2);
+  attn_bwd_d256_kernel<<<grid, kThreads, d256::SMEM, st>>>(tq, tk, tv, tdo, prm);
+  return tbf16_host::check_launch();
+}
+
 }  // namespace
 
 extern "C" {
@@ -652,7 +1065,7 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq <= 0 || Sk <= 0 || dout_d <= 0 || dout_d > D || !a || !ev ||
       !lse || lse_ld != lse_stride(Sq) || !G_out || !flag || !ws || B * Hq > 65535 || B * Hkv > 65535)
     return TBF16_ERR_INVALID;
-  if (D != 64 && D != 128) return TBF16_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128 && D != 256) return TBF16_ERR_UNSUPPORTED;
   if (ws_bytes < workspace_bytes(B, Hq, Sq, D)) return TBF16_ERR_INVALID;
   if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16) ||
       !tbf16_host::aligned16(o16) || !tbf16_host::aligned16(dout) || !tbf16_host::aligned16(dq) ||
@@ -676,8 +1089,12 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
     attn_bwd_prep_kernel<64><<<pgrid, 256, 0, st>>>(static_cast<const uint16_t*>(dout), dout_sb, dout_sh, dout_ss,
                                                     (int)dout_d, static_cast<const __half*>(o16), ev, G_out, (int)Hq,
                                                     (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta);
-  else
+  else if (D == 128)
     attn_bwd_prep_kernel<128><<<pgrid, 256, 0, st>>>(static_cast<const uint16_t*>(dout), dout_sb, dout_sh, dout_ss,
+                                                     (int)dout_d, static_cast<const __half*>(o16), ev, G_out, (int)Hq,
+                                                     (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta);
+  else
+    attn_bwd_prep_kernel<256><<<pgrid, 256, 0, st>>>(static_cast<const uint16_t*>(dout), dout_sb, dout_sh, dout_ss,
                                                      (int)dout_d, static_cast<const __half*>(o16), ev, G_out, (int)Hq,
                                                      (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta);
   // 3. main kernel (dQ accumulated in fp32)
@@ -696,7 +1113,9 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
   prm.err = dev->err;
   prm.flag = flag;
   prm.q_tiles = (int)((Sq + BQ - 1) / BQ);
-  int rc = D == 64 ? launch_bwd<64>(q16, k16, v16, w.do16, prm, Sk, st) : launch_bwd<128>(q16, k16, v16, w.do16, prm, Sk, st);
+  int rc = D == 64    ? launch_bwd<64>(q16, k16, v16, w.do16, prm, Sk, st)
+           : D == 128 ? launch_bwd<128>(q16, k16, v16, w.do16, prm, Sk, st)
+                      : launch_bwd_d256(q16, k16, v16, w.do16, prm, Sk, st);
   if (rc) return rc;
   // 4. dq
   const int64_t n4 = rows * D / 4;

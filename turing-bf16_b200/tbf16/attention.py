@@ -17,7 +17,7 @@ from ._ext import BF16, F16, call, ptr, require_cuda, stream_ptr
 
 _DTYPE = {torch.bfloat16: BF16, torch.float16: F16}
 KERNEL_D = (64, 128, 256)      # forward kernel head dims (others are zero-padded up)
-KERNEL_D_TRAIN = (64, 128)     # backward kernel head dims
+KERNEL_D_TRAIN = (64, 128, 256)  # backward kernel head dims
 
 
 def _fast(x: torch.Tensor):

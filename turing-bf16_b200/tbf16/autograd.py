@@ -262,9 +262,9 @@ class ScaledSDPAFn(torch.autograd.Function):
         D0 = q.shape[-1]
         q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v)
         B, Hq, Sq, D = q16.shape
-        Dk = 64 if D <= 64 else 128
-        if D > 128:
-            raise NotImplementedError("tbf16 attention on B200: head dims up to 128 in this build")
+        if D > 256:
+            raise NotImplementedError("tbf16 attention on B200: head dims up to 256")
+        Dk = 64 if D <= 64 else 128 if D <= 128 else 256
         if Dk != D:
             q16, k16, v16 = (F.pad(t, (0, Dk - D)) for t in (q16, k16, v16))
         sc = 1.0 / math.sqrt(D0) if scale is None else float(scale)

@@ -37,10 +37,10 @@ MIN_DIM = int(os.environ.get("TBF16_MIN_DIM", 128))
 # threshold).
 MIN_QUERY_ROWS = 16
 
-# Head dims the scaled attention takes (the kernels zero-pad smaller ones to 64 / 128 / 256): the forward
-# up to 256, the reference's limit; the backward up to MAX_HEAD_DIM_TRAIN.
+# Head dims the scaled attention takes (the kernels zero-pad smaller ones to 64 / 128 / 256), forward and
+# backward: up to 256, the reference's limit.
 MAX_HEAD_DIM = 256
-MAX_HEAD_DIM_TRAIN = 128
+MAX_HEAD_DIM_TRAIN = 256
 
 _native_sdpa = F.scaled_dot_product_attention
 
@@ -64,7 +64,7 @@ def _as_autocast_would(*ts):
 def attention_route(q, k, v, min_rows=MIN_QUERY_ROWS) -> str:
     """'scaled', 'scaled_train' or 'native' for an F.scaled_dot_product_attention call on q, k, v:
     bf16 CUDA 4-D tensors with head dim <= MAX_HEAD_DIM and at least min_rows query rows take the scaled
-    kernels; with autograd recording, head dims above MAX_HEAD_DIM_TRAIN stay native."""
+    kernels ('scaled_train' when autograd records, for head dims up to MAX_HEAD_DIM_TRAIN)."""
     if not (_bf16_cuda(q, k, v) and q.dim() == 4 and q.shape[-1] <= MAX_HEAD_DIM and q.shape[-2] >= min_rows):
         return "native"
     if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):

@@ -109,10 +109,10 @@ class _ShardedSDPAFn(torch.autograd.Function):
     @torch.autocast("cuda", enabled=False)
     def forward(ctx, q, k, v, attn_mask, is_causal, scale, group):
         D0 = q.shape[-1]
-        if D0 > 128:
-            raise NotImplementedError("tbf16 sharded training attention: head dims up to 128")
+        if D0 > 256:
+            raise NotImplementedError("tbf16 sharded training attention: head dims up to 256")
         q16, k16, v16, a, ev = prepare_qkv_sharded(q, k, v, v_exp=0, group=group)
-        Dk = 64 if D0 <= 64 else 128
+        Dk = 64 if D0 <= 64 else 128 if D0 <= 128 else 256
         if Dk != D0:
             q16, k16, v16 = (torch.nn.functional.pad(t, (0, Dk - D0)) for t in (q16, k16, v16))
         sc = 1.0 / math.sqrt(D0) if scale is None else float(scale)
