@@ -293,9 +293,10 @@ def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None, kv_head
     (:177-189) never triggers here because nothing is rounded to fp16 after dO16.
 
     Also returned for error bounds: abs_dq, abs_dk (the dQ / dK contractions over P (|dP| + sum |dO16| |O|),
-    the magnitudes that the rounding of P, delta and dS scale with, scaled like the gradients), abs_dv
-    (over P |dO16|), and dq16 / dk16 / dv16 before their power-of-two scales (the reference rounds
-    these to fp16). kv_heads: as in sdpa_fwd (G stays global)."""
+    the magnitudes that the relative rounding of P, delta and dS scale with, scaled like the gradients),
+    abs_dv (over P |dO16|), sub_dq / sub_dk / sub_dv (the same contractions with P replaced by 1: what the
+    absolute 2^-25 rounding of fp16 values near zero scales with), and dq16 / dk16 / dv16 before their
+    power-of-two scales (the reference rounds these to fp16). kv_heads: as in sdpa_fwd (G stays global)."""
     f = sdpa_fwd(q, k, v, attn_mask, is_causal, scale, v_exp=0, kv_heads=kv_heads)
     q16, k16, v16, a, ev, p, o = f["q16"], f["k16"], f["v16"], f["a"], f["ev"], f["p"], f["o16"]
     Hq = q16.shape[1]
@@ -324,8 +325,12 @@ def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None, kv_head
         return g if Hkv == Hq else g.view(B, Hkv, Hq // Hkv, *g.shape[2:]).sum(2)
 
     two = lambda ex: torch.ldexp(torch.ones(()), ex.double())[..., None, None]
-    # |dS| with the magnitudes its rounding errors scale with: P times (|dP| + sum_d |dO16| |O|)
+    # |dS| with the magnitudes its rounding errors scale with: P times (|dP| + sum_d |dO16| |O|), plus the
+    # absolute error of fp16 rounding near zero: P and dS below fp16's smallest subnormal (2^-24) round to
+    # zero in an fp16 pipeline (this build's and the reference's alike), an absolute 2^-25 per element,
+    # which the sub_* terms carry in units of 2^-24 (keys / queries that are all but never attended)
     dsa = p * (dp.abs() + (do16.abs() * o.abs()).sum(-1, keepdim=True))
+    dsa_sub = dp.abs() + (do16.abs() * o.abs()).sum(-1, keepdim=True) + 1.0
     dq = bf16_rn(dq16 * two(a - G))
     dk = bf16_rn(reduce_kv(dk16) * two(-a - G))
     dv = bf16_rn(reduce_kv(dv16) * two(-ev - G))
@@ -333,7 +338,10 @@ def sdpa_bwd(q, k, v, dout, attn_mask=None, is_causal=False, scale=None, kv_head
             "do16": do16, "delta": delta, "dq16": dq16, "dk16": reduce_kv(dk16), "dv16": reduce_kv(dv16),
             "abs_dq": (dsa @ kk.abs()) * f["scale"] * two(a - G),
             "abs_dk": reduce_kv(dsa.transpose(-1, -2) @ q16.double().abs()) * f["scale"] * two(-a - G),
-            "abs_dv": reduce_kv(p.transpose(-1, -2) @ do16.abs()) * two(-ev - G)}
+            "abs_dv": reduce_kv(p.transpose(-1, -2) @ do16.abs()) * two(-ev - G),
+            "sub_dq": (dsa_sub @ kk.abs()) * f["scale"] * two(a - G),
+            "sub_dk": reduce_kv(dsa_sub.transpose(-1, -2) @ q16.double().abs()) * f["scale"] * two(-a - G),
+            "sub_dv": reduce_kv(torch.ones_like(p).transpose(-1, -2) @ do16.abs()) * two(-ev - G)}
 
 
 # ----------------------------------------------------------------------------- GEMMs

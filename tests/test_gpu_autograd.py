@@ -1,15 +1,16 @@
 """Training path parity: tbf16.autograd.linear (ScaledLinearFn) and tbf16.autograd.sdpa (ScaledSDPAFn)
 against the oracle's fp64 restatement of the reference's algorithm (autograd.py:58-90, 149-193) on the
-same seeded inputs, and against plain fp64 autograd. Cases follow the reference's tests/test_autograd.py:
-gaussian, tiny and huge gradients, odd sizes, long M, GQA, causal, dO x1e-10, dO x1e6 with v x1e4,
-peaky q/k, and boolean / float sliding-window + padding masks."""
+same seeded inputs (elementwise), and against plain fp64 autograd (relative error below 2e-3). Cases
+follow the reference's tests/test_autograd.py: gaussian, tiny and huge gradients, odd sizes, long M,
+GQA, causal, dO x1e-10, dO x1e6 with v x1e4, peaky q/k, and boolean / float sliding-window + padding
+masks, at head dims 64, 128 and 256 (and 200, zero-padded)."""
 import math
 
 import pytest
 import torch
 import torch.nn.functional as F
 
-from helpers import assert_close_ulp, gemm_tolerance, rel_err, report
+from helpers import assert_close_ulp, bf16_ulp, gemm_tolerance, rel_err, report
 from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -49,7 +50,7 @@ def test_linear_train(name, M, K, N, xs, gs):
         errs[what] = rel_err(got, exact)
     report(f"linear_train {name} vs fp64", **errs)
     for what, e in errs.items():
-        assert e < 3e-3, (what, e)
+        assert e < 2e-3, (what, e)
 
 
 def _ref_attn(q, k, v, causal, allowed=None):
@@ -91,16 +92,30 @@ def test_sdpa_train(name, Hq, Hkv, S, D, causal, qs, gs, vs):
                            [q.cuda(), k.cuda(), v.cuda()], do.cuda())
     ref = orc.sdpa_bwd(q, k, v, do, is_causal=causal)
     exact = _grads(lambda q, k, v: _ref_attn(q, k, v, causal), [q.double(), k.double(), v.double()], do.double())
-    errs, errs_orc = {}, {}
+    # elementwise against the oracle: one bf16 ulp plus the fp16 rounding of P (2^-10 of the head's V scale)
+    # for the output, and for the gradients 2^-9 of the magnitudes the fp16 rounding of P, delta and dS
+    # scale with (oracle abs_dq / abs_dk / abs_dv), plus 2^-24 of what fp16's rounding near zero scales
+    # with (sub_dq / sub_dk / sub_dv: P or dS below fp16's smallest subnormal flush to zero)
+    f = orc.sdpa_fwd(q, k, v, is_causal=causal, v_exp=0)
+    vmax = orc._expand_kv(v.double().abs().amax(dim=(-2, -1), keepdim=True), Hq)
+    two_ev = torch.ldexp(torch.ones(()), orc.expand_heads(f["ev"], Hq).double())[..., None, None]
+    tols = {"o": bf16_ulp(ref["out"]) + 2.0 ** -10 * vmax
+                 + 2.0 ** -21 * f["zmax"][..., None] * (f["pv_abs"] + f["o16"].abs()) * two_ev,
+            "dq": bf16_ulp(ref["dq"]) + 2.0 ** -9 * ref["abs_dq"] + 2.0 ** -24 * ref["sub_dq"],
+            "dk": bf16_ulp(ref["dk"]) + 2.0 ** -9 * ref["abs_dk"] + 2.0 ** -24 * ref["sub_dk"],
+            "dv": bf16_ulp(ref["dv"]) + 2.0 ** -9 * ref["abs_dv"] + 2.0 ** -24 * ref["sub_dv"]}
+    errs, worst = {}, {}
     for got, orc_v, ex, what in ((o, ref["out"], exact[0], "o"), (dq, ref["dq"], exact[1], "dq"),
                                  (dk, ref["dk"], exact[2], "dk"), (dv, ref["dv"], exact[3], "dv")):
         assert torch.isfinite(got.float()).all(), what
-        errs[what], errs_orc[what] = rel_err(got, ex), rel_err(got, orc_v)
+        errs[what] = rel_err(got, ex)
+        d = (got.cpu().double() - orc_v.double()).abs()
+        worst[what] = float((d / tols[what]).max())
     report(f"sdpa_train {name} vs fp64", **errs)
-    report(f"sdpa_train {name} vs oracle", **errs_orc)
+    report(f"sdpa_train {name} vs oracle, worst error / tolerance", **worst)
     for what in errs:
-        assert errs_orc[what] < 4e-3, (what, errs_orc[what])
-        assert errs[what] < 6e-3, (what, errs[what])
+        assert worst[what] <= 1.0, (what, worst[what])
+        assert errs[what] < 2e-3, (what, errs[what])
 
 
 def test_sdpa_train_exponent_G_bit_exact():
@@ -140,4 +155,4 @@ def test_sdpa_train_masks(kind, D):
         errs[what] = rel_err(got, ex)
     report(f"sdpa_train masks {kind} D={D} vs fp64", **errs)
     for what, e in errs.items():
-        assert e < 6e-3, (what, e)
+        assert e < 2e-3, (what, e)
