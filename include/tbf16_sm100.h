@@ -293,7 +293,7 @@ int tbf16_conv_grouped(const void* x, const int64_t* geom, int64_t O, int64_t gr
  * b*mask_sb + h*mask_sh + i*mask_sq + j (strides may be 0 to broadcast). lse (nullable): fp32 (B*Hq, lse_ld)
  * natural-log logsumexp of the scaled, masked logits (the backward wants lse_ld = Sq rounded up to a
  * multiple of 128). o16 (nullable): fp16 (B, Hq, Sq, D) copy of the output before the 2^ev scale (the
- * reference's out16, kept for the backward). D in {64, 128}. */
+ * reference's out16, kept for the backward). D in {64, 128, 256}. */
 int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                    int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev, const void* mask, int64_t mask_sb,
                    int64_t mask_sh, int64_t mask_sq, void* out, float* lse, int64_t lse_ld, void* o16, void* stream);
@@ -320,13 +320,37 @@ int64_t tbf16_attn_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_
  * (dout_sb, dout_sh, dout_ss) and contiguous last dim (dout_d <= D; missing columns are zero).
  * dq (B, Hq, Sq, D), dk, dv (B, Hkv, Sk, D): contiguous bf16. G_out: one int32 (device). flag: device
  * word, bit 2 set if any dS or gradient is non-finite (the caller's overflow check). ws: workspace of
- * tbf16_attn_bwd_workspace_size bytes. D in {64, 128}. */
+ * tbf16_attn_bwd_workspace_size bytes. D in {64, 128, 256}. */
 int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse, int64_t lse_ld,
                    const void* dout,
                    int64_t dout_sb, int64_t dout_sh, int64_t dout_ss, int64_t dout_d, const int32_t* a, const int32_t* ev,
                    int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
                    const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk,
                    void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, void* stream);
+
+/* Attention dropout, the dropout_p of the reference's ScaledSDPAFn / sdpa (tbf16/autograd.py:159-160,
+ * 179-181, passed there to torch's memory-efficient attention): tbf16_attn_fwd_dropout and
+ * tbf16_attn_bwd_dropout are tbf16_attn_fwd_out and tbf16_attn_bwd with the softmax weights of dropped
+ * (query, key) pairs zeroed for P.V and dV (kept ones scaled by 1 / keep probability; the row sum, lse
+ * and delta are those of the undropped softmax, so the output is the unbiased dropout estimate and the
+ * gradients are exact for that output). dropout_p in [0, 1); seed selects the mask, which depends only on
+ * (seed, batch*head, query, key), so the backward with the same seed sees the forward's mask. The mask is
+ * a counter-based hash (murmur3's 32-bit finaliser), not torch's Philox stream: masks differ from the
+ * reference's, their distribution does not. tbf16_attn_dropout_keep writes the mask (1 = kept) as bytes
+ * [BH, Sq, Sk] for checking. */
+int tbf16_attn_fwd_dropout(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
+                           int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
+                           const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out,
+                           int64_t out_sb, int64_t out_sh, int64_t out_ss, float* lse, int64_t lse_ld, void* o16,
+                           float dropout_p, uint64_t seed, void* stream);
+int tbf16_attn_bwd_dropout(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse,
+                           int64_t lse_ld, const void* dout, int64_t dout_sb, int64_t dout_sh, int64_t dout_ss,
+                           int64_t dout_d, const int32_t* a, const int32_t* ev, int64_t B, int64_t Hq, int64_t Hkv,
+                           int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const void* mask, int64_t mask_sb,
+                           int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk, void* dv, int32_t* G_out,
+                           unsigned int* flag, void* ws, int64_t ws_bytes, float dropout_p, uint64_t seed, void* stream);
+int tbf16_attn_dropout_keep(uint8_t* keep, int64_t BH, int64_t Sq, int64_t Sk, float dropout_p, uint64_t seed,
+                            void* stream);
 
 #ifdef __cplusplus
 }

@@ -557,3 +557,40 @@ def to_u16(t: torch.Tensor) -> np.ndarray:
 
 if os.environ.get("TBF16_ORACLE_BUILD_ON_IMPORT"):
     lib()
+
+
+# ----------------------------------------------------------------------------- attention dropout mask
+
+def _fmix32(x: np.ndarray) -> np.ndarray:
+    """murmur3's 32-bit finaliser on uint32 arrays (wrapping arithmetic)."""
+    x = x.astype(np.uint32)
+    x ^= x >> np.uint32(16)
+    x = (x * np.uint32(0x85EBCA6B)).astype(np.uint32)
+    x ^= x >> np.uint32(13)
+    x = (x * np.uint32(0xC2B2AE35)).astype(np.uint32)
+    x ^= x >> np.uint32(16)
+    return x
+
+
+def dropout_params(p: float):
+    """(threshold, 1 / keep probability): a key is kept when its 16 hash bits are >= round(p * 65536)."""
+    thr = int(round(p * 65536.0))
+    return thr, 65536.0 / (65536 - thr)
+
+
+def dropout_keep(seed: int, BH: int, Sq: int, Sk: int, p: float) -> torch.Tensor:
+    """bool (BH, Sq, Sk) keep mask of this build's attention dropout (no counterpart in the reference,
+    whose dropout is torch's Philox stream): row key = fmix32((fmix32(bh ^ seed_lo) + i * 0x9e3779b9) ^
+    seed_hi), pair bits = fmix32(row key ^ (j / 2) * 0x7feb352d), key j takes the low (even j) or high (odd j)
+    16 bits, kept when >= round(p * 65536). Restated here so the GPU's mask can be checked bit for bit."""
+    with np.errstate(over="ignore"):
+        thr, _ = dropout_params(p)
+        s_lo, s_hi = np.uint32(seed & 0xFFFFFFFF), np.uint32((seed >> 32) & 0xFFFFFFFF)
+        bh = np.arange(BH, dtype=np.uint32)[:, None]
+        i = np.arange(Sq, dtype=np.uint32)[None, :]
+        rk = _fmix32(((_fmix32(bh ^ s_lo) + (i * np.uint32(0x9E3779B9)).astype(np.uint32)).astype(np.uint32)) ^ s_hi)
+        j = np.arange(Sk, dtype=np.uint32)
+        jp = ((j >> np.uint32(1)) * np.uint32(0x7FEB352D)).astype(np.uint32)
+        bits = _fmix32(rk[:, :, None] ^ jp[None, None, :])
+        half = np.where((j & 1) == 1, bits >> np.uint32(16), bits & np.uint32(0xFFFF))
+        return torch.from_numpy(half >= thr)

@@ -64,6 +64,11 @@ struct AttnBwdParams {
   unsigned int* err;
   unsigned int* flag;       // bit 2: non-finite values seen
   int q_tiles;
+  // attention dropout (kernels instantiated with DROP): per-row hash keys [B*Hq, lse_ld] from the prep
+  // kernel, keep threshold and 1 / keep probability (see drop_keep)
+  const uint32_t* rowkey;
+  uint32_t drop_thr;
+  float inv_keep;
 };
 
 template <int D>
@@ -80,8 +85,10 @@ struct BwdCfg {
   // for TMA reduce-adds (4 warps x 2 boxes of 4 KB)
   static constexpr bool DQ_T = D == 128;
   static constexpr int DQS_OFF = DS_OFF + 32768;
-  static constexpr int VEC_OFF = DQS_OFF + (DQ_T ? 0 : 32768); // [2 stages] lse (natural log) and delta
-  static constexpr int BAR_OFF = VEC_OFF + 2048;
+  // [2 stages] of the query tile's lse (natural log), delta and (with dropout) row hash keys, 128 each
+  static constexpr int VEC_OFF = DQS_OFF + (DQ_T ? 0 : 32768);
+  static constexpr int VEC_STAGE = 1536;
+  static constexpr int BAR_OFF = VEC_OFF + 2 * VEC_STAGE;
   // the dynamic shared window starts 1024-byte aligned (checked on entry), so no alignment slack
   static constexpr int SMEM = BAR_OFF + 256;
   static constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
@@ -89,7 +96,7 @@ struct BwdCfg {
   static_assert(256 + 2 * D <= 512, "TMEM");
 };
 
-template <int D>
+template <int D, bool DROP>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -174,14 +181,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bh = b * p.Hq + h;
         const int st = t & 1;
         if (!mbar_wait(&q_empty[st], ((t >> 1) & 1) ^ 1, abort, p.err)) break;
-        mbar_arrive_expect_tx(&q_full[st], C::TILE + 1024);
+        mbar_arrive_expect_tx(&q_full[st], C::TILE + 1024 + (DROP ? 512 : 0));
 #pragma unroll
         for (int a = 0; a < C::ATOMS; ++a)
           tma_load_3d(smem + C::Q_OFF + st * C::TILE + a * 16384, &tmQ, &q_full[st], a * 64, q0, bh);
         // this tile's 128 lse and delta values (rows padded to 128, so always in bounds and aligned)
-        float* vec = reinterpret_cast<float*>(smem + C::VEC_OFF + st * 1024);
+        float* vec = reinterpret_cast<float*>(smem + C::VEC_OFF + st * C::VEC_STAGE);
         bulk_load(vec, p.lse + (int64_t)bh * p.lse_ld + q0, 512, &q_full[st]);
         bulk_load(vec + 128, p.delta + (int64_t)bh * p.lse_ld + q0, 512, &q_full[st]);
+        if constexpr (DROP) bulk_load(vec + 256, p.rowkey + (int64_t)bh * p.lse_ld + q0, 512, &q_full[st]);
       }
     }
   } else if (warp == 2) {
@@ -304,13 +312,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     bool bad = false;
     uint32_t pp[32];  // P of this thread's key against the warp's 64 queries, packed fp16 pairs
+    uint64_t keep_bits = 0;  // dropout: bit c set when query column cq + c keeps this key
 
     // P(t): 2^(scale s - lse) for queries [cq, cq + 64), written to TMEM over S^T columns
     // [cq, cq + 32) (inside this warp's own S^T columns) as the A operand of dV += P^T dO
     auto compute_p = [&](int t) -> bool {
       const int h = hk * p.group + t / n_i;
       const int q0 = (i_first + t % n_i) * BQ;
-      const float* lse_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * 1024);
+      const float* lse_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * C::VEC_STAGE);
       if (!mbar_wait_warp(&q_full[t & 1], (t >> 1) & 1, abort, p.err) || !mbar_wait_warp(s_full, t & 1, abort, p.err))
         return false;
       tc_fence_after();
@@ -363,7 +372,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // dV(t-1) has read the previous P^T: it precedes S(t) in the MMA pipe
-      tmem_st32(tmem + lane_base + C::T_S + cq, pp);
+      if constexpr (DROP) {
+        // dV sees P with the dropped entries zeroed (1 / keep probability applied to dV at the end);
+        // dS keeps the full P and this thread's keep bits
+        const uint32_t* rks = reinterpret_cast<const uint32_t*>(lse_s) + 256;
+        uint32_t pt[32];
+        uint64_t kb = 0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const bool k0b = drop_keep(rks[cq + 2 * c], (uint32_t)kj, p.drop_thr);
+          const bool k1b = drop_keep(rks[cq + 2 * c + 1], (uint32_t)kj, p.drop_thr);
+          pt[c] = pp[c] & ((k0b ? 0x0000ffffu : 0u) | (k1b ? 0xffff0000u : 0u));
+          kb |= (uint64_t)((k0b ? 1u : 0u) | (k1b ? 2u : 0u)) << (2 * c);
+        }
+        keep_bits = kb;
+        tmem_st32(tmem + lane_base + C::T_S + cq, pt);
+      } else {
+        tmem_st32(tmem + lane_base + C::T_S + cq, pp);
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -373,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     ok = n_t > 0 && compute_p(0);
     for (int t = 0; ok && t < n_t; ++t) {
-      const float* delta_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * 1024) + 128;
+      const float* delta_s = reinterpret_cast<const float*>(smem + C::VEC_OFF + (t & 1) * C::VEC_STAGE) + 128;
       // ---- dS(t) = P (dP - delta) for this warp's 64 queries (when dP(t) completes, dK(t-1) and
       // dQ(t-1) have read dS(t-1)); masked / padded queries have P = 0 and a finite dP and delta
       // (padding rows of delta are zeroed), so their dS is 0. A dS that does not fit fp16 raises the flag.
@@ -396,8 +422,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 4; u += 2) {
               const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pp[(E + u) >> 1]));
-              const uint64_t dd = f2_fma(u == 0 ? f2_pack(dl.x, dl.y) : f2_pack(dl.z, dl.w), m1,
-                                         f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])));
+              uint64_t dd;
+              if constexpr (DROP) {  // dP of a dropped entry is 0; kept ones are scaled by 1 / keep probability
+                const float g0 = (keep_bits >> (E + u)) & 1 ? p.inv_keep : 0.f;
+                const float g1 = (keep_bits >> (E + u + 1)) & 1 ? p.inv_keep : 0.f;
+                dd = f2_fma(f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])), f2_pack(g0, g1),
+                            f2_mul(u == 0 ? f2_pack(dl.x, dl.y) : f2_pack(dl.z, dl.w), m1));
+              } else {
+                dd = f2_fma(u == 0 ? f2_pack(dl.x, dl.y) : f2_pack(dl.z, dl.w), m1,
+                            f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])));
+              }
               float d0, d1;
               f2_unpack(f2_mul(f2_pack(pf.x, pf.y), dd), d0, d1);
               pk[(e + u) >> 1] = pack_f16(d0, d1);
@@ -423,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n_t > 0 && mbar_wait_warp(kv_done, 0, abort, p.err)) {
       tc_fence_after();
       const float sk = p.scale * exp2i(-__ldg(p.a) - __ldg(p.G));
-      const float sv = exp2i(-__ldg(p.ev + bhk) - __ldg(p.G));
+      const float sv = exp2i(-__ldg(p.ev + bhk) - __ldg(p.G)) * (DROP ? p.inv_keep : 1.f);
       const int64_t orow = ((int64_t)bhk * p.Sk + min(kj, p.Sk - 1)) * D + half * (D / 2);
       bool nf = false;
 #pragma unroll
@@ -574,13 +608,14 @@ constexpr int V_OFF = K_OFF + 65536;
 constexpr int Q_OFF = V_OFF + 65536;        // 4 atoms x 64 rows x 128 B
 constexpr int DO_OFF = Q_OFF + 32768;
 constexpr int DS_OFF = DO_OFF + 32768;      // dS^T: 128 keys x 64 queries fp16, one atom
-constexpr int VEC_OFF = DS_OFF + 16384;     // lse[64], delta[64]
-constexpr int BAR_OFF = VEC_OFF + 512;
+constexpr int VEC_OFF = DS_OFF + 16384;     // lse[64], delta[64], dropout row keys[64]
+constexpr int BAR_OFF = VEC_OFF + 768;
 constexpr int SMEM = BAR_OFF + 256;
 constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_DV = 256, T_DK = 384;
 static_assert(SMEM <= 227 * 1024, "shared memory");
 }  // namespace d256
 
+template <bool DROP>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_d256_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -657,12 +692,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q0 = (i_first + t % n_i) * QROWS;
         const int bh = b * p.Hq + h;
         if (!mbar_wait(q_empty, (t & 1) ^ 1, abort, p.err)) break;
-        mbar_arrive_expect_tx(q_full, 32768 + 512);
+        mbar_arrive_expect_tx(q_full, 32768 + 512 + (DROP ? 256 : 0));
 #pragma unroll
         for (int a = 0; a < 4; ++a) tma_load_3d(smem + Q_OFF + a * 8192, &tmQ, q_full, a * 64, q0, bh);
         float* vec = reinterpret_cast<float*>(smem + VEC_OFF);
         bulk_load(vec, p.lse + (int64_t)bh * p.lse_ld + q0, 256, q_full);
         bulk_load(vec + 64, p.delta + (int64_t)bh * p.lse_ld + q0, 256, q_full);
+        if constexpr (DROP) bulk_load(vec + 128, p.rowkey + (int64_t)bh * p.lse_ld + q0, 256, q_full);
       }
     }
   } else if (warp == 2) {
@@ -753,6 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* vec = reinterpret_cast<const float*>(smem + VEC_OFF);
     bool ok = true, bad = false;
     uint32_t pp[16];  // P of this thread's key against the warp's 32 queries, packed fp16 pairs
+    uint32_t keep_bits = 0;  // dropout: bit c set when query column cq + c keeps this key
 
     auto compute_p = [&](int t) -> bool {
       const int h = hk * p.group + t / n_i;
@@ -777,7 +814,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pp[e >> 1] = pack_f16(pc[0], pc[1]);
       }
-      tmem_st16(tmem + lane_base + T_S + cq, pp);  // P^T over this warp's own S^T columns
+      if constexpr (DROP) {  // dV sees P with dropped entries zeroed; dS keeps the full P and the keep bits
+        const uint32_t* rks = reinterpret_cast<const uint32_t*>(vec) + 128;
+        uint32_t pt[16];
+        uint32_t kb = 0;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const bool k0b = drop_keep(rks[cq + 2 * c], (uint32_t)kj, p.drop_thr);
+          const bool k1b = drop_keep(rks[cq + 2 * c + 1], (uint32_t)kj, p.drop_thr);
+          pt[c] = pp[c] & ((k0b ? 0x0000ffffu : 0u) | (k1b ? 0xffff0000u : 0u));
+          kb |= ((k0b ? 1u : 0u) | (k1b ? 2u : 0u)) << (2 * c);
+        }
+        keep_bits = kb;
+        tmem_st16(tmem + lane_base + T_S + cq, pt);
+      } else {
+        tmem_st16(tmem + lane_base + T_S + cq, pp);  // P^T over this warp's own S^T columns
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -798,8 +850,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pp[e >> 1]));
-          const float d0 = pf.x * (__uint_as_float(rr[e]) - vec[64 + cq + e]);
-          const float d1 = pf.y * (__uint_as_float(rr[e + 1]) - vec[64 + cq + e + 1]);
+          float dp0 = __uint_as_float(rr[e]), dp1 = __uint_as_float(rr[e + 1]);
+          if constexpr (DROP) {
+            dp0 = (keep_bits >> e) & 1 ? dp0 * p.inv_keep : 0.f;
+            dp1 = (keep_bits >> (e + 1)) & 1 ? dp1 * p.inv_keep : 0.f;
+          }
+          const float d0 = pf.x * (dp0 - vec[64 + cq + e]);
+          const float d1 = pf.y * (dp1 - vec[64 + cq + e + 1]);
           pk[e >> 1] = pack_f16(d0, d1);
           ovf |= __vcmpeq2(pk[e >> 1] & 0x7c007c00u, 0x7c007c00u);
         }
@@ -822,7 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n_t > 0 && mbar_wait_warp(kv_done, 0, abort, p.err)) {
       tc_fence_after();
       const float sk = p.scale * exp2i(-__ldg(p.a) - __ldg(p.G));
-      const float sv = exp2i(-__ldg(p.ev + bhk) - __ldg(p.G));
+      const float sv = exp2i(-__ldg(p.ev + bhk) - __ldg(p.G)) * (DROP ? p.inv_keep : 1.f);
       bool nf = false;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
@@ -922,7 +979,8 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const uint16_t* __re
                                                             const int32_t* __restrict__ ev, const int32_t* __restrict__ G,
                                                             int Hq, int Hkv, int group, int Sq, int64_t rows,
                                                             int64_t lse_ld, __half* __restrict__ do16,
-                                                            float* __restrict__ delta) {
+                                                            float* __restrict__ delta, uint32_t* __restrict__ rowkey,
+                                                            uint32_t seed_lo, uint32_t seed_hi) {
   constexpr int TPR = D / 8;
   const int64_t row = (int64_t)blockIdx.x * (256 / TPR) + threadIdx.x / TPR;
   const int c = (threadIdx.x % TPR) * 8;
@@ -952,7 +1010,11 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const uint16_t* __re
   }
 #pragma unroll
   for (int o = TPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (row < rows && threadIdx.x % TPR == 0) delta[(row / Sq) * lse_ld + row % Sq] = acc;
+  if (row < rows && threadIdx.x % TPR == 0) {
+    delta[(row / Sq) * lse_ld + row % Sq] = acc;
+    if (rowkey)
+      rowkey[(row / Sq) * lse_ld + row % Sq] = drop_row_key(seed_lo, seed_hi, (uint32_t)(row / Sq), (uint32_t)(row % Sq));
+  }
 }
 
 // dq = bf16(dq_acc * scale * 2^(a - G)), contiguous (B, Hq, Sq, D).
@@ -975,6 +1037,7 @@ struct Workspace {
   __half* do16;
   float* delta;
   float* amax;
+  uint32_t* rowkey;  // dropout row hash keys, [B*Hq, lse_ld]
 };
 
 int64_t lse_stride(int64_t Sq) { return (Sq + 127) / 128 * 128; }
@@ -990,16 +1053,18 @@ Workspace carve(void* ws, int64_t B, int64_t Hq, int64_t Sq, int64_t D) {
   w.delta = reinterpret_cast<float*>(p);
   p += ((4 * B * Hq * lse_stride(Sq) + 255) / 256) * 256;
   w.amax = reinterpret_cast<float*>(p);
+  p += ((4 * B * Hq + 255) / 256) * 256;
+  w.rowkey = reinterpret_cast<uint32_t*>(p);
   return w;
 }
 
 int64_t workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D) {
   const int64_t n = B * Hq * Sq * D;
-  return ((4 * n + 255) / 256) * 256 + ((2 * n + 255) / 256) * 256 + ((4 * B * Hq * lse_stride(Sq) + 255) / 256) * 256 +
+  return ((4 * n + 255) / 256) * 256 + ((2 * n + 255) / 256) * 256 + 2 * ((4 * B * Hq * lse_stride(Sq) + 255) / 256) * 256 +
          ((4 * B * Hq + 255) / 256) * 256;
 }
 
-template <int D>
+template <int D, bool DROP>
 int launch_bwd(const void* q16, const void* k16, const void* v16, const void* do16, const AttnBwdParams& prm,
                int64_t Sk, cudaStream_t st) {
   using C = BwdCfg<D>;
@@ -1013,15 +1078,16 @@ int launch_bwd(const void* q16, const void* k16, const void* v16, const void* do
   if (int rc = tbf16_host::make_tmap_3d_f32(&tdq, prm.dq_acc, D, prm.Sq, BHq, D, (uint64_t)prm.Sq * D, 32, 32)) return rc;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->device & 63]) {
-    if (cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_bwd_kernel<D, DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
   dim3 grid((unsigned)BHk, (unsigned)((Sk + BKV - 1) / BKV));
-  attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
+  attn_bwd_kernel<D, DROP><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
   return tbf16_host::check_launch();
 }
 
+template <bool DROP>
 int launch_bwd_d256(const void* q16, const void* k16, const void* v16, const void* do16, AttnBwdParams prm, int64_t Sk,
                     cudaStream_t st) {
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
@@ -1034,13 +1100,14 @@ int launch_bwd_d256(const void* q16, const void* k16, const void* v16, const voi
   if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, Sk, BHk, D, (uint64_t)Sk * D, 64, d256::KROWS)) return rc;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->device & 63]) {
-    if (cudaFuncSetAttribute(attn_bwd_d256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d256::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_bwd_d256_kernel<DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize, d256::SMEM) !=
+        cudaSuccess)
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
   prm.q_tiles = (int)((prm.Sq + d256::QROWS - 1) / d256::QROWS);
   dim3 grid((unsigned)BHk, (unsigned)((Sk + d256::KROWS - 1) / d256::KROWS), 2);
-  attn_bwd_d256_kernel<<<grid, kThreads, d256::SMEM, st>>>(tq, tk, tv, tdo, prm);
+  attn_bwd_d256_kernel<DROP><<<grid, kThreads, d256::SMEM, st>>>(tq, tk, tv, tdo, prm);
   return tbf16_host::check_launch();
 }
 
@@ -1055,13 +1122,22 @@ int64_t tbf16_attn_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_
   return workspace_bytes(B, Hq, Sq, D);
 }
 
-int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse, int64_t lse_ld,
-                   const void* dout,
-                   int64_t dout_sb, int64_t dout_sh, int64_t dout_ss, int64_t dout_d, const int32_t* a, const int32_t* ev,
-                   int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
-                   const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk,
-                   void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int attn_bwd_impl(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse, int64_t lse_ld,
+                  const void* dout, int64_t dout_sb, int64_t dout_sh, int64_t dout_ss, int64_t dout_d, const int32_t* a,
+                  const int32_t* ev, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale,
+                  int causal, const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, int t_do, void* dq,
+                  void* dk, void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, float dropout_p,
+                  uint64_t seed, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
+  uint32_t thr = 0;
+  float inv_keep = 1.f;
+  if (!tbf16_host::dropout_params(dropout_p, &thr, &inv_keep)) return TBF16_ERR_INVALID;
+  const bool drop = thr > 0;
+  const uint32_t seed_lo = (uint32_t)seed, seed_hi = (uint32_t)(seed >> 32);
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq <= 0 || Sk <= 0 || dout_d <= 0 || dout_d > D || !a || !ev ||
       !lse || lse_ld != lse_stride(Sq) || !G_out || !flag || !ws || B * Hq > 65535 || B * Hkv > 65535)
     return TBF16_ERR_INVALID;
@@ -1088,15 +1164,18 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
   if (D == 64)
     attn_bwd_prep_kernel<64><<<pgrid, 256, 0, st>>>(static_cast<const uint16_t*>(dout), dout_sb, dout_sh, dout_ss,
                                                     (int)dout_d, static_cast<const __half*>(o16), ev, G_out, (int)Hq,
-                                                    (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta);
+                                                    (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta,
+                                                     drop ? w.rowkey : nullptr, seed_lo, seed_hi);
   else if (D == 128)
     attn_bwd_prep_kernel<128><<<pgrid, 256, 0, st>>>(static_cast<const uint16_t*>(dout), dout_sb, dout_sh, dout_ss,
                                                      (int)dout_d, static_cast<const __half*>(o16), ev, G_out, (int)Hq,
-                                                     (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta);
+                                                     (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta,
+                                                     drop ? w.rowkey : nullptr, seed_lo, seed_hi);
   else
     attn_bwd_prep_kernel<256><<<pgrid, 256, 0, st>>>(static_cast<const uint16_t*>(dout), dout_sb, dout_sh, dout_ss,
                                                      (int)dout_d, static_cast<const __half*>(o16), ev, G_out, (int)Hq,
-                                                     (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta);
+                                                     (int)Hkv, group, (int)Sq, rows, lse_ld, w.do16, w.delta,
+                                                     drop ? w.rowkey : nullptr, seed_lo, seed_hi);
   // 3. main kernel (dQ accumulated in fp32)
   if (cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * rows * D, st) != cudaSuccess) return TBF16_ERR_LAUNCH;
   AttnBwdParams prm;
@@ -1113,9 +1192,18 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
   prm.err = dev->err;
   prm.flag = flag;
   prm.q_tiles = (int)((Sq + BQ - 1) / BQ);
-  int rc = D == 64    ? launch_bwd<64>(q16, k16, v16, w.do16, prm, Sk, st)
-           : D == 128 ? launch_bwd<128>(q16, k16, v16, w.do16, prm, Sk, st)
-                      : launch_bwd_d256(q16, k16, v16, w.do16, prm, Sk, st);
+  prm.rowkey = w.rowkey;
+  prm.drop_thr = thr;
+  prm.inv_keep = inv_keep;
+  int rc;
+  if (drop)
+    rc = D == 64    ? launch_bwd<64, true>(q16, k16, v16, w.do16, prm, Sk, st)
+         : D == 128 ? launch_bwd<128, true>(q16, k16, v16, w.do16, prm, Sk, st)
+                    : launch_bwd_d256<true>(q16, k16, v16, w.do16, prm, Sk, st);
+  else
+    rc = D == 64    ? launch_bwd<64, false>(q16, k16, v16, w.do16, prm, Sk, st)
+         : D == 128 ? launch_bwd<128, false>(q16, k16, v16, w.do16, prm, Sk, st)
+                    : launch_bwd_d256<false>(q16, k16, v16, w.do16, prm, Sk, st);
   if (rc) return rc;
   // 4. dq
   const int64_t n4 = rows * D / 4;
@@ -1123,6 +1211,33 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
   attn_bwd_dq_kernel<<<g, 256, 0, st>>>(reinterpret_cast<const float4*>(w.dq_acc), n4, scale, a, G_out,
                                         static_cast<uint2*>(dq), flag);
   return tbf16_host::check_launch();
+}
+
+}  // namespace
+
+extern "C" {
+
+int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse, int64_t lse_ld,
+                   const void* dout,
+                   int64_t dout_sb, int64_t dout_sh, int64_t dout_ss, int64_t dout_d, const int32_t* a, const int32_t* ev,
+                   int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
+                   const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk,
+                   void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, void* stream) {
+  return attn_bwd_impl(q16, k16, v16, o16, lse, lse_ld, dout, dout_sb, dout_sh, dout_ss, dout_d, a, ev, B, Hq, Hkv, Sq,
+                       Sk, D, scale, causal, mask, mask_sb, mask_sh, mask_sq, t_do, dq, dk, dv, G_out, flag, ws, ws_bytes,
+                       0.f, 0, stream);
+}
+
+int tbf16_attn_bwd_dropout(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse,
+                           int64_t lse_ld, const void* dout, int64_t dout_sb, int64_t dout_sh, int64_t dout_ss,
+                           int64_t dout_d, const int32_t* a, const int32_t* ev, int64_t B, int64_t Hq, int64_t Hkv,
+                           int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const void* mask, int64_t mask_sb,
+                           int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk, void* dv, int32_t* G_out,
+                           unsigned int* flag, void* ws, int64_t ws_bytes, float dropout_p, uint64_t seed,
+                           void* stream) {
+  return attn_bwd_impl(q16, k16, v16, o16, lse, lse_ld, dout, dout_sb, dout_sh, dout_ss, dout_d, a, ev, B, Hq, Hkv, Sq,
+                       Sk, D, scale, causal, mask, mask_sb, mask_sh, mask_sq, t_do, dq, dk, dv, G_out, flag, ws, ws_bytes,
+                       dropout_p, seed, stream);
 }
 
 }  // extern "C"

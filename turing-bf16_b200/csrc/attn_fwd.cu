@@ -45,6 +45,9 @@ struct AttnFwdParams {
   int64_t mb, mh, mi;
   unsigned int* err;
   int m_tiles;
+  // attention dropout (kernels instantiated with DROP): keep threshold, seed, 1 / keep probability
+  uint32_t drop_thr, seed_lo, seed_hi;
+  float inv_keep;
 };
 
 template <int D>
@@ -65,7 +68,7 @@ struct FwdCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-template <int D>
+template <int D, bool DROP>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
@@ -192,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quad * 32 + lane;  // query row within the tile
     const int qi = m0 + r;           // query index
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -253,6 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float p0 = ex2(fmaf(s[c], c_scale, -base)), p1 = ex2(fmaf(s[c + 1], c_scale, -base));
         sum8[(c >> 1) & 7] += p0 + p1;
         pk[c / 2] = pack_f16(p0, p1);
+        if constexpr (DROP) pk[c / 2] &= drop_pair_mask(rk, (uint32_t)(k0 + c) >> 1, p.drop_thr);
       }
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       // O and the P buffer are free once the previous P.V has completed
@@ -281,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && n_kv > 0 && mbar_wait_warp(pv_done, (n_kv - 1) & 1, abort, p.err)) {
       tc_fence_after();
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float inv_l = l > 0.f ? (DROP ? p.inv_keep : 1.f) / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
       __nv_bfloat16* orow = p.out + (int64_t)(bh / p.Hq) * p.osb + (int64_t)(bh % p.Hq) * p.osh +
                             (int64_t)min(qi, p.Sq - 1) * p.oss;
@@ -363,7 +368,7 @@ struct FwdPPCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-template <int D>
+template <int D, bool DROP>
 __global__ void __launch_bounds__(kPPThreads, 1)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
@@ -527,6 +532,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + t * 256;
     const uint32_t o_addr = s_addr + 128;
+    const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -587,6 +593,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
         sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
         rr[e >> 1] = pack_f16(p0, p1);
+        // dropout: the row sum keeps every key; P.V sees only the kept ones (scaled back at the end)
+        if constexpr (DROP) rr[e >> 1] &= drop_pair_mask(rk, (uint32_t)(k0 + e) >> 1, p.drop_thr);
       }
       {
         float a0, a1;
@@ -622,7 +630,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     }
     if (ok && nt > 0 && mbar_wait_warp(&pv_done[t], 0, abort, p.err)) {
       tc_fence_after();
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float inv_l = l > 0.f ? (DROP ? p.inv_keep : 1.f) / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
       __nv_bfloat16* orow = p.out + (int64_t)(bh / p.Hq) * p.osb + (int64_t)(bh % p.Hq) * p.osh +
                             (int64_t)min(qi, p.Sq - 1) * p.oss;
@@ -664,7 +672,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   }
 }
 
-template <int D>
+template <int D, bool DROP>
 int launch_fwd_pp(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
   using C = FwdPPCfg<D>;
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
@@ -676,16 +684,17 @@ int launch_fwd_pp(const void* q16, const void* k16, const void* v16, const AttnF
   if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, prm.Sk, BHk, D, (uint64_t)prm.Sk * D, 64, BN)) return rc;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->device & 63]) {
-    if (cudaFuncSetAttribute(attn_fwd_pp_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_fwd_pp_kernel<D, DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
   dim3 grid = prm.causal ? dim3((unsigned)BHq, (prm.m_tiles + 1) / 2) : dim3((prm.m_tiles + 1) / 2, (unsigned)BHq);
-  attn_fwd_pp_kernel<D><<<grid, kPPThreads, C::SMEM, st>>>(tq, tk, tv, prm);
+  attn_fwd_pp_kernel<D, DROP><<<grid, kPPThreads, C::SMEM, st>>>(tq, tk, tv, prm);
   return tbf16_host::check_launch();
 }
 
-template <int D>
+template <int D, bool DROP>
 int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
   using C = FwdCfg<D>;
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
@@ -697,12 +706,12 @@ int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdP
   if (int rc = tbf16_host::make_tmap_3d(&tv, v16, D, prm.Sk, BHk, D, (uint64_t)prm.Sk * D, 64, BN)) return rc;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->device & 63]) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_fwd_kernel<D, DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
   const dim3 grid = prm.causal ? dim3((unsigned)BHq, prm.m_tiles) : dim3(prm.m_tiles, (unsigned)BHq);
-  attn_fwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
+  attn_fwd_kernel<D, DROP><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
   return tbf16_host::check_launch();
 }
 
@@ -716,12 +725,16 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
                             Hq * Sq * D, Sq * D, D, lse, lse_ld, o16, stream);
 }
 
-extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,
-                                  int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
-                                  const int32_t* ev, const void* mask, int64_t mask_sb, int64_t mask_sh,
-                                  int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh, int64_t out_ss,
-                                  float* lse, int64_t lse_ld, void* o16, void* stream) {
+static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
+                         int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
+                         const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, int64_t out_sb,
+                         int64_t out_sh, int64_t out_ss, float* lse, int64_t lse_ld, void* o16, float dropout_p,
+                         uint64_t seed, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
+  uint32_t thr = 0;
+  float inv_keep = 1.f;
+  if (!tbf16_host::dropout_params(dropout_p, &thr, &inv_keep)) return TBF16_ERR_INVALID;
+  const bool drop = thr > 0;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq < 0 || Sk < 0 || !ev || !out || B * Hq > 65535 ||
       Sq > INT32_MAX || Sk > INT32_MAX)
     return TBF16_ERR_INVALID;
@@ -750,6 +763,10 @@ extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* 
   prm.mb = mask_sb; prm.mh = mask_sh; prm.mi = mask_sq;
   prm.err = dev->err;
   prm.m_tiles = (int)((Sq + BM - 1) / BM);
+  prm.drop_thr = thr;
+  prm.seed_lo = (uint32_t)seed;
+  prm.seed_hi = (uint32_t)(seed >> 32);
+  prm.inv_keep = inv_keep;
   if (Sk == 0) return TBF16_ERR_UNSUPPORTED;
   auto st = static_cast<cudaStream_t>(stream);
   // D <= 128: the two-query-tile kernel (P in TMEM); TBF16_ATTN_FWD=1 selects the one-tile kernel
@@ -757,7 +774,62 @@ extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* 
     const char* e = getenv("TBF16_ATTN_FWD");
     return e && e[0] == '1';
   }();
-  if (D == 64) return one_cta ? launch_fwd<64>(q16, k16, v16, prm, st) : launch_fwd_pp<64>(q16, k16, v16, prm, st);
-  if (D == 128) return one_cta ? launch_fwd<128>(q16, k16, v16, prm, st) : launch_fwd_pp<128>(q16, k16, v16, prm, st);
-  return launch_fwd<256>(q16, k16, v16, prm, st);
+  if (drop) {
+    if (D == 64) return one_cta ? launch_fwd<64, true>(q16, k16, v16, prm, st) : launch_fwd_pp<64, true>(q16, k16, v16, prm, st);
+    if (D == 128)
+      return one_cta ? launch_fwd<128, true>(q16, k16, v16, prm, st) : launch_fwd_pp<128, true>(q16, k16, v16, prm, st);
+    return launch_fwd<256, true>(q16, k16, v16, prm, st);
+  }
+  if (D == 64) return one_cta ? launch_fwd<64, false>(q16, k16, v16, prm, st) : launch_fwd_pp<64, false>(q16, k16, v16, prm, st);
+  if (D == 128)
+    return one_cta ? launch_fwd<128, false>(q16, k16, v16, prm, st) : launch_fwd_pp<128, false>(q16, k16, v16, prm, st);
+  return launch_fwd<256, false>(q16, k16, v16, prm, st);
+}
+
+extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,
+                                  int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
+                                  const int32_t* ev, const void* mask, int64_t mask_sb, int64_t mask_sh,
+                                  int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh, int64_t out_ss,
+                                  float* lse, int64_t lse_ld, void* o16, void* stream) {
+  return attn_fwd_impl(q16, k16, v16, B, Hq, Hkv, Sq, Sk, D, scale, causal, ev, mask, mask_sb, mask_sh, mask_sq, out,
+                       out_sb, out_sh, out_ss, lse, lse_ld, o16, 0.f, 0, stream);
+}
+
+extern "C" int tbf16_attn_fwd_dropout(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,
+                                      int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale, int causal,
+                                      const int32_t* ev, const void* mask, int64_t mask_sb, int64_t mask_sh,
+                                      int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh, int64_t out_ss,
+                                      float* lse, int64_t lse_ld, void* o16, float dropout_p, uint64_t seed,
+                                      void* stream) {
+  return attn_fwd_impl(q16, k16, v16, B, Hq, Hkv, Sq, Sk, D, scale, causal, ev, mask, mask_sb, mask_sh, mask_sq, out,
+                       out_sb, out_sh, out_ss, lse, lse_ld, o16, dropout_p, seed, stream);
+}
+
+namespace {
+__global__ void dropout_keep_kernel(uint8_t* __restrict__ keep, int64_t BH, int64_t Sq, int64_t Sk, uint32_t thr,
+                                    uint32_t seed_lo, uint32_t seed_hi) {
+  const int64_t n = BH * Sq * Sk;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / Sk;
+    const uint32_t j = (uint32_t)(idx % Sk);
+    const uint32_t rk = drop_row_key(seed_lo, seed_hi, (uint32_t)(row / Sq), (uint32_t)(row % Sq));
+    keep[idx] = drop_keep(rk, j, thr) ? 1 : 0;
+  }
+}
+}  // namespace
+
+extern "C" int tbf16_attn_dropout_keep(uint8_t* keep, int64_t BH, int64_t Sq, int64_t Sk, float dropout_p,
+                                       uint64_t seed, void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  uint32_t thr = 0;
+  float inv_keep = 1.f;
+  if (!keep || BH < 0 || Sq < 0 || Sk < 0 || !tbf16_host::dropout_params(dropout_p, &thr, &inv_keep))
+    return TBF16_ERR_INVALID;
+  const int64_t n = BH * Sq * Sk;
+  if (n == 0) return TBF16_OK;
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)dev->sms * 32);
+  dropout_keep_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(keep, BH, Sq, Sk, thr, (uint32_t)seed,
+                                                                           (uint32_t)(seed >> 32));
+  return tbf16_host::check_launch();
 }

@@ -460,6 +460,36 @@ __device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& 
   p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
+// ------------------------------------------------------------------ attention dropout
+// keep(bh, i, j) for query row i and key j of head bh, identical in the forward and backward kernels: a
+// counter-based hash (murmur3's 32-bit finaliser) of a per-row key and the key pair j / 2 gives 32 bits,
+// 16 per key of the pair; a key is kept when its 16 bits are >= thr = round(p * 65536), so the keep
+// probability is exactly (65536 - thr) / 65536 and kept values are scaled by its inverse.
+__host__ __device__ __forceinline__ uint32_t fmix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x85ebca6bu;
+  x ^= x >> 13;
+  x *= 0xc2b2ae35u;
+  x ^= x >> 16;
+  return x;
+}
+__host__ __device__ __forceinline__ uint32_t drop_row_key(uint32_t seed_lo, uint32_t seed_hi, uint32_t bh, uint32_t i) {
+  return fmix32((fmix32(bh ^ seed_lo) + i * 0x9e3779b9u) ^ seed_hi);
+}
+__host__ __device__ __forceinline__ uint32_t drop_pair_bits(uint32_t row_key, uint32_t j_pair) {
+  return fmix32(row_key ^ (j_pair * 0x7feb352du));
+}
+// Keep mask of keys (2 jp, 2 jp + 1) as a packed-fp16 lane mask (0xffff per kept half).
+__device__ __forceinline__ uint32_t drop_pair_mask(uint32_t row_key, uint32_t j_pair, uint32_t thr) {
+  const uint32_t bits = drop_pair_bits(row_key, j_pair);
+  return ((bits & 0xffffu) >= thr ? 0x0000ffffu : 0u) | ((bits >> 16) >= thr ? 0xffff0000u : 0u);
+}
+// Whether key j is kept in row `row_key` (the backward's per-element form).
+__device__ __forceinline__ bool drop_keep(uint32_t row_key, uint32_t j, uint32_t thr) {
+  const uint32_t bits = drop_pair_bits(row_key, j >> 1);
+  return ((j & 1) ? (bits >> 16) : (bits & 0xffffu)) >= thr;
+}
+
 // Byte offset of 16-byte chunk c (0..15 for 128 fp16 columns) of row r in a K-major tile made of
 // 64-column 128B-swizzled atoms of 128 rows each.
 __device__ __forceinline__ uint32_t swz_off(int r, int c) {
@@ -537,4 +567,15 @@ int make_tmap_2d_out(CUtensorMap* map, const void* base, uint64_t cols, uint64_t
 // The same for fp32 elements with a 64- or 128-byte swizzle (box0 * 4 <= the swizzle span).
 int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                      uint64_t stride2, uint32_t box0, uint32_t box1, int swizzle_bytes = 128);
+// Attention dropout: threshold (a key is kept when its 16 hash bits are >= thr) and 1 / keep probability
+// for dropout_p in [0, 1); false outside that range.
+inline bool dropout_params(float dropout_p, uint32_t* thr, float* inv_keep) {
+  if (!(dropout_p >= 0.f && dropout_p < 1.f)) return false;
+  const uint32_t t = (uint32_t)lrintf(dropout_p * 65536.f);
+  if (t >= 65536u) return false;
+  *thr = t;
+  *inv_keep = 65536.f / (float)(65536u - t);
+  return true;
+}
+
 }  // namespace tbf16_host

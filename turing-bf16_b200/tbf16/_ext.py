@@ -57,6 +57,12 @@ SIGNATURES = {
     "tbf16_attn_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                        _i64,
                        ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
+    "tbf16_attn_fwd_dropout": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64,
+                               _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, ctypes.c_float, ctypes.c_uint64, _vp],
+    "tbf16_attn_bwd_dropout": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64,
+                               _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp,
+                               _vp, _vp, _i64, ctypes.c_float, ctypes.c_uint64, _vp],
+    "tbf16_attn_dropout_keep": [_vp, _i64, _i64, _i64, ctypes.c_float, ctypes.c_uint64, _vp],
     "tbf16_device_check": [_i32],
     "tbf16_device_status": [_vp, _i32],
     "tbf16_selftest_bounded_wait": [ctypes.c_uint64, _vp],

@@ -105,10 +105,18 @@ def additive_mask(attn_mask, B, H, Sq, Sk, device):
     return m
 
 
+def dropout_seed() -> int:
+    """A 64-bit seed for the attention dropout mask, drawn from torch's default CPU generator (so
+    torch.manual_seed makes the masks reproducible)."""
+    lo, hi = torch.randint(0, 1 << 32, (2,), dtype=torch.int64).tolist()
+    return (hi << 32) | lo
+
+
 def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None, d_orig=None, need_lse=False,
-                 need_o16=False):
+                 need_o16=False, dropout_p=0.0, seed=0):
     """The tcgen05 forward on prepared fp16 operands -> (bf16 out (B, Hq, Sq, D), lse or None), plus the
-    fp16 pre-scale output o16 when need_o16 (then the return is (out, lse, o16), all at the kernel's D)."""
+    fp16 pre-scale output o16 when need_o16 (then the return is (out, lse, o16), all at the kernel's D).
+    dropout_p > 0 drops softmax weights by the mask `seed` selects (tbf16_attn_fwd_dropout)."""
     B, Hq, Sq, D = q16.shape
     Hkv, Sk = k16.shape[1], k16.shape[2]
     d_orig = d_orig or D
@@ -130,8 +138,12 @@ def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None,
     o16 = torch.empty((B, Hq, Sq, Dk), device=dev, dtype=torch.float16) if need_o16 else None
     m = additive_mask(attn_mask, B, Hq, Sq, Sk, dev)
     ms = m.stride()[:3] if m is not None else (0, 0, 0)
-    call("tbf16_attn_fwd_out", ptr(q16), ptr(k16), ptr(v16), B, Hq, Hkv, Sq, Sk, Dk, sc, int(bool(is_causal)),
-         ptr(ev.contiguous()), ptr(m), *ms, ptr(out), *out.stride()[:3], ptr(lse), lse_ld, ptr(o16), stream_ptr(dev))
+    args = (ptr(q16), ptr(k16), ptr(v16), B, Hq, Hkv, Sq, Sk, Dk, sc, int(bool(is_causal)), ptr(ev.contiguous()), ptr(m),
+            *ms, ptr(out), *out.stride()[:3], ptr(lse), lse_ld, ptr(o16))
+    if dropout_p:
+        call("tbf16_attn_fwd_dropout", *args, float(dropout_p), int(seed), stream_ptr(dev))
+    else:
+        call("tbf16_attn_fwd_out", *args, stream_ptr(dev))
     if need_o16:
         return out, lse, o16
     if Dk != D:
@@ -143,12 +155,11 @@ def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None,
 def sdpa(q, k, v, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, enable_gqa=False):
     """Inference scaled attention (reference attention.py:56-65): V's max near 2^13 keeps channels far
     below it out of fp16's subnormals; the output is a convex combination of V rows, so it cannot
-    overflow."""
-    if dropout_p:
-        raise NotImplementedError("tbf16.sdpa: attention dropout is not implemented on B200 (inference path)")
+    overflow. dropout_p is applied as the reference passes it on to torch's SDPA (a fresh mask per call)."""
     if q.shape[1] != k.shape[1] and not enable_gqa:
         raise RuntimeError("tbf16.sdpa: different numbers of query and key heads need enable_gqa=True")
     D0 = q.shape[-1]
     q16, k16, v16, _, ev = prepare_qkv(q, k, v, v_exp=13)
-    out, _ = attn_forward(q16, k16, v16, ev, attn_mask, is_causal, scale, d_orig=D0)
+    seed = dropout_seed() if dropout_p else 0
+    out, _ = attn_forward(q16, k16, v16, ev, attn_mask, is_causal, scale, d_orig=D0, dropout_p=dropout_p, seed=seed)
     return out[..., :D0] if out.shape[-1] != D0 else out

@@ -211,11 +211,12 @@ def linear(x, w, bias=None):
     return ScaledLinearFn.apply(x, w, bias)
 
 
-def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale, d_orig, t_do_offset=0):
+def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale, d_orig, t_do_offset=0,
+                  dropout_p=0.0, seed=0):
     """Runs tbf16_attn_bwd with the reference's retry loop: t_do = 12 - ceil(log2 d), lowered by 8 and
     redone while the kernel reports a non-finite value (at most 6 attempts). t_do_offset (>= 0) lowers
     the target further: a head-sharded call passes how far the global dO exponent exceeds its own heads'
-    maximum, so G comes out as the unsharded call's."""
+    maximum, so G comes out as the unsharded call's. dropout_p, seed: the forward's dropout mask."""
     B, Hq, Sq, Dk = q16.shape
     Hkv, Sk = k16.shape[1], k16.shape[2]
     dev = q16.device
@@ -234,10 +235,13 @@ def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale
     t_do = 12 - math.ceil(math.log2(d_orig)) - int(t_do_offset)
     for _attempt in range(6):
         flag.zero_()
-        call("tbf16_attn_bwd", ptr(q16), ptr(k16), ptr(v16), ptr(o16), ptr(lse), lse.shape[-1], ptr(dout),
-             *dout.stride()[:3],
-             dout.shape[-1], ptr(a), ptr(ev), B, Hq, Hkv, Sq, Sk, Dk, float(scale), int(bool(is_causal)), ptr(mask16),
-             *ms, int(t_do), ptr(dq), ptr(dk), ptr(dv), ptr(G), ptr(flag), ptr(ws), nbytes, stream_ptr(dev))
+        args = (ptr(q16), ptr(k16), ptr(v16), ptr(o16), ptr(lse), lse.shape[-1], ptr(dout), *dout.stride()[:3],
+                dout.shape[-1], ptr(a), ptr(ev), B, Hq, Hkv, Sq, Sk, Dk, float(scale), int(bool(is_causal)), ptr(mask16),
+                *ms, int(t_do), ptr(dq), ptr(dk), ptr(dv), ptr(G), ptr(flag), ptr(ws), nbytes)
+        if dropout_p:
+            call("tbf16_attn_bwd_dropout", *args, float(dropout_p), int(seed), stream_ptr(dev))
+        else:
+            call("tbf16_attn_bwd", *args, stream_ptr(dev))
         if not CHECK_OVERFLOW:
             break
         if not bool(flag):  # host sync, once per attention call
@@ -255,8 +259,6 @@ class ScaledSDPAFn(torch.autograd.Function):
     @staticmethod
     @torch.autocast("cuda", enabled=False)
     def forward(ctx, q, k, v, attn_mask, dropout_p, is_causal, scale, enable_gqa):
-        if dropout_p:
-            raise NotImplementedError("tbf16 attention dropout is not implemented on B200")
         if q.shape[1] != k.shape[1] and not enable_gqa:
             raise RuntimeError("tbf16.sdpa: different numbers of query and key heads need enable_gqa=True")
         D0 = q.shape[-1]
@@ -269,20 +271,23 @@ class ScaledSDPAFn(torch.autograd.Function):
             q16, k16, v16 = (F.pad(t, (0, Dk - D)) for t in (q16, k16, v16))
         sc = 1.0 / math.sqrt(D0) if scale is None else float(scale)
         mask16 = attention.additive_mask(attn_mask, B, Hq, Sq, k.shape[2], q.device)
-        out, lse, o16 = attention.attn_forward(q16, k16, v16, ev, mask16, is_causal, sc, need_lse=True, need_o16=True)
+        seed = attention.dropout_seed() if dropout_p else 0
+        out, lse, o16 = attention.attn_forward(q16, k16, v16, ev, mask16, is_causal, sc, need_lse=True, need_o16=True,
+                                               dropout_p=dropout_p, seed=seed)
         ctx.save_for_backward(q16, k16, v16, o16, lse, a, ev, mask16)
-        ctx.args = (is_causal, sc, D0)
+        ctx.args = (is_causal, sc, D0, float(dropout_p), seed)
         return out[..., :D0].contiguous() if Dk != D0 else out
 
     @staticmethod
     @torch.autocast("cuda", enabled=False)
     def backward(ctx, dout):
         q16, k16, v16, o16, lse, a, ev, mask16 = ctx.saved_tensors
-        is_causal, sc, D0 = ctx.args
+        is_causal, sc, D0, dropout_p, seed = ctx.args
         Dk = q16.shape[-1]
         if D0 % 8:
             dout = F.pad(dout, (0, 8 - D0 % 8))
-        dq, dk, dv, _ = attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, sc, D0)
+        dq, dk, dv, _ = attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, sc, D0,
+                                      dropout_p=dropout_p, seed=seed)
         if Dk != D0:
             dq, dk, dv = (t[..., :D0].contiguous() for t in (dq, dk, dv))
         return dq, dk, dv, None, None, None, None, None
