@@ -352,6 +352,19 @@ int tbf16_attn_bwd_dropout(const void* q16, const void* k16, const void* v16, co
 int tbf16_attn_dropout_keep(uint8_t* keep, int64_t BH, int64_t Sq, int64_t Sk, float dropout_p, uint64_t seed,
                             void* stream);
 
+/* The backward of one rank's heads in a head-sharded call (no counterpart in the reference, whose
+ * ScaledSDPAFn sees every head in one process): tbf16_attn_bwd_dropout with the dO exponent taken as
+ * max(this rank's heads, *e_global), where e_global (device int32) is the all_reduce(MAX) over the ranks
+ * of max_{b,h}(head_exp(dout) + ev_q) (autograd.py:175 there), so G, and with it every gradient, equals
+ * the unsharded call's without a host round trip. dropout_p = 0 for no dropout. */
+int tbf16_attn_bwd_sharded(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse,
+                           int64_t lse_ld, const void* dout, int64_t dout_sb, int64_t dout_sh, int64_t dout_ss,
+                           int64_t dout_d, const int32_t* a, const int32_t* ev, int64_t B, int64_t Hq, int64_t Hkv,
+                           int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const void* mask, int64_t mask_sb,
+                           int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk, void* dv, int32_t* G_out,
+                           unsigned int* flag, void* ws, int64_t ws_bytes, float dropout_p, uint64_t seed,
+                           const int32_t* e_global, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

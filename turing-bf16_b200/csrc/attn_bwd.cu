@@ -954,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // G = t_do - max_{b,h}(frexp(amax_do[b,h]) + ev[b, h / group]); one block.
 __global__ void __launch_bounds__(256) attn_bwd_exp_kernel(const float* __restrict__ amax_do, int BHq, int Hq, int Hkv,
                                                            int group, const int32_t* __restrict__ ev, int t_do,
-                                                           int32_t* __restrict__ G) {
+                                                           const int32_t* __restrict__ e_floor, int32_t* __restrict__ G) {
   __shared__ int red[8];
   int e = INT_MIN;
   for (int i = threadIdx.x; i < BHq; i += blockDim.x) {
@@ -967,6 +967,7 @@ __global__ void __launch_bounds__(256) attn_bwd_exp_kernel(const float* __restri
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 0; w < (int)blockDim.x / 32; ++w) e = max(e, red[w]);
+    if (e_floor) e = max(e, *e_floor);  // head-sharded call: the maximum over every rank's heads
     *G = t_do - e;
   }
 }
@@ -1131,7 +1132,7 @@ int attn_bwd_impl(const void* q16, const void* k16, const void* v16, const void*
                   const int32_t* ev, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, float scale,
                   int causal, const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, int t_do, void* dq,
                   void* dk, void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, float dropout_p,
-                  uint64_t seed, void* stream) {
+                  uint64_t seed, const int32_t* e_floor, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
   uint32_t thr = 0;
   float inv_keep = 1.f;
@@ -1154,7 +1155,7 @@ int attn_bwd_impl(const void* q16, const void* k16, const void* v16, const void*
   const int group = (int)(Hq / Hkv);
   // 1. G from the global max of head_exp(dout) + ev_q
   if (int rc = tbf16_head_amax(dout, TBF16_BF16, B, Hq, Sq, dout_d, dout_sb, dout_sh, dout_ss, w.amax, stream)) return rc;
-  attn_bwd_exp_kernel<<<1, 256, 0, st>>>(w.amax, (int)(B * Hq), (int)Hq, (int)Hkv, group, ev, t_do, G_out);
+  attn_bwd_exp_kernel<<<1, 256, 0, st>>>(w.amax, (int)(B * Hq), (int)Hq, (int)Hkv, group, ev, t_do, e_floor, G_out);
   // 2. dO16 and delta (the padding rows of delta are zeroed: the main kernel reads whole 128-row tiles)
   const int64_t rows = B * Hq * Sq;
   if (lse_ld != Sq && cudaMemsetAsync(w.delta, 0, sizeof(float) * B * Hq * lse_ld, st) != cudaSuccess)
@@ -1225,7 +1226,7 @@ int tbf16_attn_bwd(const void* q16, const void* k16, const void* v16, const void
                    void* dv, int32_t* G_out, unsigned int* flag, void* ws, int64_t ws_bytes, void* stream) {
   return attn_bwd_impl(q16, k16, v16, o16, lse, lse_ld, dout, dout_sb, dout_sh, dout_ss, dout_d, a, ev, B, Hq, Hkv, Sq,
                        Sk, D, scale, causal, mask, mask_sb, mask_sh, mask_sq, t_do, dq, dk, dv, G_out, flag, ws, ws_bytes,
-                       0.f, 0, stream);
+                       0.f, 0, nullptr, stream);
 }
 
 int tbf16_attn_bwd_dropout(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse,
@@ -1237,7 +1238,20 @@ int tbf16_attn_bwd_dropout(const void* q16, const void* k16, const void* v16, co
                            void* stream) {
   return attn_bwd_impl(q16, k16, v16, o16, lse, lse_ld, dout, dout_sb, dout_sh, dout_ss, dout_d, a, ev, B, Hq, Hkv, Sq,
                        Sk, D, scale, causal, mask, mask_sb, mask_sh, mask_sq, t_do, dq, dk, dv, G_out, flag, ws, ws_bytes,
-                       dropout_p, seed, stream);
+                       dropout_p, seed, nullptr, stream);
+}
+
+int tbf16_attn_bwd_sharded(const void* q16, const void* k16, const void* v16, const void* o16, const float* lse,
+                           int64_t lse_ld, const void* dout, int64_t dout_sb, int64_t dout_sh, int64_t dout_ss,
+                           int64_t dout_d, const int32_t* a, const int32_t* ev, int64_t B, int64_t Hq, int64_t Hkv,
+                           int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const void* mask, int64_t mask_sb,
+                           int64_t mask_sh, int64_t mask_sq, int t_do, void* dq, void* dk, void* dv, int32_t* G_out,
+                           unsigned int* flag, void* ws, int64_t ws_bytes, float dropout_p, uint64_t seed,
+                           const int32_t* e_global, void* stream) {
+  if (!e_global) return TBF16_ERR_INVALID;
+  return attn_bwd_impl(q16, k16, v16, o16, lse, lse_ld, dout, dout_sb, dout_sh, dout_ss, dout_d, a, ev, B, Hq, Hkv, Sq,
+                       Sk, D, scale, causal, mask, mask_sb, mask_sh, mask_sq, t_do, dq, dk, dv, G_out, flag, ws, ws_bytes,
+                       dropout_p, seed, e_global, stream);
 }
 
 }  // extern "C"

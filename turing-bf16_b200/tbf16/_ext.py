@@ -63,6 +63,9 @@ SIGNATURES = {
                                _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp,
                                _vp, _vp, _i64, ctypes.c_float, ctypes.c_uint64, _vp],
     "tbf16_attn_dropout_keep": [_vp, _i64, _i64, _i64, ctypes.c_float, ctypes.c_uint64, _vp],
+    "tbf16_attn_bwd_sharded": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64,
+                               _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp,
+                               _vp, _vp, _i64, ctypes.c_float, ctypes.c_uint64, _vp, _vp],
     "tbf16_device_check": [_i32],
     "tbf16_device_status": [_vp, _i32],
     "tbf16_selftest_bounded_wait": [ctypes.c_uint64, _vp],

@@ -212,11 +212,12 @@ def linear(x, w, bias=None):
 
 
 def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale, d_orig, t_do_offset=0,
-                  dropout_p=0.0, seed=0):
+                  dropout_p=0.0, seed=0, e_global=None):
     """Runs tbf16_attn_bwd with the reference's retry loop: t_do = 12 - ceil(log2 d), lowered by 8 and
     redone while the kernel reports a non-finite value (at most 6 attempts). t_do_offset (>= 0) lowers
     the target further: a head-sharded call passes how far the global dO exponent exceeds its own heads'
-    maximum, so G comes out as the unsharded call's. dropout_p, seed: the forward's dropout mask."""
+    maximum, so G comes out as the unsharded call's; or, without a host round trip, e_global: a device
+    int32 holding that global exponent (tbf16_attn_bwd_sharded). dropout_p, seed: the forward's mask."""
     B, Hq, Sq, Dk = q16.shape
     Hkv, Sk = k16.shape[1], k16.shape[2]
     dev = q16.device
@@ -238,7 +239,9 @@ def attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, scale
         args = (ptr(q16), ptr(k16), ptr(v16), ptr(o16), ptr(lse), lse.shape[-1], ptr(dout), *dout.stride()[:3],
                 dout.shape[-1], ptr(a), ptr(ev), B, Hq, Hkv, Sq, Sk, Dk, float(scale), int(bool(is_causal)), ptr(mask16),
                 *ms, int(t_do), ptr(dq), ptr(dk), ptr(dv), ptr(G), ptr(flag), ptr(ws), nbytes)
-        if dropout_p:
+        if e_global is not None:
+            call("tbf16_attn_bwd_sharded", *args, float(dropout_p), int(seed), ptr(e_global), stream_ptr(dev))
+        elif dropout_p:
             call("tbf16_attn_bwd_dropout", *args, float(dropout_p), int(seed), stream_ptr(dev))
         else:
             call("tbf16_attn_bwd", *args, stream_ptr(dev))

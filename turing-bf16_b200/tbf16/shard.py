@@ -101,9 +101,8 @@ def global_dout_exponent(dout, ev, group=None, head_exp=attention.head_exp):
 
 class _ShardedSDPAFn(torch.autograd.Function):
     """Training attention on this rank's heads with the unsharded call's scales: the forward's a from the
-    global eq, ek (prepare_qkv_sharded); the backward's G from the global dO exponent. The backward kernel
-    derives G from its own heads' maximum, so its target t_do is lowered by (e_global - e_local), read on
-    the host: one synchronisation per call, as the overflow check already costs."""
+    global eq, ek (prepare_qkv_sharded); the backward's G from the global dO exponent, which stays on the
+    device (all_reduce into an int32 the backward kernel reads: tbf16_attn_bwd_sharded)."""
 
     @staticmethod
     @torch.autocast("cuda", enabled=False)
@@ -130,10 +129,9 @@ class _ShardedSDPAFn(torch.autograd.Function):
         is_causal, sc, D0, group = ctx.args
         if D0 % 8:
             dout = torch.nn.functional.pad(dout, (0, 8 - D0 % 8))
-        e_local, e_global = global_dout_exponent(dout, ev, group)
-        offset = int(e_global) - int(e_local)
+        _, e_global = global_dout_exponent(dout, ev, group)
         dq, dk, dv, _ = autograd.attn_backward(q16, k16, v16, o16, lse, a, ev, dout, mask16, is_causal, sc, D0,
-                                               t_do_offset=offset)
+                                               e_global=e_global.reshape(1))
         if q16.shape[-1] != D0:
             dq, dk, dv = (t[..., :D0].contiguous() for t in (dq, dk, dv))
         return dq, dk, dv, None, None, None, None
