@@ -398,6 +398,7 @@ struct Head4 {
   int H, S, D8;
   float* amax;         // [B*H]
   int is_f16;
+  int nbh;             // B*H (set by the launcher)
 };
 
 __device__ __forceinline__ void load8(const uint16_t* p, int is_f16, float (&f)[8]) {
@@ -517,6 +518,65 @@ __global__ void __launch_bounds__(256) head_scale_cast_kernel(ScaleCast c0, Scal
   }
 }
 
+// Row-structured forms for head dims of 64, 128 and 256 (D8 = D / 8 sixteen-byte chunks per row, a power of
+// two dividing the block): a block owns one (b, h) slice and a range of rows, thread t handles chunk t % D8
+// of rows t / D8, t / D8 + 256 / D8, ... -- no 64-bit division per chunk, one exponent per block, and
+// consecutive threads touch consecutive 16-byte chunks. grid (row blocks, B*H of the widest tensor, tensors).
+template <int D8>
+__global__ void __launch_bounds__(256) head_amax_rows_kernel(Head4 t0, Head4 t1, Head4 t2, int rows_per_block) {
+  const Head4 t = blockIdx.z == 0 ? t0 : blockIdx.z == 1 ? t1 : t2;
+  const int bh = blockIdx.y;
+  const int s0 = blockIdx.x * rows_per_block;
+  const int s1 = min(t.S, s0 + rows_per_block);
+  if (bh >= t.nbh || s0 >= s1) return;  // the grid covers the widest tensor
+  const int b = bh / t.H, h = bh % t.H;
+  const uint16_t* base = t.x + b * t.sb + h * t.sh + (threadIdx.x % D8) * 8;
+  float m = 0.f;
+  for (int s = s0 + (int)threadIdx.x / D8; s < s1; s += 256 / D8) {
+    float f[8];
+    load8(base + (int64_t)s * t.ss, t.is_f16, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+  }
+  __shared__ float red[8];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(t.amax) + bh, __float_as_int(v));
+  }
+}
+
+template <int D8>
+__global__ void __launch_bounds__(256) head_scale_cast_rows_kernel(ScaleCast c0, ScaleCast c1, ScaleCast c2,
+                                                                   int rows_per_block) {
+  const ScaleCast c = blockIdx.z == 0 ? c0 : blockIdx.z == 1 ? c1 : c2;
+  const int bh = blockIdx.y;
+  if (c.x == nullptr || (int64_t)bh * c.S * D8 >= c.total8) return;  // this tensor has fewer (b, h) slices
+  const int b = bh / c.H, h = bh % c.H;
+  const int s0 = blockIdx.x * rows_per_block;
+  const int s1 = min(c.S, s0 + rows_per_block);
+  const float sc = exp2i(c.e_sign * __ldg(c.e + b * c.e_sb + h * c.e_sh));
+  const int sub = (int)threadIdx.x % D8;
+  const uint16_t* src = c.x + b * c.sb + h * c.sh + sub * 8;
+  uint4* dst = reinterpret_cast<uint4*>(c.y) + (int64_t)bh * c.S * D8 + sub;
+  for (int s = s0 + (int)threadIdx.x / D8; s < s1; s += 256 / D8) {
+    float f[8];
+    load8(src + (int64_t)s * c.ss, c.in_f16, f);
+    uint4 o;
+    if (c.out_f16) {
+      o.x = pack_f16(f[0] * sc, f[1] * sc); o.y = pack_f16(f[2] * sc, f[3] * sc);
+      o.z = pack_f16(f[4] * sc, f[5] * sc); o.w = pack_f16(f[6] * sc, f[7] * sc);
+    } else {
+      o.x = pack_bf16(f[0] * sc, f[1] * sc); o.y = pack_bf16(f[2] * sc, f[3] * sc);
+      o.z = pack_bf16(f[4] * sc, f[5] * sc); o.w = pack_bf16(f[6] * sc, f[7] * sc);
+    }
+    dst[(int64_t)s * D8] = o;
+  }
+}
+
 bool ok8(int64_t v) { return v % 8 == 0; }
 
 int grid_for(int64_t work, int threads, int waves = 8) {
@@ -543,13 +603,42 @@ Head4 make_head4(const void* x, int64_t H, int64_t S, int64_t D, int64_t sb, int
   return h;
 }
 
-int launch_head_amax(const Head4& a, const Head4& b, const Head4& c, int ntensors, int64_t BH, int64_t S,
-                     cudaStream_t st) {
+int launch_head_amax(Head4 a, Head4 b, Head4 c, int ntensors, int64_t BH, int64_t S, cudaStream_t st) {
   const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
   const int sms = d ? d->sms : 148;
   const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>((sms * 8 + BH - 1) / BH, (S + 63) / 64));
   const int rows = (int)((S + chunks - 1) / chunks);
+  a.nbh = b.nbh = c.nbh = (int)BH;
+  const int D8 = a.D8;
+  if (BH <= 65535 && (D8 == 8 || D8 == 16 || D8 == 32)) {  // row-structured form for head dims 64 / 128 / 256
+    const dim3 grid(chunks, (unsigned)BH, ntensors);
+    if (D8 == 8) head_amax_rows_kernel<8><<<grid, 256, 0, st>>>(a, b, c, rows);
+    else if (D8 == 16) head_amax_rows_kernel<16><<<grid, 256, 0, st>>>(a, b, c, rows);
+    else head_amax_rows_kernel<32><<<grid, 256, 0, st>>>(a, b, c, rows);
+    return tbf16_host::check_launch();
+  }
   head_amax_kernel<<<dim3((unsigned)BH, chunks, ntensors), 256, 0, st>>>(a, b, c, rows);
+  return tbf16_host::check_launch();
+}
+
+// Launches the scale-cast of up to three tensors (same head dim): the row-structured form for D8 in
+// {8, 16, 32}, the flat form otherwise. max_bh / max_s: the widest tensor's B*H and S.
+int launch_scale_cast(const ScaleCast& c0, const ScaleCast& c1, const ScaleCast& c2, int ntensors, int64_t max_bh,
+                      int64_t max_s, int64_t max_total8, cudaStream_t st) {
+  const int D8 = c0.D8;
+  if (max_bh <= 65535 && (D8 == 8 || D8 == 16 || D8 == 32)) {
+    const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+    const int sms = d ? d->sms : 148;
+    // about 8 blocks per SM over the launch, at least 64 rows a block
+    const int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((sms * 8 + max_bh - 1) / max_bh, (max_s + 63) / 64));
+    const int rows = (int)((max_s + chunks - 1) / chunks);
+    const dim3 grid((unsigned)chunks, (unsigned)max_bh, ntensors);
+    if (D8 == 8) head_scale_cast_rows_kernel<8><<<grid, 256, 0, st>>>(c0, c1, c2, rows);
+    else if (D8 == 16) head_scale_cast_rows_kernel<16><<<grid, 256, 0, st>>>(c0, c1, c2, rows);
+    else head_scale_cast_rows_kernel<32><<<grid, 256, 0, st>>>(c0, c1, c2, rows);
+    return tbf16_host::check_launch();
+  }
+  head_scale_cast_kernel<<<dim3(grid_for(max_total8, 256), 1, ntensors), 256, 0, st>>>(c0, c1, c2);
   return tbf16_host::check_launch();
 }
 
@@ -667,8 +756,7 @@ int tbf16_head_scale_cast(const void* x, int in_dtype, int64_t B, int64_t H, int
   c.total8 = total8;
   ScaleCast none = c;
   none.x = nullptr;
-  head_scale_cast_kernel<<<dim3(grid_for(total8, 256), 1, 1), 256, 0, static_cast<cudaStream_t>(stream)>>>(c, none, none);
-  return tbf16_host::check_launch();
+  return launch_scale_cast(c, none, none, 1, B * H, S, total8, static_cast<cudaStream_t>(stream));
 }
 
 int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb, int64_t ksh,
@@ -710,7 +798,7 @@ int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, cons
   cv.x = static_cast<const uint16_t*>(v); cv.sb = vsb; cv.sh = vsh; cv.ss = vss;
   cv.e = ev_out; cv.e_sb = Hkv; cv.e_sh = 1; cv.y = static_cast<uint16_t*>(v16);
   const int64_t work = std::max(cq.total8, ck.total8);
-  if (work > 0) head_scale_cast_kernel<<<dim3(grid_for(work, 256), 1, 3), 256, 0, st>>>(cq, ck, cv);
+  if (work > 0) return launch_scale_cast(cq, ck, cv, 3, B * Hq, std::max(Sq, Sk), work, st);
   return tbf16_host::check_launch();
 }
 
