@@ -157,7 +157,7 @@ def host_info():
     return {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "cpu_model": model}
 
 
-def cpu_attention_sample(H=16, S=16384, D=128, rows=1024, causal=False, steps=2):
+def cpu_attention_sample(H=16, S=16384, D=128, rows=1024, causal=False, steps=2, min_seconds=5.0):
     """The reference's inference attention (tbf16/attention.py:38-65) on the host cores: exponents and fp16
     copies by the oracle's C restatement of its head_amax / head_scale_cast, torch's CPU fp16
     scaled_dot_product_attention (what the reference calls with ops._USE_CUDA = False), the output scaled
@@ -175,16 +175,19 @@ def cpu_attention_sample(H=16, S=16384, D=128, rows=1024, causal=False, steps=2)
 
     run()
     t0 = time.perf_counter()
-    for _ in range(steps):
+    done = 0
+    while done < steps or time.perf_counter() - t0 < min_seconds:
         run()
-    dt = (time.perf_counter() - t0) / steps
+        done += 1
+    dt = (time.perf_counter() - t0) / done
     flop = 4.0 * H * rows * S * D
-    return flop / dt / 1e12, (f"{rows} query rows x {S} keys x {H} heads (D={D}) per step, {steps} steps "
-                              f"({dt * steps:.1f} s), torch CPU fp16 SDPA")
+    return flop / dt / 1e12, (f"{rows} query rows x {S} keys x {H} heads (D={D}) per step, {done} steps "
+                              f"({dt * done:.1f} s), torch CPU fp16 SDPA")
 
 
-def run_cpu_reference(M, N, K, steps, warmup, rows=256):
-    """Time the CPU implementation on `rows`-row samples of the workload; returns (TFLOPS, sample text)."""
+def run_cpu_reference(M, N, K, steps, warmup, rows=256, min_seconds=0.0):
+    """Time the CPU implementation on `rows`-row samples of the workload: `steps` samples, continued until
+    `min_seconds` of CPU work have run; returns (TFLOPS, threads, sample text)."""
     import inputs
     from oracle import oracle as orc
     orc.lib()
@@ -195,11 +198,13 @@ def run_cpu_reference(M, N, K, steps, warmup, rows=256):
     for _ in range(max(1, warmup)):
         cpu_linear_sample(x, w16, ws, rows)
     t0 = time.perf_counter()
-    for _ in range(steps):
+    done = 0
+    while done < steps or time.perf_counter() - t0 < min_seconds:
         cpu_linear_sample(x, w16, ws, rows)
+        done += 1
     dt = time.perf_counter() - t0
-    tflops = 2.0 * rows * N * K * steps / dt / 1e12
-    return tflops, threads, f"{rows} rows x N={N} x K={K} per step, {steps} steps ({dt:.1f} s), torch CPU fp16 GEMM"
+    tflops = 2.0 * rows * N * K * done / dt / 1e12
+    return tflops, threads, f"{rows} rows x N={N} x K={K} per step, {done} steps ({dt:.1f} s), torch CPU fp16 GEMM"
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -393,7 +398,7 @@ def main():
     if world > 1:
         line["collectives"] = collectives_run(pk, world, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1)
+        tf, threads, sample = run_cpu_reference(M, N, K, steps=8, warmup=1, min_seconds=10.0)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
                                 "sample": sample, "host": host_info()}
         if not args.no_attention:
