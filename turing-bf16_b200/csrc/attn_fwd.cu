@@ -335,15 +335,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------------
-// Head dims 64 and 128: one CTA per SM works on two 128-row query tiles of the same head ("tile 0"
-// and "tile 1") that share every K and V tile. TMEM holds S and O of both tiles (S0 [0,128),
-// O0 [128,256), S1 [256,384), O1 [384,512)); P is written back over its S columns as packed fp16 and
-// the P.V MMA reads its A operand from TMEM. The MMA warp alternates the tiles,
+// Head dims 64 and 128: a persistent kernel, one CTA per SM, whose work items are pairs of 128-row
+// query tiles of one head ("tile 0" and "tile 1") that share every K and V tile. TMEM holds S and O
+// of both tiles (S0 [0,128), O0 [128,256), S1 [256,384), O1 [384,512)); P is written back over its S
+// columns as packed fp16 and the P.V MMA reads its A operand from TMEM. Within an item the MMA warp
+// alternates the tiles,
 //   S0_0 S1_0 | PV0_0 S0_1 | PV1_0 S1_1 | PV0_1 S0_2 | PV1_1 S1_2 | ...
 // so the tensor core computes one tile's P.V and next S while the other tile's softmax runs. The
 // MMA pipe executes one CTA's MMAs in issue order: S0_{j+1} overwrites P0_j only after PV0_j has
 // read it, and when S0_{j+1} completes PV0_j has completed too (O0 may be rescaled without another
-// wait). K and V go through two-stage rings.
+// wait). K and V go through two-stage rings that run on across items.
+// Between items nothing drains: the Q tiles are released once the item's last S MMA completes (the
+// next item's Q loads during the last P.V steps), the next item's first S MMAs run while the softmax
+// warps write the previous item's output, and its first P.V (which overwrites O) waits for the
+// softmax warps' first P of the new item, which they produce only after reading O out.
+// Items are ordered heads fastest and heaviest (last) query pairs first for causal attention, query
+// pairs fastest otherwise (CTAs in flight share a head's K and V in L2), and dealt to the CTAs in a
+// snake order (round r gives item r * G + c to CTA c, or to CTA G - 1 - c when r is odd), which
+// balances the causal triangle almost as well as longest-first list scheduling.
 //   warps 0-3  softmax + epilogue of tile 0 (warp w reads TMEM lanes 32 (w % 4) ..)
 //   warps 4-7  softmax + epilogue of tile 1
 //   warp 8     TMA producer          warp 9  MMA issuer (+ TMEM allocation)     warps 10-11 idle
@@ -368,6 +377,41 @@ struct FwdPPCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
+// One work item of the two-tile kernel: (batch * head, first query row, key tiles of each tile).
+struct PPItem {
+  int bh, m0, n0, n1;
+};
+
+// The CTA's r-th item (snake order over gridDim.x CTAs); false past the last item. Every role of the
+// CTA walks the same sequence.
+__device__ __forceinline__ bool pp_item(const AttnFwdParams& p, int r, PPItem& it) {
+  const int G = (int)gridDim.x;
+  const int pairs = (p.m_tiles + 1) >> 1;
+  const int n_items = p.B * p.Hq * pairs;
+  const int k = r * G + ((r & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  if (k >= n_items) return false;
+  const int BHq = p.B * p.Hq;
+  int pair;
+  if (p.causal) {
+    pair = pairs - 1 - k / BHq;
+    it.bh = k % BHq;
+  } else {
+    pair = k % pairs;
+    it.bh = k / pairs;
+  }
+  it.m0 = pair * 2 * BM;
+  // key tiles per query tile (tile 1 may lie past the end of the sequence: no work)
+  auto kv_tiles = [&](int t) -> int {
+    const int r0 = it.m0 + t * BM;
+    if (r0 >= p.Sq) return 0;
+    const int kv_end = p.causal ? min(p.Sk, r0 + BM) : p.Sk;
+    return (kv_end + BN - 1) / BN;
+  };
+  it.n0 = kv_tiles(0);
+  it.n1 = kv_tiles(1);
+  return true;
+}
+
 template <int D, bool DROP>
 __global__ void __launch_bounds__(kPPThreads, 1)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -377,37 +421,22 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [tile]
-  uint64_t* p_full = bars + 11;  // [tile]
-  uint64_t* pv_done = bars + 13; // [tile]
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;   // [2]
+  uint64_t* k_empty = bars + 4;  // [2]
+  uint64_t* v_full = bars + 6;   // [2]
+  uint64_t* v_empty = bars + 8;  // [2]
+  uint64_t* s_full = bars + 10;  // [tile]
+  uint64_t* p_full = bars + 12;  // [tile]
+  uint64_t* pv_done = bars + 14; // [tile]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // causal: heads fastest and the heaviest (last) query pairs first, so the longest CTAs start first;
-  // otherwise query pairs fastest, so the CTAs in flight share a head's K and V in L2
-  const int bh = p.causal ? (int)blockIdx.x : (int)blockIdx.y;
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int bhk = b * p.Hkv + h / p.group;
-  const int pairs = (p.m_tiles + 1) >> 1;
-  const int pair = p.causal ? (pairs - 1 - (int)blockIdx.y) : (int)blockIdx.x;
-  const int m0 = pair * 2 * BM;
-  // key tiles per query tile (tile 1 may lie past the end of the sequence: no work)
-  auto kv_tiles = [&](int t) -> int {
-    const int r0 = m0 + t * BM;
-    if (r0 >= p.Sq) return 0;
-    const int kv_end = p.causal ? min(p.Sk, r0 + BM) : p.Sk;
-    return (kv_end + BN - 1) / BN;
-  };
-  const int n0 = kv_tiles(0), n1 = kv_tiles(1);
-  const int n_kv = max(n0, n1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -434,79 +463,96 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     setmaxnreg_dec<kPPRegsOther>();
     if (warp == 8) {
     // ---------------------------------------------------------------- TMA producer
-    if (lane == 0 && n_kv > 0) {
-      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+    if (lane == 0) {
+      uint32_t g = 0;  // K/V ring slots used so far (across items)
+      PPItem it;
+      for (int r = 0; pp_item(p, r, it); ++r) {
+        const int bhk = (it.bh / p.Hq) * p.Hkv + (it.bh % p.Hq) / p.group;
+        const int n_kv = max(it.n0, it.n1);
+        // the previous item's S MMAs have all completed before its Q tiles are overwritten
+        if (r > 0 && !mbar_wait(q_empty, (r - 1) & 1, abort, p.err)) break;
+        mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_3d(smem + C::Q_OFF + t * C::TILE_BYTES + a * 16384, &tmQ, q_full, a * 64, m0 + t * BM, bh);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) break;
-        mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_3d(smem + C::Q_OFF + t * C::TILE_BYTES + a * 16384, &tmQ, q_full, a * 64, it.m0 + t * BM, it.bh);
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_3d(smem + C::K_OFF + st * C::TILE_BYTES + a * 16384, &tmK, &k_full[st], a * 64, j * BN, bhk);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) break;
-        mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_3d(smem + C::K_OFF + st * C::TILE_BYTES + a * 16384, &tmK, &k_full[st], a * 64, j * BN, bhk);
+          if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + a * 16384, &tmV, &v_full[st], a * 64, j * BN, bhk);
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + a * 16384, &tmV, &v_full[st], a * 64, j * BN, bhk);
+        }
+        if (!ok) break;
       }
     }
     } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp runs the loop so operands stay warp-uniform; one elected lane issues.
-    if (n_kv > 0) {
-      constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, false, false);
-      constexpr uint32_t idesc_o = idesc_f16_f32(BM, D, false, true);
-      // descriptors: a k16 step adds its byte offset / 16 to the 14-bit start-address field (shared
-      // addresses stay below 2^18 bytes, so it cannot carry out)
-      const uint64_t qd0 = smem_desc_sw128(smem_u32(smem + C::Q_OFF), 16, 1024);
-      const uint64_t kd0 = smem_desc_sw128(smem_u32(smem + C::K_OFF), 16, 1024);
-      const uint64_t vd0 = smem_desc_sw128(smem_u32(smem + C::V_OFF), 16384, 1024);
-      constexpr uint32_t kTile16 = C::TILE_BYTES >> 4;
-      auto issue_s = [&](int t, int j) {  // S_t = Q_t K_j^T into the S columns of tile t
-        const uint64_t qd = qd0 + t * kTile16, kd = kd0 + (j & 1) * kTile16;
+    constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, false, false);
+    constexpr uint32_t idesc_o = idesc_f16_f32(BM, D, false, true);
+    // descriptors: a k16 step adds its byte offset / 16 to the 14-bit start-address field (shared
+    // addresses stay below 2^18 bytes, so it cannot carry out)
+    const uint64_t qd0 = smem_desc_sw128(smem_u32(smem + C::Q_OFF), 16, 1024);
+    const uint64_t kd0 = smem_desc_sw128(smem_u32(smem + C::K_OFF), 16, 1024);
+    const uint64_t vd0 = smem_desc_sw128(smem_u32(smem + C::V_OFF), 16384, 1024);
+    constexpr uint32_t kTile16 = C::TILE_BYTES >> 4;
+    auto issue_s = [&](int t, uint32_t slot) {  // S_t = Q_t K^T (K in ring slot `slot`) into tile t's S columns
+      const uint64_t qd = qd0 + t * kTile16, kd = kd0 + (slot & 1) * kTile16;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off16 = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-          umma_f16_ss(tmem + t * 256, qd + off16, kd + off16, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-      };
-      auto issue_pv = [&](int t, int j) {  // O_t += P_t V_j, P (128 x 128 fp16) from TMEM
-        const uint64_t vd = vd0 + (j & 1) * kTile16;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-      };
-      bool ok = mbar_wait_warp(q_full, 0, abort, p.err) && mbar_wait_warp(&k_full[0], 0, abort, p.err);
-      if (ok) {
-        tc_fence_after();
-        if (elect_one()) {
-          if (n0 > 0) issue_s(0, 0);
-          if (n1 > 0) issue_s(1, 0);
-          umma_commit(&k_empty[0]);
-        }
-        __syncwarp();
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off16 = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+        umma_f16_ss(tmem + t * 256, qd + off16, kd + off16, idesc_s, kk > 0 ? 1u : 0u);
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
+      umma_commit(&s_full[t]);
+    };
+    auto issue_pv = [&](int t, uint32_t slot, bool first) {  // O_t (+)= P_t V, P (128 x 128 fp16) from TMEM
+      const uint64_t vd = vd0 + (slot & 1) * kTile16;
+#pragma unroll
+      for (int kk = 0; kk < BN / 16; ++kk)
+        umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, vd + (kk * 2048 >> 4), idesc_o,
+                    (!first || kk > 0) ? 1u : 0u);
+    };
+    uint32_t g = 0;              // K/V ring slots consumed so far (across items)
+    uint32_t pw[2] = {0u, 0u};   // p_full phases consumed per tile
+    bool ok = true;
+    PPItem it;
+    for (int r = 0; ok && pp_item(p, r, it); ++r) {
+      const int n_kv = max(it.n0, it.n1);
+      ok = mbar_wait_warp(q_full, r & 1, abort, p.err) && mbar_wait_warp(&k_full[g & 1], (g >> 1) & 1, abort, p.err);
+      if (!ok) break;
+      tc_fence_after();
+      if (elect_one()) {
+        if (it.n0 > 0) issue_s(0, g);
+        if (it.n1 > 0) issue_s(1, g);
+        umma_commit(&k_empty[g & 1]);
+        if (n_kv == 1) umma_commit(q_empty);
+      }
+      __syncwarp();
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t gj = g + j;
+        const int st = gj & 1;
         const bool next = j + 1 < n_kv;
-        if (!mbar_wait_warp(&v_full[st], (j >> 1) & 1, abort, p.err)) break;
-        if (next && !mbar_wait_warp(&k_full[st ^ 1], ((j + 1) >> 1) & 1, abort, p.err)) break;
+        if (!mbar_wait_warp(&v_full[st], (gj >> 1) & 1, abort, p.err)) { ok = false; break; }
+        if (next && !mbar_wait_warp(&k_full[st ^ 1], ((gj + 1) >> 1) & 1, abort, p.err)) { ok = false; break; }
         for (int t = 0; t < 2; ++t) {
-          const int nt = t == 0 ? n0 : n1;
+          const int nt = t == 0 ? it.n0 : it.n1;
           if (j >= nt) continue;
-          if (!mbar_wait_warp(&p_full[t], j & 1, abort, p.err)) { ok = false; break; }
+          if (!mbar_wait_warp(&p_full[t], pw[t] & 1, abort, p.err)) { ok = false; break; }
+          ++pw[t];
           tc_fence_after();
           if (elect_one()) {
-            issue_pv(t, j);
-            if (j + 1 < nt) issue_s(t, j + 1);
+            issue_pv(t, gj, j == 0);
+            if (j + 1 < nt) issue_s(t, gj + 1);
             else umma_commit(&pv_done[t]);
           }
           __syncwarp();
@@ -515,9 +561,12 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         if (elect_one()) {
           umma_commit(&v_empty[st]);
           if (next) umma_commit(&k_empty[st ^ 1]);
+          // every S MMA of the item has been issued: the Q tiles are free once they complete
+          if (j == n_kv - 2) umma_commit(q_empty);
         }
         __syncwarp();
       }
+      g += n_kv;
     }
     }
   } else {
@@ -526,114 +575,124 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     const int t = warp >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int m_t = m0 + t * BM;
-    const int qi = m_t + r;
-    const int nt = t == 0 ? n0 : n1;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + t * 256;
     const uint32_t o_addr = s_addr + 128;
-    const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
-    float m_used = -INFINITY, l = 0.f;
+    uint32_t sw = 0, dw = 0;  // s_full and pv_done phases consumed
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (!mbar_wait_warp(&s_full[t], j & 1, abort, p.err)) { ok = false; break; }
-      tc_fence_after();
-      const int k0 = j * BN;
-      const bool full_tile = p.mask == nullptr && k0 + BN <= p.Sk && (!p.causal || k0 + BN - 1 <= m_t);
-      // Logits of a full tile stay raw (s) and are scaled inside the exp, p = 2^(s * c - m) with
-      // c = scale * log2(e) > 0 (the max commutes with it). A partial tile (sequence end, causal
-      // diagonal, user mask) maps s to the scaled, masked logit first and uses c = 1.
-      const float c_scale = full_tile ? p.scale_log2 : 1.f;
-      // the whole 128-column S row in registers: four loads in flight, one wait
-      uint32_t rr[BN];
+    PPItem it;
+    for (int ri = 0; ok && pp_item(p, ri, it); ++ri) {
+      const int bh = it.bh;
+      const int b = bh / p.Hq, h = bh % p.Hq;
+      const int bhk = b * p.Hkv + h / p.group;
+      const int m_t = it.m0 + t * BM;
+      const int qi = m_t + r;
+      const int nt = t == 0 ? it.n0 : it.n1;
+      const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nt; ++j) {
+        if (!mbar_wait_warp(&s_full[t], sw & 1, abort, p.err)) { ok = false; break; }
+        ++sw;
+        tc_fence_after();
+        const int k0 = j * BN;
+        const bool full_tile = p.mask == nullptr && k0 + BN <= p.Sk && (!p.causal || k0 + BN - 1 <= m_t);
+        // Logits of a full tile stay raw (s) and are scaled inside the exp, p = 2^(s * c - m) with
+        // c = scale * log2(e) > 0 (the max commutes with it). A partial tile (sequence end, causal
+        // diagonal, user mask) maps s to the scaled, masked logit first and uses c = 1.
+        const float c_scale = full_tile ? p.scale_log2 : 1.f;
+        // the whole 128-column S row in registers: four loads in flight, one wait
+        uint32_t rr[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
-      tmem_ld_wait();
-      if (!full_tile) {
-        const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
-#pragma unroll
-        for (int e = 0; e < BN; ++e) {
-          const int kj = k0 + e;
-          const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
-          float v = __uint_as_float(rr[e]) * p.scale_log2;
-          if (mrow && valid) v += __half2float(__ushort_as_half(mrow[e])) * 1.4426950408889634f;
-          rr[e] = __float_as_uint(valid ? v : -INFINITY);
-        }
-      }
-      // row max: 8 independent 3-input max chains
-      float m8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
-#pragma unroll
-      for (int e = 8; e < BN; e += 2) m8[(e >> 1) & 7] = max3f(m8[(e >> 1) & 7], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
-      const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * c_scale;
-      float alpha = 1.f;
-      bool rescale = false;
-      if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
-        alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
-        rescale = j > 0;
-        m_used = mx;
-        l *= alpha;
-      }
-      // P = 2^(logit - m) packed to fp16 in place (pair e/2 overwrites a register already read); the
-      // scaling and the row sum run on fp32 pairs, and three pairs in eight take the FMA-pipe exp2 so
-      // the MUFU pipe is not the only exp unit
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      const uint64_t c2 = f2_pack(c_scale, c_scale), nb2 = f2_pack(-base, -base);
-      uint64_t sum4[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int e = 0; e < BN; e += 2) {
-        float x0, x1, p0, p1;
-        f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), c2, nb2), x0, x1);
-        if (((e >> 1) & 7) >= 8 - kPolyPairsOf8) {
-          ex2_poly2(x0, x1, p0, p1);
-        } else {
-          p0 = ex2(x0);
-          p1 = ex2(x1);
-        }
-        sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
-        rr[e >> 1] = pack_f16(p0, p1);
-        // dropout: the row sum keeps every key; P.V sees only the kept ones (scaled back at the end)
-        if constexpr (DROP) rr[e >> 1] &= drop_pair_mask(rk, (uint32_t)(k0 + e) >> 1, p.drop_thr);
-      }
-      {
-        float a0, a1;
-        f2_unpack(f2_add(f2_add(sum4[0], sum4[1]), f2_add(sum4[2], sum4[3])), a0, a1);
-        l += a0 + a1;
-      }
-      // P of keys [0, 128) onto S columns [0, 64)
-      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
-      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
-      // O is complete up to P.V_{j-1} (it precedes S_j in the MMA pipe): rescale it in place if needed,
-      // the whole row in one TMEM round trip (the S registers are free again)
-      if (__any_sync(0xffffffffu, rescale)) {
-        uint32_t o[D];
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
         tmem_ld_wait();
-        const float a = rescale ? alpha : 1.f;
-        const uint64_t a2 = f2_pack(a, a);
+        if (!full_tile) {
+          const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
 #pragma unroll
-        for (int e = 0; e < D; e += 2) {
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2, 0), x0, x1);
-          o[e] = __float_as_uint(x0);
-          o[e + 1] = __float_as_uint(x1);
+          for (int e = 0; e < BN; ++e) {
+            const int kj = k0 + e;
+            const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
+            float v = __uint_as_float(rr[e]) * p.scale_log2;
+            if (mrow && valid) v += __half2float(__ushort_as_half(mrow[e])) * 1.4426950408889634f;
+            rr[e] = __float_as_uint(valid ? v : -INFINITY);
+          }
         }
+        // row max: 8 independent 3-input max chains
+        float m8[8];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) tmem_st32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
+#pragma unroll
+        for (int e = 8; e < BN; e += 2) m8[(e >> 1) & 7] = max3f(m8[(e >> 1) & 7], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+        const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * c_scale;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
+          alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+          rescale = j > 0;
+          m_used = mx;
+          l *= alpha;
+        }
+        // P = 2^(logit - m) packed to fp16 in place (pair e/2 overwrites a register already read); the
+        // scaling and the row sum run on fp32 pairs, and three pairs in eight take the FMA-pipe exp2 so
+        // the MUFU pipe is not the only exp unit
+        const float base = m_used == -INFINITY ? 0.f : m_used;
+        const uint64_t c2 = f2_pack(c_scale, c_scale), nb2 = f2_pack(-base, -base);
+        uint64_t sum4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int e = 0; e < BN; e += 2) {
+          float x0, x1, p0, p1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), c2, nb2), x0, x1);
+          if (((e >> 1) & 7) >= 8 - kPolyPairsOf8) {
+            ex2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
+          rr[e >> 1] = pack_f16(p0, p1);
+          // dropout: the row sum keeps every key; P.V sees only the kept ones (scaled back at the end)
+          if constexpr (DROP) rr[e >> 1] &= drop_pair_mask(rk, (uint32_t)(k0 + e) >> 1, p.drop_thr);
+        }
+        {
+          float a0, a1;
+          f2_unpack(f2_add(f2_add(sum4[0], sum4[1]), f2_add(sum4[2], sum4[3])), a0, a1);
+          l += a0 + a1;
+        }
+        // P of keys [0, 128) onto S columns [0, 64)
+        tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+        tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+        // O is complete up to P.V_{j-1} (it precedes S_j in the MMA pipe): rescale it in place if needed,
+        // the whole row in one TMEM round trip (the S registers are free again)
+        if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t o[D];
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+          tmem_ld_wait();
+          const float a = rescale ? alpha : 1.f;
+          const uint64_t a2 = f2_pack(a, a);
+#pragma unroll
+          for (int e = 0; e < D; e += 2) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2, 0), x0, x1);
+            o[e] = __float_as_uint(x0);
+            o[e + 1] = __float_as_uint(x1);
+          }
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) tmem_st32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
       }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    }
-    if (ok && nt > 0 && mbar_wait_warp(&pv_done[t], 0, abort, p.err)) {
+      if (!ok || nt == 0) continue;
+      if (!mbar_wait_warp(&pv_done[t], dw & 1, abort, p.err)) { ok = false; break; }
+      ++dw;
       tc_fence_after();
+      // O leaves TMEM here; the next item's first P.V overwrites it only after this warp's next
+      // p_full arrival, which follows these loads (tcgen05.wait::ld, then the fence before the arrive)
       const float inv_l = l > 0.f ? (DROP ? p.inv_keep : 1.f) / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
-      __nv_bfloat16* orow = p.out + (int64_t)(bh / p.Hq) * p.osb + (int64_t)(bh % p.Hq) * p.osh +
-                            (int64_t)min(qi, p.Sq - 1) * p.oss;
+      __nv_bfloat16* orow = p.out + (int64_t)b * p.osb + (int64_t)h * p.osh + (int64_t)min(qi, p.Sq - 1) * p.oss;
       __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -689,7 +748,10 @@ int launch_fwd_pp(const void* q16, const void* k16, const void* v16, const AttnF
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
-  dim3 grid = prm.causal ? dim3((unsigned)BHq, (prm.m_tiles + 1) / 2) : dim3((prm.m_tiles + 1) / 2, (unsigned)BHq);
+  // one CTA per SM (shared memory and the 512 TMEM columns allow no second), never more than the items
+  const int64_t items = BHq * ((prm.m_tiles + 1) / 2);
+  if (items > INT32_MAX - 2 * (int64_t)dev->sms) return TBF16_ERR_INVALID;  // item indices are int
+  const unsigned grid = (unsigned)std::min<int64_t>(items, dev->sms);
   attn_fwd_pp_kernel<D, DROP><<<grid, kPPThreads, C::SMEM, st>>>(tq, tk, tv, prm);
   return tbf16_host::check_launch();
 }
@@ -712,6 +774,361 @@ int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdP
   }
   const dim3 grid = prm.causal ? dim3((unsigned)BHq, prm.m_tiles) : dim3(prm.m_tiles, (unsigned)BHq);
   attn_fwd_kernel<D, DROP><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
+  return tbf16_host::check_launch();
+}
+
+// ------------------------------------------------------------------------------------------------
+// Head dim 256: a CTA pair (cluster of two, cta_group::2 MMAs issued by the even CTA) per 256 query
+// rows of one head; CTA c of the pair owns query rows m0 + 128 c .. + 127 (its TMEM lanes).
+//   S = Q K^T    M = 256 (the pair's rows), N = 128 keys, K = 256: each CTA holds its own Q rows and
+//                half of the key tile (keys 64 c .. 64 c + 63 of it, all 256 dims), 32 KB a stage
+//   O += P V     M = 256, N = 256 dims, K = 128 keys: P is read from each CTA's TMEM (TS form), each
+//                CTA holds dims 128 c .. 128 c + 127 of the V tile (128 keys), 32 KB a stage
+// so that two K and two V stages fit beside the 64 KB Q tile. TMEM per CTA: S0 [0,128), S1 [128,256),
+// O [256,512); P is written over its S buffer's first 64 columns as packed fp16. The MMA warp issues
+//   S_0 S_1 | PV_0 S_2 | PV_1 S_3 | ...
+// so each step's softmax runs while the tensor core computes the previous step's P.V and the next S.
+// In issue order S_{j+2} (overwriting P_j) follows PV_j. The softmax rescales O (lazily, when its
+// running max grows by more than 2^8) only after PV_{j-1} has completed, and PV_j waits for both
+// CTAs' P_j, so the rescale lands between them.
+//   warps 0-3  softmax + epilogue (one query row per thread)    warp 4  TMA producer (both CTAs)
+//   warp 5     MMA issuer (even CTA) + TMEM allocation (both)
+namespace fwd256 {
+constexpr int THREADS = 192;
+constexpr int ROWS = 128;                 // query rows per CTA
+constexpr int KEYS = 128;                 // keys per tile
+constexpr int Q_BYTES = 4 * 16384;        // 128 rows x 256 dims, four 64-dim atoms
+constexpr int KH_BYTES = 4 * 8192;        // 64 keys x 256 dims, four 64-dim atoms
+constexpr int VH_BYTES = 2 * 16384;       // 128 keys x 128 dims, two 64-dim atoms
+constexpr int Q_OFF = 0;
+constexpr int K_OFF = Q_OFF + Q_BYTES;
+constexpr int V_OFF = K_OFF + 2 * KH_BYTES;
+constexpr int BAR_OFF = V_OFF + 2 * VH_BYTES;
+constexpr int SMEM = 1024 + BAR_OFF + 256;
+static_assert(SMEM <= 227 * 1024, "shared memory");
+}  // namespace fwd256
+
+template <bool DROP>
+__global__ void __launch_bounds__(fwd256::THREADS, 1)
+    attn_fwd_d256_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
+  using namespace fwd256;
+  constexpr int D = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  uint64_t* q_full = bars + 0;    // even CTA's: both CTAs' Q bytes
+  uint64_t* k_full = bars + 1;    // [2] even CTA's
+  uint64_t* v_full = bars + 3;    // [2] even CTA's
+  uint64_t* k_empty = bars + 5;   // [2] both (commit to both CTAs)
+  uint64_t* v_empty = bars + 7;   // [2] both
+  uint64_t* s_full = bars + 9;    // [2] both
+  uint64_t* p_full = bars + 11;   // [2] even CTA's: 4 softmax warps of each CTA
+  uint64_t* pv_done = bars + 13;  // both
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  // causal: heads fastest and the heaviest (last) row pairs first; otherwise row pairs fastest
+  const int item = (int)(blockIdx.x >> 1);
+  const int BHq = p.B * p.Hq;
+  const int pairs = (p.Sq + 2 * ROWS - 1) / (2 * ROWS);
+  const int bh = p.causal ? item % BHq : item / pairs;
+  const int pr = p.causal ? pairs - 1 - item / BHq : item % pairs;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int bhk = b * p.Hkv + h / p.group;
+  const int m0 = pr * 2 * ROWS;          // the pair's first query row
+  const int mc = m0 + (int)rank * ROWS;  // this CTA's first query row
+  const int kv_end = p.causal ? min(p.Sk, m0 + 2 * ROWS) : p.Sk;
+  const int n_kv = (kv_end + KEYS - 1) / KEYS;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 8);
+    }
+    mbar_init(pv_done, 1);
+    *abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 5) tmem_alloc_pair(tmem_slot, 512);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0 && n_kv > 0) {
+      if (leader) mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) tma_load_3d_pair(smem + Q_OFF + a * 16384, &tmQ, q_full, a * 64, mc, bh);
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
+        if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * KH_BYTES);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tma_load_3d_pair(smem + K_OFF + st * KH_BYTES + a * 8192, &tmK, &k_full[st], a * 64,
+                           j * KEYS + (int)rank * (KEYS / 2), bhk);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
+        if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * VH_BYTES);
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d_pair(smem + V_OFF + st * VH_BYTES + a * 16384, &tmV, &v_full[st], (int)rank * 128 + a * 64,
+                           j * KEYS, bhk);
+      }
+      // the even CTA's last releases of this CTA's stages have landed before the CTA may exit
+      for (int st = 0; ok && st < 2; ++st) {
+        const int uses = (n_kv + 1 - st) / 2;
+        if (uses > 0)
+          ok = mbar_wait(&k_empty[st], (uses - 1) & 1, abort, p.err) && mbar_wait(&v_empty[st], (uses - 1) & 1, abort, p.err);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    if (leader && lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(2 * ROWS, KEYS, false, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(2 * ROWS, D, false, true);
+      const uint64_t qd0 = smem_desc_sw128(smem_u32(smem + Q_OFF), 16, 1024);
+      const uint64_t kd0 = smem_desc_sw128(smem_u32(smem + K_OFF), 16, 1024);
+      const uint64_t vd0 = smem_desc_sw128(smem_u32(smem + V_OFF), 16384, 1024);
+      auto issue_s = [&](int j) -> bool {  // S_j into S buffer j & 1 of both CTAs
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        const uint64_t kd = kd0 + (uint64_t)((st * KH_BYTES) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t offq = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          const uint32_t offk = ((kk >> 2) * 8192 + (kk & 3) * 32) >> 4;
+          umma_f16_ss_pair(tmem + st * KEYS, qd0 + offq, kd + offk, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit_pair(&s_full[st], 0x3);
+        umma_commit_pair(&k_empty[st], 0x3);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {  // O += P_j V_j, P from both CTAs' TMEM
+        const int st = j & 1;
+        if (!mbar_wait_cluster(&p_full[st], (j >> 1) & 1, abort, p.err)) return false;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        const uint64_t vd = vd0 + (uint64_t)((st * VH_BYTES) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < KEYS / 16; ++kk)
+          umma_f16_ts_pair(tmem + 256, tmem + st * KEYS + kk * 8, vd + ((kk * 2048) >> 4), idesc_o,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_pair(&v_empty[st], 0x3);
+        umma_commit_pair(pv_done, 0x3);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort, p.err) && issue_s(0) && (n_kv < 2 || issue_s(1));
+      for (int j = 0; ok && j < n_kv; ++j) ok = issue_pv(j) && (j + 2 >= n_kv || issue_s(j + 2));
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qi = mc + r;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t o_addr = tmem + lane_base + 256;
+    const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, abort, p.err)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t s_addr = tmem + lane_base + sb * KEYS;
+      const int k0 = j * KEYS;
+      uint32_t rr[KEYS];
+      float alpha = 1.f;
+      bool rescale = false;
+      const bool dead = p.causal && k0 > mc + ROWS - 1;
+      if (dead) {
+        // every key of the tile lies after every row of this CTA (the pair's last tile, even CTA): P = 0
+#pragma unroll
+        for (int e = 0; e < KEYS / 2; ++e) rr[e] = 0u;
+      } else {
+        const bool full_tile = p.mask == nullptr && k0 + KEYS <= p.Sk && (!p.causal || k0 + KEYS - 1 <= mc);
+        const float c_scale = full_tile ? p.scale_log2 : 1.f;
+#pragma unroll
+        for (int c = 0; c < KEYS / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
+        tmem_ld_wait();
+        if (!full_tile) {
+          const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
+#pragma unroll
+          for (int e = 0; e < KEYS; ++e) {
+            const int kj = k0 + e;
+            const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
+            float v = __uint_as_float(rr[e]) * p.scale_log2;
+            if (mrow && valid) v += __half2float(__ushort_as_half(mrow[e])) * 1.4426950408889634f;
+            rr[e] = __float_as_uint(valid ? v : -INFINITY);
+          }
+        }
+        float m8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
+#pragma unroll
+        for (int e = 8; e < KEYS; e += 2)
+          m8[(e >> 1) & 7] = max3f(m8[(e >> 1) & 7], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+        const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * c_scale;
+        if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
+          alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+          rescale = j > 0;
+          m_used = mx;
+          l *= alpha;
+        }
+        const float base = m_used == -INFINITY ? 0.f : m_used;
+        const uint64_t c2 = f2_pack(c_scale, c_scale), nb2 = f2_pack(-base, -base);
+        uint64_t sum4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int e = 0; e < KEYS; e += 2) {
+          float x0, x1, p0, p1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), c2, nb2), x0, x1);
+          if (((e >> 1) & 7) >= 8 - kPolyPairsOf8) {
+            ex2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
+          rr[e >> 1] = pack_f16(p0, p1);
+          if constexpr (DROP) rr[e >> 1] &= drop_pair_mask(rk, (uint32_t)(k0 + e) >> 1, p.drop_thr);
+        }
+        {
+          float a0, a1;
+          f2_unpack(f2_add(f2_add(sum4[0], sum4[1]), f2_add(sum4[2], sum4[3])), a0, a1);
+          l += a0 + a1;
+        }
+      }
+      // O is complete once P.V_{j-1} has: wait for it at every step (so that no phase of the barrier is
+      // skipped), then rescale O if this row's max moved. P.V_j cannot start before this warp's arrival
+      // below, so the barrier is never more than one phase ahead of the wait.
+      if (j > 0) {
+        if (!mbar_wait_warp(pv_done, (j - 1) & 1, abort, p.err)) { ok = false; break; }
+        tc_fence_after();
+      }
+      if (!dead && __any_sync(0xffffffffu, rescale)) {
+        const float a = rescale ? alpha : 1.f;
+        const uint64_t a2 = f2_pack(a, a);
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t o[64];
+          tmem_ld32(o_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+          tmem_ld32(o_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2, 0), x0, x1);
+            o[e] = __float_as_uint(x0);
+            o[e + 1] = __float_as_uint(x1);
+          }
+          tmem_st32(o_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+          tmem_st32(o_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+        }
+      }
+      // P of the tile's 128 keys onto the S buffer's columns [0, 64)
+      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&p_full[sb]);
+        else mbar_arrive_remote(&p_full[sb], 0);
+      }
+    }
+    if (ok && n_kv > 0 && mbar_wait_warp(pv_done, (n_kv - 1) & 1, abort, p.err)) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? (DROP ? p.inv_keep : 1.f) / l : 0.f;
+      const float sc = exp2i(__ldg(p.ev + bhk));
+      __nv_bfloat16* orow = p.out + (int64_t)b * p.osb + (int64_t)h * p.osh + (int64_t)min(qi, p.Sq - 1) * p.oss;
+      __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c * 32, o);
+        tmem_ld_wait();
+        if (qi < p.Sq) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(o[8 * g + e]) * inv_l;
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) =
+                make_uint4(pack_bf16(v[0] * sc, v[1] * sc), pack_bf16(v[2] * sc, v[3] * sc),
+                           pack_bf16(v[4] * sc, v[5] * sc), pack_bf16(v[6] * sc, v[7] * sc));
+            if (o16row)
+              *reinterpret_cast<uint4*>(o16row + c * 32 + g * 8) = make_uint4(
+                  pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
+          }
+        }
+      }
+      if (p.lse && qi < p.Sq) p.lse[(int64_t)bh * p.lse_ld + qi] = (m_used + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {  // let copies and MMAs already in flight land before the CTA's memory goes away
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  cluster_sync();  // the even CTA's MMAs have finished reading the odd CTA's shared memory and TMEM
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+template <bool DROP>
+int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  if (!dev) return TBF16_ERR_DEVICE;
+  CUtensorMap tq, tk, tv;
+  const int64_t BHq = (int64_t)prm.B * prm.Hq, BHk = (int64_t)prm.B * prm.Hkv;
+  if (int rc = tbf16_host::make_tmap_3d(&tq, q16, 256, prm.Sq, BHq, 256, (uint64_t)prm.Sq * 256, 64, fwd256::ROWS)) return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tk, k16, 256, prm.Sk, BHk, 256, (uint64_t)prm.Sk * 256, 64, fwd256::KEYS / 2))
+    return rc;
+  if (int rc = tbf16_host::make_tmap_3d(&tv, v16, 256, prm.Sk, BHk, 256, (uint64_t)prm.Sk * 256, 64, fwd256::KEYS))
+    return rc;
+  auto kern = attn_fwd_d256_pair_kernel<DROP>;
+  static bool attr_done[64] = {false};
+  if (!attr_done[dev->device & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd256::SMEM) != cudaSuccess)
+      return tbf16_host::check_launch();
+    attr_done[dev->device & 63] = true;
+  }
+  const int64_t items = BHq * ((prm.Sq + 2 * fwd256::ROWS - 1) / (2 * fwd256::ROWS));
+  if (2 * items > INT32_MAX) return TBF16_ERR_INVALID;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * items));
+  cfg.blockDim = dim3(fwd256::THREADS);
+  cfg.dynamicSmemBytes = fwd256::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, prm) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
 
@@ -769,7 +1186,8 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
   prm.inv_keep = inv_keep;
   if (Sk == 0) return TBF16_ERR_UNSUPPORTED;
   auto st = static_cast<cudaStream_t>(stream);
-  // D <= 128: the two-query-tile kernel (P in TMEM); TBF16_ATTN_FWD=1 selects the one-tile kernel
+  // D <= 128: the persistent two-query-tile kernel, D = 256: the CTA-pair kernel (P in TMEM in both);
+  // TBF16_ATTN_FWD=1 selects the one-tile kernel
   static const bool one_cta = [] {
     const char* e = getenv("TBF16_ATTN_FWD");
     return e && e[0] == '1';
@@ -778,12 +1196,12 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
     if (D == 64) return one_cta ? launch_fwd<64, true>(q16, k16, v16, prm, st) : launch_fwd_pp<64, true>(q16, k16, v16, prm, st);
     if (D == 128)
       return one_cta ? launch_fwd<128, true>(q16, k16, v16, prm, st) : launch_fwd_pp<128, true>(q16, k16, v16, prm, st);
-    return launch_fwd<256, true>(q16, k16, v16, prm, st);
+    return one_cta ? launch_fwd<256, true>(q16, k16, v16, prm, st) : launch_fwd_d256_pair<true>(q16, k16, v16, prm, st);
   }
   if (D == 64) return one_cta ? launch_fwd<64, false>(q16, k16, v16, prm, st) : launch_fwd_pp<64, false>(q16, k16, v16, prm, st);
   if (D == 128)
     return one_cta ? launch_fwd<128, false>(q16, k16, v16, prm, st) : launch_fwd_pp<128, false>(q16, k16, v16, prm, st);
-  return launch_fwd<256, false>(q16, k16, v16, prm, st);
+  return one_cta ? launch_fwd<256, false>(q16, k16, v16, prm, st) : launch_fwd_d256_pair<false>(q16, k16, v16, prm, st);
 }
 
 extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,

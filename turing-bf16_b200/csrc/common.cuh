@@ -379,6 +379,42 @@ __device__ __forceinline__ void tma_load_5d_pair(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(m)), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
+// 3-D tiled load for a CTA pair (no multicast), completing on the even CTA's barrier like tma_load_2d_pair.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m, uint64_t* bar_local, int x, int y,
+                                                 int z) {
+  const uint32_t mbar = smem_u32(bar_local) & 0xFEFFFFFFu;
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(mbar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+// Bounded wait with cluster-scope acquire, for a phase completed by arrivals from the other CTA of the
+// pair (its writes, released at cluster scope by the arrive, are visible after it).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, "
+      "0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  unsigned int* err, uint64_t timeout_ns = 2000000000ull) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      atomicOr(err, kErrWaitTimeout);
+      *abort = 1;
+      return false;
+    }
+  }
+}
 // TMEM allocation / release for a CTA pair: one warp with the same warp index in each CTA.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols));
@@ -394,6 +430,15 @@ __device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_des
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// D[tmem of both CTAs] (+)= A[tmem of both CTAs] * B[smem of both CTAs]: the TS form of umma_f16_ss_pair
+// (each CTA's TMEM holds its 128 rows of A).
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 // Arrive once on the mbarrier at this offset in every CTA of `mask` when the pair's MMAs issued so far complete.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar_local, uint16_t mask) {
