@@ -778,19 +778,25 @@ int launch_fwd(const void* q16, const void* k16, const void* v16, const AttnFwdP
 }
 
 // ------------------------------------------------------------------------------------------------
-// Head dim 256: a CTA pair (cluster of two, cta_group::2 MMAs issued by the even CTA) per 256 query
-// rows of one head; CTA c of the pair owns query rows m0 + 128 c .. + 127 (its TMEM lanes).
+// Head dim 256: a persistent kernel over CTA pairs (clusters of two, cta_group::2 MMAs issued by the
+// even CTA), one pair per two SMs; a work item is 256 query rows of one head, CTA c of the pair
+// owning rows m0 + 128 c .. + 127 (its TMEM lanes).
 //   S = Q K^T    M = 256 (the pair's rows), N = 128 keys, K = 256: each CTA holds its own Q rows and
 //                half of the key tile (keys 64 c .. 64 c + 63 of it, all 256 dims), 32 KB a stage
 //   O += P V     M = 256, N = 256 dims, K = 128 keys: P is read from each CTA's TMEM (TS form), each
 //                CTA holds dims 128 c .. 128 c + 127 of the V tile (128 keys), 32 KB a stage
 // so that two K and two V stages fit beside the 64 KB Q tile. TMEM per CTA: S0 [0,128), S1 [128,256),
-// O [256,512); P is written over its S buffer's first 64 columns as packed fp16. The MMA warp issues
-//   S_0 S_1 | PV_0 S_2 | PV_1 S_3 | ...
+// O [256,512); P is written over its S buffer's first 64 columns as packed fp16. Steps are counted
+// across items (the K/V rings, S buffers and barrier phases run on); per item the MMA warp issues
+//   S_0 S_1 | PV_0 S_2 | PV_1 S_3 | ... | PV_n-1
 // so each step's softmax runs while the tensor core computes the previous step's P.V and the next S.
 // In issue order S_{j+2} (overwriting P_j) follows PV_j. The softmax rescales O (lazily, when its
 // running max grows by more than 2^8) only after PV_{j-1} has completed, and PV_j waits for both
-// CTAs' P_j, so the rescale lands between them.
+// CTAs' P_j, so the rescale lands between them. Between items: the Q tiles are released once the
+// item's last S has completed (the next Q loads during the last steps), the next item's S_0 and S_1
+// run while the softmax warps write the output, and its PV_0 (which overwrites O) waits for their
+// first P of the new item, produced after they have read O out. Items are ordered heads fastest and
+// heaviest first (causal) or row pairs fastest, and dealt to the pairs in snake order.
 //   warps 0-3  softmax + epilogue (one query row per thread)    warp 4  TMA producer (both CTAs)
 //   warp 5     MMA issuer (even CTA) + TMEM allocation (both)
 namespace fwd256 {
@@ -806,6 +812,31 @@ constexpr int V_OFF = K_OFF + 2 * KH_BYTES;
 constexpr int BAR_OFF = V_OFF + 2 * VH_BYTES;
 constexpr int SMEM = 1024 + BAR_OFF + 256;
 static_assert(SMEM <= 227 * 1024, "shared memory");
+
+struct Item {
+  int bh, m0, n_kv;
+};
+// The pair's r-th item (snake order over the gridDim.x / 2 pairs); false past the last one. Every role
+// of both CTAs walks the same sequence.
+__device__ __forceinline__ bool item_at(const AttnFwdParams& p, int r, Item& it) {
+  const int G = (int)(gridDim.x >> 1), c = (int)(blockIdx.x >> 1);
+  const int pairs = (p.Sq + 2 * ROWS - 1) / (2 * ROWS);
+  const int BHq = p.B * p.Hq;
+  const int k = r * G + ((r & 1) ? G - 1 - c : c);
+  if (k >= BHq * pairs) return false;
+  int pr;
+  if (p.causal) {
+    pr = pairs - 1 - k / BHq;
+    it.bh = k % BHq;
+  } else {
+    pr = k % pairs;
+    it.bh = k / pairs;
+  }
+  it.m0 = pr * 2 * ROWS;
+  const int kv_end = p.causal ? min(p.Sk, it.m0 + 2 * ROWS) : p.Sk;
+  it.n_kv = (kv_end + KEYS - 1) / KEYS;
+  return true;
+}
 }  // namespace fwd256
 
 template <bool DROP>
@@ -818,34 +849,24 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* q_full = bars + 0;    // even CTA's: both CTAs' Q bytes
-  uint64_t* k_full = bars + 1;    // [2] even CTA's
-  uint64_t* v_full = bars + 3;    // [2] even CTA's
-  uint64_t* k_empty = bars + 5;   // [2] both (commit to both CTAs)
-  uint64_t* v_empty = bars + 7;   // [2] both
-  uint64_t* s_full = bars + 9;    // [2] both
-  uint64_t* p_full = bars + 11;   // [2] even CTA's: 4 softmax warps of each CTA
-  uint64_t* pv_done = bars + 13;  // both
+  uint64_t* q_empty = bars + 1;   // both (commit to both CTAs)
+  uint64_t* k_full = bars + 2;    // [2] even CTA's
+  uint64_t* v_full = bars + 4;    // [2] even CTA's
+  uint64_t* k_empty = bars + 6;   // [2] both
+  uint64_t* v_empty = bars + 8;   // [2] both
+  uint64_t* s_full = bars + 10;   // [2] both
+  uint64_t* p_full = bars + 12;   // [2] even CTA's: 4 softmax warps of each CTA
+  uint64_t* pv_done = bars + 14;  // both
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  // causal: heads fastest and the heaviest (last) row pairs first; otherwise row pairs fastest
-  const int item = (int)(blockIdx.x >> 1);
-  const int BHq = p.B * p.Hq;
-  const int pairs = (p.Sq + 2 * ROWS - 1) / (2 * ROWS);
-  const int bh = p.causal ? item % BHq : item / pairs;
-  const int pr = p.causal ? pairs - 1 - item / BHq : item % pairs;
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int bhk = b * p.Hkv + h / p.group;
-  const int m0 = pr * 2 * ROWS;          // the pair's first query row
-  const int mc = m0 + (int)rank * ROWS;  // this CTA's first query row
-  const int kv_end = p.causal ? min(p.Sk, m0 + 2 * ROWS) : p.Sk;
-  const int n_kv = (kv_end + KEYS - 1) / KEYS;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
@@ -869,45 +890,56 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
 
   if (warp == 4) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
-    if (lane == 0 && n_kv > 0) {
-      if (leader) mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
-#pragma unroll
-      for (int a = 0; a < 4; ++a) tma_load_3d_pair(smem + Q_OFF + a * 16384, &tmQ, q_full, a * 64, mc, bh);
+    if (lane == 0) {
+      uint32_t g = 0;  // K/V ring slots used so far (across items)
+      int r = 0;
       bool ok = true;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
-        if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * KH_BYTES);
+      Item it;
+      for (; ok && item_at(p, r, it); ++r) {
+        const int bhk = (it.bh / p.Hq) * p.Hkv + (it.bh % p.Hq) / p.group;
+        // the previous item's S MMAs have all completed before the Q tiles are overwritten
+        if (r > 0 && !mbar_wait(q_empty, (r - 1) & 1, abort, p.err)) { ok = false; break; }
+        if (leader) mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
 #pragma unroll
         for (int a = 0; a < 4; ++a)
-          tma_load_3d_pair(smem + K_OFF + st * KH_BYTES + a * 8192, &tmK, &k_full[st], a * 64,
-                           j * KEYS + (int)rank * (KEYS / 2), bhk);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
-        if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * VH_BYTES);
+          tma_load_3d_pair(smem + Q_OFF + a * 16384, &tmQ, q_full, a * 64, it.m0 + (int)rank * ROWS, it.bh);
+        for (int j = 0; j < it.n_kv; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * KH_BYTES);
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
-          tma_load_3d_pair(smem + V_OFF + st * VH_BYTES + a * 16384, &tmV, &v_full[st], (int)rank * 128 + a * 64,
-                           j * KEYS, bhk);
+          for (int a = 0; a < 4; ++a)
+            tma_load_3d_pair(smem + K_OFF + st * KH_BYTES + a * 8192, &tmK, &k_full[st], a * 64,
+                             j * KEYS + (int)rank * (KEYS / 2), bhk);
+          if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * VH_BYTES);
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+            tma_load_3d_pair(smem + V_OFF + st * VH_BYTES + a * 16384, &tmV, &v_full[st], (int)rank * 128 + a * 64,
+                             j * KEYS, bhk);
+        }
       }
-      // the even CTA's last releases of this CTA's stages have landed before the CTA may exit
+      // the even CTA's last releases of this CTA's Q tiles and ring stages have landed before the CTA
+      // may exit
+      if (ok && r > 0) ok = mbar_wait(q_empty, (r - 1) & 1, abort, p.err);
       for (int st = 0; ok && st < 2; ++st) {
-        const int uses = (n_kv + 1 - st) / 2;
+        const uint32_t uses = (g + 1 - st) / 2;
         if (uses > 0)
           ok = mbar_wait(&k_empty[st], (uses - 1) & 1, abort, p.err) && mbar_wait(&v_empty[st], (uses - 1) & 1, abort, p.err);
       }
     }
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer (even CTA)
-    if (leader && lane == 0 && n_kv > 0) {
+    if (leader && lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(2 * ROWS, KEYS, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(2 * ROWS, D, false, true);
       const uint64_t qd0 = smem_desc_sw128(smem_u32(smem + Q_OFF), 16, 1024);
       const uint64_t kd0 = smem_desc_sw128(smem_u32(smem + K_OFF), 16, 1024);
       const uint64_t vd0 = smem_desc_sw128(smem_u32(smem + V_OFF), 16384, 1024);
-      auto issue_s = [&](int j) -> bool {  // S_j into S buffer j & 1 of both CTAs
-        const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort, p.err)) return false;
+      auto issue_s = [&](uint32_t gs) -> bool {  // S of ring slot gs into S buffer gs & 1 of both CTAs
+        const int st = gs & 1;
+        if (!mbar_wait(&k_full[st], (gs >> 1) & 1, abort, p.err)) return false;
         tc_fence_after();
         const uint64_t kd = kd0 + (uint64_t)((st * KH_BYTES) >> 4);
 #pragma unroll
@@ -920,139 +952,164 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
         umma_commit_pair(&k_empty[st], 0x3);
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {  // O += P_j V_j, P from both CTAs' TMEM
-        const int st = j & 1;
-        if (!mbar_wait_cluster(&p_full[st], (j >> 1) & 1, abort, p.err)) return false;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort, p.err)) return false;
+      auto issue_pv = [&](uint32_t gs, bool first) -> bool {  // O (+)= P V of slot gs, P from both CTAs' TMEM
+        const int st = gs & 1;
+        if (!mbar_wait_cluster(&p_full[st], (gs >> 1) & 1, abort, p.err)) return false;
+        if (!mbar_wait(&v_full[st], (gs >> 1) & 1, abort, p.err)) return false;
         tc_fence_after();
         const uint64_t vd = vd0 + (uint64_t)((st * VH_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < KEYS / 16; ++kk)
           umma_f16_ts_pair(tmem + 256, tmem + st * KEYS + kk * 8, vd + ((kk * 2048) >> 4), idesc_o,
-                           (j > 0 || kk > 0) ? 1u : 0u);
+                           (!first || kk > 0) ? 1u : 0u);
         umma_commit_pair(&v_empty[st], 0x3);
         umma_commit_pair(pv_done, 0x3);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, abort, p.err) && issue_s(0) && (n_kv < 2 || issue_s(1));
-      for (int j = 0; ok && j < n_kv; ++j) ok = issue_pv(j) && (j + 2 >= n_kv || issue_s(j + 2));
+      uint32_t g = 0;  // steps (ring slots) issued so far (across items)
+      bool ok = true;
+      Item it;
+      for (int r = 0; ok && item_at(p, r, it); ++r) {
+        const int n = it.n_kv;
+        ok = mbar_wait(q_full, r & 1, abort, p.err) && issue_s(g) && (n < 2 || issue_s(g + 1));
+        if (ok && n <= 2) umma_commit_pair(q_empty, 0x3);  // every S of the item issued
+        for (int j = 0; ok && j < n; ++j) {
+          ok = issue_pv(g + j, j == 0) && (j + 2 >= n || issue_s(g + j + 2));
+          if (ok && j + 2 == n - 1) umma_commit_pair(q_empty, 0x3);
+        }
+        g += n;
+      }
     }
   } else {
     // ---------------------------------------------------------------- softmax + epilogue (both CTAs)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qi = mc + r;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t o_addr = tmem + lane_base + 256;
-    const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
-    float m_used = -INFINITY, l = 0.f;
+    uint32_t g = 0;  // steps consumed so far (across items)
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, abort, p.err)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t s_addr = tmem + lane_base + sb * KEYS;
-      const int k0 = j * KEYS;
-      uint32_t rr[KEYS];
-      float alpha = 1.f;
-      bool rescale = false;
-      const bool dead = p.causal && k0 > mc + ROWS - 1;
-      if (dead) {
-        // every key of the tile lies after every row of this CTA (the pair's last tile, even CTA): P = 0
-#pragma unroll
-        for (int e = 0; e < KEYS / 2; ++e) rr[e] = 0u;
-      } else {
-        const bool full_tile = p.mask == nullptr && k0 + KEYS <= p.Sk && (!p.causal || k0 + KEYS - 1 <= mc);
-        const float c_scale = full_tile ? p.scale_log2 : 1.f;
-#pragma unroll
-        for (int c = 0; c < KEYS / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
-        tmem_ld_wait();
-        if (!full_tile) {
-          const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
-#pragma unroll
-          for (int e = 0; e < KEYS; ++e) {
-            const int kj = k0 + e;
-            const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
-            float v = __uint_as_float(rr[e]) * p.scale_log2;
-            if (mrow && valid) v += __half2float(__ushort_as_half(mrow[e])) * 1.4426950408889634f;
-            rr[e] = __float_as_uint(valid ? v : -INFINITY);
-          }
-        }
-        float m8[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
-#pragma unroll
-        for (int e = 8; e < KEYS; e += 2)
-          m8[(e >> 1) & 7] = max3f(m8[(e >> 1) & 7], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
-        const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * c_scale;
-        if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
-          alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
-          rescale = j > 0;
-          m_used = mx;
-          l *= alpha;
-        }
-        const float base = m_used == -INFINITY ? 0.f : m_used;
-        const uint64_t c2 = f2_pack(c_scale, c_scale), nb2 = f2_pack(-base, -base);
-        uint64_t sum4[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int e = 0; e < KEYS; e += 2) {
-          float x0, x1, p0, p1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), c2, nb2), x0, x1);
-          if (((e >> 1) & 7) >= 8 - kPolyPairsOf8) {
-            ex2_poly2(x0, x1, p0, p1);
-          } else {
-            p0 = ex2(x0);
-            p1 = ex2(x1);
-          }
-          sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
-          rr[e >> 1] = pack_f16(p0, p1);
-          if constexpr (DROP) rr[e >> 1] &= drop_pair_mask(rk, (uint32_t)(k0 + e) >> 1, p.drop_thr);
-        }
-        {
-          float a0, a1;
-          f2_unpack(f2_add(f2_add(sum4[0], sum4[1]), f2_add(sum4[2], sum4[3])), a0, a1);
-          l += a0 + a1;
-        }
-      }
-      // O is complete once P.V_{j-1} has: wait for it at every step (so that no phase of the barrier is
-      // skipped), then rescale O if this row's max moved. P.V_j cannot start before this warp's arrival
-      // below, so the barrier is never more than one phase ahead of the wait.
-      if (j > 0) {
-        if (!mbar_wait_warp(pv_done, (j - 1) & 1, abort, p.err)) { ok = false; break; }
+    Item it;
+    for (int ri = 0; ok && item_at(p, ri, it); ++ri) {
+      const int bh = it.bh;
+      const int b = bh / p.Hq, h = bh % p.Hq;
+      const int bhk = b * p.Hkv + h / p.group;
+      const int mc = it.m0 + (int)rank * ROWS;  // this CTA's first query row
+      const int qi = mc + r;
+      const int n_kv = it.n_kv;
+      const uint32_t rk = DROP ? drop_row_key(p.seed_lo, p.seed_hi, (uint32_t)bh, (uint32_t)qi) : 0u;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t gs = g + j;
+        const int sb = gs & 1;
+        if (!mbar_wait_warp(&s_full[sb], (gs >> 1) & 1, abort, p.err)) { ok = false; break; }
         tc_fence_after();
-      }
-      if (!dead && __any_sync(0xffffffffu, rescale)) {
-        const float a = rescale ? alpha : 1.f;
-        const uint64_t a2 = f2_pack(a, a);
-#pragma unroll 1
-        for (int c = 0; c < D / 64; ++c) {
-          uint32_t o[64];
-          tmem_ld32(o_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-          tmem_ld32(o_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-          tmem_ld_wait();
+        const uint32_t s_addr = tmem + lane_base + sb * KEYS;
+        const int k0 = j * KEYS;
+        uint32_t rr[KEYS];
+        float alpha = 1.f;
+        bool rescale = false;
+        const bool dead = p.causal && k0 > mc + ROWS - 1;
+        if (dead) {
+          // every key of the tile lies after every row of this CTA (the pair's last tile, even CTA): P = 0
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            float x0, x1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2, 0), x0, x1);
-            o[e] = __float_as_uint(x0);
-            o[e + 1] = __float_as_uint(x1);
+          for (int e = 0; e < KEYS / 2; ++e) rr[e] = 0u;
+        } else {
+          const bool full_tile = p.mask == nullptr && k0 + KEYS <= p.Sk && (!p.causal || k0 + KEYS - 1 <= mc);
+          const float c_scale = full_tile ? p.scale_log2 : 1.f;
+#pragma unroll
+          for (int c = 0; c < KEYS / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]));
+          tmem_ld_wait();
+          if (!full_tile) {
+            const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)min(qi, p.Sq - 1) * p.mi + k0 : nullptr;
+#pragma unroll
+            for (int e = 0; e < KEYS; ++e) {
+              const int kj = k0 + e;
+              const bool valid = kj < p.Sk && (!p.causal || kj <= qi);
+              float v = __uint_as_float(rr[e]) * p.scale_log2;
+              if (mrow && valid) v += __half2float(__ushort_as_half(mrow[e])) * 1.4426950408889634f;
+              rr[e] = __float_as_uint(valid ? v : -INFINITY);
+            }
           }
-          tmem_st32(o_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-          tmem_st32(o_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+          float m8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(rr[e]);
+#pragma unroll
+          for (int e = 8; e < KEYS; e += 2)
+            m8[(e >> 1) & 7] = max3f(m8[(e >> 1) & 7], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+          const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * c_scale;
+          if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
+            alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+            rescale = j > 0;
+            m_used = mx;
+            l *= alpha;
+          }
+          const float base = m_used == -INFINITY ? 0.f : m_used;
+          const uint64_t c2 = f2_pack(c_scale, c_scale), nb2 = f2_pack(-base, -base);
+          uint64_t sum4[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int e = 0; e < KEYS; e += 2) {
+            float x0, x1, p0, p1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), c2, nb2), x0, x1);
+            if (((e >> 1) & 7) >= 8 - kPolyPairsOf8) {
+              ex2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            sum4[(e >> 1) & 3] = f2_add(sum4[(e >> 1) & 3], f2_pack(p0, p1));
+            rr[e >> 1] = pack_f16(p0, p1);
+            if constexpr (DROP) rr[e >> 1] &= drop_pair_mask(rk, (uint32_t)(k0 + e) >> 1, p.drop_thr);
+          }
+          {
+            float a0, a1;
+            f2_unpack(f2_add(f2_add(sum4[0], sum4[1]), f2_add(sum4[2], sum4[3])), a0, a1);
+            l += a0 + a1;
+          }
+        }
+        // O is complete once P.V of the previous step has: wait for it at every step of the item (the
+        // epilogue waited for the last one of the previous item), so that no phase of the barrier is
+        // skipped, then rescale O if this row's max moved. This step's P.V cannot start before this
+        // warp's arrival below, so the barrier is never more than one phase ahead of the wait.
+        if (j > 0) {
+          if (!mbar_wait_warp(pv_done, (gs - 1) & 1, abort, p.err)) { ok = false; break; }
+          tc_fence_after();
+        }
+        if (!dead && __any_sync(0xffffffffu, rescale)) {
+          const float a = rescale ? alpha : 1.f;
+          const uint64_t a2 = f2_pack(a, a);
+#pragma unroll 1
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t o[64];
+            tmem_ld32(o_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+            tmem_ld32(o_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 64; e += 2) {
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2, 0), x0, x1);
+              o[e] = __float_as_uint(x0);
+              o[e + 1] = __float_as_uint(x1);
+            }
+            tmem_st32(o_addr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+            tmem_st32(o_addr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+          }
+        }
+        // P of the tile's 128 keys onto the S buffer's columns [0, 64)
+        tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+        tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&p_full[sb]);
+          else mbar_arrive_remote_tmem(&p_full[sb], 0);
         }
       }
-      // P of the tile's 128 keys onto the S buffer's columns [0, 64)
-      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
-      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (leader) mbar_arrive(&p_full[sb]);
-        else mbar_arrive_remote(&p_full[sb], 0);
-      }
-    }
-    if (ok && n_kv > 0 && mbar_wait_warp(pv_done, (n_kv - 1) & 1, abort, p.err)) {
+      if (!ok) break;
+      g += n_kv;
+      // epilogue: O leaves TMEM here; the next item's first P.V overwrites it only after this warp's
+      // next p_full arrival, which follows these loads
+      if (!mbar_wait_warp(pv_done, (g - 1) & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
       const float inv_l = l > 0.f ? (DROP ? p.inv_keep : 1.f) / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
@@ -1065,15 +1122,15 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
         tmem_ld_wait();
         if (qi < p.Sq) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
+          for (int gg = 0; gg < 4; ++gg) {
             float v[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(o[8 * g + e]) * inv_l;
-            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) =
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(o[8 * gg + e]) * inv_l;
+            *reinterpret_cast<uint4*>(orow + c * 32 + gg * 8) =
                 make_uint4(pack_bf16(v[0] * sc, v[1] * sc), pack_bf16(v[2] * sc, v[3] * sc),
                            pack_bf16(v[4] * sc, v[5] * sc), pack_bf16(v[6] * sc, v[7] * sc));
             if (o16row)
-              *reinterpret_cast<uint4*>(o16row + c * 32 + g * 8) = make_uint4(
+              *reinterpret_cast<uint4*>(o16row + c * 32 + gg * 8) = make_uint4(
                   pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
           }
         }
@@ -1114,10 +1171,13 @@ int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, cons
       return tbf16_host::check_launch();
     attr_done[dev->device & 63] = true;
   }
+  // one pair per two SMs (shared memory and the 512 TMEM columns allow no second CTA), never more than
+  // the items
   const int64_t items = BHq * ((prm.Sq + 2 * fwd256::ROWS - 1) / (2 * fwd256::ROWS));
-  if (2 * items > INT32_MAX) return TBF16_ERR_INVALID;
+  if (items > INT32_MAX - dev->sms) return TBF16_ERR_INVALID;  // item indices are int
+  const int64_t pairs = std::min<int64_t>(items, dev->sms / 2);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * items));
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(fwd256::THREADS);
   cfg.dynamicSmemBytes = fwd256::SMEM;
   cfg.stream = st;
