@@ -323,53 +323,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&q_full[t & 1], (t >> 1) & 1, abort, p.err) || !mbar_wait_warp(s_full, t & 1, abort, p.err))
         return false;
       tc_fence_after();
-      // fully valid tiles (no user mask, keys and queries in range, whole tile below the causal
-      // diagonal) skip the per-element checks; 3 of every 8 exp2 pairs run on the FMA pipe. The 64
-      // columns go in two halves of 32, so only 32 logits are live at a time.
+      // Fully valid tiles (no user mask, keys and queries in range, whole tile below the causal diagonal)
+      // go straight to the exp; 3 of every 8 exp2 pairs run on the FMA pipe. The 64 columns go in two
+      // halves of 32, so only 32 logits are live at a time. Other tiles first turn S^T into scaled,
+      // masked logits (-inf where masked) in TMEM with a short loop, take the same exp path with c = 1,
+      // and zero P outside this key's valid query columns afterwards (padded queries' lse slots are not
+      // written by the forward). A fully unrolled per-element form of this once-per-CTA path cost more
+      // in instruction fetch than the tile's arithmetic.
       const bool full_tile = p.mask == nullptr && k0 + BKV <= p.Sk && q0 + BQ <= p.Sq && (!p.causal || k0 + BKV - 1 <= q0);
-      const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
+      uint64_t vbits = ~0ull;  // bit c: query column cq + c is valid for this key
+      if (!full_tile) {
+        const int lo = p.causal ? kj - q0 : 0;      // valid columns: lo <= col < hi
+        const int hi = kj < p.Sk ? p.Sq - q0 : 0;
+        const uint16_t* mrow = p.mask ? p.mask + b * p.mb + h * p.mh + (int64_t)q0 * p.mi + min(kj, p.Sk - 1) : nullptr;
+        const uint32_t s_tm = tmem + lane_base + C::T_S + cq;
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(s_tm + c, o);
+          tmem_ld_wait();
+          if (mrow) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = cq + c + i;
+              const bool valid = col >= lo && col < hi;
+              float v = __uint_as_float(o[i]) * p.scale_log2;
+              if (valid) v += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
+              o[i] = __float_as_uint(valid ? v : -INFINITY);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = cq + c + i;
+              o[i] = __float_as_uint(col >= lo && col < hi ? __uint_as_float(o[i]) * p.scale_log2 : -INFINITY);
+            }
+          }
+          tmem_st32(s_tm + c, o);
+        }
+        tmem_st_wait();
+        const int va = max(0, min(64, lo - cq)), vz = max(0, min(64, hi - cq));
+        auto below = [](int n) -> uint64_t { return n >= 64 ? ~0ull : ((1ull << n) - 1); };
+        vbits = vz > va ? below(vz) & ~below(va) : 0ull;
+      }
+      const uint64_t c2 = full_tile ? f2_pack(p.scale_log2, p.scale_log2) : f2_pack(1.f, 1.f);
+      const uint64_t nl2e = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t rr[32];
         tmem_ld32(tmem + lane_base + C::T_S + cq + 32 * hh, rr);
         tmem_ld_wait();
-        if (full_tile) {
-          const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2e = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const int E = 32 * hh + e;
-            const float4 ls = reinterpret_cast<const float4*>(lse_s)[(cq + E) >> 2];
+        for (int e = 0; e < 32; e += 4) {
+          const int E = 32 * hh + e;
+          const float4 ls = reinterpret_cast<const float4*>(lse_s)[(cq + E) >> 2];
 #pragma unroll
-            for (int u = 0; u < 4; u += 2) {
-              float x0, x1, p0, p1;
-              const uint64_t nl = f2_mul(u == 0 ? f2_pack(ls.x, ls.y) : f2_pack(ls.z, ls.w), nl2e);
-              f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])), c2, nl), x0, x1);
-              if ((((E + u) >> 1) & 7) >= 5) {
-                ex2_poly2(x0, x1, p0, p1);
-              } else {
-                p0 = ex2(x0);
-                p1 = ex2(x1);
-              }
-              pp[(E + u) >> 1] = pack_f16(p0, p1);
+          for (int u = 0; u < 4; u += 2) {
+            float x0, x1, p0, p1;
+            const uint64_t nl = f2_mul(u == 0 ? f2_pack(ls.x, ls.y) : f2_pack(ls.z, ls.w), nl2e);
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[e + u]), __uint_as_float(rr[e + u + 1])), c2, nl), x0, x1);
+            if ((((E + u) >> 1) & 7) >= 5) {
+              ex2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
             }
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int E = 32 * hh + e;
-            float pc[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int col = cq + E + u;
-              const int qi = q0 + col;
-              const bool valid = kj < p.Sk && qi < p.Sq && (!p.causal || kj <= qi);
-              float sv = __uint_as_float(rr[e + u]) * p.scale_log2;
-              if (mrow && valid) sv += __half2float(__ushort_as_half(mrow[(int64_t)col * p.mi])) * 1.4426950408889634f;
-              pc[u] = valid ? ex2(sv - lse_s[col] * 1.4426950408889634f) : 0.f;
-            }
-            pp[E >> 1] = pack_f16(pc[0], pc[1]);
+            pp[(E + u) >> 1] = pack_f16(p0, p1);
           }
         }
+      }
+      if (!full_tile) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          pp[c] &= ((vbits >> (2 * c)) & 1 ? 0x0000ffffu : 0u) | ((vbits >> (2 * c + 1)) & 1 ? 0xffff0000u : 0u);
       }
       // dV(t-1) has read the previous P^T: it precedes S(t) in the MMA pipe
       if constexpr (DROP) {
