@@ -799,6 +799,32 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
             del q, k, v, q16, k16, v16
         res["torch_bf16_sdpa_note"] = ("torch's native bf16 F.scaled_dot_product_attention on the same inputs "
                                        "(no fp16 scaling): informational")
+        # head dim 256 (Gemma-3's), the CTA-pair kernel: B=1, H=16, same input distribution
+        res["d256"] = {"config": f"B=1 H={H} D=256, Q,K x2^8, V x2^h, kernel only", "by_S": {}}
+        for S2 in (2048, 8192):
+            q, k, v = inputs.attention_qkv(1, H, S2, 256, seed=0, device="cuda")
+            q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
+            row = {}
+            for causal in (False, True):
+                flop = 4.0 * H * S2 * S2 * 256 * (0.5 if causal else 1.0)
+                for name, fn in (("kernel", lambda: attention.attn_forward(q16, k16, v16, ev, is_causal=causal)),
+                                 ("torch_bf16_sdpa", lambda: torch.nn.functional.scaled_dot_product_attention(
+                                     q, k, v, is_causal=causal))):
+                    for _ in range(2):
+                        fn()
+                    torch.cuda.synchronize()
+                    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s0.record()
+                    for _ in range(iters):
+                        fn()
+                    s1.record()
+                    torch.cuda.synchronize()
+                    t = s0.elapsed_time(s1) / iters
+                    row[f"{'causal' if causal else 'noncausal'}_{name}"] = {
+                        "ms": round(t, 4), "tflops": round(flop / (t / 1e3) / 1e12, 1),
+                        "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
+            res["d256"]["by_S"][S2] = row
+            del q, k, v, q16, k16, v16
     q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda")
     for causal in (False, True):
         flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)
