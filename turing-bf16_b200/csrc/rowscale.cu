@@ -401,6 +401,14 @@ struct Head4 {
   int nbh;             // B*H (set by the launcher)
 };
 
+__device__ __forceinline__ void unpack8(const uint4 v, int is_f16, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = is_f16 ? f16lo(w[j]) : bf16lo(w[j]);
+    f[2 * j + 1] = is_f16 ? f16hi(w[j]) : bf16hi(w[j]);
+  }
+}
 __device__ __forceinline__ void load8(const uint16_t* p, int is_f16, float (&f)[8]) {
   const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -531,12 +539,22 @@ __global__ void __launch_bounds__(256) head_amax_rows_kernel(Head4 t0, Head4 t1,
   if (bh >= t.nbh || s0 >= s1) return;  // the grid covers the widest tensor
   const int b = bh / t.H, h = bh % t.H;
   const uint16_t* base = t.x + b * t.sb + h * t.sh + (threadIdx.x % D8) * 8;
+  constexpr int RS = 256 / D8;  // rows a block covers per step
   float m = 0.f;
-  for (int s = s0 + (int)threadIdx.x / D8; s < s1; s += 256 / D8) {
-    float f[8];
-    load8(base + (int64_t)s * t.ss, t.is_f16, f);
+  int s = s0 + (int)threadIdx.x / D8;
+  for (; s < s1; s += 8 * RS) {  // up to eight independent 16-byte loads in flight per thread
+    uint4 v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+    for (int u = 0; u < 8; ++u)
+      v[u] = s + u * RS < s1 ? __ldg(reinterpret_cast<const uint4*>(base + (int64_t)(s + u * RS) * t.ss))
+                             : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      float f[8];
+      unpack8(v[u], t.is_f16, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+    }
   }
   __shared__ float red[8];
   m = warp_max(m);
@@ -562,9 +580,9 @@ __global__ void __launch_bounds__(256) head_scale_cast_rows_kernel(ScaleCast c0,
   const int sub = (int)threadIdx.x % D8;
   const uint16_t* src = c.x + b * c.sb + h * c.sh + sub * 8;
   uint4* dst = reinterpret_cast<uint4*>(c.y) + (int64_t)bh * c.S * D8 + sub;
-  for (int s = s0 + (int)threadIdx.x / D8; s < s1; s += 256 / D8) {
+  auto convert = [&](const uint4 v) -> uint4 {
     float f[8];
-    load8(src + (int64_t)s * c.ss, c.in_f16, f);
+    unpack8(v, c.in_f16, f);
     uint4 o;
     if (c.out_f16) {
       o.x = pack_f16(f[0] * sc, f[1] * sc); o.y = pack_f16(f[2] * sc, f[3] * sc);
@@ -573,7 +591,18 @@ __global__ void __launch_bounds__(256) head_scale_cast_rows_kernel(ScaleCast c0,
       o.x = pack_bf16(f[0] * sc, f[1] * sc); o.y = pack_bf16(f[2] * sc, f[3] * sc);
       o.z = pack_bf16(f[4] * sc, f[5] * sc); o.w = pack_bf16(f[6] * sc, f[7] * sc);
     }
-    dst[(int64_t)s * D8] = o;
+    return o;
+  };
+  constexpr int RS = 256 / D8;  // rows a block covers per step
+  int s = s0 + (int)threadIdx.x / D8;
+  for (; s < s1; s += 8 * RS) {  // up to eight independent 16-byte loads in flight per thread
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (s + u * RS < s1) v[u] = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)(s + u * RS) * c.ss));
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (s + u * RS < s1) dst[(int64_t)(s + u * RS) * D8] = convert(v[u]);
   }
 }
 
