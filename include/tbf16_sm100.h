@@ -126,6 +126,23 @@ int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, cons
                       int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int v_exp, void* q16, void* k16, void* v16,
                       int32_t* a_out, int32_t* ev_out, float* ws, void* stream);
 
+/* tbf16_prepare_qkv in two phases for attention sharded over heads (this build's head-parallel form of
+ * attention.py:38-48; the reference runs on one GPU): eq and ek are maxima over ALL (b, h), so each rank
+ * computes its own, the caller all-reduces them (MAX), and the second phase scales with the result.
+ * Phase 1: eqk[0..1] (int32, device) = this rank's eq, ek (INT_MIN when B = 0); ws (B*Hq + 2*B*Hkv
+ * floats) keeps the per-head maxima, v's included. Phase 2: a from the all-reduced eqk (same rule as
+ * tbf16_prepare_qkv), ev from ws's v maxima, q16 / k16 / v16 as tbf16_prepare_qkv writes them. Same
+ * arguments and layouts as tbf16_prepare_qkv; ws must be the one phase 1 filled. */
+int tbf16_qkv_local_exponents(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb,
+                              int64_t ksh, int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B,
+                              int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int32_t* eqk, float* ws,
+                              void* stream);
+int tbf16_prepare_qkv_global(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb,
+                             int64_t ksh, int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B,
+                             int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int v_exp, const int32_t* eqk,
+                             const float* ws, void* q16, void* k16, void* v16, int32_t* a_out, int32_t* ev_out,
+                             void* stream);
+
 /* ------------------------------------------------------------------ scaled GEMMs (tcgen05) */
 
 /* Fused scaled linear. Replaces linear(x, w16, ws, bias, cfg, t, l1) (tbf16/csrc/gemm_sm75.cu:257-284,

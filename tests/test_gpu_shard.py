@@ -36,6 +36,18 @@ def _check_rank(rank, world):
     y = shard.linear_column_parallel(x, *shard.shard_weight(w16, ws, None, rank, world))
     if int(ulp_distance(y, full).max()) > 1:
         bad["column_parallel"] = int(ulp_distance(y, full).max())
+    # the two-phase sharded prepare (local exponents, all_reduce, global scale) equals the slice of the
+    # unsharded prepare_qkv: GQA 8/4, a head dim (100) the kernels pad to 104, rank 1's q heads hotter
+    q2, k2, v2 = inputs.attention_qkv(2, 8, 300, 100, seed=34, device=dev, Hkv=4)
+    q2[:, 4:] *= 64
+    g0, g1 = shard.shard_range(4, rank, world)
+    got = shard.prepare_qkv_sharded(q2[:, 2 * g0:2 * g1], k2[:, g0:g1], v2[:, g0:g1], v_exp=13)
+    want = attention.prepare_qkv(q2, k2, v2, v_exp=13)
+    want = (want[0][:, 2 * g0:2 * g1, ..., :100], want[1][:, g0:g1, ..., :100], want[2][:, g0:g1, ..., :100],
+            want[3], want[4][:, g0:g1])
+    for name, g, w in zip(("q16", "k16", "v16", "a", "ev"), got, want):
+        if g.shape != w.shape or not torch.equal(g, w):
+            bad[f"prepare_qkv_sharded {name}"] = (tuple(g.shape), tuple(w.shape))
     # head-sharded attention (inference): rank 1's heads are hotter, so the exchange matters
     q, k, v = inputs.attention_qkv(1, 8, 512, 128, seed=33, device=dev)
     q[:, 4:] *= 64

@@ -489,6 +489,50 @@ __global__ void __launch_bounds__(256) qkv_exponents_kernel(const float* __restr
   }
 }
 
+// Sharded attention, phase 1: this rank's eq, ek (max frexp exponents of its q and k head maxima).
+__global__ void __launch_bounds__(256) qk_max_exponents_kernel(const float* __restrict__ amax_q, int nq,
+                                                               const float* __restrict__ amax_k, int nk,
+                                                               int32_t* __restrict__ eqk) {
+  __shared__ int red[2][8];
+  int eq = INT_MIN, ek = INT_MIN;
+  for (int i = threadIdx.x; i < nq; i += blockDim.x) eq = max(eq, frexp_exp(amax_q[i]));
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) ek = max(ek, frexp_exp(amax_k[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    eq = max(eq, __shfl_xor_sync(0xffffffffu, eq, o));
+    ek = max(ek, __shfl_xor_sync(0xffffffffu, ek, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = eq;
+    red[1][threadIdx.x >> 5] = ek;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)blockDim.x / 32; ++w) {
+      red[0][0] = max(red[0][0], red[0][w]);
+      red[1][0] = max(red[1][0], red[1][w]);
+    }
+    eqk[0] = red[0][0];
+    eqk[1] = red[1][0];
+  }
+}
+
+// Sharded attention, phase 2: a from the all-reduced eq, ek (the rule of qkv_exponents_kernel), and ev
+// from this rank's v head maxima.
+__global__ void __launch_bounds__(256) qkv_exponents_global_kernel(const int32_t* __restrict__ eqk,
+                                                                   const float* __restrict__ amax_v, int nk, int v_exp,
+                                                                   int32_t* __restrict__ a_out,
+                                                                   int32_t* __restrict__ ev_out) {
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) ev_out[i] = frexp_exp(amax_v[i]) - v_exp;
+  if (threadIdx.x == 0) {
+    const int eq = eqk[0], ek = eqk[1];
+    int a = ek - eq;
+    a = (a >= 0) ? a / 2 : -((-a + 1) / 2);  // floor division by 2
+    a = max(min(a, 14 - eq), ek - 14);
+    *a_out = a;
+  }
+}
+
 struct ScaleCast {
   const uint16_t* x;
   int64_t sb, sh, ss;
@@ -671,6 +715,27 @@ int launch_scale_cast(const ScaleCast& c0, const ScaleCast& c1, const ScaleCast&
   return tbf16_host::check_launch();
 }
 
+// q16 = fp16(q * 2^a), k16 = fp16(k * 2^-a), v16 = fp16(v * 2^-ev[b, hk]): one launch for the three.
+int scale_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb, int64_t ksh,
+              int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B, int64_t Hq, int64_t Hkv,
+              int64_t Sq, int64_t Sk, int64_t D, void* q16, void* k16, void* v16, const int32_t* a,
+              const int32_t* ev, cudaStream_t st) {
+  ScaleCast cq;
+  cq.x = static_cast<const uint16_t*>(q); cq.sb = qsb; cq.sh = qsh; cq.ss = qss;
+  cq.H = (int)Hq; cq.S = (int)Sq; cq.D8 = (int)(D / 8);
+  cq.e = a; cq.e_sb = 0; cq.e_sh = 0; cq.e_sign = 1;
+  cq.y = static_cast<uint16_t*>(q16); cq.in_f16 = 0; cq.out_f16 = 1; cq.total8 = B * Hq * Sq * D / 8;
+  ScaleCast ck = cq;
+  ck.x = static_cast<const uint16_t*>(k); ck.sb = ksb; ck.sh = ksh; ck.ss = kss;
+  ck.H = (int)Hkv; ck.S = (int)Sk; ck.e_sign = -1; ck.y = static_cast<uint16_t*>(k16); ck.total8 = B * Hkv * Sk * D / 8;
+  ScaleCast cv = ck;
+  cv.x = static_cast<const uint16_t*>(v); cv.sb = vsb; cv.sh = vsh; cv.ss = vss;
+  cv.e = ev; cv.e_sb = Hkv; cv.e_sh = 1; cv.y = static_cast<uint16_t*>(v16);
+  const int64_t work = std::max(cq.total8, ck.total8);
+  if (work > 0) return launch_scale_cast(cq, ck, cv, 3, B * Hq, std::max(Sq, Sk), work, st);
+  return tbf16_host::check_launch();
+}
+
 }  // namespace
 
 extern "C" {
@@ -815,20 +880,55 @@ int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, cons
     if (int st2 = launch_head_amax(hk, hv, hv, 2, B * Hkv, Sk, st)) return st2;
   }
   qkv_exponents_kernel<<<1, 256, 0, st>>>(amax_q, (int)(B * Hq), amax_k, (int)(B * Hkv), amax_v, v_exp, a_out, ev_out);
-  ScaleCast cq;
-  cq.x = static_cast<const uint16_t*>(q); cq.sb = qsb; cq.sh = qsh; cq.ss = qss;
-  cq.H = (int)Hq; cq.S = (int)Sq; cq.D8 = (int)(D / 8);
-  cq.e = a_out; cq.e_sb = 0; cq.e_sh = 0; cq.e_sign = 1;
-  cq.y = static_cast<uint16_t*>(q16); cq.in_f16 = 0; cq.out_f16 = 1; cq.total8 = B * Hq * Sq * D / 8;
-  ScaleCast ck = cq;
-  ck.x = static_cast<const uint16_t*>(k); ck.sb = ksb; ck.sh = ksh; ck.ss = kss;
-  ck.H = (int)Hkv; ck.S = (int)Sk; ck.e_sign = -1; ck.y = static_cast<uint16_t*>(k16); ck.total8 = B * Hkv * Sk * D / 8;
-  ScaleCast cv = ck;
-  cv.x = static_cast<const uint16_t*>(v); cv.sb = vsb; cv.sh = vsh; cv.ss = vss;
-  cv.e = ev_out; cv.e_sb = Hkv; cv.e_sh = 1; cv.y = static_cast<uint16_t*>(v16);
-  const int64_t work = std::max(cq.total8, ck.total8);
-  if (work > 0) return launch_scale_cast(cq, ck, cv, 3, B * Hq, std::max(Sq, Sk), work, st);
+  return scale_qkv(q, qsb, qsh, qss, k, ksb, ksh, kss, v, vsb, vsh, vss, B, Hq, Hkv, Sq, Sk, D, q16, k16, v16, a_out,
+                   ev_out, st);
+}
+
+int tbf16_qkv_local_exponents(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb,
+                              int64_t ksh, int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B,
+                              int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int32_t* eqk, float* ws,
+                              void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (int st = check_4d(q, B, Hq, Sq, D, qsb, qsh, qss)) return st;
+  if (int st = check_4d(k, B, Hkv, Sk, D, ksb, ksh, kss)) return st;
+  if (int st = check_4d(v, B, Hkv, Sk, D, vsb, vsh, vss)) return st;
+  if (!eqk || !ws || Hkv <= 0 || Hq % Hkv != 0 || B < 0) return TBF16_ERR_INVALID;
+  auto st = static_cast<cudaStream_t>(stream);
+  float* amax_q = ws;
+  float* amax_k = ws + B * Hq;
+  float* amax_v = amax_k + B * Hkv;
+  if (cudaMemsetAsync(ws, 0, sizeof(float) * (B * Hq + 2 * B * Hkv), st) != cudaSuccess) return TBF16_ERR_LAUNCH;
+  Head4 hq = make_head4(q, Hq, Sq, D, qsb, qsh, qss, amax_q, 0);
+  Head4 hk = make_head4(k, Hkv, Sk, D, ksb, ksh, kss, amax_k, 0);
+  Head4 hv = make_head4(v, Hkv, Sk, D, vsb, vsh, vss, amax_v, 0);
+  if (B > 0 && Sq > 0) {
+    if (int st2 = launch_head_amax(hq, hq, hq, 1, B * Hq, Sq, st)) return st2;
+  }
+  if (B > 0 && Sk > 0) {
+    if (int st2 = launch_head_amax(hk, hv, hv, 2, B * Hkv, Sk, st)) return st2;
+  }
+  // with no rows (B = 0) eq = ek = INT_MIN, neutral in the all-reduce (MAX)
+  qk_max_exponents_kernel<<<1, 256, 0, st>>>(amax_q, (int)(B * Hq), amax_k, (int)(B * Hkv), eqk);
   return tbf16_host::check_launch();
+}
+
+int tbf16_prepare_qkv_global(const void* q, int64_t qsb, int64_t qsh, int64_t qss, const void* k, int64_t ksb,
+                             int64_t ksh, int64_t kss, const void* v, int64_t vsb, int64_t vsh, int64_t vss, int64_t B,
+                             int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int v_exp, const int32_t* eqk,
+                             const float* ws, void* q16, void* k16, void* v16, int32_t* a_out, int32_t* ev_out,
+                             void* stream) {
+  if (int st = tbf16_host::require_sm100()) return st;
+  if (int st = check_4d(q, B, Hq, Sq, D, qsb, qsh, qss)) return st;
+  if (int st = check_4d(k, B, Hkv, Sk, D, ksb, ksh, kss)) return st;
+  if (int st = check_4d(v, B, Hkv, Sk, D, vsb, vsh, vss)) return st;
+  if (!q16 || !k16 || !v16 || !a_out || !ev_out || !eqk || !ws || Hkv <= 0 || Hq % Hkv != 0 || B < 0)
+    return TBF16_ERR_INVALID;
+  if (!tbf16_host::aligned16(q16) || !tbf16_host::aligned16(k16) || !tbf16_host::aligned16(v16)) return TBF16_ERR_ALIGN;
+  auto st = static_cast<cudaStream_t>(stream);
+  const float* amax_v = ws + B * Hq + B * Hkv;
+  qkv_exponents_global_kernel<<<1, 256, 0, st>>>(eqk, amax_v, (int)(B * Hkv), v_exp, a_out, ev_out);
+  return scale_qkv(q, qsb, qsh, qss, k, ksb, ksh, kss, v, vsb, vsh, vss, B, Hq, Hkv, Sq, Sk, D, q16, k16, v16, a_out,
+                   ev_out, st);
 }
 
 }  // extern "C"

@@ -32,6 +32,10 @@ SIGNATURES = {
     "tbf16_head_scale_cast": [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp],
     "tbf16_prepare_qkv": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "tbf16_qkv_local_exponents": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
+                                  _i64, _i64, _i64, _i64, _vp, _vp, _vp],
+    "tbf16_prepare_qkv_global": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                 _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "tbf16_linear": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i32, _i32, _vp],
     "tbf16_linear_scaled": [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp],
     "tbf16_gemm_f16": [_vp, _i32, _i64, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp],

@@ -21,6 +21,7 @@ import torch
 import torch.distributed as dist
 
 from . import attention, autograd
+from ._ext import call, ptr, stream_ptr
 from .ops import scaled_linear
 
 
@@ -68,9 +69,43 @@ def global_qk_exponents(q, k, group=None, head_exp=attention.head_exp):
     return e[0], e[1]
 
 
+def _prepare_qkv_sharded_device(q, k, v, v_exp, group):
+    """The CUDA form of prepare_qkv_sharded: tbf16_qkv_local_exponents (this rank's eq, ek and the head
+    maxima), one all_reduce(MAX) of the two int32, tbf16_prepare_qkv_global (a, ev and the fp16 copies):
+    two C calls and one collective, no host synchronisation."""
+    D0 = q.shape[-1]
+    q, k, v = (attention._as_kernel_layout(t) for t in (q, k, v))
+    if not (q.dtype == k.dtype == v.dtype == torch.bfloat16):
+        raise RuntimeError("tbf16.prepare_qkv_sharded: bf16 q, k, v expected")
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    if k.shape[0] != B or k.shape[3] != D or v.shape != k.shape or Hq % Hkv:
+        raise RuntimeError(f"tbf16.prepare_qkv_sharded: incompatible shapes {tuple(q.shape)} {tuple(k.shape)}")
+    dev = q.device
+    eqk = torch.empty(2, device=dev, dtype=torch.int32)
+    ws = torch.empty(B * Hq + 2 * B * Hkv, device=dev, dtype=torch.float32)
+    strides = (ptr(q), *q.stride()[:3], ptr(k), *k.stride()[:3], ptr(v), *v.stride()[:3], B, Hq, Hkv, Sq, Sk, D)
+    call("tbf16_qkv_local_exponents", *strides, ptr(eqk), ptr(ws), stream_ptr(dev))
+    dist.all_reduce(eqk, op=dist.ReduceOp.MAX, group=group)
+    q16 = torch.empty((B, Hq, Sq, D), device=dev, dtype=torch.float16)
+    k16 = torch.empty((B, Hkv, Sk, D), device=dev, dtype=torch.float16)
+    v16 = torch.empty((B, Hkv, Sk, D), device=dev, dtype=torch.float16)
+    a = torch.empty((), device=dev, dtype=torch.int32)
+    ev = torch.empty((B, Hkv), device=dev, dtype=torch.int32)
+    call("tbf16_prepare_qkv_global", *strides, int(v_exp), ptr(eqk), ptr(ws), ptr(q16), ptr(k16), ptr(v16), ptr(a),
+         ptr(ev), stream_ptr(dev))
+    if D != D0:  # the kernels' 8-element padding, sliced back as head_scale does
+        q16, k16, v16 = (t[..., :D0].contiguous() for t in (q16, k16, v16))
+    return q16, k16, v16, a, ev
+
+
 def prepare_qkv_sharded(q, k, v, v_exp=0, group=None, head_exp=attention.head_exp, head_scale=attention.head_scale):
     """prepare_qkv for this rank's heads with the global eq, ek: (q16, k16, v16, a, ev), identical to the
-    corresponding slice of the unsharded prepare_qkv (ev is per (b, h_kv), so it needs no exchange)."""
+    corresponding slice of the unsharded prepare_qkv (ev is per (b, h_kv), so it needs no exchange).
+    On CUDA with the library's own ops this is two C calls around one all_reduce; with other head_exp /
+    head_scale (the CPU checks of the exchange over gloo) it is composed from them."""
+    if q.is_cuda and head_exp is attention.head_exp and head_scale is attention.head_scale:
+        return _prepare_qkv_sharded_device(q, k, v, v_exp, group)
     eq, ek = global_qk_exponents(q, k, group, head_exp)
     a = torch.div(ek - eq, 2, rounding_mode="floor")
     a = torch.maximum(torch.minimum(a, 14 - eq), ek - 14)
