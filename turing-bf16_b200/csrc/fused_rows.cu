@@ -223,11 +223,19 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) n
   __shared__ float red[kMaxThreads / 32];
   RowGroup<WARP> rg(red);
   if (WARP && rg.row >= p.M) return;
-  uint4 v[NCH];
+  uint4 v[NCH], rvs[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int i = rg.tid + rg.nthr * c;
     v[c] = i < p.K8 ? __ldg(p.x + rg.row * p.ldx8 + i) : make_uint4(0, 0, 0, 0);
+  }
+  // the residual row's loads go out with x's, not after the first norm's reduction
+  if (p.res) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = rg.tid + rg.nthr * c;
+      rvs[c] = i < p.K8 ? __ldg(p.res + rg.row * p.ldr8 + i) : make_uint4(0, 0, 0, 0);
+    }
   }
   if (p.wa) norm_in_place<NCH, STYLE, WARP>(rg, v, p.wa, p.K8, p.K, p.eps, p.offset);
   if (p.res) {
@@ -235,7 +243,7 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) n
     for (int c = 0; c < NCH; ++c) {
       const int i = rg.tid + rg.nthr * c;
       if (i < p.K8) {
-        const uint4 rv = __ldg(p.res + rg.row * p.ldr8 + i);
+        const uint4 rv = rvs[c];
         v[c] = make_uint4(pack_bf16(bf16lo(rv.x) + bf16lo(v[c].x), bf16hi(rv.x) + bf16hi(v[c].x)),
                           pack_bf16(bf16lo(rv.y) + bf16lo(v[c].y), bf16hi(rv.y) + bf16hi(v[c].y)),
                           pack_bf16(bf16lo(rv.z) + bf16lo(v[c].z), bf16hi(rv.z) + bf16hi(v[c].z)),
