@@ -1034,7 +1034,7 @@ def collectives_run(pk, world, rank, iters=5):
 def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16=None):
     """Same metric through the public API for host-resident activations (tbf16.ops.linear_host): every
     step uploads x from pinned host memory and reads y back into pinned host memory inside the timed
-    region; the call pipelines 2048-row chunks over three streams (upload, tbf16_linear, download)."""
+    region; the call pipelines 1024-row chunks over three streams (upload, tbf16_linear, download)."""
     from tbf16 import ops
     hx = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
     hx.copy_(x.cpu())
@@ -1058,7 +1058,7 @@ def e2e_run(M, N, K, x, w16, ws, y, s_inv, stream, args, world, x16=None):
     return {"value": round(2.0 * M * N * K * world * steps / (ms / 1e3) / 1e12, 3), "unit": "TFLOPS",
             "h2d_bytes_per_step": 2 * M * K, "d2h_bytes_per_step": 2 * M * N, "steps": steps,
             "ms_per_step": round(ms / steps, 3),
-            "path": "tbf16.ops.linear_host: pinned host x and y, 2048-row chunks pipelined over upload / tbf16_linear / download streams"}
+            "path": "tbf16.ops.linear_host: pinned host x and y, 1024-row chunks pipelined over upload / tbf16_linear / download streams"}
 
 
 if __name__ == "__main__":

@@ -182,7 +182,7 @@ def scaled_linear(x: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias
 
 
 def linear_host(x_host: torch.Tensor, w16: torch.Tensor, w_sinv: torch.Tensor, bias=None, out=None,
-                chunk_rows: int = 2048) -> torch.Tensor:
+                chunk_rows: int = 1024) -> torch.Tensor:
     """scaled_linear for activations in pinned host memory: y_host (M, N) bf16 = x_host @ W^T + b.
 
     Rows go through in chunks on three streams, so the upload of chunk c+1, the linear of chunk c and
