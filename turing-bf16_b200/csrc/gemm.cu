@@ -369,19 +369,26 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int M, i
 // warps release an accumulator on the even CTA's barrier. No multicast loads.
 constexpr int kPairStages = 6;
 // PN: the pair tile's width (256 x PN outputs; 256 for the headline shapes, 192 / 160 / 128 for products
-// whose last wave of 256-wide tiles would leave most pairs idle).
+// whose last wave of 256-wide tiles would leave most pairs idle, 320 for products that fit one wave of
+// 320-wide tiles but not of 256-wide ones, e.g. 2048 x 2560: 64 tiles on 74 pairs instead of 80).
+// PN = 320 (WIDE) issues two N = 160 MMAs per k16 step into one 320-column accumulator: TMEM holds only
+// one, so the next tile's MMAs wait for the epilogue -- it is chosen only when no pair gets a second tile.
 template <int PN>
 struct PairCfg {
-  static_assert(PN % 32 == 0 && PN >= 128 && PN <= 256, "pair tile width");
+  static_assert((PN % 32 == 0 && PN >= 128 && PN <= 256) || PN == 320, "pair tile width");
+  static constexpr bool WIDE = PN > 256;
+  static constexpr int NACC = WIDE ? 1 : 2;            // PN-column accumulators in TMEM
+  static constexpr int STAGES = WIDE ? 5 : kPairStages;
   static constexpr int A_BYTES = BM * BK * 2;          // this CTA's 128 rows
   static constexpr int B_BYTES = (PN / 2) * BK * 2;    // this CTA's half of the PN B rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int THREADS = 32 * (2 + kEpiWarps);
-  static constexpr int TMEM_COLS = 512;                // two PN-column accumulators
+  static constexpr int TMEM_COLS = 512;
   static constexpr int EPI_BYTES = kEpiWarps * 2 * 32 * 64;  // per epilogue warp two 32 x 32 bf16 tiles
-  static constexpr int BAR_BYTES = 8 * (2 * kPairStages + 4) + 16;
-  static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(NACC * PN <= TMEM_COLS, "TMEM");
 };
 
 template <bool A_MN, bool B_MN, bool CONV, int PN>
@@ -389,8 +396,8 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
     scaled_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmY, const GemmParams p) {
   using C = PairCfg<PN>;
-  static_assert(PN == 256 || (!B_MN && !CONV), "narrow pair tiles take K-major B only");
-  constexpr int S = kPairStages;
+  static_assert(PN == 256 || (!B_MN && !CONV), "narrow and wide pair tiles take K-major B only");
+  constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES + C::EPI_BYTES);  // even CTA's are used
@@ -474,7 +481,13 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
           }
         };
         auto load_b = [&](uint8_t* sB, uint64_t* bar, int kb) {
-          if (!B_MN) {
+          if (C::WIDE) {
+            // two boxes of PN / 4 rows: tile columns [PN/4 rank, +PN/4) and [PN/2 + PN/4 rank, +PN/4), so
+            // that the first N = PN/2 MMA (PN/4 rows from each CTA) writes tile columns [0, PN/2) and the
+            // second [PN/2, PN) in order
+            tma_load_2d_pair(sB, &tmB, bar, kb * BK, tn * PN + (int)rank * (PN / 4));
+            tma_load_2d_pair(sB + (PN / 4) * BK * 2, &tmB, bar, kb * BK, tn * PN + PN / 2 + (int)rank * (PN / 4));
+          } else if (!B_MN) {
             tma_load_2d_pair(sB, &tmB, bar, kb * BK, n0);
           } else {
 #pragma unroll
@@ -508,7 +521,7 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(256, PN, A_MN, B_MN);
+      constexpr uint32_t idesc = idesc_f16_f32(256, C::WIDE ? PN / 2 : PN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -530,13 +543,16 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
             const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024)
                                      : smem_desc_sw128(b_addr + k * 32, 16, 1024);
             umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (C::WIDE)
+              umma_f16_ss_pair(d_tmem + PN / 2, ad, smem_desc_sw128(b_addr + (PN / 4) * BK * 2 + k * 32, 16, 1024),
+                               idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
         umma_commit_pair(&tfull[acc], 0x3);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++acc == C::NACC) { acc = 0; acc_phase ^= 1; }
       }
     }
   } else {
@@ -601,7 +617,7 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(&tempty[acc], 0);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++acc == C::NACC) { acc = 0; acc_phase ^= 1; }
         continue;
       }
       __nv_bfloat16* yrow = p.y + (int64_t)(mok ? m : 0) * p.ldy;
@@ -636,7 +652,7 @@ __global__ void __launch_bounds__(PairCfg<PN>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(&tempty[acc], 0);  // the even CTA's MMA may reuse the accumulator
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      if (++acc == C::NACC) { acc = 0; acc_phase ^= 1; }
     }
   }
 
@@ -665,7 +681,7 @@ int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, i
   if (!d) return TBF16_ERR_DEVICE;
   CUtensorMap tb;
   int rc = B_MN ? tbf16_host::make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64)
-                : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, PN / 2);
+                : tbf16_host::make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, C::WIDE ? PN / 4 : PN / 2);
   if (rc) return rc;
   CUtensorMap ty;
   rc = tbf16_host::make_tmap_2d_out(&ty, y, (uint64_t)N, (uint64_t)M, (uint64_t)ldy, 32, 32);
@@ -725,13 +741,15 @@ int launch_pair_core(const CUtensorMap& ta, const void* B, int64_t ldb, int M, i
 // graph): 600 x 1000 x 1024 16.7 -> 13.1 us at 128; 2048 x 2560 x 2048 33.1 -> 31.4 us and x 10240
 // 109.7 -> 107.5 us at 160 -- far less than the waves suggest, because a narrow tile moves more operand
 // bytes per flop and the kernel is close to the L2 -> shared-memory rate with every SM loading (4096^3:
-// 101.6 us at 256, 128 us at 160). TBF16_GEMM_PN = 256 / 192 / 160 / 128 forces one.
+// 101.6 us at 256, 128 us at 160). 320 (one tile per pair at most, see PairCfg) moves fewer operand bytes
+// per flop than 256 and is taken whenever it has the least cost. TBF16_GEMM_PN = 320 / 256 / 192 / 160 /
+// 128 forces one.
 int pair_width(int M, int N, int pairs) {
   static const int env = [] {
     const char* e = getenv("TBF16_GEMM_PN");
     return e ? atoi(e) : 0;
   }();
-  if (env == 256 || env == 192 || env == 160 || env == 128) return env;
+  if (env == 320 || env == 256 || env == 192 || env == 160 || env == 128) return env;
   const int64_t tm = (M + 255) / 256;
   auto cost = [&](int pn) {
     const int64_t tiles = tm * ((N + pn - 1) / pn);
@@ -747,6 +765,7 @@ int pair_width(int M, int N, int pairs) {
       best = pn;
     }
   }
+  if (tm * ((N + 319) / 320) <= pairs && cost(320) < best_cost) best = 320;
   return best;
 }
 
@@ -760,6 +779,7 @@ int launch_gemm_pair(const void* A, int64_t lda, const void* B, int64_t ldb, int
   if (!B_MN) {
     const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
     switch (pair_width(M, N, d ? d->sms / 2 : 74)) {
+      case 320: return launch_pair_core<A_MN, false, false, 320>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
       case 192: return launch_pair_core<A_MN, false, false, 192>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
       case 160: return launch_pair_core<A_MN, false, false, 160>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
       case 128: return launch_pair_core<A_MN, false, false, 128>(ta, B, ldb, M, N, K, sa, sb, bias, y, ldy, nullptr, st, pdl);
