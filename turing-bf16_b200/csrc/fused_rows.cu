@@ -28,6 +28,7 @@ namespace {
 constexpr int kMaxThreads = 1024;
 constexpr int kMaxChunks = 2;       // 16-byte vectors per thread and input in the block-per-row kernels
 constexpr int kWarpRowsMaxK8 = 128;  // rows up to 1024 elements: one warp per row (up to 4 vectors a lane)
+constexpr int kWarpNormMaxK8 = 512;  // many-row norms take a warp per row up to 4096 elements (16 a lane)
 constexpr int kWarpRowsPerBlock = 8;
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -178,7 +179,7 @@ struct NormRows {
 };
 
 // v = RMSNorm(v) with weight w, in place: mean of squares in fp32 (per thread, then the group's
-// fixed-order reduction), then the style's rounding.
+// fixed-order reduction), then the style's rounding. WARP: w is the block's shared-memory copy.
 template <int NCH, int STYLE, bool WARP>
 __device__ __forceinline__ void norm_in_place(RowGroup<WARP>& rg, uint4 (&v)[NCH], const uint4* __restrict__ w, int K8,
                                               int K, float eps, float offset) {
@@ -197,7 +198,7 @@ __device__ __forceinline__ void norm_in_place(RowGroup<WARP>& rg, uint4 (&v)[NCH
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int i = rg.tid + rg.nthr * c;
-    const uint4 wv = i < K8 ? __ldg(w + i) : make_uint4(0, 0, 0, 0);
+    const uint4 wv = i < K8 ? (WARP ? w[i] : __ldg(w + i)) : make_uint4(0, 0, 0, 0);
     const uint32_t xw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
     uint32_t yw[4];
@@ -217,27 +218,46 @@ __device__ __forceinline__ void norm_in_place(RowGroup<WARP>& rg, uint4 (&v)[NCH
   }
 }
 
+// A warp per row: two 256-thread blocks per SM for rows of up to 10 vectors a lane (2560 elements, where
+// the 12-vector form took 201 registers and left one block per SM, so 2048 rows ran in two rounds of 148
+// blocks; capping it at 128 registers spilled), and the norm
+// weights, which every row of the block reads, staged once in shared memory while the rows load (no L2
+// round trip after each norm's reduction).
 template <int NCH, int STYLE, bool WARP>
-__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) norm_rows_kernel(const NormRows p) {
+__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads, (WARP && NCH <= 10) ? 2 : 1)
+    norm_rows_kernel(const NormRows p) {
   pdl_launch_dependents();
   __shared__ float red[kMaxThreads / 32];
+  __shared__ uint4 wsm[WARP ? 2 * kWarpNormMaxK8 : 1];
   RowGroup<WARP> rg(red);
-  if (WARP && rg.row >= p.M) return;
+  const bool live = !WARP || rg.row < p.M;
   uint4 v[NCH], rvs[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int i = rg.tid + rg.nthr * c;
-    v[c] = i < p.K8 ? __ldg(p.x + rg.row * p.ldx8 + i) : make_uint4(0, 0, 0, 0);
+    v[c] = live && i < p.K8 ? __ldg(p.x + rg.row * p.ldx8 + i) : make_uint4(0, 0, 0, 0);
   }
   // the residual row's loads go out with x's, not after the first norm's reduction
   if (p.res) {
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int i = rg.tid + rg.nthr * c;
-      rvs[c] = i < p.K8 ? __ldg(p.res + rg.row * p.ldr8 + i) : make_uint4(0, 0, 0, 0);
+      rvs[c] = live && i < p.K8 ? __ldg(p.res + rg.row * p.ldr8 + i) : make_uint4(0, 0, 0, 0);
     }
   }
-  if (p.wa) norm_in_place<NCH, STYLE, WARP>(rg, v, p.wa, p.K8, p.K, p.eps, p.offset);
+  const uint4* wa = p.wa;
+  const uint4* wb = p.wb;
+  if (WARP) {
+    for (int i = threadIdx.x; i < p.K8; i += blockDim.x) {
+      if (p.wa) wsm[i] = __ldg(p.wa + i);
+      if (p.wb) wsm[kWarpNormMaxK8 + i] = __ldg(p.wb + i);
+    }
+    __syncthreads();
+    wa = p.wa ? wsm : nullptr;
+    wb = p.wb ? wsm + kWarpNormMaxK8 : nullptr;
+    if (!live) return;
+  }
+  if (wa) norm_in_place<NCH, STYLE, WARP>(rg, v, wa, p.K8, p.K, p.eps, p.offset);
   if (p.res) {
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
@@ -258,7 +278,7 @@ __global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) n
       if (i < p.K8) p.a_out[rg.row * p.lda8 + i] = v[c];
     }
   }
-  if (p.wb) norm_in_place<NCH, STYLE, WARP>(rg, v, p.wb, p.K8, p.K, p.eps, p.offset);
+  if (wb) norm_in_place<NCH, STYLE, WARP>(rg, v, wb, p.K8, p.K, p.eps, p.offset);
   float amax = 0.f;
   if (p.y16) {
     float m = 0.f;
@@ -424,7 +444,8 @@ RowLaunch row_launch(int64_t K8, int64_t M, int64_t warp_max_k8) {
   if (K8 <= kWarpRowsMaxK8) return {true, K8 <= 32 ? 1 : (K8 <= 64 ? 2 : 4), 32 * kWarpRowsPerBlock};
   // enough rows to fill the GPU with warps: a warp per row, 8 or 16 vectors a lane (no block barriers,
   // many loads in flight per thread)
-  if (K8 <= warp_max_k8 && M >= 1024) return {true, K8 <= 256 ? 8 : (K8 <= 384 ? 12 : 16), 32 * kWarpRowsPerBlock};
+  if (K8 <= warp_max_k8 && M >= 1024)
+    return {true, K8 <= 256 ? 8 : K8 <= 320 ? 10 : K8 <= 384 ? 12 : 16, 32 * kWarpRowsPerBlock};
   for (int c = 1; c <= kMaxChunks; c *= 2)
     if (K8 <= (int64_t)kMaxThreads * c) {
       const int64_t per = (K8 + c - 1) / c;
@@ -436,7 +457,7 @@ RowLaunch row_launch(int64_t K8, int64_t M, int64_t warp_max_k8) {
 int launch_norm_rows(const NormRows& p, int style, cudaStream_t st) {
   static const int warp_max = [] {  // rows (in 16-byte vectors) up to which many-row norms take a warp per row
     const char* e = getenv("TBF16_NORM_WARP_MAX_K8");
-    return e ? atoi(e) : 512;
+    return e ? std::min(atoi(e), kWarpNormMaxK8) : kWarpNormMaxK8;  // 16 vectors a lane at most
   }();
   const RowLaunch L = row_launch(p.K8, p.M, warp_max);
   if (!L.nch || p.M > INT32_MAX) return TBF16_ERR_UNSUPPORTED;  // rows above TBF16_FUSED_MAX_ROW
@@ -450,6 +471,7 @@ int launch_norm_rows(const NormRows& p, int style, cudaStream_t st) {
       case 2: TBF16_NORM_STYLE(2, true); break;
       case 4: TBF16_NORM_STYLE(4, true); break;
       case 8: TBF16_NORM_STYLE(8, true); break;
+      case 10: TBF16_NORM_STYLE(10, true); break;
       case 12: TBF16_NORM_STYLE(12, true); break;
       default: TBF16_NORM_STYLE(16, true); break;
     }
