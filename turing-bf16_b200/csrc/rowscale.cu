@@ -694,6 +694,34 @@ int launch_head_amax(Head4 a, Head4 b, Head4 c, int ntensors, int64_t BH, int64_
   return tbf16_host::check_launch();
 }
 
+// Head maxima of q (B*Hq slices of Sq rows) and of k and v (B*Hkv slices of Sk rows each): one launch of
+// the row-structured kernel over the three when it applies (blocks past a tensor's own slices or rows
+// return at once; the maxima are atomicMax over row blocks, so the chunking does not change them), else
+// one launch for q and one for k and v.
+int launch_head_amax_qkv(Head4 hq, Head4 hk, Head4 hv, int64_t BHq, int64_t Sq, int64_t BHk, int64_t Sk,
+                         cudaStream_t st) {
+  const int64_t BH = std::max(BHq, BHk), S = std::max(Sq, Sk);
+  const int D8 = hq.D8;
+  if (Sq > 0 && Sk > 0 && BH <= 65535 && (D8 == 8 || D8 == 16 || D8 == 32)) {
+    const tbf16_host::DeviceInfo* d = tbf16_host::device_info();
+    const int sms = d ? d->sms : 148;
+    const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>((sms * 8 + BH - 1) / BH, (S + 63) / 64));
+    const int rows = (int)((S + chunks - 1) / chunks);
+    hq.nbh = (int)BHq;
+    hk.nbh = hv.nbh = (int)BHk;
+    const dim3 grid(chunks, (unsigned)BH, 3);
+    if (D8 == 8) head_amax_rows_kernel<8><<<grid, 256, 0, st>>>(hq, hk, hv, rows);
+    else if (D8 == 16) head_amax_rows_kernel<16><<<grid, 256, 0, st>>>(hq, hk, hv, rows);
+    else head_amax_rows_kernel<32><<<grid, 256, 0, st>>>(hq, hk, hv, rows);
+    return tbf16_host::check_launch();
+  }
+  if (Sq > 0)
+    if (int rc = launch_head_amax(hq, hq, hq, 1, BHq, Sq, st)) return rc;
+  if (Sk > 0)
+    if (int rc = launch_head_amax(hk, hv, hv, 2, BHk, Sk, st)) return rc;
+  return TBF16_OK;
+}
+
 // Launches the scale-cast of up to three tensors (same head dim): the row-structured form for D8 in
 // {8, 16, 32}, the flat form otherwise. max_bh / max_s: the widest tensor's B*H and S.
 int launch_scale_cast(const ScaleCast& c0, const ScaleCast& c1, const ScaleCast& c2, int ntensors, int64_t max_bh,
@@ -872,13 +900,7 @@ int tbf16_prepare_qkv(const void* q, int64_t qsb, int64_t qsh, int64_t qss, cons
   Head4 hq = make_head4(q, Hq, Sq, D, qsb, qsh, qss, amax_q, 0);
   Head4 hk = make_head4(k, Hkv, Sk, D, ksb, ksh, kss, amax_k, 0);
   Head4 hv = make_head4(v, Hkv, Sk, D, vsb, vsh, vss, amax_v, 0);
-  // q has B*Hq slices, k and v B*Hkv each: one launch for q, one for k and v together.
-  if (Sq > 0) {
-    if (int st2 = launch_head_amax(hq, hq, hq, 1, B * Hq, Sq, st)) return st2;
-  }
-  if (Sk > 0) {
-    if (int st2 = launch_head_amax(hk, hv, hv, 2, B * Hkv, Sk, st)) return st2;
-  }
+  if (int st2 = launch_head_amax_qkv(hq, hk, hv, B * Hq, Sq, B * Hkv, Sk, st)) return st2;
   qkv_exponents_kernel<<<1, 256, 0, st>>>(amax_q, (int)(B * Hq), amax_k, (int)(B * Hkv), amax_v, v_exp, a_out, ev_out);
   return scale_qkv(q, qsb, qsh, qss, k, ksb, ksh, kss, v, vsb, vsh, vss, B, Hq, Hkv, Sq, Sk, D, q16, k16, v16, a_out,
                    ev_out, st);
@@ -901,12 +923,8 @@ int tbf16_qkv_local_exponents(const void* q, int64_t qsb, int64_t qsh, int64_t q
   Head4 hq = make_head4(q, Hq, Sq, D, qsb, qsh, qss, amax_q, 0);
   Head4 hk = make_head4(k, Hkv, Sk, D, ksb, ksh, kss, amax_k, 0);
   Head4 hv = make_head4(v, Hkv, Sk, D, vsb, vsh, vss, amax_v, 0);
-  if (B > 0 && Sq > 0) {
-    if (int st2 = launch_head_amax(hq, hq, hq, 1, B * Hq, Sq, st)) return st2;
-  }
-  if (B > 0 && Sk > 0) {
-    if (int st2 = launch_head_amax(hk, hv, hv, 2, B * Hkv, Sk, st)) return st2;
-  }
+  if (B > 0)
+    if (int st2 = launch_head_amax_qkv(hq, hk, hv, B * Hq, Sq, B * Hkv, Sk, st)) return st2;
   // with no rows (B = 0) eq = ek = INT_MIN, neutral in the all-reduce (MAX)
   qk_max_exponents_kernel<<<1, 256, 0, st>>>(amax_q, (int)(B * Hq), amax_k, (int)(B * Hkv), eqk);
   return tbf16_host::check_launch();
