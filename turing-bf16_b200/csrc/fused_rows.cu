@@ -117,8 +117,11 @@ __device__ __forceinline__ void emit_row(const RowGroup<WARP>& rg, const uint4 (
   if (rg.tid == 0 && y16) s_inv[rg.row] = inv_pow2_from_biased(se);
 }
 
+// Block per row: at most 32 registers a thread, so that two blocks of up to 1024 threads (three of the
+// 640 a 10240-wide GeGLU row takes) stay on an SM: with 46 the 10240-wide form kept two rows in flight per
+// SM and ran 30.9 us at 2048 rows, at 32 (a 20-byte spill) 28.3 us.
 template <int NCH, int ACT, bool WARP>
-__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads) glu_rows_kernel(const uint4* __restrict__ g, int64_t ldg8,
+__global__ void __launch_bounds__(WARP ? 32 * kWarpRowsPerBlock : kMaxThreads, WARP ? 1 : 2) glu_rows_kernel(const uint4* __restrict__ g, int64_t ldg8,
                                                                const uint4* __restrict__ u, int64_t ldu8, int64_t M,
                                                                int I8, int t, uint4* __restrict__ y16, int64_t ldy8,
                                                                float* __restrict__ s_inv, uint4* __restrict__ out,
