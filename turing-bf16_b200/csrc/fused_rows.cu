@@ -437,8 +437,9 @@ __global__ void __launch_bounds__(256) glu_bwd_kernel(const uint4* __restrict__ 
 }
 
 // Launch shape for rows of K8 16-byte vectors: short rows one warp each (vectors per lane nch of 1, 2, 4);
-// longer rows one block each, nch (1 or 2) vectors per thread and the fewest warps that cover the row, so
-// that each thread holds little and many blocks fit an SM. nch = 0: the row is too long.
+// longer rows one block each, nch (1 or 2) vectors per thread and the fewest warps that cover the row (up
+// to 512 while two vectors a thread do), so that each thread holds little and many blocks fit an SM.
+// nch = 0: the row is too long.
 struct RowLaunch {
   bool warp;
   int nch, threads;
@@ -449,8 +450,10 @@ RowLaunch row_launch(int64_t K8, int64_t M, int64_t warp_max_k8) {
   // many loads in flight per thread)
   if (K8 <= warp_max_k8 && M >= 1024)
     return {true, K8 <= 256 ? 8 : K8 <= 320 ? 10 : K8 <= 384 ? 12 : 16, 32 * kWarpRowsPerBlock};
+  // at most 512 threads where two vectors a thread cover the row: four blocks (rows) per SM instead of two
+  // (8192-wide SiLU rows over 8192 rows: 90.3 -> 64.2 us)
   for (int c = 1; c <= kMaxChunks; c *= 2)
-    if (K8 <= (int64_t)kMaxThreads * c) {
+    if (K8 <= (int64_t)(K8 <= 512 * kMaxChunks ? 512 : kMaxThreads) * c) {
       const int64_t per = (K8 + c - 1) / c;
       return {false, c, (int)((per + 31) / 32 * 32)};
     }
