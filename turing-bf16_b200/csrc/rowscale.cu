@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(256) row_pass_kernel(const uint4* __restrict__
   }
 }
 
-// The same for few long rows (decode and small batches) and for rows longer than 4096 elements: one
+// The same for few long rows (decode and small batches) and for rows longer than 2048 elements: one
 // 256-thread block per row, thread t holding the row's 16-byte chunks t, t + 256, ... in registers, so a
 // 16-row linear input spreads over 16 SMs instead of two, each thread waits for at most NCH loads, and
 // long rows need no more than 8 vectors a thread. The max (or fp64 L1 sum) is reduced over
@@ -227,11 +227,12 @@ __global__ void __launch_bounds__(256) row_pass_block_kernel(const uint4* __rest
 }
 
 // A block per row up to this many rows (8 per block would leave SMs idle), and for every row count when
-// the rows are longer than 4096 elements: the warp-per-row form then holds 32 vectors a lane (255
-// registers with spills, one block per SM) and at 8192 x 8192 took 51.2 us (max rule, fp16 copy) and
-// 65.5 us (L1) against 45.1 and 47.1 us for a block per row.
+// the rows are longer than 2048 elements: the warp-per-row form then holds 16 or 32 vectors a lane (153
+// to 255 registers, one block per SM, spills at 32) and took, over 8192 rows, 30.7 / 34.8 us at 4096
+// columns and 51.2 / 65.5 us at 8192 (max rule with the fp16 copy / L1) against 26.6 / 28.7 and 45.1 /
+// 47.1 us for a block per row.
 constexpr int64_t kBlockRowsMax = 1024;
-constexpr int kBlockRowsAnyK8 = 512;
+constexpr int kBlockRowsAnyK8 = 256;
 
 template <bool L1, bool FUSED_RULE, bool WRITE_Y>
 bool launch_row_pass_t(const void* x, int64_t rows, int K8, int64_t ldx8, int t, void* y, int64_t ldy8, float* s_inv,
