@@ -131,12 +131,13 @@ def test_skinny_linear_vs_oracle(M, K, N, bias):
 
 # Products whose last wave of 256-wide pair tiles would leave most CTA pairs idle take other pair tile
 # widths: 2048 x 3072 -> 192 columns, 600 x 1000 and 520 x 520 -> 128 (M and N tails, the last tile partly
-# past N); 2048 x 2560 (Gemma's o_proj / down_proj at 2048 tokens) and 2000 x 2504 (M and N tails) fit one
+# past N); 2048 x 2560 (Gemma's o_proj / down_proj at 2048 tokens), 2000 x 2504 (M and N tails) and 1800 x
+# 2392 (the last tile's second 160 columns wholly past N: both CTAs' second boxes are zero fill) fit one
 # wave of 320-wide tiles (two N = 160 MMAs per k16 step into one accumulator, each CTA's B rows loaded as
 # two boxes).
 @pytest.mark.parametrize("M,K,N,bias,rows", [(2048, 1024, 3072, True, 64), (2048, 2048, 2560, False, 64),
-                                             (2000, 1032, 2504, True, 64), (600, 1032, 1000, True, None),
-                                             (520, 256, 520, False, None)])
+                                             (2000, 1032, 2504, True, 64), (1800, 520, 2392, False, None),
+                                             (600, 1032, 1000, True, None), (520, 256, 520, False, None)])
 def test_narrow_pair_tiles_vs_oracle(M, K, N, bias, rows):
     x = inputs.gemm_x(M, K, seed=M + N)
     w = inputs.gemm_w(N, K, seed=K + 3)
