@@ -23,7 +23,10 @@ def _check(y, x, w16, ws, b):
 
 @pytest.mark.parametrize("M,K,N,bias", [(1, 4096, 4096, False), (1, 1024, 1000, True), (2, 520, 264, True),
                                         (3, 8192, 1024, False), (5, 72, 33, True), (8, 4096, 4096, True),
-                                        (8, 16384, 256, False)])
+                                        (8, 16384, 256, False),
+                                        # two-vector form for 1-2 rows up to K = 4096: at the bound, one past
+                                        # it (four-vector form), and a second vector only some threads hold
+                                        (2, 4096, 1032, True), (2, 4104, 520, False), (1, 2056, 777, True)])
 def test_gemv_vs_oracle(M, K, N, bias):
     from tbf16 import ops
     x = inputs.gemm_x(M, K, seed=M + K)
