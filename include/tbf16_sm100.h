@@ -369,6 +369,22 @@ int tbf16_attn_bwd_dropout(const void* q16, const void* k16, const void* v16, co
 int tbf16_attn_dropout_keep(uint8_t* keep, int64_t BH, int64_t Sq, int64_t Sk, float dropout_p, uint64_t seed,
                             void* stream);
 
+/* tbf16_attn_fwd_dropout (dropout_p = 0: tbf16_attn_fwd_out) with a device workspace. Head dim 256 with
+ * few 256-row query blocks for the device's CTA pairs (one short sequence, few heads: a 2048-token
+ * prefill of 8 heads is 64 blocks on 74 pairs) cuts the longest blocks into two parts over their key
+ * tiles, run by different pairs and added in fp32 through ws; each part rounds its softmax weights to
+ * fp16 against its own running max, so outputs match the plain call's within that rounding, and are the
+ * same bits whichever part finishes first. tbf16_attn_fwd_ws_size gives the bytes (0: the plain schedule,
+ * ws may be null); a smaller or null ws runs the plain schedule. ws: 16-byte aligned, not shared with a
+ * concurrent call. Same replacement as tbf16_attn_fwd (tbf16/attention.py:63-65,
+ * tbf16/autograd.py:159-164). */
+int64_t tbf16_attn_fwd_ws_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D, int causal);
+int tbf16_attn_fwd_ws(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                      int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev, const void* mask,
+                      int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh,
+                      int64_t out_ss, float* lse, int64_t lse_ld, void* o16, float dropout_p, uint64_t seed, void* ws,
+                      int64_t ws_bytes, void* stream);
+
 /* The backward of one rank's heads in a head-sharded call (no counterpart in the reference, whose
  * ScaledSDPAFn sees every head in one process): tbf16_attn_bwd_dropout with the dO exponent taken as
  * max(this rank's heads, *e_global), where e_global (device int32) is the all_reduce(MAX) over the ranks

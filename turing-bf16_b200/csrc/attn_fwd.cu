@@ -16,6 +16,10 @@
 //               sum, P -> fp16 into a 128B-swizzled K-major shared tile; epilogue O / l * 2^ev -> bf16.
 // TMEM: S0 [0,128), S1 [128,256), O [256, 256+D). Every mbarrier wait is bounded.
 #include <algorithm>
+#include <memory>
+#include <mutex>
+#include <queue>
+#include <vector>
 
 #include "common.cuh"
 
@@ -41,6 +45,7 @@ struct AttnFwdParams {
   float* lse;         // [B * Hq, lse_ld] natural-log logsumexp, nullable
   int64_t lse_ld;
   __half* o16;        // [B, Hq, Sq, D] fp16 O before the 2^ev scale (training), nullable
+  void* split_ws;     // key-split launches of the head-dim-256 kernel: tickets, flags, parts' O
   const uint16_t* mask;  // additive fp16 bias, nullable; element (b,h,i,j) at b*mb + h*mh + i*mi + j
   int64_t mb, mh, mi;
   unsigned int* err;
@@ -825,12 +830,48 @@ constexpr int BAR_OFF = V_OFF + 2 * VH_BYTES;
 constexpr int SMEM = 1024 + BAR_OFF + 256;
 static_assert(SMEM <= 227 * 1024, "shared memory");
 
-struct Item {
-  int bh, m0, n_kv;
+// Key-split launches. When the items are too few for the pairs (one 2048-token sequence of 8 heads is
+// 64 items on 74 pairs, and the last 256 rows' 16 key tiles set the kernel's time), the host cuts the
+// heaviest items into two parts over their key tiles and deals all parts to the pairs longest first
+// (LPT). Both parts of an item end with their own (O, running max, row sum) for the same rows; per 32-row
+// warp slot, whichever finishes first (a ticket in the workspace) writes its part there and raises a
+// flag, the second one waits for that flag, adds the two parts and writes the output. The first never
+// waits on anything but its own pair's MMAs, so the wait always ends.
+constexpr int kSchedPairs = 80;      // >= the pairs of a 148-SM device
+constexpr int kSchedEntries = 256;   // parts of one launch
+constexpr int kSplitItems = 128;     // split items of one launch
+constexpr int kSplitSlots = kSplitItems * 8;  // (item, CTA, softmax warp)
+constexpr int64_t kSplitHdrBytes = 2 * kSplitSlots * 4;  // tickets, then flags
+constexpr int kSlotFloats = 256 * 32 + 64;    // a warp's 32 rows x 256 dims of O, then 32 maxima, 32 sums
+template <bool SPLIT>
+struct Sched {
+  uint16_t start[kSchedPairs + 1];  // pair c runs e[start[c]] .. e[start[c + 1] - 1] in order
+  uint64_t e[kSchedEntries];        // bh | row pair << 16 | first key tile << 30 | key tiles << 43 | sid << 56
 };
-// The pair's r-th item (snake order over the gridDim.x / 2 pairs); false past the last one. Every role
-// of both CTAs walks the same sequence.
-__device__ __forceinline__ bool item_at(const AttnFwdParams& p, int r, Item& it) {
+template <>
+struct Sched<false> {
+  int unused;
+};
+
+struct Item {
+  int bh, m0, kb, n_kv, sid;  // key tiles kb .. kb + n_kv - 1; sid > 0: part of split item sid - 1
+};
+// The pair's r-th item; false past the last one. Every role of both CTAs walks the same sequence.
+// Without a schedule: snake order over the gridDim.x / 2 pairs.
+template <bool SPLIT>
+__device__ __forceinline__ bool item_at(const AttnFwdParams& p, const Sched<SPLIT>& sc, int r, Item& it) {
+  if constexpr (SPLIT) {
+    const int c = (int)(blockIdx.x >> 1);
+    const int k = sc.start[c] + r;
+    if (k >= sc.start[c + 1]) return false;
+    const uint64_t e = sc.e[k];
+    it.bh = (int)(e & 0xffffu);
+    it.m0 = (int)((e >> 16) & 0x3fffu) * 2 * ROWS;
+    it.kb = (int)((e >> 30) & 0x1fffu);
+    it.n_kv = (int)((e >> 43) & 0x1fffu);
+    it.sid = (int)(e >> 56);
+    return true;
+  }
   const int G = (int)(gridDim.x >> 1), c = (int)(blockIdx.x >> 1);
   const int pairs = (p.Sq + 2 * ROWS - 1) / (2 * ROWS);
   const int BHq = p.B * p.Hq;
@@ -846,15 +887,49 @@ __device__ __forceinline__ bool item_at(const AttnFwdParams& p, int r, Item& it)
   }
   it.m0 = pr * 2 * ROWS;
   const int kv_end = p.causal ? min(p.Sk, it.m0 + 2 * ROWS) : p.Sk;
+  it.kb = 0;
   it.n_kv = (kv_end + KEYS - 1) / KEYS;
+  it.sid = 0;
   return true;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+// Warp-wide bounded wait for a flag another CTA raises: lane 0 polls, then every lane takes its own
+// acquire so that its loads of the flagged data follow it.
+__device__ __forceinline__ bool flag_wait_warp(const int* f, volatile int* abort, unsigned int* err,
+                                               uint64_t timeout_ns = 2000000000ull) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0 && ld_acquire_gpu(f) == 0) {
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_gpu(f) == 0) {
+      if (*abort) { ok = false; break; }
+      if (global_timer_ns() - t0 > timeout_ns) {
+        atomicOr(err, kErrWaitTimeout);
+        *abort = 1;
+        ok = false;
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (ok) (void)ld_acquire_gpu(f);
+  return ok;
 }
 }  // namespace fwd256
 
-template <bool DROP>
+template <bool DROP, bool SPLIT>
 __global__ void __launch_bounds__(fwd256::THREADS, 1)
     attn_fwd_d256_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                              const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
+                              const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p,
+                              const __grid_constant__ fwd256::Sched<SPLIT> sched) {
   using namespace fwd256;
   constexpr int D = 256;
   extern __shared__ uint8_t smem_raw[];
@@ -907,7 +982,7 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
       int r = 0;
       bool ok = true;
       Item it;
-      for (; ok && item_at(p, r, it); ++r) {
+      for (; ok && item_at(p, sched, r, it); ++r) {
         const int bhk = (it.bh / p.Hq) * p.Hkv + (it.bh % p.Hq) / p.group;
         // the previous item's S MMAs have all completed before the Q tiles are overwritten
         if (r > 0 && !mbar_wait(q_empty, (r - 1) & 1, abort, p.err)) { ok = false; break; }
@@ -923,13 +998,13 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
 #pragma unroll
           for (int a = 0; a < 4; ++a)
             tma_load_3d_pair(smem + K_OFF + st * KH_BYTES + a * 8192, &tmK, &k_full[st], a * 64,
-                             j * KEYS + (int)rank * (KEYS / 2), bhk);
+                             (it.kb + j) * KEYS + (int)rank * (KEYS / 2), bhk);
           if (!mbar_wait(&v_empty[st], ph ^ 1, abort, p.err)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * VH_BYTES);
 #pragma unroll
           for (int a = 0; a < 2; ++a)
             tma_load_3d_pair(smem + V_OFF + st * VH_BYTES + a * 16384, &tmV, &v_full[st], (int)rank * 128 + a * 64,
-                             j * KEYS, bhk);
+                             (it.kb + j) * KEYS, bhk);
         }
       }
       // the even CTA's last releases of this CTA's Q tiles and ring stages have landed before the CTA
@@ -981,7 +1056,7 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
       uint32_t g = 0;  // steps (ring slots) issued so far (across items)
       bool ok = true;
       Item it;
-      for (int r = 0; ok && item_at(p, r, it); ++r) {
+      for (int r = 0; ok && item_at(p, sched, r, it); ++r) {
         const int n = it.n_kv;
         ok = mbar_wait(q_full, r & 1, abort, p.err) && issue_s(g) && (n < 2 || issue_s(g + 1));
         if (ok && n <= 2) umma_commit_pair(q_empty, 0x3);  // every S of the item issued
@@ -1001,7 +1076,7 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
     uint32_t g = 0;  // steps consumed so far (across items)
     bool ok = true;
     Item it;
-    for (int ri = 0; ok && item_at(p, ri, it); ++ri) {
+    for (int ri = 0; ok && item_at(p, sched, ri, it); ++ri) {
       const int bh = it.bh;
       const int b = bh / p.Hq, h = bh % p.Hq;
       const int bhk = b * p.Hkv + h / p.group;
@@ -1016,7 +1091,7 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
         if (!mbar_wait_warp(&s_full[sb], (gs >> 1) & 1, abort, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t s_addr = tmem + lane_base + sb * KEYS;
-        const int k0 = j * KEYS;
+        const int k0 = (it.kb + j) * KEYS;
         uint32_t rr[KEYS];
         float alpha = 1.f;
         bool rescale = false;
@@ -1111,31 +1186,129 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
       }
       if (!ok) break;
       g += n_kv;
+      // a split item's part takes its ticket once its last P is handed over, so the atomic's round trip
+      // overlaps the last P.V (which part is first only decides who writes and who adds)
+      const int slot = ((it.sid - 1) * 2 + (int)rank) * 4 + quad;
+      int ticket_v = 0;
+      if constexpr (SPLIT)
+        if (it.sid > 0 && lane == 0) ticket_v = atomicAdd(static_cast<int*>(p.split_ws) + slot, 1);
       // epilogue: O leaves TMEM here; the next item's first P.V overwrites it only after this warp's
       // next p_full arrival, which follows these loads
       if (!mbar_wait_warp(pv_done, (g - 1) & 1, abort, p.err)) { ok = false; break; }
       tc_fence_after();
+      float f_own = 1.f, f_oth = 0.f;  // weights of this part's O and of the other part's
+      const float4* oth = nullptr;     // the other part's O (a split item's second part to finish)
+      if constexpr (SPLIT) {
+        if (it.sid > 0) {
+          int* flag = static_cast<int*>(p.split_ws) + kSplitSlots + slot;
+          float* part =
+              reinterpret_cast<float*>(static_cast<uint8_t*>(p.split_ws) + kSplitHdrBytes) + (int64_t)slot * kSlotFloats;
+          const int t = __shfl_sync(0xffffffffu, ticket_v, 0);
+          if (t == 0) {
+            // first part to finish: O (groups of 4 dims, lanes fastest), then its max and sum, to the slot
+            float4* o4 = reinterpret_cast<float4*>(part);
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(o_addr + c * 32, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                __stcg(o4 + (c * 8 + q) * 32 + lane,
+                       make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
+                                   __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3])));
+            }
+            __stcg(part + D * 32 + lane, m_used);
+            __stcg(part + D * 32 + 32 + lane, l);
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) st_release_gpu(flag, 1);
+            continue;
+          }
+          if (!flag_wait_warp(flag, abort, p.err)) { ok = false; break; }
+          const float m2 = __ldcg(part + D * 32 + lane), l2 = __ldcg(part + D * 32 + 32 + lane);
+          const float mn = fmaxf(m_used, m2);
+          f_own = m_used == -INFINITY ? 0.f : ex2(m_used - mn);
+          f_oth = m2 == -INFINITY ? 0.f : ex2(m2 - mn);
+          // products and sum rounded separately (no FMA), so the result does not depend on which part
+          // finished first
+          l = __fadd_rn(__fmul_rn(l, f_own), __fmul_rn(l2, f_oth));
+          m_used = mn;
+          oth = reinterpret_cast<const float4*>(part);
+        }
+      }
       const float inv_l = l > 0.f ? (DROP ? p.inv_keep : 1.f) / l : 0.f;
       const float sc = exp2i(__ldg(p.ev + bhk));
       __nv_bfloat16* orow = p.out + (int64_t)b * p.osb + (int64_t)h * p.osh + (int64_t)min(qi, p.Sq - 1) * p.oss;
       __half* o16row = p.o16 ? p.o16 + ((int64_t)bh * p.Sq + min(qi, p.Sq - 1)) * D : nullptr;
+      // 8 output values of dims 8 gg .. of chunk c, normalised here: bf16 times 2^ev, and the fp16 copy
+      auto emit8 = [&](int c, int gg, float (&v)[8]) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] *= inv_l;
+        *reinterpret_cast<uint4*>(orow + c * 32 + gg * 8) =
+            make_uint4(pack_bf16(v[0] * sc, v[1] * sc), pack_bf16(v[2] * sc, v[3] * sc),
+                       pack_bf16(v[4] * sc, v[5] * sc), pack_bf16(v[6] * sc, v[7] * sc));
+        if (o16row)
+          *reinterpret_cast<uint4*>(o16row + c * 32 + gg * 8) = make_uint4(
+              pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
+      };
+      bool combined = false;
+      if constexpr (SPLIT) {
+        if (oth) {
+          // the other part's O added chunk by chunk; its loads run two chunks ahead of this loop's stores
+          // (a load cannot move past a store that may alias it, so loaded in place each group would be
+          // one L2 round trip)
+          constexpr int NC = D / 32;
+          float4 pa[8], pb[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            pa[q] = __ldcg(oth + q * 32 + lane);
+            pb[q] = __ldcg(oth + (8 + q) * 32 + lane);
+          }
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            float4 cur[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              cur[q] = (c & 1) ? pb[q] : pa[q];
+              if (c + 2 < NC) {
+                if (c & 1) pb[q] = __ldcg(oth + ((c + 2) * 8 + q) * 32 + lane);
+                else pa[q] = __ldcg(oth + ((c + 2) * 8 + q) * 32 + lane);
+              }
+            }
+            uint32_t o[32];
+            tmem_ld32(o_addr + c * 32, o);
+            tmem_ld_wait();
+            if (qi < p.Sq) {
+#pragma unroll
+              for (int gg = 0; gg < 4; ++gg) {
+                const float w[8] = {cur[2 * gg].x,     cur[2 * gg].y,     cur[2 * gg].z,     cur[2 * gg].w,
+                                    cur[2 * gg + 1].x, cur[2 * gg + 1].y, cur[2 * gg + 1].z, cur[2 * gg + 1].w};
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  v[e] = __fadd_rn(__fmul_rn(__uint_as_float(o[8 * gg + e]), f_own), __fmul_rn(w[e], f_oth));
+                emit8(c, gg, v);
+              }
+            }
+          }
+          combined = true;
+        }
+      }
+      if (!combined) {
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + c * 32, o);
-        tmem_ld_wait();
-        if (qi < p.Sq) {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_ld_wait();
+          if (qi < p.Sq) {
 #pragma unroll
-          for (int gg = 0; gg < 4; ++gg) {
-            float v[8];
+            for (int gg = 0; gg < 4; ++gg) {
+              float v[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(o[8 * gg + e]) * inv_l;
-            *reinterpret_cast<uint4*>(orow + c * 32 + gg * 8) =
-                make_uint4(pack_bf16(v[0] * sc, v[1] * sc), pack_bf16(v[2] * sc, v[3] * sc),
-                           pack_bf16(v[4] * sc, v[5] * sc), pack_bf16(v[6] * sc, v[7] * sc));
-            if (o16row)
-              *reinterpret_cast<uint4*>(o16row + c * 32 + gg * 8) = make_uint4(
-                  pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
+              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(o[8 * gg + e]);
+              emit8(c, gg, v);
+            }
           }
         }
       }
@@ -1157,8 +1330,142 @@ __global__ void __launch_bounds__(fwd256::THREADS, 1)
   }
 }
 
-template <bool DROP>
-int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm, cudaStream_t st) {
+// ---------------------------------------------------------------- key-split planning (host)
+// Cost of a part in key-tile steps of a pair (~2 us each at S = 1-4k): its tiles, plus kItemSteps for the
+// pipeline fill (~1.5 us) and the output write (~3.4 us) a part adds, plus kCombineSteps for the exchange
+// through the workspace (put on the second part: ~3.6 us to write a part's O, ~1.5 us more to add it).
+// Figures from a %globaltimer trace of the kernel; a split is taken when the estimate drops below
+// kSplitGain of the plain schedule's (measured: estimates of 0.59 / 0.62 / 0.76 ran 0.71 / 0.89 / 0.90 of
+// the plain time, 0.81 / 0.87 ran 1.07 / 1.02).
+constexpr double kItemSteps = 2.5, kCombineSteps = 2.0, kSplitGain = 0.78;
+
+struct SplitPlan {
+  bool split = false;
+  int pairs = 0;   // pairs in the grid
+  int splits = 0;  // split items
+  fwd256::Sched<true> sched;
+};
+
+struct SplitPart {
+  double w;
+  uint64_t e;
+};
+
+// Longest-processing-time list schedule of the parts on G pairs (parts sorted longest first, each to
+// the least-loaded pair, ties to the lower pair); returns the largest load, and each pair's parts in
+// order when `assign` is given.
+double lpt_schedule(std::vector<SplitPart>& parts, int G, std::vector<std::vector<int>>* assign) {
+  std::stable_sort(parts.begin(), parts.end(), [](const SplitPart& a, const SplitPart& b) { return a.w > b.w; });
+  using Load = std::pair<double, int>;
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int c = 0; c < G; ++c) heap.push({0.0, c});
+  double span = 0.0;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    Load ld = heap.top();
+    heap.pop();
+    ld.first += parts[i].w + kItemSteps;
+    span = std::max(span, ld.first);
+    if (assign) (*assign)[ld.second].push_back((int)i);
+    heap.push(ld);
+  }
+  return span;
+}
+
+uint64_t sched_entry(int64_t bh, int pr, int kb, int n, int sid) {
+  return (uint64_t)bh | (uint64_t)pr << 16 | (uint64_t)kb << 30 | (uint64_t)n << 43 | (uint64_t)sid << 56;
+}
+
+// The parts of every item when those longer than `target` steps are cut in two (the first part as long
+// as the target allows, the rest second); empty when the cut exceeds the schedule's limits.
+std::vector<SplitPart> split_parts(int64_t BHq, int rpairs, int Sk, bool causal, double target, int* splits) {
+  std::vector<SplitPart> parts;
+  *splits = 0;
+  for (int pr = 0; pr < rpairs; ++pr) {
+    const int kv_end = causal ? std::min(Sk, (pr + 1) * 2 * fwd256::ROWS) : Sk;
+    const int n = (kv_end + fwd256::KEYS - 1) / fwd256::KEYS;
+    for (int64_t bh = 0; bh < BHq; ++bh) {
+      if (target > 0 && n >= 2 && n + kItemSteps > target) {
+        const int a = std::max(1, std::min(n - 1, (int)(target - kItemSteps - kCombineSteps)));
+        const int sid = ++*splits;
+        if (sid > fwd256::kSplitItems) return {};
+        parts.push_back({(double)a, sched_entry(bh, pr, 0, a, sid)});
+        parts.push_back({(double)(n - a) + kCombineSteps, sched_entry(bh, pr, a, n - a, sid)});
+      } else {
+        parts.push_back({(double)n, sched_entry(bh, pr, 0, n, 0)});
+      }
+      if ((int)parts.size() > fwd256::kSchedEntries) return {};
+    }
+  }
+  return parts;
+}
+
+// Split plan for a head-dim-256 launch: cut items over their key tiles when the estimated schedule
+// length drops below kSplitGain of the plain one (few items for the pairs: short sequences, few heads).
+void plan_split(int64_t BHq, int Sq, int Sk, bool causal, int max_pairs, SplitPlan& plan) {
+  plan = SplitPlan{};
+  const int rpairs = (Sq + 2 * fwd256::ROWS - 1) / (2 * fwd256::ROWS);
+  const int n_max = (Sk + fwd256::KEYS - 1) / fwd256::KEYS;
+  if (BHq * rpairs > fwd256::kSchedEntries || n_max > 8191 || max_pairs > fwd256::kSchedPairs || max_pairs < 1) return;
+  int splits = 0;
+  std::vector<SplitPart> whole = split_parts(BHq, rpairs, Sk, causal, 0.0, &splits);
+  double total = 0.0;
+  for (const SplitPart& q : whole) total += q.w + kItemSteps;
+  const double base = lpt_schedule(whole, (int)std::min<int64_t>((int64_t)whole.size(), max_pairs), nullptr);
+  double best = base, best_target = 0.0;
+  const int lo = std::max(2, (int)(total / max_pairs)), hi = n_max + 2;
+  const int step = std::max(1, (hi - lo) / 48);
+  for (int t = lo; t <= hi; t += step) {
+    std::vector<SplitPart> parts = split_parts(BHq, rpairs, Sk, causal, (double)t, &splits);
+    if (parts.empty() || splits == 0) continue;
+    const double span = lpt_schedule(parts, (int)std::min<size_t>(parts.size(), (size_t)max_pairs), nullptr);
+    if (span < best) {
+      best = span;
+      best_target = t;
+    }
+  }
+  if (best_target == 0.0 || best > kSplitGain * base) return;
+  std::vector<SplitPart> parts = split_parts(BHq, rpairs, Sk, causal, best_target, &splits);
+  const int G = (int)std::min<size_t>(parts.size(), (size_t)max_pairs);
+  std::vector<std::vector<int>> assign(G);
+  lpt_schedule(parts, G, &assign);
+  int k = 0;
+  for (int c = 0; c < G; ++c) {
+    plan.sched.start[c] = (uint16_t)k;
+    for (int i : assign[c]) plan.sched.e[k++] = parts[i].e;
+  }
+  for (int c = G; c <= fwd256::kSchedPairs; ++c) plan.sched.start[c] = (uint16_t)k;
+  plan.split = true;
+  plan.pairs = G;
+  plan.splits = splits;
+}
+
+// Plans by shape, computed once each (a handful of shapes per model).
+std::shared_ptr<const SplitPlan> split_plan(int64_t BHq, int Sq, int Sk, bool causal, int max_pairs) {
+  struct Entry {
+    int64_t BHq;
+    int Sq, Sk, causal, max_pairs;
+    std::shared_ptr<const SplitPlan> plan;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : cache)
+    if (e.BHq == BHq && e.Sq == Sq && e.Sk == Sk && e.causal == (int)causal && e.max_pairs == max_pairs) return e.plan;
+  auto plan = std::make_shared<SplitPlan>();
+  plan_split(BHq, Sq, Sk, causal, max_pairs, *plan);
+  if (cache.size() >= 64) cache.erase(cache.begin());
+  cache.push_back({BHq, Sq, Sk, (int)causal, max_pairs, plan});
+  return plan;
+}
+
+int64_t split_ws_bytes(const SplitPlan& plan) {
+  return plan.split ? fwd256::kSplitHdrBytes + (int64_t)plan.splits * 8 * fwd256::kSlotFloats * 4 : 0;
+}
+
+// plan: a key-split schedule (prm.split_ws holds split_ws_bytes(*plan)), or null for the plain order.
+template <bool DROP, bool SPLIT>
+int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, const AttnFwdParams& prm,
+                         const SplitPlan* plan, cudaStream_t st) {
   const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
   if (!dev) return TBF16_ERR_DEVICE;
   CUtensorMap tq, tk, tv;
@@ -1168,7 +1475,7 @@ int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, cons
     return rc;
   if (int rc = tbf16_host::make_tmap_3d(&tv, v16, 256, prm.Sk, BHk, 256, (uint64_t)prm.Sk * 256, 64, fwd256::KEYS))
     return rc;
-  auto kern = attn_fwd_d256_pair_kernel<DROP>;
+  auto kern = attn_fwd_d256_pair_kernel<DROP, SPLIT>;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->device & 63]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd256::SMEM) != cudaSuccess)
@@ -1179,7 +1486,13 @@ int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, cons
   // the items
   const int64_t items = BHq * ((prm.Sq + 2 * fwd256::ROWS - 1) / (2 * fwd256::ROWS));
   if (items > INT32_MAX - dev->sms) return TBF16_ERR_INVALID;  // item indices are int
-  const int64_t pairs = std::min<int64_t>(items, dev->sms / 2);
+  const int64_t pairs = SPLIT ? plan->pairs : std::min<int64_t>(items, dev->sms / 2);
+  fwd256::Sched<SPLIT> sched{};
+  if constexpr (SPLIT) {
+    sched = plan->sched;
+    // tickets and flags start at zero every launch
+    if (cudaMemsetAsync(prm.split_ws, 0, fwd256::kSplitHdrBytes, st) != cudaSuccess) return tbf16_host::check_launch();
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(fwd256::THREADS);
@@ -1192,7 +1505,7 @@ int launch_fwd_d256_pair(const void* q16, const void* k16, const void* v16, cons
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, prm) != cudaSuccess) return tbf16_host::check_launch();
+  if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, prm, sched) != cudaSuccess) return tbf16_host::check_launch();
   return tbf16_host::check_launch();
 }
 
@@ -1206,11 +1519,17 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
                             Hq * Sq * D, Sq * D, D, lse, lse_ld, o16, stream);
 }
 
+// TBF16_ATTN_FWD=1 selects the one-tile kernels
+static bool attn_one_cta() {
+  const char* e = getenv("TBF16_ATTN_FWD");
+  return e && e[0] == '1';
+}
+
 static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
                          int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
                          const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out, int64_t out_sb,
                          int64_t out_sh, int64_t out_ss, float* lse, int64_t lse_ld, void* o16, float dropout_p,
-                         uint64_t seed, void* stream) {
+                         uint64_t seed, void* ws, int64_t ws_bytes, void* stream) {
   if (int st = tbf16_host::require_sm100()) return st;
   uint32_t thr = 0;
   float inv_keep = 1.f;
@@ -1240,6 +1559,7 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
   prm.lse_ld = lse_ld;
   if (lse && lse_ld < Sq) return TBF16_ERR_INVALID;
   prm.o16 = static_cast<__half*>(o16);
+  prm.split_ws = nullptr;
   prm.mask = static_cast<const uint16_t*>(mask);
   prm.mb = mask_sb; prm.mh = mask_sh; prm.mi = mask_sq;
   prm.err = dev->err;
@@ -1252,20 +1572,48 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
   auto st = static_cast<cudaStream_t>(stream);
   // D <= 128: the persistent two-query-tile kernel, D = 256: the CTA-pair kernel (P in TMEM in both);
   // TBF16_ATTN_FWD=1 selects the one-tile kernel
-  static const bool one_cta = [] {
-    const char* e = getenv("TBF16_ATTN_FWD");
-    return e && e[0] == '1';
-  }();
+  static const bool one_cta = attn_one_cta();
+  if (D == 256 && !one_cta && ws && ws_bytes > 0 && tbf16_host::aligned16(ws)) {
+    // a key-split schedule when the caller's workspace holds it (tbf16_attn_fwd_ws_size)
+    std::shared_ptr<const SplitPlan> plan = split_plan(B * Hq, (int)Sq, (int)Sk, causal != 0, dev->sms / 2);
+    if (plan->split && ws_bytes >= split_ws_bytes(*plan)) {
+      prm.split_ws = ws;
+      return drop ? launch_fwd_d256_pair<true, true>(q16, k16, v16, prm, plan.get(), st)
+                  : launch_fwd_d256_pair<false, true>(q16, k16, v16, prm, plan.get(), st);
+    }
+  }
   if (drop) {
     if (D == 64) return one_cta ? launch_fwd<64, true>(q16, k16, v16, prm, st) : launch_fwd_pp<64, true>(q16, k16, v16, prm, st);
     if (D == 128)
       return one_cta ? launch_fwd<128, true>(q16, k16, v16, prm, st) : launch_fwd_pp<128, true>(q16, k16, v16, prm, st);
-    return one_cta ? launch_fwd<256, true>(q16, k16, v16, prm, st) : launch_fwd_d256_pair<true>(q16, k16, v16, prm, st);
+    return one_cta ? launch_fwd<256, true>(q16, k16, v16, prm, st)
+                   : launch_fwd_d256_pair<true, false>(q16, k16, v16, prm, nullptr, st);
   }
   if (D == 64) return one_cta ? launch_fwd<64, false>(q16, k16, v16, prm, st) : launch_fwd_pp<64, false>(q16, k16, v16, prm, st);
   if (D == 128)
     return one_cta ? launch_fwd<128, false>(q16, k16, v16, prm, st) : launch_fwd_pp<128, false>(q16, k16, v16, prm, st);
-  return one_cta ? launch_fwd<256, false>(q16, k16, v16, prm, st) : launch_fwd_d256_pair<false>(q16, k16, v16, prm, st);
+  return one_cta ? launch_fwd<256, false>(q16, k16, v16, prm, st)
+                 : launch_fwd_d256_pair<false, false>(q16, k16, v16, prm, nullptr, st);
+}
+
+// Head-dim-256 forwards with few items for the pairs run a key-split schedule in a caller's workspace.
+extern "C" int64_t tbf16_attn_fwd_ws_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                                          int causal) {
+  if (D != 256 || B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Sq <= 0 || Sk <= 0 || B * Hq > 65535 ||
+      Sq > INT32_MAX || Sk > INT32_MAX || attn_one_cta())
+    return 0;
+  const tbf16_host::DeviceInfo* dev = tbf16_host::device_info();
+  if (!dev) return 0;
+  return split_ws_bytes(*split_plan(B * Hq, (int)Sq, (int)Sk, causal != 0, dev->sms / 2));
+}
+
+extern "C" int tbf16_attn_fwd_ws(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
+                                 int64_t Sq, int64_t Sk, int64_t D, float scale, int causal, const int32_t* ev,
+                                 const void* mask, int64_t mask_sb, int64_t mask_sh, int64_t mask_sq, void* out,
+                                 int64_t out_sb, int64_t out_sh, int64_t out_ss, float* lse, int64_t lse_ld, void* o16,
+                                 float dropout_p, uint64_t seed, void* ws, int64_t ws_bytes, void* stream) {
+  return attn_fwd_impl(q16, k16, v16, B, Hq, Hkv, Sq, Sk, D, scale, causal, ev, mask, mask_sb, mask_sh, mask_sq, out,
+                       out_sb, out_sh, out_ss, lse, lse_ld, o16, dropout_p, seed, ws, ws_bytes, stream);
 }
 
 extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,
@@ -1274,7 +1622,7 @@ extern "C" int tbf16_attn_fwd_out(const void* q16, const void* k16, const void* 
                                   int64_t mask_sq, void* out, int64_t out_sb, int64_t out_sh, int64_t out_ss,
                                   float* lse, int64_t lse_ld, void* o16, void* stream) {
   return attn_fwd_impl(q16, k16, v16, B, Hq, Hkv, Sq, Sk, D, scale, causal, ev, mask, mask_sb, mask_sh, mask_sq, out,
-                       out_sb, out_sh, out_ss, lse, lse_ld, o16, 0.f, 0, stream);
+                       out_sb, out_sh, out_ss, lse, lse_ld, o16, 0.f, 0, nullptr, 0, stream);
 }
 
 extern "C" int tbf16_attn_fwd_dropout(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq,
@@ -1284,7 +1632,7 @@ extern "C" int tbf16_attn_fwd_dropout(const void* q16, const void* k16, const vo
                                       float* lse, int64_t lse_ld, void* o16, float dropout_p, uint64_t seed,
                                       void* stream) {
   return attn_fwd_impl(q16, k16, v16, B, Hq, Hkv, Sq, Sk, D, scale, causal, ev, mask, mask_sb, mask_sh, mask_sq, out,
-                       out_sb, out_sh, out_ss, lse, lse_ld, o16, dropout_p, seed, stream);
+                       out_sb, out_sh, out_ss, lse, lse_ld, o16, dropout_p, seed, nullptr, 0, stream);
 }
 
 namespace {

@@ -67,6 +67,9 @@ SIGNATURES = {
                                _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp,
                                _vp, _vp, _i64, ctypes.c_float, ctypes.c_uint64, _vp],
     "tbf16_attn_dropout_keep": [_vp, _i64, _i64, _i64, ctypes.c_float, ctypes.c_uint64, _vp],
+    "tbf16_attn_fwd_ws": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _vp, _i64,
+                          _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, ctypes.c_float, ctypes.c_uint64, _vp,
+                          _i64, _vp],
     "tbf16_attn_bwd_sharded": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64,
                                _i64, _i64, _i64, ctypes.c_float, _i32, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp,
                                _vp, _vp, _i64, ctypes.c_float, ctypes.c_uint64, _vp, _vp],
@@ -78,6 +81,7 @@ SIGNATURES = {
 # entry points returning a size (int64) rather than a status
 SIGNATURES_I64 = {
     "tbf16_attn_bwd_workspace_size": [_i64, _i64, _i64, _i64, _i64, _i64],
+    "tbf16_attn_fwd_ws_size": [_i64, _i64, _i64, _i64, _i64, _i64, _i32],
 }
 
 BF16, F16 = 0, 1

@@ -13,7 +13,7 @@ import math
 
 import torch
 
-from ._ext import BF16, F16, call, ptr, require_cuda, stream_ptr
+from ._ext import BF16, F16, call, lib, ptr, require_cuda, stream_ptr
 
 _DTYPE = {torch.bfloat16: BF16, torch.float16: F16}
 KERNEL_D = (64, 128, 256)      # forward kernel head dims (others are zero-padded up)
@@ -112,11 +112,24 @@ def dropout_seed() -> int:
     return (hi << 32) | lo
 
 
+_FWD_WS = {}
+
+
+def _fwd_ws_size(B, Hq, Hkv, Sq, Sk, D, causal):
+    """Workspace bytes of the key-split head-dim-256 forward for this shape (0: plain schedule)."""
+    key = (B, Hq, Hkv, Sq, Sk, D, causal, torch.cuda.current_device())
+    n = _FWD_WS.get(key)
+    if n is None:
+        n = _FWD_WS[key] = int(lib().tbf16_attn_fwd_ws_size(B, Hq, Hkv, Sq, Sk, D, int(causal))) if D == 256 else 0
+    return n
+
+
 def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None, d_orig=None, need_lse=False,
                  need_o16=False, dropout_p=0.0, seed=0):
     """The tcgen05 forward on prepared fp16 operands -> (bf16 out (B, Hq, Sq, D), lse or None), plus the
     fp16 pre-scale output o16 when need_o16 (then the return is (out, lse, o16), all at the kernel's D).
-    dropout_p > 0 drops softmax weights by the mask `seed` selects (tbf16_attn_fwd_dropout)."""
+    dropout_p > 0 drops softmax weights by the mask `seed` selects. Head dim 256 with few query blocks for
+    the GPU runs the key-split schedule in a workspace from torch's allocator (tbf16_attn_fwd_ws)."""
     B, Hq, Sq, D = q16.shape
     Hkv, Sk = k16.shape[1], k16.shape[2]
     d_orig = d_orig or D
@@ -140,10 +153,10 @@ def attn_forward(q16, k16, v16, ev, attn_mask=None, is_causal=False, scale=None,
     ms = m.stride()[:3] if m is not None else (0, 0, 0)
     args = (ptr(q16), ptr(k16), ptr(v16), B, Hq, Hkv, Sq, Sk, Dk, sc, int(bool(is_causal)), ptr(ev.contiguous()), ptr(m),
             *ms, ptr(out), *out.stride()[:3], ptr(lse), lse_ld, ptr(o16))
-    if dropout_p:
-        call("tbf16_attn_fwd_dropout", *args, float(dropout_p), int(seed), stream_ptr(dev))
-    else:
-        call("tbf16_attn_fwd_out", *args, stream_ptr(dev))
+    ws_bytes = _fwd_ws_size(B, Hq, Hkv, Sq, Sk, Dk, bool(is_causal))
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+    call("tbf16_attn_fwd_ws", *args, float(dropout_p), int(seed) if dropout_p else 0, ptr(ws), ws_bytes,
+         stream_ptr(dev))
     if need_o16:
         return out, lse, o16
     if Dk != D:
