@@ -863,6 +863,44 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
                         "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
             res["d256"]["by_S"][S2] = row
             del q, k, v, q16, k16, v16
+        # few 256-row query blocks for the 74 CTA pairs (one sequence, few heads: the Gemma prefill's
+        # attention first): the key-split schedule attn_forward takes against the plain one
+        from tbf16 import _ext
+        res["d256_few_blocks"] = {"what": "attn_forward (key-split schedule, workspace from torch's allocator) "
+                                          "against tbf16_attn_fwd_out (plain schedule), causal, kernel only (CUDA graph of 10 calls)"}
+        for (Hq, Hk, S2) in ((8, 4, 2048), (4, 4, 4096), (1, 1, 8192)):
+            q, k, v = inputs.attention_qkv(1, Hq, S2, 256, seed=0, device="cuda", Hkv=Hk, qk_exp=4)
+            q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
+            plain_out = torch.empty(1, Hq, S2, 256, device="cuda", dtype=torch.bfloat16)
+            flop = 4.0 * Hq * S2 * S2 * 256 * 0.5
+            row = {"ws_bytes": attention._fwd_ws_size(1, Hq, Hk, S2, S2, 256, True)}
+            plain = lambda: _ext.call("tbf16_attn_fwd_out", _ext.ptr(q16), _ext.ptr(k16), _ext.ptr(v16), 1, Hq, Hk, S2,
+                                      S2, 256, 1.0 / 16.0, 1, _ext.ptr(ev), None, 0, 0, 0, _ext.ptr(plain_out),
+                                      *plain_out.stride()[:3], None, 0, None, _ext.stream_ptr(q.device))
+            for name, fn in (("split", lambda: attention.attn_forward(q16, k16, v16, ev, is_causal=True)),
+                             ("plain", plain)):
+                # ten calls captured in a CUDA graph: the eager loop would time the host's launch path
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(10):
+                        fn()
+                g.replay()
+                torch.cuda.synchronize()
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                for _ in range(max(iters, 3)):
+                    g.replay()
+                s1.record()
+                torch.cuda.synchronize()
+                t = s0.elapsed_time(s1) / (10 * max(iters, 3))
+                del g
+                row[name] = {"us": round(t * 1e3, 1), "tflops": round(flop / (t / 1e3) / 1e12, 1),
+                             "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
+            res["d256_few_blocks"][f"H{Hq}/{Hk} S{S2}"] = row
+            del q, k, v, q16, k16, v16, plain_out
     q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda")
     for causal in (False, True):
         flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)
