@@ -228,6 +228,8 @@ def main():
     ap.add_argument("--attn-S", type=int, default=16384)
     ap.add_argument("--attn-D", type=int, default=128, help="with --only-attention: head dim (64, 128, 256)")
     ap.add_argument("--attn-train", action="store_true", help="with --only-attention: also time fwd+bwd (config 4)")
+    ap.add_argument("--attn-H", type=int, default=16, help="with --only-attention: query heads")
+    ap.add_argument("--attn-Hkv", type=int, default=0, help="with --only-attention: key/value heads (GQA; 0: --attn-H)")
     ap.add_argument("--sweep", action="store_true",
                     help="config-2 GEMM sweep (M = 1 .. 16384 at N = K = 4096 and 8192, L2 flushed) and the "
                          "config-4 MLP linears fwd+bwd; prints one JSON line and exits")
@@ -252,8 +254,9 @@ def main():
               "l2": "inputs larger than L2 (384 MB per step)"}
 
     if args.only_attention:
-        print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, D=args.attn_D, iters=max(1, args.steps),
-                                                     train=args.attn_train)}))
+        print(json.dumps({"attention": attention_run(peaks(), S=args.attn_S, H=args.attn_H, D=args.attn_D,
+                                                     iters=max(1, args.steps), train=args.attn_train,
+                                                     Hkv=args.attn_Hkv or args.attn_H)}))
         return
     if args.only_prefill:
         print(json.dumps({"prefill": prefill_run(world)}))
@@ -803,12 +806,13 @@ def train_linear_run(pk, iters=9):
                       "what": "autograd.glu_linear: SiLU(gate) * up fused into the down linear's row pass and its backward"}}
 
 
-def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
+def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True, Hkv=None):
     """Config 3 (B=1, H=16, D=128, S=16k, Q/K overflow fp16): the scaled attention forward (prepare_qkv
     + tcgen05 flash attention) in TFLOPS, causal and not; kernel-only time against the bf16 peak."""
     import inputs
     from tbf16 import attention
-    res = {"config": f"B=1 H={H} S={S} D={D}, Q,K x2^8, V x2^h"}
+    Hkv = Hkv or H
+    res = {"config": f"B=1 H={H} Hkv={Hkv} S={S} D={D}, Q,K x2^8, V x2^h"}
     if S == 16384 and D == 128:  # config 3's other lengths, and torch's native bf16 SDPA (informational)
         res["by_S"] = {}
         for S2 in (4096, 8192, 16384):
@@ -901,17 +905,17 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True):
                              "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
             res["d256_few_blocks"][f"H{Hq}/{Hk} S{S2}"] = row
             del q, k, v, q16, k16, v16, plain_out
-    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda")
+    q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda", Hkv=Hkv)
     for causal in (False, True):
         flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)
         q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
         for _ in range(2):
-            attention.sdpa(q, k, v, is_causal=causal)
+            attention.sdpa(q, k, v, is_causal=causal, enable_gqa=Hkv != H)
         torch.cuda.synchronize()
         s0, s1, s2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         s0.record()
         for _ in range(iters):
-            attention.sdpa(q, k, v, is_causal=causal)
+            attention.sdpa(q, k, v, is_causal=causal, enable_gqa=Hkv != H)
         s1.record()
         for _ in range(iters):
             attention.attn_forward(q16, k16, v16, ev, is_causal=causal)
