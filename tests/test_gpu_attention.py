@@ -37,7 +37,11 @@ def _check_out(out, q, k, v, causal, mask=None, scale=None, v_exp=13):
 
 @pytest.mark.parametrize("B,H,Hkv,S,D,causal", [(1, 2, 2, 128, 64, False), (1, 2, 2, 256, 128, True),
                                                 (2, 4, 2, 200, 128, False), (1, 4, 1, 333, 64, True),
-                                                (1, 16, 16, 1024, 128, True), (2, 2, 2, 96, 128, True)])
+                                                (1, 16, 16, 1024, 128, True), (2, 2, 2, 96, 128, True),
+                                                # more 256-row items than SMs: the persistent two-tile kernel
+                                                # (fewer go to the one-tile kernel), ragged lengths included
+                                                (4, 40, 8, 333, 128, True), (3, 64, 64, 200, 64, False),
+                                                (2, 48, 16, 520, 128, False)])
 def test_sdpa_forward_vs_oracle(B, H, Hkv, S, D, causal):
     from tbf16 import attention
     q, k, v = inputs.attention_qkv(B, H, S, D, seed=S + H, Hkv=Hkv)  # raw logits overflow fp16

@@ -1573,6 +1573,11 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
   // D <= 128: the persistent two-query-tile kernel, D = 256: the CTA-pair kernel (P in TMEM in both);
   // TBF16_ATTN_FWD=1 selects the one-tile kernel
   static const bool one_cta = attn_one_cta();
+  // D <= 128 with no more two-tile items (256 query rows) than SMs: the two-tile kernel would leave SMs
+  // idle, and the one-tile kernel's twice as many CTAs win (graph-timed, causal, D = 128, 2048 tokens:
+  // 64 items 31.6 against 46.3 us, 96 items 33.1 against 48.4, 128 items 36.3 against 48.0; from 192
+  // items, 1.3 waves, the two-tile kernel is faster: 49.4 against 57.4)
+  const bool one = one_cta || (D <= 128 && (int64_t)B * Hq * ((Sq + 2 * BM - 1) / (2 * BM)) <= dev->sms);
   if (D == 256 && !one_cta && ws && ws_bytes > 0 && tbf16_host::aligned16(ws)) {
     // a key-split schedule when the caller's workspace holds it (tbf16_attn_fwd_ws_size)
     std::shared_ptr<const SplitPlan> plan = split_plan(B * Hq, (int)Sq, (int)Sk, causal != 0, dev->sms / 2);
@@ -1583,15 +1588,15 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
     }
   }
   if (drop) {
-    if (D == 64) return one_cta ? launch_fwd<64, true>(q16, k16, v16, prm, st) : launch_fwd_pp<64, true>(q16, k16, v16, prm, st);
+    if (D == 64) return one ? launch_fwd<64, true>(q16, k16, v16, prm, st) : launch_fwd_pp<64, true>(q16, k16, v16, prm, st);
     if (D == 128)
-      return one_cta ? launch_fwd<128, true>(q16, k16, v16, prm, st) : launch_fwd_pp<128, true>(q16, k16, v16, prm, st);
+      return one ? launch_fwd<128, true>(q16, k16, v16, prm, st) : launch_fwd_pp<128, true>(q16, k16, v16, prm, st);
     return one_cta ? launch_fwd<256, true>(q16, k16, v16, prm, st)
                    : launch_fwd_d256_pair<true, false>(q16, k16, v16, prm, nullptr, st);
   }
-  if (D == 64) return one_cta ? launch_fwd<64, false>(q16, k16, v16, prm, st) : launch_fwd_pp<64, false>(q16, k16, v16, prm, st);
+  if (D == 64) return one ? launch_fwd<64, false>(q16, k16, v16, prm, st) : launch_fwd_pp<64, false>(q16, k16, v16, prm, st);
   if (D == 128)
-    return one_cta ? launch_fwd<128, false>(q16, k16, v16, prm, st) : launch_fwd_pp<128, false>(q16, k16, v16, prm, st);
+    return one ? launch_fwd<128, false>(q16, k16, v16, prm, st) : launch_fwd_pp<128, false>(q16, k16, v16, prm, st);
   return one_cta ? launch_fwd<256, false>(q16, k16, v16, prm, st)
                  : launch_fwd_d256_pair<false, false>(q16, k16, v16, prm, nullptr, st);
 }
