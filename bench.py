@@ -905,6 +905,36 @@ def attention_run(pk, S=16384, H=16, D=128, iters=5, train=True, Hkv=None):
                              "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
             res["d256_few_blocks"][f"H{Hq}/{Hk} S{S2}"] = row
             del q, k, v, q16, k16, v16, plain_out
+        # head dims <= 128 with few 256-row items: the one-tile kernel unless TBF16_ATTN_FWD=2 forces the
+        # persistent two-tile kernel (run both ways to compare)
+        res["d128_few_blocks"] = {"kernel": "two-tile (forced)" if os.environ.get("TBF16_ATTN_FWD") == "2" else
+                                  "by shape: one-tile when 256-row items <= SMs",
+                                  "what": "attn_forward, causal, D=128, CUDA graph of 10 calls"}
+        for (Hq, S2) in ((8, 2048), (16, 2048), (2, 8192), (32, 2048)):
+            q, k, v = inputs.attention_qkv(1, Hq, S2, 128, seed=0, device="cuda", qk_exp=4)
+            q16, k16, v16, a, ev = attention.prepare_qkv(q, k, v, v_exp=13)
+            fn = lambda: attention.attn_forward(q16, k16, v16, ev, is_causal=True)
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(10):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for _ in range(max(iters, 3)):
+                g.replay()
+            s1.record()
+            torch.cuda.synchronize()
+            t = s0.elapsed_time(s1) / (10 * max(iters, 3))
+            flop = 4.0 * Hq * S2 * S2 * 128 * 0.5
+            res["d128_few_blocks"][f"H{Hq} S{S2} items {Hq * ((S2 + 255) // 256)}"] = {
+                "us": round(t * 1e3, 1), "tflops": round(flop / (t / 1e3) / 1e12, 1),
+                "frac": round(flop / (t / 1e3) / 1e12 / pk["tflops"], 4)}
+            del g, q, k, v, q16, k16, v16
     q, k, v = inputs.attention_qkv(1, H, S, D, seed=0, device="cuda", Hkv=Hkv)
     for causal in (False, True):
         flop = 4.0 * H * S * S * D * (0.5 if causal else 1.0)

@@ -1519,10 +1519,14 @@ extern "C" int tbf16_attn_fwd(const void* q16, const void* k16, const void* v16,
                             Hq * Sq * D, Sq * D, D, lse, lse_ld, o16, stream);
 }
 
-// TBF16_ATTN_FWD=1 selects the one-tile kernels
+// TBF16_ATTN_FWD=1 selects the one-tile kernels, =2 the two-tile / CTA-pair kernels whatever the shape
 static bool attn_one_cta() {
   const char* e = getenv("TBF16_ATTN_FWD");
   return e && e[0] == '1';
+}
+static bool attn_multi_tile() {
+  const char* e = getenv("TBF16_ATTN_FWD");
+  return e && e[0] == '2';
 }
 
 static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int64_t B, int64_t Hq, int64_t Hkv,
@@ -1577,7 +1581,8 @@ static int attn_fwd_impl(const void* q16, const void* k16, const void* v16, int6
   // idle, and the one-tile kernel's twice as many CTAs win (graph-timed, causal, D = 128, 2048 tokens:
   // 64 items 31.6 against 46.3 us, 96 items 33.1 against 48.4, 128 items 36.3 against 48.0; from 192
   // items, 1.3 waves, the two-tile kernel is faster: 49.4 against 57.4)
-  const bool one = one_cta || (D <= 128 && (int64_t)B * Hq * ((Sq + 2 * BM - 1) / (2 * BM)) <= dev->sms);
+  static const bool multi = attn_multi_tile();
+  const bool one = one_cta || (!multi && D <= 128 && (int64_t)B * Hq * ((Sq + 2 * BM - 1) / (2 * BM)) <= dev->sms);
   if (D == 256 && !one_cta && ws && ws_bytes > 0 && tbf16_host::aligned16(ws)) {
     // a key-split schedule when the caller's workspace holds it (tbf16_attn_fwd_ws_size)
     std::shared_ptr<const SplitPlan> plan = split_plan(B * Hq, (int)Sq, (int)Sk, causal != 0, dev->sms / 2);
